@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""Benchmark of the GDN decode hot path (config 4 at N=8).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1).  A step is one decode of one token for
+every (sequence, v-head) of the rank's batch: B=256 sequences per rank, Hq=16,
+Hv=32, d=128, fp32 state in the k-last layout.  Scaling is weak: each rank owns
+its own 256 sequences and their states (sharding by sequence, no collective on
+the data path), so at N=8 the job is BASELINE config 4 (B=2048).
+
+Metric: decode state-stream throughput in GB/s, counted with the algorithmic
+131,844 bytes per (sequence, v-head) per step (2 x 64 KiB state + q/k share + v +
+o + gates), summed over ranks and divided by the max-over-ranks device time of
+the K timed steps.  ``ms_per_step`` is that time per step; ``decode_us_per_step``
+the same in microseconds.  The state ping-pongs between two 512 MiB buffers per
+rank, larger than the 126 MB L2, so no step reads a cached state.
+
+Extra keys: ``roofline`` (dominant kernel vs the measured HBM copy peak),
+``cpu_baseline`` (the C restatement of the reference recurrence on the host
+cores, rank 0 at N=1), ``e2e`` (the public ``gdn_b200.decode.run`` call with
+per-step inputs copied from pinned host memory and the output read back),
+``clocks`` (SM clocks sampled through NVML during the timed region), and
+``prefill`` (chunked prefill tokens/s on BASELINE config 3's shape, heads
+sharded over ranks).
+
+``--impl reference`` times the reference's CPU implementation of the same
+step (the C restatement of definitions/gdn/gdn_decode_qk4_v8_d128_k_last.md:61-133
+in oracle/gdn_oracle.c, all host threads) on rank 0 and prints the same line
+with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "mlsys-flashlinfer-contest_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+HQ, HV, D = 16, 32, 128
+B_PER_RANK = 256
+UNIT_BYTES = 2 * D * D * 4 + D * 2 + D * 2 + D * 2 + 4  # 131,844 B per (seq, v-head)
+METRIC = "gdn_decode_state_GBps"
+UNIT = "GB/s"
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Polls SM clock, max clock and clock-event reasons through NVML."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons = [], 0
+        self.period = period_s
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            idx = device_index
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if vis:
+                parts = [p.strip() for p in vis.split(",") if p.strip()]
+                if device_index < len(parts) and parts[device_index].isdigit():
+                    idx = int(parts[device_index])
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # pragma: no cover - depends on the box
+            self.err = repr(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                self.reasons |= int(r)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "nvml unavailable"}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- helpers
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1590.0)), \
+                float(d.get("bf16_tflops_sustained", 1400.0)), "measured"
+        except Exception:
+            pass
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profiled_traffic(name: str):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>),
+    a line 'dram_bytes_per_launch: <int>'."""
+    p = REPO / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].split()[0]))
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_count_info():
+    n = os.cpu_count() or 1
+    model = ""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return n, model
+
+
+def time_cpu_decode(budget_s: float = 10.0, max_steps: int = 400):
+    """The C restatement of the reference decode on the host cores, on the same
+    B=256 x Hv=32 workload; repeats full steps until the budget is spent."""
+    from oracle import c_oracle
+    from gdn_b200 import workloads as W
+    inp = W.make_decode_inputs(B_PER_RANK, HQ, HV, seed=1234)
+    nthreads = c_oracle.max_threads()
+    out = torch.empty_like(inp.v)
+    ns = torch.empty_like(inp.state)
+    args = list(inp.args())
+    c_oracle.decode(*args, nthreads=nthreads, out=out, new_state=ns)  # warm-up
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        c_oracle.decode(*args, nthreads=nthreads, out=out, new_state=ns)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or steps >= max_steps:
+            break
+    per_step = el / steps
+    value = B_PER_RANK * HV * UNIT_BYTES / per_step / 1e9
+    n, model = cpu_count_info()
+    return {"value": round(value, 3), "unit": UNIT, "cores": nthreads, "kind": "port",
+            "sample": f"{steps} full decode steps (B={B_PER_RANK}, Hv={HV}) of the C restatement "
+                      f"in oracle/gdn_oracle.c, {el:.2f} s, {nthreads} threads on {n} cpus "
+                      f"({model})",
+            "s_per_step": per_step}
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank, dist):
+    from gdn_b200 import decode, workloads as W
+    from gdn_b200 import _native as NAT
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L = NAT.lib()
+    inp = W.make_decode_inputs(B_PER_RANK, HQ, HV, seed=1000 + rank, device=dev)
+    s0 = inp.state
+    s1 = torch.empty_like(s0)
+    out = torch.empty_like(inp.v)
+    stream = torch.cuda.current_stream(dev)
+    sh = NAT.stream_handle(dev)
+    P = NAT.ptr
+    scale = float(inp.scale)
+    fixed = [P(inp.q), P(inp.k), P(inp.v)]
+    gates = [P(inp.A_log), P(inp.a), P(inp.dt_bias), P(inp.b)]
+
+    def step(src, dst):
+        rc = L.gdn_decode(fixed[0], fixed[1], fixed[2], P(src), gates[0], gates[1], gates[2],
+                          gates[3], scale, P(out), P(dst), B_PER_RANK, HQ, HQ, HV, D, sh)
+        if rc:
+            NAT.check(rc, "gdn_decode")
+
+    bufs = (s0, s1)
+    for i in range(args.warmup):
+        step(bufs[i % 2], bufs[(i + 1) % 2])
+    torch.cuda.synchronize()
+
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    sampler = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            step(bufs[i % 2], bufs[(i + 1) % 2])
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    total_ms = evs[0].elapsed_time(evs[-1])
+    per_launch = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    bytes_per_step_rank = B_PER_RANK * HV * UNIT_BYTES
+    value = bytes_per_step_rank * world * args.steps / (max_ms / 1e3) / 1e9
+    ms_per_step = max_ms / args.steps
+    launch_ms = statistics.mean(per_launch)
+    hbm_peak, _, _, peak_src = measured_peaks()
+    achieved = bytes_per_step_rank / (launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "gdn_decode_kernel<4,true>", "achieved": round(achieved, 1),
+                "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, copy)" if peak_src == "measured" else peak_src,
+                "algorithmic_bytes_per_launch": bytes_per_step_rank,
+                "launch_ms": round(launch_ms, 5),
+                "traffic": profiled_traffic("gdn_decode_b256.md")}
+
+    # ---- end to end through the public API: per-step q/k/v/a/b from pinned
+    # host memory, output read back to pinned host memory; the state stays
+    # resident in HBM across steps (the decode state cache).
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, inp, dev, stream, dist, world)
+
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill_bench(args, rank, world, local_rank, dev, dist)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = time_cpu_decode(args.cpu_budget)
+        cpu.pop("s_per_step", None)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "decode_us_per_step": round(ms_per_step * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE config distributions)",
+            "config": {"workload": "GDN decode, BASELINE config 1 per rank (B=256, T=1, Hq=Hk=16, "
+                                   "Hv=32, d=128, fp32 k-last state); N ranks = B=256*N "
+                                   "(N=8 is config 4)",
+                       "batch_per_rank": B_PER_RANK, "global_batch": B_PER_RANK * world,
+                       "num_q_heads": HQ, "num_v_heads": HV, "head_size": D,
+                       "parallelism": f"dp{world} (sequence shards, no collective)",
+                       "l2": "inputs larger than L2: 512 MiB state per rank, ping-pong buffers"},
+            "gpu_launches": args.steps,
+            "roofline": roofline,
+            "clocks": sampler.summary(),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "prefill": prefill,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, inp, dev, stream, dist, world):
+    from gdn_b200 import decode
+    host = {}
+    for name in ("q", "k", "v", "a", "b"):
+        t = getattr(inp, name)
+        host[name] = torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t.cpu())
+    o_host = torch.empty(inp.v.shape, dtype=torch.bfloat16, pin_memory=True)
+    state = inp.state.clone()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = o_host.numel() * o_host.element_size()
+    steps = max(args.steps // 4, 10)
+
+    def one(state):
+        d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
+        o, ns = decode.run(d["q"], d["k"], d["v"], state, inp.A_log, d["a"], inp.dt_bias, d["b"],
+                           inp.scale)
+        o_host.copy_(o, non_blocking=True)
+        return ns
+
+    for _ in range(3):
+        state = one(state)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        state = one(state)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = B_PER_RANK * HV * UNIT_BYTES * world * steps / (ms / 1e3) / 1e9
+    return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps, "us_per_step": round(ms / steps * 1e3, 2),
+            "api": "gdn_b200.decode.run", "state": "resident in HBM across steps"}
+
+
+def run_prefill_bench(args, rank, world, local_rank, dev, dist):
+    """Prefill tokens/s on BASELINE config 3's shape (4 x 16384 tokens), v-heads
+    sharded over ranks (Hv/N per rank, with the matching qk-heads)."""
+    from gdn_b200 import prefill, workloads as W
+    if HV % world or HQ % world:
+        return None
+    hv, hq = HV // world, HQ // world
+    lengths = [args.prefill_len] * args.prefill_seqs
+    inp = W.make_prefill_inputs(lengths, hq, hv, seed=77 + rank, device=dev)
+    T = sum(lengths)
+    out = torch.empty_like(inp.v)
+    ns = torch.empty_like(inp.state)
+    fn = prefill.launch
+
+    def once():
+        fn(*inp.args(), out, ns)
+
+    once()
+    torch.cuda.synchronize()
+    reps = args.prefill_steps
+    stream = torch.cuda.current_stream(dev)
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        once()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    res = {"metric": "gdn_prefill_tokens_per_s", "value": round(T / (ms / 1e3), 1),
+           "unit": "tokens/s", "ms_per_call": round(ms, 4), "steps": reps,
+           "workload": f"{args.prefill_seqs} x {args.prefill_len} tokens, Hq={HQ}, Hv={HV} "
+                       f"({hv} v-heads per rank)", "path": "gdn_b200.prefill.launch"}
+    return res
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    cpu = time_cpu_decode(args.cpu_budget)
+    per_step = cpu.pop("s_per_step")
+    line = {
+        "metric": METRIC, "value": cpu["value"], "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
+        "decode_us_per_step": round(per_step * 1e6, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE config distributions)",
+        "config": {"workload": "GDN decode, BASELINE config 1 (B=256, T=1, Hq=Hk=16, Hv=32, "
+                               "d=128); rank 0 only", "batch_per_rank": B_PER_RANK,
+                   "global_batch": B_PER_RANK, "num_q_heads": HQ, "num_v_heads": HV,
+                   "head_size": D, "parallelism": "host cpu threads"},
+        "impl": "reference",
+        "cpu_baseline": cpu,
+        "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--batch-per-rank", type=int, default=B_PER_RANK,
+                    help="sequences per rank (default 256 = BASELINE config 1; smaller only for profiling)")
+    ap.add_argument("--prefill-seqs", type=int, default=4)
+    ap.add_argument("--prefill-len", type=int, default=16384)
+    ap.add_argument("--prefill-steps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    global B_PER_RANK
+    B_PER_RANK = args.batch_per_rank
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local_rank))
+        dist = tdist
+    try:
+        run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,127 @@
+/*
+ * gdn_b200 -- C ABI of the B200 (sm_100a) Gated DeltaNet decode / prefill kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream handle
+ * (a cudaStream_t passed as void*; NULL = the legacy default stream).  Nothing
+ * is allocated, freed or synchronised inside a call: the caller owns every
+ * buffer, including the prefill workspace, and the call returns as soon as the
+ * kernels are enqueued.  Tensors are dense and contiguous in the layouts of the
+ * reference definitions (definitions/gdn/gdn_decode_qk4_v8_d128_k_last.md,
+ * definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md):
+ *
+ *   bf16 tensors are passed as `const void *` holding IEEE bfloat16 values;
+ *   head_size must be 128; num_k_heads == num_q_heads;
+ *   num_v_heads % num_q_heads == 0 (GVA: v-head h reads q/k head h / (Hv/Hq));
+ *   the recurrent state is fp32 in the k-last layout [.., Hv, V=128, K=128].
+ *
+ * Return value: GDN_OK, or an error code whose message is available from
+ * gdn_last_error() (thread-local).  The codes map onto the exception types of
+ * the reference's TVM-FFI checks (gdn_decode/solution/python/gdn_decode_utils.h:16-122):
+ * GDN_ERR_VALUE -> ValueError, GDN_ERR_TYPE -> TypeError, GDN_ERR_CUDA -> RuntimeError.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_ABI_VERSION 1
+
+enum gdn_status {
+  GDN_OK = 0,
+  GDN_ERR_VALUE = 1,   /* bad size, count, pointer or alignment */
+  GDN_ERR_TYPE = 2,    /* reserved for dtype errors raised by bindings */
+  GDN_ERR_CUDA = 3,    /* a CUDA launch or runtime call failed */
+};
+
+/* ABI version of the loaded library (GDN_ABI_VERSION). */
+int gdn_abi_version(void);
+
+/* Message of the last failed call on this thread ("" after a success). */
+const char *gdn_last_error(void);
+
+/*
+ * Decode one token per sequence.
+ * Replaces the reference's decode FFI entry points
+ *   gdn_decode_small_batch  (gdn_decode/solution/python/gdn_decode_small_batch.cu:194-232)
+ *   large_batch run         (gdn_decode/solution/python/gdn_decode_kernel_large_batch.py:343-406)
+ * behind the solution entry gdn_decode/solution/python/gdn_decode_final.py:23-36.
+ *
+ *   q, k      [B, 1, Hq, 128] bf16         v        [B, 1, Hv, 128] bf16
+ *   state     [B, Hv, 128, 128] fp32 or NULL (= zero initial state)
+ *   A_log, dt_bias [Hv] fp32               a, b     [B, 1, Hv] bf16
+ *   scale     0 selects 1/sqrt(128)
+ *   output    [B, 1, Hv, 128] bf16         new_state [B, Hv, 128, 128] fp32
+ * new_state may equal state (in-place update); any other overlap is rejected.
+ * q, k need 8-byte alignment, state and new_state 16-byte alignment.
+ */
+int gdn_decode(const void *q, const void *k, const void *v, const float *state,
+               const float *A_log, const void *a, const float *dt_bias, const void *b,
+               float scale, void *output, float *new_state, int64_t batch_size,
+               int64_t num_q_heads, int64_t num_k_heads, int64_t num_v_heads,
+               int64_t head_size, void *stream);
+
+/*
+ * Prefill packed variable-length sequences.
+ * Replaces the solution entry gdn_prefill/solution/python/gdn_prefill_mix.py:13-38
+ * and the FFI calls it makes: gdn_prefill_recurrent_v1 (cuda_recurrent_v1.cu:232-277)
+ * for tiny inputs, else the chunked pipeline of chunk_v12.py:36-116 (prep_meta_v2,
+ * kkt_inv_uw_v1, h_v2b, o_v1).
+ *
+ *   q, k      [T, Hq, 128] bf16            v        [T, Hv, 128] bf16
+ *   state     [N, Hv, 128, 128] fp32 or NULL (= zero initial states)
+ *   a, b      [T, Hv] bf16                 cu_seqlens [N+1] int64, device memory,
+ *                                          non-decreasing, cu_seqlens[N] == T
+ *   output    [T, Hv, 128] bf16            new_state [N, Hv, 128, 128] fp32
+ *   workspace device buffer of at least gdn_prefill_workspace_bytes(T, N, Hq, Hv)
+ *             bytes, 256-byte aligned (may be NULL when that size is 0)
+ * A sequence of length 0 gets a zero final state (as in the definition).
+ * cu_seqlens is read only on the device; values outside [0, T] are clamped.
+ */
+int gdn_prefill(const void *q, const void *k, const void *v, const float *state,
+                const float *A_log, const void *a, const float *dt_bias, const void *b,
+                const int64_t *cu_seqlens, float scale, void *output, float *new_state,
+                int64_t total_seq_len, int64_t num_seqs, int64_t num_q_heads,
+                int64_t num_k_heads, int64_t num_v_heads, int64_t head_size, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/* Workspace bytes gdn_prefill needs for these sizes (0 when none). */
+size_t gdn_prefill_workspace_bytes(int64_t total_seq_len, int64_t num_seqs, int64_t num_q_heads,
+                                   int64_t num_v_heads);
+
+/*
+ * Token-recurrent prefill on CUDA cores (no workspace).
+ * Replaces gdn_prefill_recurrent_v1 (gdn_prefill/solution/python/cuda_recurrent_v1.cu:232-277).
+ * Same arguments as gdn_prefill without the workspace.
+ */
+int gdn_prefill_recurrent(const void *q, const void *k, const void *v, const float *state,
+                          const float *A_log, const void *a, const float *dt_bias, const void *b,
+                          const int64_t *cu_seqlens, float scale, void *output, float *new_state,
+                          int64_t total_seq_len, int64_t num_seqs, int64_t num_q_heads,
+                          int64_t num_k_heads, int64_t num_v_heads, int64_t head_size,
+                          void *stream);
+
+/*
+ * Chunk metadata (chunk size 64) for packed sequences.
+ * Replaces prep_meta_v2 (gdn_prefill/solution/python/cuda_prep_meta_v2.cu:72-94),
+ * without its N <= 256 limit.
+ *   cu_seqlens     [N+1] int64 (device)
+ *   chunk_offsets  [N+1] int32 (device, out): chunks before each sequence; [N] = total
+ *   chunk_indices  [max_chunks, 2] int32 (device, out): (sequence, chunk) pairs
+ */
+int gdn_prep_meta(const int64_t *cu_seqlens, int64_t num_seqs, int32_t *chunk_offsets,
+                  int32_t *chunk_indices, int64_t max_chunks, void *stream);
+
+/* Upper bound on the number of 64-token chunks of T tokens in N sequences
+ * (N + (T - N) / 64 for T >= N; the reference's bound in chunk_v12.py:53). */
+int64_t gdn_chunk_upper_bound(int64_t total_seq_len, int64_t num_seqs);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

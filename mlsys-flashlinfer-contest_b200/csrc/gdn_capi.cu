@@ -1,0 +1,153 @@
+// C ABI of the gdn_b200 library: validation, dispatch and error reporting.
+// Declarations and the contract of each entry point: include/gdn_b200.h.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/gdn_b200.h"
+#include "gdn_internal.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = '\0';
+  return GDN_OK;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "%s failed: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+// [p, p+bytes) and [q, q+bytes) overlap without being identical
+bool partial_overlap(const void* p, const void* q, size_t bytes) {
+  if (p == nullptr || q == nullptr || p == q) return false;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p), b = reinterpret_cast<uintptr_t>(q);
+  return a < b + bytes && b < a + bytes;
+}
+
+int check_heads(int64_t Hq, int64_t Hk, int64_t Hv, int64_t D) {
+  if (D != gdn::kHead) return fail(GDN_ERR_VALUE, "head_size must be 128 (got %lld)", (long long)D);
+  if (Hq <= 0 || Hk <= 0) return fail(GDN_ERR_VALUE, "head counts must be positive");
+  if (Hk != Hq)
+    return fail(GDN_ERR_VALUE, "num_k_heads (%lld) must equal num_q_heads (%lld)", (long long)Hk,
+                (long long)Hq);
+  if (Hv < Hq || Hv % Hq != 0)
+    return fail(GDN_ERR_VALUE, "num_v_heads (%lld) must be a multiple of num_q_heads (%lld)",
+                (long long)Hv, (long long)Hq);
+  return GDN_OK;
+}
+
+int64_t upper_bound_chunks(int64_t T, int64_t N) {
+  if (T <= 0 || N <= 0) return 0;
+  if (T < N) return T;
+  return N + (T - N) / gdn::kChunk;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_abi_version(void) { return GDN_ABI_VERSION; }
+
+const char* gdn_last_error(void) { return g_err; }
+
+int64_t gdn_chunk_upper_bound(int64_t T, int64_t N) { return upper_bound_chunks(T, N); }
+
+int gdn_decode(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+               const void* a, const float* dt_bias, const void* b, float scale, void* output,
+               float* new_state, int64_t B, int64_t Hq, int64_t Hk, int64_t Hv, int64_t D,
+               void* stream) {
+  if (int e = check_heads(Hq, Hk, Hv, D)) return e;
+  if (B < 0) return fail(GDN_ERR_VALUE, "batch_size must be non-negative");
+  if (B == 0) return ok();
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !new_state)
+    return fail(GDN_ERR_VALUE, "null pointer argument");
+  if (!aligned(q, 8) || !aligned(k, 8))
+    return fail(GDN_ERR_VALUE, "q and k must be 8-byte aligned");
+  if (!aligned(new_state, 16) || (state && !aligned(state, 16)))
+    return fail(GDN_ERR_VALUE, "state and new_state must be 16-byte aligned");
+  const size_t state_bytes = static_cast<size_t>(B) * Hv * gdn::kHead * gdn::kHead * 4;
+  if (partial_overlap(state, new_state, state_bytes))
+    return fail(GDN_ERR_VALUE, "new_state overlaps state without being the same buffer");
+  gdn::DecodeArgs p{q, k, v, state, A_log, a, dt_bias, b, scale == 0.0f ? 0.08838834764831845f : scale,
+                    output, new_state, B, Hq, Hv};
+  return cuda_status(gdn::launch_decode(p, 0, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
+}
+
+static int check_prefill(const void* q, const void* k, const void* v, const float* state,
+                         const float* A_log, const void* a, const float* dt_bias, const void* b,
+                         const int64_t* cu, void* out, float* new_state, int64_t T, int64_t N,
+                         int64_t Hq, int64_t Hk, int64_t Hv, int64_t D) {
+  if (int e = check_heads(Hq, Hk, Hv, D)) return e;
+  if (N <= 0) return fail(GDN_ERR_VALUE, "must have at least one sequence");
+  if (T < 0) return fail(GDN_ERR_VALUE, "total_seq_len must be non-negative");
+  if (!cu || !A_log || !dt_bias || !new_state) return fail(GDN_ERR_VALUE, "null pointer argument");
+  if (T > 0 && (!q || !k || !v || !a || !b || !out)) return fail(GDN_ERR_VALUE, "null pointer argument");
+  if (!aligned(q, 8) || !aligned(k, 8)) return fail(GDN_ERR_VALUE, "q and k must be 8-byte aligned");
+  if (!aligned(new_state, 16) || (state && !aligned(state, 16)))
+    return fail(GDN_ERR_VALUE, "state and new_state must be 16-byte aligned");
+  if (!aligned(cu, 8)) return fail(GDN_ERR_VALUE, "cu_seqlens must be 8-byte aligned");
+  const size_t state_bytes = static_cast<size_t>(N) * Hv * gdn::kHead * gdn::kHead * 4;
+  if (partial_overlap(state, new_state, state_bytes))
+    return fail(GDN_ERR_VALUE, "new_state overlaps state without being the same buffer");
+  return GDN_OK;
+}
+
+int gdn_prefill_recurrent(const void* q, const void* k, const void* v, const float* state,
+                          const float* A_log, const void* a, const float* dt_bias, const void* b,
+                          const int64_t* cu_seqlens, float scale, void* output, float* new_state,
+                          int64_t T, int64_t N, int64_t Hq, int64_t Hk, int64_t Hv, int64_t D,
+                          void* stream) {
+  if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
+                            N, Hq, Hk, Hv, D))
+    return e;
+  gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                     scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv};
+  return cuda_status(gdn::launch_prefill_recurrent(p, static_cast<cudaStream_t>(stream)),
+                     "gdn_prefill_recurrent launch");
+}
+
+size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv) {
+  (void)T;
+  (void)N;
+  (void)Hq;
+  (void)Hv;
+  return 0;
+}
+
+int gdn_prefill(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                const void* a, const float* dt_bias, const void* b, const int64_t* cu_seqlens,
+                float scale, void* output, float* new_state, int64_t T, int64_t N, int64_t Hq,
+                int64_t Hk, int64_t Hv, int64_t D, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  return gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                               new_state, T, N, Hq, Hk, Hv, D, stream);
+}
+
+int gdn_prep_meta(const int64_t* cu_seqlens, int64_t N, int32_t* chunk_offsets,
+                  int32_t* chunk_indices, int64_t max_chunks, void* stream) {
+  if (N < 0) return fail(GDN_ERR_VALUE, "num_seqs must be non-negative");
+  if (!cu_seqlens || !chunk_offsets || (max_chunks > 0 && !chunk_indices))
+    return fail(GDN_ERR_VALUE, "null pointer argument");
+  if (!aligned(chunk_indices, 8)) return fail(GDN_ERR_VALUE, "chunk_indices must be 8-byte aligned");
+  return cuda_status(gdn::launch_prep_meta(cu_seqlens, N, chunk_offsets, chunk_indices, max_chunks,
+                                           static_cast<cudaStream_t>(stream)),
+                     "gdn_prep_meta launch");
+}
+
+}  // extern "C"

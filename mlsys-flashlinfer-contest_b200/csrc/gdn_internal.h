@@ -1,0 +1,57 @@
+// Internal launch interfaces between the C-ABI layer (gdn_capi.cu) and the
+// kernel translation units.  Not part of the public header.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gdn {
+
+#ifndef GDN_CONSTANTS_DEFINED
+#define GDN_CONSTANTS_DEFINED
+constexpr int kHead = 128;   // head_size (K = V = 128, fixed by the definitions)
+constexpr int kChunk = 64;   // chunk length of the chunked prefill
+#endif
+
+struct DecodeArgs {
+  const void* q;        // [B,1,Hq,128] bf16
+  const void* k;        // [B,1,Hk,128] bf16 (Hk == Hq)
+  const void* v;        // [B,1,Hv,128] bf16
+  const float* state;   // [B,Hv,128,128] fp32 k-last, or nullptr (zero state)
+  const float* A_log;   // [Hv]
+  const void* a;        // [B,1,Hv] bf16
+  const float* dt_bias; // [Hv]
+  const void* b;        // [B,1,Hv] bf16
+  float scale;          // already resolved (0 -> 1/sqrt(128))
+  void* out;            // [B,1,Hv,128] bf16
+  float* new_state;     // [B,Hv,128,128] fp32 (may equal state)
+  int64_t B, Hq, Hv;
+};
+
+// rows_per_cta: 0 = choose from the problem size, else 32, 64 or 128.
+cudaError_t launch_decode(const DecodeArgs& a, int rows_per_cta, cudaStream_t s);
+
+struct PrefillArgs {
+  const void* q;           // [T,Hq,128] bf16
+  const void* k;           // [T,Hk,128] bf16
+  const void* v;           // [T,Hv,128] bf16
+  const float* state;      // [N,Hv,128,128] fp32 or nullptr
+  const float* A_log;      // [Hv]
+  const void* a;           // [T,Hv] bf16
+  const float* dt_bias;    // [Hv]
+  const void* b;           // [T,Hv] bf16
+  const int64_t* cu_seqlens;  // [N+1] int64, device
+  float scale;
+  void* out;               // [T,Hv,128] bf16
+  float* new_state;        // [N,Hv,128,128] fp32
+  int64_t T, N, Hq, Hv;
+};
+
+cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);
+
+// chunk metadata: offsets [N+1] int32, indices [max_chunks,2] int32
+cudaError_t launch_prep_meta(const int64_t* cu_seqlens, int64_t N, int32_t* chunk_offsets,
+                             int32_t* chunk_indices, int64_t max_chunks, cudaStream_t s);
+
+}  // namespace gdn

@@ -1,0 +1,96 @@
+"""GDN decode entry point with the solution signature of the reference.
+
+``run(q, k, v, state, A_log, a, dt_bias, b, scale) -> (output, new_state)`` is the
+drop-in for ``gdn_decode/solution/python/gdn_decode_final.py::run`` (:23-36): same
+argument order and meaning (definition input order, scale 0/None = 1/sqrt(128),
+``state`` optional), same return tuple.  The reference returns fresh tensors for
+B < 8 and updates ``state`` in place for B >= 8
+(gdn_decode_kernel_large_batch.py:348,405-406); here ``run`` is out-of-place for
+every B (definition-exact) and ``run_inplace`` is the explicit in-place form.
+Both launch the single fused sm_100a decode kernel through the C ABI
+(``gdn_decode`` in include/gdn_b200.h) on the current CUDA stream.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+from ._checks import HEAD, cuda_contig, dim, dtype, resolve_scale, same_device
+
+
+def _validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state):
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a), ("dt_bias", dt_bias),
+                    ("b", b), ("output", output), ("new_state", new_state)):
+        cuda_contig(name, t)
+    for name, t, d in (("q", q, 4), ("k", k, 4), ("v", v, 4), ("A_log", A_log, 1), ("a", a, 3),
+                       ("dt_bias", dt_bias, 1), ("b", b, 3), ("output", output, 4),
+                       ("new_state", new_state, 4)):
+        dim(name, t, d)
+    if state is not None:
+        cuda_contig("state", state)
+        dim("state", state, 4)
+        dtype("state", state, torch.float32)
+    same_device(q, k=k, v=v, state=state, A_log=A_log, a=a, dt_bias=dt_bias, b=b, output=output,
+                new_state=new_state)
+    for name, t in (("q", q), ("k", k), ("v", v), ("a", a), ("b", b), ("output", output)):
+        dtype(name, t, torch.bfloat16)
+    for name, t in (("A_log", A_log), ("dt_bias", dt_bias), ("new_state", new_state)):
+        dtype(name, t, torch.float32)
+    B, T, Hq, K = q.shape
+    Hk, Hv, V = k.shape[2], v.shape[2], v.shape[3]
+    if k.shape[0] != B or v.shape[0] != B:
+        raise ValueError("batch mismatch among q/k/v")
+    if k.shape[1] != T or v.shape[1] != T:
+        raise ValueError("sequence length mismatch among q/k/v")
+    if T != 1:
+        raise ValueError("decode requires T=1")
+    if K != HEAD or k.shape[3] != HEAD or V != HEAD:
+        raise ValueError("head size must be 128")
+    if Hk != Hq:
+        raise ValueError("num_k_heads must equal num_q_heads")
+    if Hv % Hq != 0:
+        raise ValueError("HV must be divisible by Hq")
+    if tuple(a.shape) != (B, T, Hv):
+        raise ValueError("a must have shape [B, T, HV]")
+    if tuple(b.shape) != (B, T, Hv):
+        raise ValueError("b must have shape [B, T, HV]")
+    if tuple(A_log.shape) != (Hv,):
+        raise ValueError("A_log must have shape [HV]")
+    if tuple(dt_bias.shape) != (Hv,):
+        raise ValueError("dt_bias must have shape [HV]")
+    if tuple(output.shape) != (B, T, Hv, V):
+        raise ValueError("output must have shape [B, T, HV, V]")
+    if tuple(new_state.shape) != (B, Hv, V, K):
+        raise ValueError("new_state must have shape [B, HV, V, K]")
+    if state is not None and tuple(state.shape) != (B, Hv, V, K):
+        raise ValueError("state must have shape [B, HV, V, K]")
+    return B, Hq, Hk, Hv
+
+
+def launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+    """Destination-passing form: writes ``output`` and ``new_state`` (which may be
+    ``state`` itself) and returns them."""
+    B, Hq, Hk, Hv = _validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
+    with torch.cuda.device(q.device):
+        rc = N.lib().gdn_decode(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(state), N.ptr(A_log), N.ptr(a),
+                                N.ptr(dt_bias), N.ptr(b), resolve_scale(scale), N.ptr(output),
+                                N.ptr(new_state), B, Hq, Hk, Hv, HEAD, N.stream_handle(q.device))
+    N.check(rc, "gdn_decode")
+    return output, new_state
+
+
+def run(q, k, v, state, A_log, a, dt_bias, b, scale):
+    """Out-of-place decode: returns (output [B,1,Hv,128] bf16, new_state [B,Hv,128,128] fp32)."""
+    output = torch.empty_like(v)
+    B, Hv = v.shape[0], v.shape[2]
+    new_state = torch.empty((B, Hv, HEAD, HEAD), dtype=torch.float32, device=v.device)
+    return launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+
+
+def run_inplace(q, k, v, state, A_log, a, dt_bias, b, scale):
+    """In-place decode (the reference's large-batch behaviour): ``state`` is
+    overwritten with the new state and returned as the second element."""
+    if state is None:
+        raise ValueError("run_inplace needs a state tensor")
+    output = torch.empty_like(v)
+    return launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, state)

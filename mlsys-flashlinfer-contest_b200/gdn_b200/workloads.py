@@ -1,0 +1,163 @@
+"""Seeded synthetic GDN inputs.
+
+The contest's workload tensors (safetensors blobs of the HF dataset
+``flashinfer-ai/mlsys26-contest``) are not available offline, so every test and
+benchmark uses seeded synthetic tensors with the shapes and value distributions of
+the contest definitions ``definitions/gdn/gdn_decode_qk4_v8_d128_k_last.md:27-39``
+and ``definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md:28-41``:
+
+* q, k, v ~ N(0, 1) in bf16; q and k L2-normalised per head (in fp32, then rounded);
+* A_log = log(U(1, 16)) fp32, dt_bias ~ U(-1, 1) fp32;
+* a, b ~ N(0, 1) bf16 (decode shape [B, 1, Hv], prefill shape [T, Hv]);
+* initial state fp32 ~ N(0, 0.05^2) in the k-last layout [B or N, Hv, V, K].
+
+Generation runs on the device named by ``device`` with a ``torch.Generator``
+seeded per call; on CPU the result is bit-identical across machines that run the
+same torch build, which is what the committed golden fixtures rely on.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+HEAD_SIZE = 128
+
+
+def _gen(device, seed: int) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    return g
+
+
+def _normal(shape, gen, device, std=1.0):
+    return torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std
+
+
+def _uniform(shape, gen, device, lo, hi):
+    return torch.rand(shape, generator=gen, device=device, dtype=torch.float32) * (hi - lo) + lo
+
+
+def _l2norm_bf16(x: torch.Tensor) -> torch.Tensor:
+    x = x / x.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+    return x.to(torch.bfloat16)
+
+
+@dataclass
+class DecodeInputs:
+    q: torch.Tensor
+    k: torch.Tensor
+    v: torch.Tensor
+    state: Optional[torch.Tensor]
+    A_log: torch.Tensor
+    a: torch.Tensor
+    dt_bias: torch.Tensor
+    b: torch.Tensor
+    scale: float
+
+    def args(self):
+        """Positional arguments in the definition's input order."""
+        return (self.q, self.k, self.v, self.state, self.A_log, self.a, self.dt_bias,
+                self.b, self.scale)
+
+
+@dataclass
+class PrefillInputs:
+    q: torch.Tensor
+    k: torch.Tensor
+    v: torch.Tensor
+    state: Optional[torch.Tensor]
+    A_log: torch.Tensor
+    a: torch.Tensor
+    dt_bias: torch.Tensor
+    b: torch.Tensor
+    cu_seqlens: torch.Tensor
+    scale: float
+
+    def args(self):
+        return (self.q, self.k, self.v, self.state, self.A_log, self.a, self.dt_bias,
+                self.b, self.cu_seqlens, self.scale)
+
+
+def head_params(Hv: int, gen, device):
+    A_log = torch.log(_uniform((Hv,), gen, device, 1.0, 16.0))
+    dt_bias = _uniform((Hv,), gen, device, -1.0, 1.0)
+    return A_log, dt_bias
+
+
+def make_decode_inputs(B: int, Hq: int = 16, Hv: int = 32, seed: int = 0,
+                       device="cpu", with_state: bool = True,
+                       state_std: float = 0.05) -> DecodeInputs:
+    """Decode inputs of BASELINE configs 0/1/4 (T=1)."""
+    gen = _gen(device, seed)
+    d = HEAD_SIZE
+    q = _l2norm_bf16(_normal((B, 1, Hq, d), gen, device))
+    k = _l2norm_bf16(_normal((B, 1, Hq, d), gen, device))
+    v = _normal((B, 1, Hv, d), gen, device).to(torch.bfloat16)
+    A_log, dt_bias = head_params(Hv, gen, device)
+    a = _normal((B, 1, Hv), gen, device).to(torch.bfloat16)
+    b = _normal((B, 1, Hv), gen, device).to(torch.bfloat16)
+    state = _normal((B, Hv, d, d), gen, device, state_std) if with_state else None
+    return DecodeInputs(q, k, v, state, A_log, a, dt_bias, b, 1.0 / math.sqrt(d))
+
+
+def varlen_lengths(n: int, lo: int, hi: int, seed: int) -> list:
+    """n sequence lengths ~ U[lo, hi] (inclusive), seeded."""
+    gen = _gen("cpu", seed)
+    return [int(x) for x in torch.randint(lo, hi + 1, (n,), generator=gen)]
+
+
+def even_lengths(total: int, n: int) -> list:
+    """Equal-length rewrite of a varlen batch (the reference's even generator,
+    gdn_prefill/scripts/run_local_fast_even.py:32-44): same total, n sequences."""
+    base, rem = divmod(total, n)
+    return [base + (1 if i < rem else 0) for i in range(n)]
+
+
+def uneven_lengths(total: int, n: int) -> list:
+    """n-1 sequences of length 1 plus one long sequence with the same total
+    (gdn_prefill/scripts/run_local_fast_uneven.py)."""
+    if n <= 1:
+        return [total]
+    return [1] * (n - 1) + [total - (n - 1)]
+
+
+def make_prefill_inputs(lengths: Sequence[int], Hq: int = 16, Hv: int = 32, seed: int = 0,
+                        device="cpu", with_state=True, state_std: float = 0.05,
+                        zero_state_every_other: bool = False,
+                        cu_dtype=torch.int64) -> PrefillInputs:
+    """Packed varlen prefill inputs (BASELINE configs 2/3).
+
+    ``zero_state_every_other`` zeroes the initial state of every second sequence
+    (config 2: "initial state is zero for half the sequences")."""
+    gen = _gen(device, seed)
+    d = HEAD_SIZE
+    N = len(lengths)
+    T = int(sum(lengths))
+    q = _l2norm_bf16(_normal((T, Hq, d), gen, device))
+    k = _l2norm_bf16(_normal((T, Hq, d), gen, device))
+    v = _normal((T, Hv, d), gen, device).to(torch.bfloat16)
+    A_log, dt_bias = head_params(Hv, gen, device)
+    a = _normal((T, Hv), gen, device).to(torch.bfloat16)
+    b = _normal((T, Hv), gen, device).to(torch.bfloat16)
+    state = None
+    if with_state:
+        state = _normal((N, Hv, d, d), gen, device, state_std)
+        if zero_state_every_other:
+            state[0::2] = 0.0
+    cu = [0]
+    for L in lengths:
+        cu.append(cu[-1] + int(L))
+    cu_seqlens = torch.tensor(cu, dtype=cu_dtype, device=device)
+    return PrefillInputs(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, 1.0 / math.sqrt(d))
+
+
+# Named BASELINE.json configurations.
+def config_lengths(name: str) -> list:
+    if name == "prefill_varlen":      # config 2: 16 seqs, len ~ U[64, 1024]
+        return varlen_lengths(16, 64, 1024, seed=2)
+    if name == "prefill_long":        # config 3: 4 x 16384
+        return [16384] * 4
+    raise KeyError(name)

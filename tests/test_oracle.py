@@ -1,0 +1,122 @@
+"""CPU tests: pin the oracle to the reference's own outputs (golden fixtures),
+check the chunked restatement and the metadata against the recurrence, and
+cross-check the C restatement against the numpy one."""
+import numpy as np
+import pytest
+import torch
+
+import golden_io as G
+from oracle import gdn_oracle as O
+from oracle import c_oracle as C
+from gdn_b200 import workloads as W
+
+
+def _np_args(inp):
+    return [O.to_numpy(x) if isinstance(x, torch.Tensor) else x for x in inp.args()]
+
+
+def _o_close(o_bits, ref_bits):
+    """bf16 outputs: equal bits almost everywhere, never more than 1 ulp apart in
+    value terms (float32 accumulation order differs from torch's)."""
+    a = O.bf16_to_f32(o_bits).astype(np.float64)
+    r = O.bf16_to_f32(ref_bits).astype(np.float64)
+    tol = np.abs(r) * 2.0 ** -7 + 1e-6  # one bf16 ulp
+    assert np.all(np.abs(a - r) <= tol), float(np.abs(a - r).max())
+    assert np.mean(o_bits != ref_bits) < 0.02
+
+
+@pytest.mark.parametrize("name", G.names())
+def test_oracle_matches_reference_golden(name):
+    meta, z = G.load(name)
+    inp = G.regenerate_inputs(meta)
+    assert G.sha_inputs(list(inp.args())) == str(z["input_sha"]), "input generator drifted"
+    args = _np_args(inp)
+    if meta["kind"] == "decode":
+        o, ns = O.decode(*args)
+    else:
+        o, ns = O.prefill(*args)
+    _o_close(o, z["o"])
+    G.check_state(ns, z)
+
+
+@pytest.mark.parametrize("name", G.names())
+def test_c_oracle_matches_reference_golden(name):
+    meta, z = G.load(name)
+    inp = G.regenerate_inputs(meta)
+    if meta["kind"] == "decode":
+        o, ns = C.decode(*inp.args(), nthreads=4)
+    else:
+        o, ns = C.prefill(*inp.args(), nthreads=4)
+    _o_close(o.view(torch.int16).numpy().view(np.uint16), z["o"])
+    G.check_state(ns.numpy(), z)
+
+
+def test_prep_meta_known_answer():
+    # Report.pdf p.5 App. A: N=2 sequences with 3 and 5 chunks -> offsets [0, 3, 8]
+    off, idx = O.prep_meta([0, 150, 150 + 300])
+    assert off.tolist() == [0, 3, 8]
+    assert idx.tolist() == [[0, 0], [0, 1], [0, 2], [1, 0], [1, 1], [1, 2], [1, 3], [1, 4]]
+
+
+def test_prep_meta_edges():
+    off, idx = O.prep_meta([0, 0, 64, 65, 65, 200])
+    assert off.tolist() == [0, 0, 1, 2, 2, 5]
+    assert idx.tolist() == [[1, 0], [2, 0], [4, 0], [4, 1], [4, 2]]
+
+
+def test_chunk_upper_bound_is_tight():
+    rng = np.random.default_rng(0)
+    for _ in range(300):
+        N = int(rng.integers(1, 9))
+        lens = rng.integers(0, 200, N)
+        T = int(lens.sum())
+        off, _ = O.prep_meta(np.concatenate([[0], np.cumsum(lens)]))
+        assert off[-1] <= O.chunk_upper_bound(T, N)
+    # tight for N-1 sequences of one token plus one long sequence
+    for T, N in [(1000, 5), (64, 1), (65, 1), (7, 7), (130, 2)]:
+        lens = W.uneven_lengths(T, N)
+        off, _ = O.prep_meta(np.concatenate([[0], np.cumsum(lens)]))
+        assert off[-1] == O.chunk_upper_bound(T, N)
+
+
+def test_inverse_known_answer():
+    # gdn_prefill/doc/newton-schulz-refinement.md:14-24
+    M = np.array([[1, 0, 0], [0.5, 1, 0], [0.3, 0.4, 1]])
+    np.testing.assert_allclose(np.linalg.inv(M), [[1, 0, 0], [-0.5, 1, 0], [-0.1, -0.4, 1]],
+                               atol=1e-12)
+
+
+@pytest.mark.parametrize("lengths", [[1], [63], [64], [65], [130, 0, 7], [200, 64]])
+def test_chunked_matches_recurrence(lengths):
+    inp = W.make_prefill_inputs(lengths, 2, 4, seed=sum(lengths) + len(lengths))
+    args = _np_args(inp)
+    o_ref, s_ref = O.prefill(*args)
+    o, s = O.chunked_prefill(*args)
+    assert O.rel_err(s, s_ref) < 1e-5
+    assert O.rel_err(o, O.bf16_to_f32(o_ref)) < 5e-3  # the oracle rounds o to bf16
+    assert O.rel_err(O.round_bf16(o), O.bf16_to_f32(o_ref)) < 5e-3
+
+
+def test_state_none_equals_zero_state():
+    inp = W.make_prefill_inputs([40, 3], 2, 4, seed=7, with_state=True)
+    args = _np_args(inp)
+    args[3] = np.zeros_like(args[3])
+    o1, s1 = O.prefill(*args)
+    args[3] = None
+    o2, s2 = O.prefill(*args)
+    assert np.array_equal(o1, o2) and np.array_equal(s1, s2)
+
+
+def test_empty_sequence_gets_zero_state():
+    inp = W.make_prefill_inputs([5, 0, 4], 2, 4, seed=9)
+    o, s = O.prefill(*_np_args(inp))
+    assert np.all(s[1] == 0)
+    o2, s2 = C.prefill(*inp.args(), nthreads=2)
+    assert torch.all(s2[1] == 0)
+
+
+def test_c_oracle_threads_do_not_change_results():
+    inp = W.make_decode_inputs(3, 2, 4, seed=5)
+    o1, s1 = C.decode(*inp.args(), nthreads=1)
+    o2, s2 = C.decode(*inp.args(), nthreads=3)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
