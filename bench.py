@@ -406,6 +406,7 @@ def run_reference(args, rank, world):
 
 
 def main():
+    global B_PER_RANK
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
@@ -415,14 +416,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
-    ap.add_argument("--batch-per-rank", type=int, default=B_PER_RANK,
+    ap.add_argument("--batch-per-rank", type=int, default=256,
                     help="sequences per rank (default 256 = BASELINE config 1; smaller only for profiling)")
     ap.add_argument("--prefill-seqs", type=int, default=4)
     ap.add_argument("--prefill-len", type=int, default=16384)
     ap.add_argument("--prefill-steps", type=int, default=5)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    global B_PER_RANK
     B_PER_RANK = args.batch_per_rank
 
     world = env_int("WORLD_SIZE", 1)
