@@ -116,6 +116,50 @@ int gdn_prefill_recurrent(const void *q, const void *k, const void *v, const flo
 int gdn_prep_meta(const int64_t *cu_seqlens, int64_t num_seqs, int32_t *chunk_offsets,
                   int32_t *chunk_indices, int64_t max_chunks, void *stream);
 
+/*
+ * Fused chunked (C = 64) prefill on tcgen05 tensor cores, whatever the size.
+ * Replaces the reference's chunked pipeline (gdn_prefill/solution/python/chunk_v12.py:36-116:
+ * prep_meta_v2, kkt_inv_uw_v1, h_v2b, o_v1) with one kernel that needs no workspace.
+ * Same arguments as gdn_prefill_recurrent.
+ */
+int gdn_prefill_chunked(const void *q, const void *k, const void *v, const float *state,
+                        const float *A_log, const void *a, const float *dt_bias, const void *b,
+                        const int64_t *cu_seqlens, float scale, void *output, float *new_state,
+                        int64_t total_seq_len, int64_t num_seqs, int64_t num_q_heads,
+                        int64_t num_k_heads, int64_t num_v_heads, int64_t head_size, void *stream);
+
+/*
+ * Diagnostic form of gdn_prefill_chunked: also dumps the intermediates of one
+ * chunk (dbg_seq, dbg_head, dbg_chunk) into `debug` (fp32, at least
+ * gdn_prefill_chunked_debug_floats() elements): gamma[64], beta[64], A[64x64],
+ * P[64x64], T[64x64], U[64x128], W[64x128], Vn[64x128], QS[64x128], PV[64x128],
+ * state after the chunk [128x128].  The in-kernel counterpart of the reference's
+ * optional %globaltimer profiler argument (cuda_h_v2b.cu:56-121,829-896).
+ */
+int gdn_prefill_chunked_debug(const void *q, const void *k, const void *v, const float *state,
+                              const float *A_log, const void *a, const float *dt_bias,
+                              const void *b, const int64_t *cu_seqlens, float scale, void *output,
+                              float *new_state, int64_t total_seq_len, int64_t num_seqs,
+                              int64_t num_q_heads, int64_t num_k_heads, int64_t num_v_heads,
+                              int64_t head_size, float *debug, int64_t debug_floats,
+                              int64_t dbg_seq, int64_t dbg_head, int64_t dbg_chunk, void *stream);
+int64_t gdn_prefill_chunked_debug_floats(void);
+
+/*
+ * Device status word.  A kernel that gives up on a bounded wait (an mbarrier
+ * that does not complete within 2 s) sets a bit here and returns instead of
+ * hanging: bit 0 = chunked prefill, bit 1 = gdn_wait_probe.  Reads the word of
+ * the current device (synchronising), optionally clearing it.  No reference
+ * counterpart: the reference relies on cudaGetLastError only
+ * (gdn_decode_small_batch.cu:223-227).
+ */
+int gdn_read_status(uint32_t *status, int clear);
+
+/* Launches one CTA that waits on an mbarrier nothing arrives on, for at most
+ * timeout_ns (<= 5 s); *result (device memory, may be NULL) becomes 0 on
+ * timeout.  Exercises the timeout path without faulting or hanging the GPU. */
+int gdn_wait_probe(uint64_t timeout_ns, uint32_t *result, void *stream);
+
 /* Upper bound on the number of 64-token chunks of T tokens in N sequences
  * (N + (T - N) / 64 for T >= N; the reference's bound in chunk_v12.py:53). */
 int64_t gdn_chunk_upper_bound(int64_t total_seq_len, int64_t num_seqs);

@@ -121,11 +121,32 @@ int gdn_prefill_recurrent(const void* q, const void* k, const void* v, const flo
 }
 
 size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv) {
+  // The fused chunked kernel keeps every intermediate on chip.
   (void)T;
   (void)N;
   (void)Hq;
   (void)Hv;
   return 0;
+}
+
+// Chooses the token-recurrent kernel for tiny inputs, as the reference's
+// dispatch does (gdn_prefill/solution/python/gdn_prefill_mix.py:29:
+// N <= 2 and T <= 30 N), and the fused chunked kernel otherwise.
+static bool use_recurrent(int64_t T, int64_t N) { return N <= 2 && T <= 30 * N; }
+
+int gdn_prefill_chunked(const void* q, const void* k, const void* v, const float* state,
+                        const float* A_log, const void* a, const float* dt_bias, const void* b,
+                        const int64_t* cu_seqlens, float scale, void* output, float* new_state,
+                        int64_t T, int64_t N, int64_t Hq, int64_t Hk, int64_t Hv, int64_t D,
+                        void* stream) {
+  if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
+                            N, Hq, Hk, Hv, D))
+    return e;
+  if (T > 0x7fffffffLL - 64) return fail(GDN_ERR_VALUE, "total_seq_len too large");
+  gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                     scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv};
+  return cuda_status(gdn::launch_prefill_chunked(p, static_cast<cudaStream_t>(stream)),
+                     "gdn_prefill_chunked launch");
 }
 
 int gdn_prefill(const void* q, const void* k, const void* v, const float* state, const float* A_log,
@@ -135,8 +156,44 @@ int gdn_prefill(const void* q, const void* k, const void* v, const float* state,
                 void* stream) {
   (void)workspace;
   (void)workspace_bytes;
-  return gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
-                               new_state, T, N, Hq, Hk, Hv, D, stream);
+  if (use_recurrent(T, N))
+    return gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                                 new_state, T, N, Hq, Hk, Hv, D, stream);
+  return gdn_prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                             new_state, T, N, Hq, Hk, Hv, D, stream);
+}
+
+int gdn_prefill_chunked_debug(const void* q, const void* k, const void* v, const float* state,
+                              const float* A_log, const void* a, const float* dt_bias,
+                              const void* b, const int64_t* cu_seqlens, float scale, void* output,
+                              float* new_state, int64_t T, int64_t N, int64_t Hq, int64_t Hk,
+                              int64_t Hv, int64_t D, float* debug, int64_t debug_floats,
+                              int64_t dbg_seq, int64_t dbg_head, int64_t dbg_chunk, void* stream) {
+  if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
+                            N, Hq, Hk, Hv, D))
+    return e;
+  if (!debug || debug_floats < gdn::prefill_chunked_debug_floats())
+    return fail(GDN_ERR_VALUE, "debug buffer needs %d floats", gdn::prefill_chunked_debug_floats());
+  gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                     scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv};
+  return cuda_status(
+      gdn::launch_prefill_chunked_debug(p, debug, static_cast<int>(dbg_seq),
+                                        static_cast<int>(dbg_head), static_cast<int>(dbg_chunk),
+                                        static_cast<cudaStream_t>(stream)),
+      "gdn_prefill_chunked_debug launch");
+}
+
+int64_t gdn_prefill_chunked_debug_floats(void) { return gdn::prefill_chunked_debug_floats(); }
+
+int gdn_read_status(uint32_t* status, int clear) {
+  if (!status) return fail(GDN_ERR_VALUE, "null pointer argument");
+  return cuda_status(gdn::read_status(status, clear != 0), "gdn_read_status");
+}
+
+int gdn_wait_probe(uint64_t timeout_ns, uint32_t* result, void* stream) {
+  if (timeout_ns > 5000000000ull) return fail(GDN_ERR_VALUE, "timeout_ns must be <= 5 s");
+  return cuda_status(gdn::launch_wait_probe(timeout_ns, result, static_cast<cudaStream_t>(stream)),
+                     "gdn_wait_probe launch");
 }
 
 int gdn_prep_meta(const int64_t* cu_seqlens, int64_t N, int32_t* chunk_offsets,

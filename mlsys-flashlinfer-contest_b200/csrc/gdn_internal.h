@@ -50,6 +50,19 @@ struct PrefillArgs {
 
 cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);
 
+// fused chunked (C=64) prefill on tcgen05; no workspace
+cudaError_t launch_prefill_chunked(const PrefillArgs& a, cudaStream_t s);
+// same kernel, dumping one chunk's intermediates (gamma, beta, A, P, T, U, W,
+// Vn, QS, PV, St) of (dbg_seq, dbg_head, dbg_chunk) into `debug`
+cudaError_t launch_prefill_chunked_debug(const PrefillArgs& a, float* debug, int dbg_seq,
+                                         int dbg_head, int dbg_chunk, cudaStream_t s);
+int prefill_chunked_debug_floats();
+
+// bounded wait on an mbarrier nothing arrives on (timeout path test)
+cudaError_t launch_wait_probe(uint64_t timeout_ns, uint32_t* result, cudaStream_t s);
+// device status word (bit flags of kernels that gave up on a wait)
+cudaError_t read_status(uint32_t* out, bool clear);
+
 // chunk metadata: offsets [N+1] int32, indices [max_chunks,2] int32
 cudaError_t launch_prep_meta(const int64_t* cu_seqlens, int64_t N, int32_t* chunk_offsets,
                              int32_t* chunk_indices, int64_t max_chunks, cudaStream_t s);

@@ -1,0 +1,676 @@
+// GDN prefill, chunked (C = 64) WY/UT form on tcgen05 tensor cores (sm_100a).
+//
+// Replaces the reference's 4-kernel pipeline chunk_v12.py:36-116
+// (prep_meta_v2 -> kkt_inv_uw_v1 -> h_v2b -> o_v1) with ONE fused kernel: a
+// CTA owns one (sequence, v-head) and walks its chunks in order, keeping the
+// fp32 state in TMEM for the whole sequence.  Nothing is materialised in HBM
+// between the stages (the reference writes U/W, per-chunk bf16 state
+// snapshots h and v_new, i.e. ~2 KiB/token/head of extra traffic).
+//
+// Per chunk (tokens t, s in [0,64), gamma = within-chunk cumulative log decay,
+// S = [K,V] state at the chunk start, St = S^T = k-last [V,K] in TMEM):
+//   G|QK  = [K;Q] K^T                          (tcgen05, M=128: rows 0-63 KK^T, 64-127 QK^T)
+//   A     = strict_tril(beta_t G e^{gamma_t - gamma_s}),  P = tril(QK e^{gamma_t - gamma_s})
+//   T     = (I + A)^-1                         (fp32, CUDA cores)
+//   U     = T diag(beta) V,  W = T diag(beta e^gamma) K          (tcgen05)
+//   Vn    = U - W S,         QS = Q S                            (tcgen05, S as bf16)
+//   O     = scale (e^{gamma_t} QS + P Vn)      (tcgen05 for P Vn)
+//   St   <- e^{gamma_63} St + Vd^T K,  Vd = e^{gamma_63 - gamma_t} Vn split into
+//           bf16 hi + lo (two MMAs) so the state update keeps ~16 mantissa bits.
+// Tokens past the end of the sequence get beta = 0 and log-decay 0, which
+// makes their Vn rows exactly zero and leaves gamma_63 = gamma_{L-1}.
+// Math: same chunked algebra as cuda_kkt_inv_uw_v1.cu:1-20 (U, W, g_cu),
+// cuda_h_v2b.cu (state scan) and cuda_o_v1.cu (output); semantics as
+// definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md:62-142.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+#include "gdn_sm100.cuh"
+
+namespace gdn {
+
+__device__ uint32_t g_gdn_status = 0;
+
+namespace {
+using namespace sm100;
+
+constexpr int kThreads = 128;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait, then give up
+
+// ---- shared memory map (offsets from a 1024-aligned base) -----------------
+// Every operand tile is a stack of 128-byte rows in the SWIZZLE_128B pattern.
+constexpr uint32_t kKQStage = 32768;  // [kb 2][row 128: K rows 0-63, Q rows 64-127][128 B]
+constexpr uint32_t kVStage = 16384;   // [vb 2][t 64][128 B]
+constexpr uint32_t OFF_KQ = 0;                     // 2 stages
+constexpr uint32_t OFF_V = OFF_KQ + 2 * kKQStage;  // 2 stages
+constexpr uint32_t OFF_ST = OFF_V + 2 * kVStage;   // bf16 S: [kb 2][v 128][128 B] (K-major B)
+constexpr uint32_t OFF_P = OFF_ST + 32768;         // P: [t 64][128 B] (K-major A)
+constexpr uint32_t OFF_TB = OFF_P + 8192;          // T diag(beta): [s 64][t 128 B] (MN-major A)
+constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T diag(beta e^gamma)
+constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A / T^T [64][68]; later W [kb 2][t 64][128 B]
+constexpr uint32_t OFF_VN = OFF_AF + 17408;        // Vn bf16 [vb 2][t 64][128 B] (MN-major B)
+constexpr uint32_t OFF_VH = OFF_VN + 16384;        // Vd hi (MN-major A)
+constexpr uint32_t OFF_VL = OFF_VH + 16384;        // Vd lo
+constexpr uint32_t OFF_MISC = OFF_VL + 16384;      // gamma[64], beta[64], barriers, tmem slot
+constexpr uint32_t kSmemBytes = OFF_MISC + 1024 + 1024;  // + slack for the 1024 alignment
+constexpr int kAPitch = 68;                        // fp32 row pitch of A / T^T
+
+// ---- TMEM columns ----------------------------------------------------------
+constexpr uint32_t TM_ST = 0;     // St [v 128 lanes][k 128 cols]
+constexpr uint32_t TM_D1 = 128;   // [K;Q]K^T [128 lanes][64 cols]
+constexpr uint32_t TM_VN = 192;   // U -> Vn, then P Vn   (M=64 layout)
+constexpr uint32_t TM_W = 320;    // W, then Q S          (M=64 layout)
+constexpr uint32_t kTmemCols = 512;
+
+constexpr uint32_t kTmaBytes = 2 * kKQStage / 2 + kVStage;  // K 16K + Q 16K + V 16K
+
+struct ChunkParams {
+  const float* state;
+  const float* A_log;
+  const float* dt_bias;
+  const __nv_bfloat16* a;
+  const __nv_bfloat16* b;
+  const int64_t* cu_seqlens;
+  __nv_bfloat16* out;
+  float* new_state;
+  float* debug;  // optional dump of one chunk's intermediates
+  float scale;
+  int64_t T, N;
+  int Hq, Hv;
+  int dbg_seq, dbg_head, dbg_chunk;
+};
+
+// Debug dump layout (floats)
+constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_T = DBG_P + 4096,
+              DBG_U = DBG_T + 4096, DBG_W = DBG_U + 8192, DBG_VN = DBG_W + 8192,
+              DBG_QS = DBG_VN + 8192, DBG_PV = DBG_QS + 8192, DBG_ST = DBG_PV + 8192,
+              DBG_SIZE = DBG_ST + 16384;
+
+__device__ __forceinline__ void write_bf16_row16(uint32_t tile, uint32_t row, int cb,
+                                                 const float* v) {
+  // 16 consecutive columns [16*cb, 16*cb+16) of a 128-column bf16 row stored as
+  // two 64-column swizzled blocks of `rows` rows: block stride passed via tile.
+  const uint32_t c0 = (cb & 3) * 2;
+  sts128(tile + sw128_off(row, c0), pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  sts128(tile + sw128_off(row, c0 + 1), pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
+         pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
+}
+
+template <bool DEBUG>
+__global__ void __launch_bounds__(kThreads, 1)
+    gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
+                               const __grid_constant__ CUtensorMap tm_k,
+                               const __grid_constant__ CUtensorMap tm_v, const ChunkParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = smem_u32(smem);
+  float* gam = reinterpret_cast<float*>(smem + OFF_MISC);
+  float* bet = gam + 64;
+  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + OFF_MISC + 512);  // [2]
+  uint64_t* bar_mma = bar_tma + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  float* Af = reinterpret_cast<float*>(smem + OFF_AF);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = static_cast<int>(blockIdx.x % p.Hv);
+  const int64_t n = blockIdx.x / p.Hv;
+  const int qh = h / (p.Hv / p.Hq);
+  const int64_t bos = min(max(p.cu_seqlens[n], int64_t(0)), p.T);
+  const int64_t eos = min(max(p.cu_seqlens[n + 1], bos), p.T);
+  const int64_t Ltot = eos - bos;
+  float* ns_rows = p.new_state + (n * p.Hv + h) * (kHead * kHead);
+
+  if (Ltot <= 0) {  // empty sequence: zero final state (definition skips it)
+    for (int i = tid; i < kHead * kHead / 4; i += kThreads)
+      reinterpret_cast<float4*>(ns_rows)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
+
+  if (tid == 0) {
+    mbar_init(&bar_tma[0], 1);
+    mbar_init(&bar_tma[1], 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const float A_log_h = p.A_log[h], dt_bias_h = p.dt_bias[h];
+
+  // ---- initial state -> TMEM (thread tid owns state row v = tid) ----------
+  {
+    const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + tid * kHead : nullptr;
+#pragma unroll
+    for (int cb = 0; cb < 8; ++cb) {
+      float v[16];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        float4 x = src ? ld_stream_f4(src + cb * 16 + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[4 * q4] = x.x;
+        v[4 * q4 + 1] = x.y;
+        v[4 * q4 + 2] = x.z;
+        v[4 * q4 + 3] = x.w;
+      }
+      tmem_st16(tmem + lane_base + TM_ST + cb * 16, v);
+    }
+    tmem_wait_st();
+  }
+
+  auto issue_loads = [&](int cc, int s) {
+    const int tok = static_cast<int>(bos + static_cast<int64_t>(cc) * kChunk);
+    uint64_t* bar = &bar_tma[s];
+    mbar_arrive_expect_tx(bar, kTmaBytes);
+    uint8_t* kq = smem + OFF_KQ + s * kKQStage;
+    uint8_t* vs = smem + OFF_V + s * kVStage;
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+      tma_load_3d(kq + kb * 16384, &tm_k, bar, kb * 64, qh, tok);
+      tma_load_3d(kq + kb * 16384 + 8192, &tm_q, bar, kb * 64, qh, tok);
+      tma_load_3d(vs + kb * 8192, &tm_v, bar, kb * 64, h, tok);
+    }
+  };
+
+  uint32_t tma_phase0 = 0, tma_phase1 = 0, mma_phase = 0;
+  bool aborted = false;
+  // All threads wait on the same barrier, then agree on the outcome.
+  auto wait_all = [&](uint64_t* bar, uint32_t& phase) -> bool {
+    const bool ok = mbar_wait(bar, phase, kTimeoutNs);
+    phase ^= 1u;
+    return __syncthreads_or(ok ? 0 : 1) == 0;
+  };
+
+  if (tid == 0) issue_loads(0, 0);
+  const int nchunks = static_cast<int>((Ltot + kChunk - 1) / kChunk);
+
+  const uint32_t idesc_d1 = idesc_bf16(128, 64, false, false);
+  const uint32_t idesc_tv = idesc_bf16(64, 128, true, true);
+  const uint32_t idesc_vn = idesc_bf16(64, 128, false, false, true);
+  const uint32_t idesc_qs = idesc_bf16(64, 128, false, false);
+  const uint32_t idesc_pv = idesc_bf16(64, 128, false, true);
+  const uint32_t idesc_st = idesc_bf16(128, 128, true, true);
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int stage = c & 1;
+    const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
+    const int L = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0));
+    const bool dbg = dbg_cta && c == p.dbg_chunk;
+    const uint32_t kq = sb + OFF_KQ + stage * kKQStage;
+    const uint32_t vsm = sb + OFF_V + stage * kVStage;
+
+    tc_fence_before();
+    __syncthreads();  // previous chunk fully drained
+    tc_fence_after();
+    if (tid == 0 && c + 1 < nchunks) issue_loads(c + 1, stage ^ 1);
+
+    // ---- gates: warp 0, two tokens per lane, inclusive scan of log-decay ---
+    if (warp == 0) {
+      float lg[2], bt[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = 2 * lane + e;
+        lg[e] = 0.f;
+        bt[e] = 0.f;
+        if (t < L) {
+          const int64_t idx = (t0 + t) * p.Hv + h;
+          lg[e] = log_decay(A_log_h, __bfloat162float(p.a[idx]), dt_bias_h);
+          bt[e] = sigmoidf_acc(__bfloat162float(p.b[idx]));
+        }
+      }
+      const float pair = lg[0] + lg[1];
+      float incl = pair;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += y;
+      }
+      gam[2 * lane] = incl - pair + lg[0];
+      gam[2 * lane + 1] = incl;
+      bet[2 * lane] = bt[0];
+      bet[2 * lane + 1] = bt[1];
+      if (dbg) {
+        p.debug[DBG_GAM + 2 * lane] = gam[2 * lane];
+        p.debug[DBG_GAM + 2 * lane + 1] = incl;
+        p.debug[DBG_BET + 2 * lane] = bt[0];
+        p.debug[DBG_BET + 2 * lane + 1] = bt[1];
+      }
+    }
+    __syncthreads();
+
+    // ---- state pass: St -> bf16 operand tile; St *= e^{gamma_63} -----------
+    {
+      const float dec = __expf(gam[63]);
+#pragma unroll
+      for (int cb = 0; cb < 8; ++cb) {
+        float v[16];
+        tmem_ld16(tmem + lane_base + TM_ST + cb * 16, v);
+        tmem_wait_ld();
+        write_bf16_row16(sb + OFF_ST + (cb >> 2) * 16384, tid, cb, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] *= dec;
+        tmem_st16(tmem + lane_base + TM_ST + cb * 16, v);
+      }
+      tmem_wait_st();
+      fence_async_smem();
+    }
+    tc_fence_before();
+    if (!wait_all(&bar_tma[stage], stage ? tma_phase1 : tma_phase0)) { aborted = true; break; }
+
+    // ---- MMA 1: [K;Q] K^T ---------------------------------------------------
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+        mma_bf16_ss(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
+                    idesc_d1, ks > 0);
+      }
+      mma_commit(bar_mma);
+    }
+    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    tc_fence_after();
+
+    // ---- A (warps 0-1) and P (warps 2-3) from TMEM --------------------------
+    {
+      const int i = (tid & 63);
+      const float gi = gam[i];
+      float v[16];
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        tmem_ld16(tmem + lane_base + TM_D1 + cb * 16, v);
+        tmem_wait_ld();
+        if (warp < 2) {
+          const float bi = bet[i];
+          float a16[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = cb * 16 + jj;
+            a16[jj] = (j < i) ? bi * v[jj] * __expf(gi - gam[j]) : 0.f;
+          }
+          float4* dst = reinterpret_cast<float4*>(Af + i * kAPitch + cb * 16);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_float4(a16[4 * q4], a16[4 * q4 + 1], a16[4 * q4 + 2], a16[4 * q4 + 3]);
+          if (dbg) {
+            for (int jj = 0; jj < 16; ++jj) p.debug[DBG_A + i * 64 + cb * 16 + jj] = a16[jj];
+          }
+        } else {
+          float p16[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = cb * 16 + jj;
+            p16[jj] = (j <= i) ? v[jj] * __expf(gi - gam[j]) : 0.f;
+          }
+          const uint32_t c0 = cb * 2;
+          sts128(sb + OFF_P + sw128_off(i, c0), pack_bf16x2(p16[0], p16[1]),
+                 pack_bf16x2(p16[2], p16[3]), pack_bf16x2(p16[4], p16[5]),
+                 pack_bf16x2(p16[6], p16[7]));
+          sts128(sb + OFF_P + sw128_off(i, c0 + 1), pack_bf16x2(p16[8], p16[9]),
+                 pack_bf16x2(p16[10], p16[11]), pack_bf16x2(p16[12], p16[13]),
+                 pack_bf16x2(p16[14], p16[15]));
+          if (dbg) {
+            for (int jj = 0; jj < 16; ++jj) p.debug[DBG_P + i * 64 + cb * 16 + jj] = p16[jj];
+          }
+        }
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+
+    // ---- T = (I + A)^-1: thread (column j, parity par) keeps T[2m+par][j] ----
+    {
+      const int j = tid >> 1, par = tid & 1;
+      float Tc[32];
+#pragma unroll
+      for (int m = 0; m < 32; ++m) Tc[m] = (2 * m + par == j) ? 1.f : 0.f;
+#pragma unroll
+      for (int i = 1; i < 64; ++i) {
+        const float* arow = Af + i * kAPitch + par;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < (i + 1) / 2; ++m) acc = fmaf(arow[2 * m], Tc[m], acc);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if ((i & 1) == par) Tc[i >> 1] = ((i == j) ? 1.f : 0.f) - acc;
+      }
+      __syncthreads();  // everyone done reading A
+      float* trow = Af + j * kAPitch;  // row j of T^T = column j of T
+#pragma unroll
+      for (int m = 0; m < 32; ++m) trow[2 * m + par] = Tc[m];
+    }
+    __syncthreads();
+    {
+      // threads 0-63: T diag(beta); 64-127: T diag(beta e^gamma); row j of the
+      // MN-major tile holds column j of T.
+      const int j = tid & 63;
+      const bool hat = tid >= 64;
+      const float sc = hat ? bet[j] * __expf(gam[j]) : bet[j];
+      const float* trow = Af + j * kAPitch;
+      const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const float* x = trow + ch * 8;
+        sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0] * sc, x[1] * sc),
+               pack_bf16x2(x[2] * sc, x[3] * sc), pack_bf16x2(x[4] * sc, x[5] * sc),
+               pack_bf16x2(x[6] * sc, x[7] * sc));
+      }
+      if (dbg && !hat) {
+        for (int i = 0; i < 64; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+
+    // ---- MMA 2: U = T~ V, W = T^ K ----------------------------------------
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_TB + ks * 2048, 8192, 1024),
+                    sdesc_sw128(vsm + ks * 2048, 8192, 1024), idesc_tv, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_ss(tmem + TM_W, sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024),
+                    sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_tv, ks > 0);
+      mma_commit(bar_mma);
+    }
+    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    tc_fence_after();
+
+    // ---- W -> bf16 K-major tile (rows t = 16*warp + lane for lane < 16) -----
+    {
+      const int t = warp * 16 + lane;
+      float v[16];
+#pragma unroll
+      for (int cb = 0; cb < 8; ++cb) {
+        tmem_ld16(tmem + lane_base + TM_W + cb * 16, v);
+        tmem_wait_ld();
+        if (lane < 16) {
+          write_bf16_row16(sb + OFF_AF + (cb >> 2) * 8192, t, cb, v);
+          if (dbg)
+            for (int i = 0; i < 16; ++i) p.debug[DBG_W + t * 128 + cb * 16 + i] = v[i];
+        }
+      }
+      if (dbg) {
+#pragma unroll
+        for (int cb = 0; cb < 8; ++cb) {
+          tmem_ld16(tmem + lane_base + TM_VN + cb * 16, v);
+          tmem_wait_ld();
+          if (lane < 16)
+            for (int i = 0; i < 16; ++i) p.debug[DBG_U + t * 128 + cb * 16 + i] = v[i];
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- MMA 3: Vn = U - W S (accumulate on U), QS = Q S --------------------
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_AF + kb * 8192 + kin, 16, 1024),
+                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_vn, 1);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
+        mma_bf16_ss(tmem + TM_W, sdesc_sw128(kq + kb * 16384 + 8192 + kin, 16, 1024),
+                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_qs, ks > 0);
+      }
+      mma_commit(bar_mma);
+    }
+    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    tc_fence_after();
+
+    // ---- Vn -> bf16 (B of P Vn); Vd = e^{g63 - g_t} Vn -> hi/lo (A of state) --
+    {
+      const int t = warp * 16 + lane;
+      const bool valid = lane < 16 && t < L;
+      const float dec = valid ? __expf(gam[63] - gam[t]) : 0.f;
+      float v[16], hi[16], lo[16];
+#pragma unroll
+      for (int cb = 0; cb < 8; ++cb) {
+        tmem_ld16(tmem + lane_base + TM_VN + cb * 16, v);
+        tmem_wait_ld();
+        if (lane < 16) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float x = valid ? v[i] : 0.f;
+            v[i] = x;
+            const float d = x * dec;
+            hi[i] = __bfloat162float(__float2bfloat16_rn(d));
+            lo[i] = d - hi[i];
+          }
+          const uint32_t blk = (cb >> 2) * 8192;
+          write_bf16_row16(sb + OFF_VN + blk, t, cb, v);
+          write_bf16_row16(sb + OFF_VH + blk, t, cb, hi);
+          write_bf16_row16(sb + OFF_VL + blk, t, cb, lo);
+          if (dbg)
+            for (int i = 0; i < 16; ++i) p.debug[DBG_VN + t * 128 + cb * 16 + i] = v[i];
+        }
+      }
+      if (dbg) {
+#pragma unroll
+        for (int cb = 0; cb < 8; ++cb) {
+          tmem_ld16(tmem + lane_base + TM_W + cb * 16, v);
+          tmem_wait_ld();
+          if (lane < 16)
+            for (int i = 0; i < 16; ++i) p.debug[DBG_QS + t * 128 + cb * 16 + i] = v[i];
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- MMA 4: PV = P Vn (into the Vn columns); St += Vd_hi^T K + Vd_lo^T K --
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_P + ks * 32, 16, 1024),
+                    sdesc_sw128(sb + OFF_VN + ks * 2048, 8192, 1024), idesc_pv, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VH + ks * 2048, 8192, 1024),
+                    sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_st, 1);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VL + ks * 2048, 8192, 1024),
+                    sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_st, 1);
+      mma_commit(bar_mma);
+    }
+    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    tc_fence_after();
+
+    // ---- output rows: O = scale (e^{gamma_t} QS + PV) ------------------------
+    {
+      const int t = warp * 16 + lane;
+      const bool valid = lane < 16 && t < L;
+      const float eg = valid ? __expf(gam[t]) : 0.f;
+      __nv_bfloat16* orow = p.out + ((t0 + (valid ? t : 0)) * p.Hv + h) * kHead;
+      float qs[16], pv[16];
+#pragma unroll
+      for (int cb = 0; cb < 8; ++cb) {
+        tmem_ld16(tmem + lane_base + TM_W + cb * 16, qs);
+        tmem_ld16(tmem + lane_base + TM_VN + cb * 16, pv);
+        tmem_wait_ld();
+        if (valid) {
+          float o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = p.scale * fmaf(eg, qs[i], pv[i]);
+          uint4 w0 = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+          uint4 w1 = make_uint4(pack_bf16x2(o[8], o[9]), pack_bf16x2(o[10], o[11]),
+                                pack_bf16x2(o[12], o[13]), pack_bf16x2(o[14], o[15]));
+          reinterpret_cast<uint4*>(orow + cb * 16)[0] = w0;
+          reinterpret_cast<uint4*>(orow + cb * 16)[1] = w1;
+        }
+        if (dbg && lane < 16)
+          for (int i = 0; i < 16; ++i) p.debug[DBG_PV + t * 128 + cb * 16 + i] = pv[i];
+      }
+      if (dbg) {
+        float v[16];
+#pragma unroll
+        for (int cb = 0; cb < 8; ++cb) {
+          tmem_ld16(tmem + lane_base + TM_ST + cb * 16, v);
+          tmem_wait_ld();
+          for (int i = 0; i < 16; ++i) p.debug[DBG_ST + tid * 128 + cb * 16 + i] = v[i];
+        }
+      }
+    }
+  }
+
+  // ---- final state -> new_state (row v = tid) ---------------------------------
+  if (!aborted) {
+    tc_fence_after();
+    float* dst = ns_rows + tid * kHead;
+#pragma unroll
+    for (int cb = 0; cb < 8; ++cb) {
+      float v[16];
+      tmem_ld16(tmem + lane_base + TM_ST + cb * 16, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4)
+        st_stream_f4(dst + cb * 16 + q4 * 4,
+                     make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
+    }
+  } else {
+    if (tid == 0) atomicOr(&g_gdn_status, kStatusPrefillTimeout);
+    // let in-flight tensor-core work drain (bounded) before TMEM is released
+    if (tid == 0) {
+      mma_commit(bar_mma);
+      mbar_wait(bar_mma, mma_phase, kTimeoutNs);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// A wait on an mbarrier that nothing ever arrives on, bounded by timeout_ns:
+// exercises the timeout path (status word) without faulting or hanging.
+__global__ void gdn_wait_probe_kernel(uint64_t timeout_ns, uint32_t* result) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, timeout_ns);
+  if (threadIdx.x == 0) {
+    if (!ok) atomicOr(&g_gdn_status, kStatusProbeTimeout);
+    if (result) *result = ok ? 1u : 0u;
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+// [T, heads, 128] bf16, box = 64 tokens x 1 head x 64 dims, 128-byte swizzle.
+cudaError_t make_head_map(CUtensorMap* m, const void* base, int64_t heads, int64_t T) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHead), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHead) * 2,
+                           static_cast<cuuint64_t>(heads) * kHead * 2};
+  cuuint32_t box[3] = {64, 1, 64};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <bool DEBUG>
+cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg_head,
+                        int dbg_chunk, cudaStream_t s) {
+  if (a.N == 0) return cudaSuccess;
+  if (a.T == 0) {  // every sequence is empty: zero final states
+    return cudaMemsetAsync(a.new_state, 0,
+                           static_cast<size_t>(a.N) * a.Hv * kHead * kHead * sizeof(float), s);
+  }
+  CUtensorMap mq, mk, mv;
+  cudaError_t e;
+  if ((e = make_head_map(&mq, a.q, a.Hq, a.T)) != cudaSuccess) return e;
+  if ((e = make_head_map(&mk, a.k, a.Hq, a.T)) != cudaSuccess) return e;
+  if ((e = make_head_map(&mv, a.v, a.Hv, a.T)) != cudaSuccess) return e;
+  static bool attr_set = false;
+  if (!attr_set) {
+    e = cudaFuncSetAttribute(gdn_prefill_chunked_kernel<DEBUG>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  ChunkParams p{a.state, a.A_log, a.dt_bias,
+                static_cast<const __nv_bfloat16*>(a.a), static_cast<const __nv_bfloat16*>(a.b),
+                a.cu_seqlens, static_cast<__nv_bfloat16*>(a.out), a.new_state, debug, a.scale,
+                a.T, a.N, static_cast<int>(a.Hq), static_cast<int>(a.Hv), dbg_seq, dbg_head,
+                dbg_chunk};
+  const int64_t ctas = a.N * a.Hv;
+  if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+  gdn_prefill_chunked_kernel<DEBUG><<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(
+      mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_prefill_chunked(const PrefillArgs& a, cudaStream_t s) {
+  return launch_impl<false>(a, nullptr, 0, 0, 0, s);
+}
+
+cudaError_t launch_prefill_chunked_debug(const PrefillArgs& a, float* debug, int dbg_seq,
+                                         int dbg_head, int dbg_chunk, cudaStream_t s) {
+  return launch_impl<true>(a, debug, dbg_seq, dbg_head, dbg_chunk, s);
+}
+
+int prefill_chunked_debug_floats() { return DBG_SIZE; }
+
+cudaError_t launch_wait_probe(uint64_t timeout_ns, uint32_t* result, cudaStream_t s) {
+  gdn_wait_probe_kernel<<<1, 32, 0, s>>>(timeout_ns, result);
+  return cudaGetLastError();
+}
+
+cudaError_t read_status(uint32_t* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_gdn_status, sizeof(uint32_t));
+  if (e != cudaSuccess) return e;
+  if (clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_gdn_status, &zero, sizeof(uint32_t));
+  }
+  return e;
+}
+
+}  // namespace gdn

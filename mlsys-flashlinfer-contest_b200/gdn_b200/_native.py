@@ -26,6 +26,12 @@ SIGNATURES = {
     "gdn_prefill_recurrent": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P]),
     "gdn_prep_meta": (I, [P, I64, P, P, I64, P]),
     "gdn_chunk_upper_bound": (I64, [I64, I64]),
+    "gdn_prefill_chunked": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P]),
+    "gdn_prefill_chunked_debug": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64,
+                                      I64, P, I64, I64, I64, I64, P]),
+    "gdn_prefill_chunked_debug_floats": (I64, []),
+    "gdn_read_status": (I, [P, I]),
+    "gdn_wait_probe": (I, [ctypes.c_uint64, P, P]),
 }
 
 _lib = None

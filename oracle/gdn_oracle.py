@@ -290,3 +290,53 @@ def rel_err(x, ref) -> float:
     ref = np.asarray(ref, np.float64)
     den = max(np.linalg.norm(ref), 1e-30)
     return float(np.linalg.norm(x - ref) / den)
+
+
+def chunk_intermediates(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, n, h, c, chunk=CHUNK):
+    """fp64 intermediates of chunk ``c`` of sequence ``n``, v-head ``h``, in the
+    definitions the fused tensor-core kernel uses (it dumps the same names):
+    gam, bet (zero log-decay and beta past the sequence end), A, P, T, U, W, Vn,
+    QS, PV and the k-last state after the chunk.  Rows past the sequence end hold
+    the packed neighbours' data (or zeros past T), as the kernel's tile loads do.
+    The state at the chunk start comes from the token recurrence in fp64."""
+    T_, Hq, K = np.asarray(q).shape
+    Hv = np.asarray(v).shape[1]
+    qh = h // (Hv // Hq)
+    cu = [int(x) for x in np.asarray(cu_seqlens).reshape(-1)]
+    s0, e0 = cu[n], cu[n + 1]
+    lg_all, beta_all = log_gates(A_log, a, dt_bias, b)
+    S = (np.asarray(state[n, h], np.float64).T.copy() if state is not None
+         else np.zeros((K, HEAD)))
+    kk = np.asarray(k, np.float64)[:, qh]
+    qq = np.asarray(q, np.float64)[:, qh]
+    vv = np.asarray(v, np.float64)[:, h]
+    t0 = s0 + c * chunk
+    for t in range(s0, t0):                       # recurrence up to the chunk start
+        g = np.exp(float(lg_all[t, h]))
+        S = g * S
+        S = S + np.outer(kk[t], float(beta_all[t, h]) * (vv[t] - kk[t] @ S))
+    L = min(chunk, e0 - t0)
+    rows = np.arange(t0, t0 + chunk)
+    inb = rows < T_
+    Kc = np.where(inb[:, None], kk[np.minimum(rows, T_ - 1)], 0.0)
+    Qc = np.where(inb[:, None], qq[np.minimum(rows, T_ - 1)], 0.0)
+    Vc = np.where(inb[:, None], vv[np.minimum(rows, T_ - 1)], 0.0)
+    valid = np.arange(chunk) < L
+    lg = np.where(valid, lg_all[np.minimum(rows, T_ - 1), h].astype(np.float64), 0.0)
+    bet = np.where(valid, beta_all[np.minimum(rows, T_ - 1), h].astype(np.float64), 0.0)
+    gam = np.cumsum(lg)
+    diff = np.minimum(gam[:, None] - gam[None, :], 0.0)
+    low = np.tril(np.ones((chunk, chunk), bool), -1)
+    E = np.exp(diff)
+    A = np.where(low, bet[:, None] * (Kc @ Kc.T) * E, 0.0)
+    P = np.where(low | np.eye(chunk, dtype=bool), (Qc @ Kc.T) * E, 0.0)
+    Tm = np.linalg.inv(np.eye(chunk) + A)
+    U = Tm @ (bet[:, None] * Vc)
+    W = Tm @ ((bet * np.exp(gam))[:, None] * Kc)
+    Vn = U - W @ S
+    Vn[~valid] = 0.0
+    QS = Qc @ S
+    PV = P @ Vn
+    S_after = np.exp(gam[-1]) * S + Kc.T @ (np.exp(gam[-1] - gam)[:, None] * Vn)
+    return dict(gam=gam, bet=bet, A=A, P=P, T=Tm, U=U, W=W, Vn=Vn, QS=QS, PV=PV,
+                St=S_after.T, L=L, valid=valid)

@@ -120,3 +120,27 @@ def test_c_oracle_threads_do_not_change_results():
     o1, s1 = C.decode(*inp.args(), nthreads=1)
     o2, s2 = C.decode(*inp.args(), nthreads=3)
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
+
+
+@pytest.mark.parametrize("lengths,n,h,c", [([150], 0, 1, 1), ([40, 130], 1, 3, 2), ([64], 0, 0, 0)])
+def test_chunk_intermediates_match_recurrence(lengths, n, h, c):
+    inp = W.make_prefill_inputs(lengths, 2, 4, seed=sum(lengths) + n + h)
+    args = _np_args(inp)
+    ref = O.chunk_intermediates(*args[:9], n, h, c)
+    # the state after the chunk equals the recurrence run up to the chunk end
+    cu = np.asarray(args[8])
+    end = min(int(cu[n]) + (c + 1) * O.CHUNK, int(cu[n + 1]))
+    cut = list(args)
+    cut[8] = np.array([0, end - int(cu[n])])
+    sl = slice(int(cu[n]), end)
+    for i in (0, 1, 2, 5, 7):
+        cut[i] = args[i][sl]
+    cut[3] = args[3][n:n + 1]
+    _, s_rec = O.prefill(*cut)
+    assert O.rel_err(ref["St"], s_rec[0, h]) < 1e-5
+    # the chunk's outputs: scale (e^gamma QS + PV) equals the recurrence outputs
+    o_rec, _ = O.prefill(*cut)
+    t0 = c * O.CHUNK
+    o_chunk = O.resolve_scale(None) * (np.exp(ref["gam"])[:, None] * ref["QS"] + ref["PV"])
+    L = ref["L"]
+    assert O.rel_err(o_chunk[:L], O.bf16_to_f32(o_rec[t0:t0 + L, h])) < 5e-3
