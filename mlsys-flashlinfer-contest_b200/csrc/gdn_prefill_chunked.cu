@@ -12,7 +12,8 @@
 //   G|QK  = [K;Q] K^T                          (tcgen05, M=128: rows 0-63 KK^T, 64-127 QK^T)
 //   A     = strict_tril(beta_t G e^{gamma_t - gamma_s}),  P = tril(QK e^{gamma_t - gamma_s})
 //   T     = (I + A)^-1                         (fp32, CUDA cores)
-//   U     = T diag(beta) V,  W = T diag(beta e^gamma) K          (tcgen05)
+//   U     = beta (.) V + T_off diag(beta) V,  W = T diag(beta e^gamma) K
+//           (tcgen05; the unit diagonal of T is applied exactly in fp32)
 //   Vn    = U - W S,         QS = Q S                            (tcgen05, S as bf16)
 //   O     = scale (e^{gamma_t} QS + P Vn)      (tcgen05 for P Vn)
 //   St   <- e^{gamma_63} St + Vd^T K,  Vd = e^{gamma_63 - gamma_t} Vn split into
@@ -98,6 +99,29 @@ __device__ __forceinline__ void write_bf16_row16(uint32_t tile, uint32_t row, in
          pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
   sts128(tile + sw128_off(row, c0 + 1), pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
          pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
+}
+
+// Reads columns [16*cb, 16*cb+16) of row `row` of a 128-column bf16 tile stored
+// as two swizzled 64-column blocks of `block_bytes` each, widened to fp32.
+__device__ __forceinline__ void read_bf16_row16(uint32_t tile, uint32_t block_bytes,
+                                                uint32_t row, int cb, float* v) {
+  const uint32_t base = tile + (cb >> 2) * block_bytes;
+  const uint32_t c0 = (cb & 3) * 2;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t w0, w1, w2, w3;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                 : "r"(base + sw128_off(row, c0 + h)));
+    v[8 * h + 0] = bf16_lo(w0);
+    v[8 * h + 1] = bf16_hi(w0);
+    v[8 * h + 2] = bf16_lo(w1);
+    v[8 * h + 3] = bf16_hi(w1);
+    v[8 * h + 4] = bf16_lo(w2);
+    v[8 * h + 5] = bf16_hi(w2);
+    v[8 * h + 6] = bf16_lo(w3);
+    v[8 * h + 7] = bf16_hi(w3);
+  }
 }
 
 template <bool DEBUG>
@@ -355,6 +379,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       // threads 0-63: T diag(beta); 64-127: T diag(beta e^gamma); row j of the
       // MN-major tile holds column j of T.
+      // The T~ tile leaves out the unit diagonal: U = beta (.) V + T~_off V, and the
+      // beta (.) V term is added in fp32 when Vn is drained (a bf16 beta_j on the
+      // diagonal would cost ~2^-9 relative error on all of U).
       const int j = tid & 63;
       const bool hat = tid >= 64;
       const float sc = hat ? bet[j] * __expf(gam[j]) : bet[j];
@@ -362,10 +389,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
-        const float* x = trow + ch * 8;
-        sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0] * sc, x[1] * sc),
-               pack_bf16x2(x[2] * sc, x[3] * sc), pack_bf16x2(x[4] * sc, x[5] * sc),
-               pack_bf16x2(x[6] * sc, x[7] * sc));
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = (!hat && ch * 8 + e == j) ? 0.f : trow[ch * 8 + e] * sc;
+        sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+               pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
       }
       if (dbg && !hat) {
         for (int i = 0; i < 64; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
@@ -409,8 +437,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cb = 0; cb < 8; ++cb) {
           tmem_ld16(tmem + lane_base + TM_VN + cb * 16, v);
           tmem_wait_ld();
-          if (lane < 16)
-            for (int i = 0; i < 16; ++i) p.debug[DBG_U + t * 128 + cb * 16 + i] = v[i];
+          if (lane < 16) {
+            float vrow[16];
+            read_bf16_row16(vsm, 8192, t, cb, vrow);
+            for (int i = 0; i < 16; ++i)
+              p.debug[DBG_U + t * 128 + cb * 16 + i] = fmaf(bet[t], vrow[i], v[i]);
+          }
         }
       }
     }
@@ -449,9 +481,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem + lane_base + TM_VN + cb * 16, v);
         tmem_wait_ld();
         if (lane < 16) {
+          float vrow[16];
+          read_bf16_row16(vsm, 8192, t, cb, vrow);
+          const float bt = bet[t];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float x = valid ? v[i] : 0.f;
+            const float x = valid ? fmaf(bt, vrow[i], v[i]) : 0.f;
             v[i] = x;
             const float d = x * dec;
             hi[i] = __bfloat162float(__float2bfloat16_rn(d));
