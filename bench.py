@@ -340,43 +340,82 @@ def run_e2e(args, inp, dev, stream, dist, world):
 
 
 def run_prefill_bench(args, rank, world, local_rank, dev, dist):
-    """Prefill tokens/s on BASELINE config 3's shape (4 x 16384 tokens), v-heads
-    sharded over ranks (Hv/N per rank, with the matching qk-heads)."""
-    from gdn_b200 import prefill, workloads as W
-    if HV % world or HQ % world:
+    """Prefill tokens/s on BASELINE config 3's shape (4 x 16384 tokens): each
+    rank owns Hv/N v-heads (whole GVA groups) of every sequence; the output
+    all-gather over NCCL is timed separately (only callers that need every
+    head on every rank pay it)."""
+    from gdn_b200 import prefill, sharding as S, workloads as W
+    if HQ % world:
         return None
-    hv, hq = HV // world, HQ // world
+    sh = S.head_shard(HQ, HV, world, rank)
+    hq, hv = sh.num_q_heads, sh.num_v_heads
     lengths = [args.prefill_len] * args.prefill_seqs
     inp = W.make_prefill_inputs(lengths, hq, hv, seed=77 + rank, device=dev)
-    T = sum(lengths)
+    T, Nseq = sum(lengths), len(lengths)
     out = torch.empty_like(inp.v)
     ns = torch.empty_like(inp.state)
-    fn = prefill.launch
 
     def once():
-        fn(*inp.args(), out, ns)
+        prefill.launch(*inp.args(), out, ns)
 
-    once()
+    for _ in range(2):
+        once()
     torch.cuda.synchronize()
     reps = args.prefill_steps
     stream = torch.cuda.current_stream(dev)
     if dist:
         dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    evs[0].record(stream)
+    for i in range(reps):
         once()
-    e1.record(stream)
+        evs[i + 1].record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(reps)]
+    t = torch.tensor([statistics.mean(per)], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    # algorithmic traffic and work of one call on this rank
+    tok_bytes = 2 * hq * D * 2 + 2 * hv * D * 2 + 2 * hv * 2     # q,k + v,o + a,b
+    bytes_call = T * tok_bytes + Nseq * hv * 2 * D * D * 4        # + state in and out
+    flops_call = T * hv * 163840                                 # 5.24 MFLOP/token at Hv=32
+    hbm_peak, tc_burst, _, peak_src = measured_peaks()
+    t_hbm = bytes_call / (hbm_peak * 1e9)
+    t_tc = flops_call / (tc_burst * 1e12)
+    bound = "hbm" if t_hbm >= t_tc else "tensor"
     res = {"metric": "gdn_prefill_tokens_per_s", "value": round(T / (ms / 1e3), 1),
            "unit": "tokens/s", "ms_per_call": round(ms, 4), "steps": reps,
-           "workload": f"{args.prefill_seqs} x {args.prefill_len} tokens, Hq={HQ}, Hv={HV} "
-                       f"({hv} v-heads per rank)", "path": "gdn_b200.prefill.launch"}
+           "workload": f"BASELINE config 3: {args.prefill_seqs} x {args.prefill_len} tokens, "
+                       f"Hq={HQ}, Hv={HV} ({hv} v-heads on each of {world} ranks), random fp32 "
+                       f"initial states", "path": "gdn_b200.prefill.launch (fused chunked kernel)",
+           "gpu_launches_per_call": 1,
+           "roofline": {"bound": bound, "algorithmic_bytes_per_call": bytes_call,
+                        "algorithmic_flops_per_call": flops_call,
+                        "achieved_GBps": round(bytes_call / (ms / 1e3) / 1e9, 1),
+                        "achieved_TFLOPs": round(flops_call / (ms / 1e3) / 1e12, 2),
+                        "hbm_peak_GBps": hbm_peak, "tc_peak_TFLOPs": tc_burst,
+                        "roofline_ms": round(max(t_hbm, t_tc) * 1e3, 4),
+                        "frac": round(max(t_hbm, t_tc) * 1e3 / ms, 4), "peak_source": peak_src}}
+    if dist and world > 1:
+        from gdn_b200.sharding import all_gather_heads
+        for _ in range(2):
+            all_gather_heads(out)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            full = all_gather_heads(out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ag = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(ag, op=dist.ReduceOp.MAX)
+        recv = (world - 1) * out.numel() * out.element_size()
+        res["allgather_o"] = {"ms": round(float(ag.item()), 4), "bytes_received_per_rank": recv,
+                              "GBps_per_rank": round(recv / (float(ag.item()) / 1e3) / 1e9, 1),
+                              "value_with_gather": round(T / ((ms + float(ag.item())) / 1e3), 1)}
+        del full
     return res
 
 
@@ -420,7 +459,9 @@ def main():
                     help="sequences per rank (default 256 = BASELINE config 1; smaller only for profiling)")
     ap.add_argument("--prefill-seqs", type=int, default=4)
     ap.add_argument("--prefill-len", type=int, default=16384)
-    ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--prefill-steps", type=int, default=10)
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the prefill leg and print its JSON (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     B_PER_RANK = args.batch_per_rank
@@ -439,6 +480,13 @@ def main():
                                  device_id=torch.device("cuda", local_rank))
         dist = tdist
     try:
+        if args.prefill_only:
+            dev = torch.device("cuda", local_rank)
+            torch.cuda.set_device(dev)
+            res = run_prefill_bench(args, rank, world, local_rank, dev, dist)
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            return
         run_ours(args, rank, world, local_rank, dist)
     finally:
         if dist:

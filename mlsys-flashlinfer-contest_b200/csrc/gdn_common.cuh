@@ -27,6 +27,37 @@ __device__ __forceinline__ float log_decay(float A_log, float a, float dt_bias) 
 
 __device__ __forceinline__ float sigmoidf_acc(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// 2^x with the hardware approximation, subnormal results flushed to zero.  Used
+// on decay factors exp(gamma_i - gamma_j) <= 1, where a flushed subnormal only
+// drops a contribution already below 2^-126 of the kept terms.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// softplus with torch's threshold (identity above 20) from the hardware
+// ex2/lg2 approximations.  Below -15, log1p(e^x) equals e^x to fp32 precision,
+// so that branch returns e^x directly instead of losing it in 1 + e^x.
+__device__ __forceinline__ float softplus_t20_fast(float x) {
+  if (x > 20.0f) return x;
+  const float e = ex2_ftz(x * kLog2e);
+  return x < -15.0f ? e : kLn2 * lg2_approx(1.0f + e);
+}
+
+__device__ __forceinline__ float sigmoid_fast(float x) {
+  return __frcp_rn(1.0f + ex2_ftz(-x * kLog2e));
+}
+
 // ------------------------------------------------------------------ bf16
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }

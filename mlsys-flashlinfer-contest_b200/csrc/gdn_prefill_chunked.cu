@@ -11,7 +11,7 @@
 // S = [K,V] state at the chunk start, St = S^T = k-last [V,K] in TMEM):
 //   G|QK  = [K;Q] K^T                          (tcgen05, M=128: rows 0-63 KK^T, 64-127 QK^T)
 //   A     = strict_tril(beta_t G e^{gamma_t - gamma_s}),  P = tril(QK e^{gamma_t - gamma_s})
-//   T     = (I + A)^-1                         (fp32, CUDA cores)
+//   T     = (I + A)^-1                         (fp32, CUDA cores, blocks of 16)
 //   U     = beta (.) V + T_off diag(beta) V,  W = T diag(beta e^gamma) K
 //           (tcgen05; the unit diagonal of T is applied exactly in fp32)
 //   Vn    = U - W S,         QS = Q S                            (tcgen05, S as bf16)
@@ -38,7 +38,7 @@ __device__ uint32_t g_gdn_status = 0;
 namespace {
 using namespace sm100;
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;  // 8 warps: two per TMEM lane quarter
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait, then give up
 
 // ---- shared memory map (offsets from a 1024-aligned base) -----------------
@@ -51,12 +51,13 @@ constexpr uint32_t OFF_ST = OFF_V + 2 * kVStage;   // bf16 S: [kb 2][v 128][128 
 constexpr uint32_t OFF_P = OFF_ST + 32768;         // P: [t 64][128 B] (K-major A)
 constexpr uint32_t OFF_TB = OFF_P + 8192;          // T diag(beta): [s 64][t 128 B] (MN-major A)
 constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T diag(beta e^gamma)
-constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A / T^T [64][68]; later W [kb 2][t 64][128 B]
-constexpr uint32_t OFF_VN = OFF_AF + 17408;        // Vn bf16 [vb 2][t 64][128 B] (MN-major B)
+constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A^T [64][68]; later W [kb 2][t 64][128 B]
+constexpr uint32_t OFF_VN = OFF_AF + 17408;        // Vn bf16 [vb 2][t 64][128 B] (MN-major B);
+                                                   // during the inverse: fp32 T^T [64][68] (spills into VH)
 constexpr uint32_t OFF_VH = OFF_VN + 16384;        // Vd hi (MN-major A)
-constexpr uint32_t OFF_VL = OFF_VH + 16384;        // Vd lo
+constexpr uint32_t OFF_VL = OFF_VH + 16384;        // Vd lo; during the inverse: fp32 (A21 T11)^T [32][36]
 constexpr uint32_t OFF_MISC = OFF_VL + 16384;      // gamma[64], beta[64], barriers, tmem slot
-constexpr uint32_t kSmemBytes = OFF_MISC + 1024 + 1024;  // + slack for the 1024 alignment
+constexpr uint32_t kSmemBytes = OFF_MISC + 2048 + 1024;  // + slack for the 1024 alignment
 constexpr int kAPitch = 68;                        // fp32 row pitch of A / T^T
 
 // ---- TMEM columns ----------------------------------------------------------
@@ -88,7 +89,9 @@ struct ChunkParams {
 constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_T = DBG_P + 4096,
               DBG_U = DBG_T + 4096, DBG_W = DBG_U + 8192, DBG_VN = DBG_W + 8192,
               DBG_QS = DBG_VN + 8192, DBG_PV = DBG_QS + 8192, DBG_ST = DBG_PV + 8192,
-              DBG_SIZE = DBG_ST + 16384;
+              DBG_CLK = DBG_ST + 16384, DBG_SIZE = DBG_CLK + 16;
+// DBG_CLK: SM cycles thread 0 of the debug CTA spent in each phase, summed over
+// all chunks of its sequence (phases: see the PHASE() marks in the chunk loop).
 
 __device__ __forceinline__ void write_bf16_row16(uint32_t tile, uint32_t row, int cb,
                                                  const float* v) {
@@ -129,18 +132,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                                const __grid_constant__ CUtensorMap tm_k,
                                const __grid_constant__ CUtensorMap tm_v, const ChunkParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Align by offsetting the __shared__ array itself (not through an integer
+  // cast), so every derived pointer stays in the shared state space and its
+  // accesses compile to ld/st.shared rather than generic loads and stores.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb = smem_u32(smem);
-  float* gam = reinterpret_cast<float*>(smem + OFF_MISC);
-  float* bet = gam + 64;
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + OFF_MISC + 512);  // [2]
+  // gamma * log2(e) and beta per token, double-buffered by chunk parity: the
+  // gates of chunk c+1 are computed while chunk c's tensor-core work runs.
+  float* gates_buf = reinterpret_cast<float*>(smem + OFF_MISC);  // [2][gamma 64 | beta 64]
+  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + OFF_MISC + 1024);  // [2]
   uint64_t* bar_mma = bar_tma + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
-  float* Af = reinterpret_cast<float*>(smem + OFF_AF);
+  float* At = reinterpret_cast<float*>(smem + OFF_AF);   // A column-major: At[k][i] = A[i][k]
+  float* Tcm = reinterpret_cast<float*>(smem + OFF_VN);  // T column-major: Tcm[j][i] = T[i][j]
+  float* Mcm = reinterpret_cast<float*>(smem + OFF_VL);  // (A21 T11) column-major, pitch 36
+  float* Xcm = Mcm + 32 * 36;                            // 2 x [16][17] level-1 products
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+  const int hf = warp >> 2;      // column half handled by this warp
+  const int g = lane >> 2, tq = lane & 3;  // 16x256b fragment coordinates
+  const int r_lo = 16 * quarter + g;       // rows of an M=64 accumulator held by this thread
+  const int rowv = 32 * quarter + lane;    // row of an M=128 accumulator held by this thread
   const int h = static_cast<int>(blockIdx.x % p.Hv);
   const int64_t n = blockIdx.x / p.Hv;
   const int qh = h / (p.Hv / p.Hq);
@@ -155,6 +169,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
+  long long clk_acc[16];
+  long long clk_last = 0;
+  if constexpr (DEBUG) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) clk_acc[i] = 0;
+    clk_last = clock64();
+  }
+#define PHASE(k)                              \
+  if constexpr (DEBUG) {                      \
+    const long long now_ = clock64();         \
+    clk_acc[k] += now_ - clk_last;            \
+    clk_last = now_;                          \
+  }
 
   if (tid == 0) {
     mbar_init(&bar_tma[0], 1);
@@ -173,24 +200,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-  const float A_log_h = p.A_log[h], dt_bias_h = p.dt_bias[h];
+  const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+  const uint32_t tq_st = tmem + lane_base + TM_ST + 64 * hf;  // this thread's St columns
+  const float neg_exp_A = -expf(p.A_log[h]);
+  const float dt_bias_h = p.dt_bias[h];
 
-  // ---- initial state -> TMEM (thread tid owns state row v = tid) ----------
+  // ---- initial state -> TMEM (row rowv, columns [64 hf, 64 hf + 64)) -------
   {
-    const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + tid * kHead : nullptr;
+    const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + rowv * kHead + 64 * hf
+                               : nullptr;
 #pragma unroll
-    for (int cb = 0; cb < 8; ++cb) {
-      float v[16];
+    for (int cb = 0; cb < 2; ++cb) {
+      float v[32];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float4 x = src ? ld_stream_f4(src + cb * 16 + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q4 = 0; q4 < 8; ++q4) {
+        float4 x = src ? ld_stream_f4(src + cb * 32 + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
         v[4 * q4] = x.x;
         v[4 * q4 + 1] = x.y;
         v[4 * q4 + 2] = x.z;
         v[4 * q4 + 3] = x.w;
       }
-      tmem_st16(tmem + lane_base + TM_ST + cb * 16, v);
+      tmem_st32(tq_st + cb * 32, v);
     }
     tmem_wait_st();
   }
@@ -218,7 +248,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     return __syncthreads_or(ok ? 0 : 1) == 0;
   };
 
+  // Gates of one chunk from raw a/b values held by warp 0 (two tokens per lane):
+  // log-decay, its inclusive scan (gamma, stored in log2 units) and beta.
+  float ga_raw[2] = {0.f, 0.f}, gb_raw[2] = {0.f, 0.f};
+  auto prefetch_gates = [&](int cc) {
+    const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int64_t t = t0c + 2 * lane + e;
+      if (t < eos) {
+        ga_raw[e] = __bfloat162float(p.a[t * p.Hv + h]);
+        gb_raw[e] = __bfloat162float(p.b[t * p.Hv + h]);
+      }
+    }
+  };
+  auto compute_gates = [&](int cc) {  // warp 0 only
+    const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
+    const int Lc = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0c));
+    float lg[2], bt[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const bool valid = 2 * lane + e < Lc;
+      lg[e] = valid ? neg_exp_A * softplus_t20_fast(ga_raw[e] + dt_bias_h) : 0.f;
+      bt[e] = valid ? sigmoid_fast(gb_raw[e]) : 0.f;
+    }
+    const float pair = lg[0] + lg[1];
+    float incl = pair;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
+    }
+    float* gb = gates_buf + (cc & 1) * 128;
+    gb[2 * lane] = (incl - pair + lg[0]) * kLog2e;
+    gb[2 * lane + 1] = incl * kLog2e;
+    gb[64 + 2 * lane] = bt[0];
+    gb[64 + 2 * lane + 1] = bt[1];
+  };
+
   if (tid == 0) issue_loads(0, 0);
+  if (warp == 0) {
+    prefetch_gates(0);
+    compute_gates(0);
+    if (Ltot > kChunk) prefetch_gates(1);
+  }
   const int nchunks = static_cast<int>((Ltot + kChunk - 1) / kChunk);
 
   const uint32_t idesc_d1 = idesc_bf16(128, 64, false, false);
@@ -240,59 +313,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();  // previous chunk fully drained
     tc_fence_after();
     if (tid == 0 && c + 1 < nchunks) issue_loads(c + 1, stage ^ 1);
+    PHASE(0)
 
-    // ---- gates: warp 0, two tokens per lane, inclusive scan of log-decay ---
-    if (warp == 0) {
-      float lg[2], bt[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int t = 2 * lane + e;
-        lg[e] = 0.f;
-        bt[e] = 0.f;
-        if (t < L) {
-          const int64_t idx = (t0 + t) * p.Hv + h;
-          lg[e] = log_decay(A_log_h, __bfloat162float(p.a[idx]), dt_bias_h);
-          bt[e] = sigmoidf_acc(__bfloat162float(p.b[idx]));
-        }
-      }
-      const float pair = lg[0] + lg[1];
-      float incl = pair;
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, incl, d);
-        if (lane >= d) incl += y;
-      }
-      gam[2 * lane] = incl - pair + lg[0];
-      gam[2 * lane + 1] = incl;
-      bet[2 * lane] = bt[0];
-      bet[2 * lane + 1] = bt[1];
-      if (dbg) {
-        p.debug[DBG_GAM + 2 * lane] = gam[2 * lane];
-        p.debug[DBG_GAM + 2 * lane + 1] = incl;
-        p.debug[DBG_BET + 2 * lane] = bt[0];
-        p.debug[DBG_BET + 2 * lane + 1] = bt[1];
-      }
+    const float* gam = gates_buf + stage * 128;
+    const float* bet = gam + 64;
+    if (dbg && tid < 64) {
+      p.debug[DBG_GAM + tid] = gam[tid] / kLog2e;
+      p.debug[DBG_BET + tid] = bet[tid];
     }
-    __syncthreads();
+    PHASE(1)
 
     // ---- state pass: St -> bf16 operand tile; St *= e^{gamma_63} -----------
     {
-      const float dec = __expf(gam[63]);
+      const float dec = ex2_ftz(gam[63]);
+      float v[64];
+      tmem_ld32(tq_st, v);
+      tmem_ld32(tq_st + 32, v + 32);
+      tmem_wait_ld();
+      reg_fence(v);
+      const uint32_t tile = sb + OFF_ST + hf * 16384;
 #pragma unroll
-      for (int cb = 0; cb < 8; ++cb) {
-        float v[16];
-        tmem_ld16(tmem + lane_base + TM_ST + cb * 16, v);
-        tmem_wait_ld();
-        write_bf16_row16(sb + OFF_ST + (cb >> 2) * 16384, tid, cb, v);
+      for (int ch = 0; ch < 8; ++ch)
+        sts128(tile + sw128_off(rowv, ch), pack_bf16x2(v[8 * ch], v[8 * ch + 1]),
+               pack_bf16x2(v[8 * ch + 2], v[8 * ch + 3]), pack_bf16x2(v[8 * ch + 4], v[8 * ch + 5]),
+               pack_bf16x2(v[8 * ch + 6], v[8 * ch + 7]));
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] *= dec;
-        tmem_st16(tmem + lane_base + TM_ST + cb * 16, v);
-      }
+      for (int i = 0; i < 64; ++i) v[i] *= dec;
+      tmem_st32(tq_st, v);
+      tmem_st32(tq_st + 32, v + 32);
       tmem_wait_st();
       fence_async_smem();
     }
+    PHASE(2)
     tc_fence_before();
     if (!wait_all(&bar_tma[stage], stage ? tma_phase1 : tma_phase0)) { aborted = true; break; }
+    PHASE(3)
 
     // ---- MMA 1: [K;Q] K^T ---------------------------------------------------
     if (tid == 0) {
@@ -306,103 +361,181 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(bar_mma);
     }
     if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    PHASE(4)
     tc_fence_after();
 
-    // ---- A (warps 0-1) and P (warps 2-3) from TMEM --------------------------
+    // ---- A (quarters 0-1, stored column-major) and P (quarters 2-3) ---------
     {
-      const int i = (tid & 63);
+      const int i = rowv & 63;
       const float gi = gam[i];
-      float v[16];
+      float v[32];
+      tmem_ld32(tmem + lane_base + TM_D1 + 32 * hf, v);
+      tmem_wait_ld();
+      reg_fence(v);
+      PHASE(14)
+      if (quarter < 2) {
+        const float bi = bet[i];
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        tmem_ld16(tmem + lane_base + TM_D1 + cb * 16, v);
-        tmem_wait_ld();
-        if (warp < 2) {
-          const float bi = bet[i];
-          float a16[16];
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = cb * 16 + jj;
-            a16[jj] = (j < i) ? bi * v[jj] * __expf(gi - gam[j]) : 0.f;
-          }
-          float4* dst = reinterpret_cast<float4*>(Af + i * kAPitch + cb * 16);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            dst[q4] = make_float4(a16[4 * q4], a16[4 * q4 + 1], a16[4 * q4 + 2], a16[4 * q4 + 3]);
-          if (dbg) {
-            for (int jj = 0; jj < 16; ++jj) p.debug[DBG_A + i * 64 + cb * 16 + jj] = a16[jj];
-          }
-        } else {
-          float p16[16];
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = cb * 16 + jj;
-            p16[jj] = (j <= i) ? v[jj] * __expf(gi - gam[j]) : 0.f;
-          }
-          const uint32_t c0 = cb * 2;
-          sts128(sb + OFF_P + sw128_off(i, c0), pack_bf16x2(p16[0], p16[1]),
-                 pack_bf16x2(p16[2], p16[3]), pack_bf16x2(p16[4], p16[5]),
-                 pack_bf16x2(p16[6], p16[7]));
-          sts128(sb + OFF_P + sw128_off(i, c0 + 1), pack_bf16x2(p16[8], p16[9]),
-                 pack_bf16x2(p16[10], p16[11]), pack_bf16x2(p16[12], p16[13]),
-                 pack_bf16x2(p16[14], p16[15]));
-          if (dbg) {
-            for (int jj = 0; jj < 16; ++jj) p.debug[DBG_P + i * 64 + cb * 16 + jj] = p16[jj];
-          }
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = 32 * hf + jj;
+          const float aij = (j < i) ? bi * v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
+          At[j * kAPitch + i] = aij;
+          if (dbg) p.debug[DBG_A + i * 64 + j] = aij;
         }
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = 32 * hf + jj;
+          v[jj] = (j <= i) ? v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
+        }
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+          sts128(sb + OFF_P + sw128_off(i, 4 * hf + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
+                 pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
+                 pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
+        if (dbg)
+          for (int jj = 0; jj < 32; ++jj) p.debug[DBG_P + i * 64 + 32 * hf + jj] = v[jj];
       }
     }
+    PHASE(15)
     fence_async_smem();
     __syncthreads();
+    PHASE(5)
 
-    // ---- T = (I + A)^-1: thread (column j, parity par) keeps T[2m+par][j] ----
-    {
-      const int j = tid >> 1, par = tid & 1;
-      float Tc[32];
+    // ---- T = (I + A)^-1, fp32, blocks of 16:
+    //      level 0: the four diagonal blocks by right-looking elimination;
+    //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22;
+    //      level 2: [T20 T21; T30 T31] = -T22' (A21' T11'), primes = 32x32 halves.
+    if (tid < 64) {
+      const int b = tid >> 4, j = tid & 15, b0 = 16 * b;
+      float x[16];
 #pragma unroll
-      for (int m = 0; m < 32; ++m) Tc[m] = (2 * m + par == j) ? 1.f : 0.f;
+      for (int r = 0; r < 16; ++r) x[r] = (r == j) ? 1.f : 0.f;
 #pragma unroll
-      for (int i = 1; i < 64; ++i) {
-        const float* arow = Af + i * kAPitch + par;
-        float acc = 0.f;
+      for (int k = 0; k < 15; ++k) {
+        const float xk = x[k];
+        const float* col = At + (b0 + k) * kAPitch + b0;  // A[b0 + i][b0 + k]
 #pragma unroll
-        for (int m = 0; m < (i + 1) / 2; ++m) acc = fmaf(arow[2 * m], Tc[m], acc);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        if ((i & 1) == par) Tc[i >> 1] = ((i == j) ? 1.f : 0.f) - acc;
+        for (int q = (k + 1) / 4; q < 4; ++q) {
+          const float4 a4 = *reinterpret_cast<const float4*>(col + 4 * q);
+          if (4 * q + 0 > k) x[4 * q + 0] = fmaf(-a4.x, xk, x[4 * q + 0]);
+          if (4 * q + 1 > k) x[4 * q + 1] = fmaf(-a4.y, xk, x[4 * q + 1]);
+          if (4 * q + 2 > k) x[4 * q + 2] = fmaf(-a4.z, xk, x[4 * q + 2]);
+          if (4 * q + 3 > k) x[4 * q + 3] = fmaf(-a4.w, xk, x[4 * q + 3]);
+        }
       }
-      __syncthreads();  // everyone done reading A
-      float* trow = Af + j * kAPitch;  // row j of T^T = column j of T
+      float* tcol = Tcm + (b0 + j) * kAPitch;
 #pragma unroll
-      for (int m = 0; m < 32; ++m) trow[2 * m + par] = Tc[m];
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float4*>(tcol + b0 + 4 * q) =
+            make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+      for (int q = 0; q < 4 * b; ++q)  // rows above the diagonal block are zero
+        *reinterpret_cast<float4*>(tcol + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncthreads();
+    {  // level 1, step 1: X = A_IJ T_JJ, (I, J) = (1, 0) for tid < 128, (3, 2) otherwise
+      const int pr = tid >> 7, u = tid & 127;
+      const int J0 = 32 * pr, I0 = J0 + 16;
+      const int j = u & 15, r0 = (u >> 4) * 2;
+      float x0 = 0.f, x1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float tkj = Tcm[(J0 + j) * kAPitch + J0 + k];   // T[J0+k][J0+j]
+        x0 = fmaf(At[(J0 + k) * kAPitch + I0 + r0], tkj, x0);     // A[I0+r0][J0+k]
+        x1 = fmaf(At[(J0 + k) * kAPitch + I0 + r0 + 1], tkj, x1);
+      }
+      Xcm[pr * 272 + j * 17 + r0] = x0;
+      Xcm[pr * 272 + j * 17 + r0 + 1] = x1;
+    }
+    __syncthreads();
+    {  // level 1, step 2: T_IJ = -T_II X
+      const int pr = tid >> 7, u = tid & 127;
+      const int J0 = 32 * pr, I0 = J0 + 16;
+      const int j = u & 15, r0 = (u >> 4) * 2;
+      float t0_ = 0.f, t1_ = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float xkj = Xcm[pr * 272 + j * 17 + k];
+        t0_ = fmaf(Tcm[(I0 + k) * kAPitch + I0 + r0], xkj, t0_);   // T[I0+r0][I0+k]
+        t1_ = fmaf(Tcm[(I0 + k) * kAPitch + I0 + r0 + 1], xkj, t1_);
+      }
+      Tcm[(J0 + j) * kAPitch + I0 + r0] = -t0_;
+      Tcm[(J0 + j) * kAPitch + I0 + r0 + 1] = -t1_;
+    }
+    __syncthreads();
+    {  // level 2, step 1: M = A21' T11' (32x32): thread column j = lane, rows 4*warp..
+      const int j = lane, r0 = warp * 4;
+      float m[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kq = 0; kq < 8; ++kq) {
+        const float4 t4 = *reinterpret_cast<const float4*>(Tcm + j * kAPitch + 4 * kq);
+        const float tk[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 a = *reinterpret_cast<const float4*>(At + (4 * kq + e) * kAPitch + 32 + r0);
+          m[0] = fmaf(a.x, tk[e], m[0]);
+          m[1] = fmaf(a.y, tk[e], m[1]);
+          m[2] = fmaf(a.z, tk[e], m[2]);
+          m[3] = fmaf(a.w, tk[e], m[3]);
+        }
+      }
+      *reinterpret_cast<float4*>(Mcm + j * 36 + r0) = make_float4(m[0], m[1], m[2], m[3]);
+    }
+    __syncthreads();
+    {  // level 2, step 2: T21' = -T22' M
+      const int j = lane, r0 = warp * 4;
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kq = 0; kq < 8; ++kq) {
+        const float4 m4 = *reinterpret_cast<const float4*>(Mcm + j * 36 + 4 * kq);
+        const float mk[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float4 a =
+              *reinterpret_cast<const float4*>(Tcm + (32 + 4 * kq + e) * kAPitch + 32 + r0);
+          t[0] = fmaf(a.x, mk[e], t[0]);
+          t[1] = fmaf(a.y, mk[e], t[1]);
+          t[2] = fmaf(a.z, mk[e], t[2]);
+          t[3] = fmaf(a.w, mk[e], t[3]);
+        }
+      }
+      *reinterpret_cast<float4*>(Tcm + j * kAPitch + 32 + r0) =
+          make_float4(-t[0], -t[1], -t[2], -t[3]);
+    }
+    __syncthreads();
+    PHASE(6)
     {
-      // threads 0-63: T diag(beta); 64-127: T diag(beta e^gamma); row j of the
-      // MN-major tile holds column j of T.
-      // The T~ tile leaves out the unit diagonal: U = beta (.) V + T~_off V, and the
-      // beta (.) V term is added in fp32 when Vn is drained (a bf16 beta_j on the
-      // diagonal would cost ~2^-9 relative error on all of U).
+      // T~ = T_off diag(beta) and T^ = T diag(beta e^gamma) as MN-major bf16
+      // tiles: row j of a tile holds column j of T.  T~ leaves out the unit
+      // diagonal: U = beta (.) V + T~_off V, and beta (.) V is added in fp32 when
+      // Vn is drained (a bf16 beta_j on the diagonal would cost ~2^-9 relative
+      // error on all of U).
       const int j = tid & 63;
-      const bool hat = tid >= 64;
-      const float sc = hat ? bet[j] * __expf(gam[j]) : bet[j];
-      const float* trow = Af + j * kAPitch;
+      const bool hat = (tid >> 6) & 1;
+      const int half = tid >> 7;
+      const float sc = hat ? bet[j] * ex2_ftz(gam[j]) : bet[j];
+      const float* trow = Tcm + j * kAPitch;
       const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        float x[8];
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const int ch = 4 * half + c4;
+        const float4 x0 = *reinterpret_cast<const float4*>(trow + ch * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(trow + ch * 8 + 4);
+        float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = (!hat && ch * 8 + e == j) ? 0.f : trow[ch * 8 + e] * sc;
+        for (int e = 0; e < 8; ++e) x[e] = (!hat && ch * 8 + e == j) ? 0.f : x[e] * sc;
         sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
                pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
       }
       if (dbg && !hat) {
-        for (int i = 0; i < 64; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
+        for (int i = 32 * half; i < 32 * half + 32; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
       }
     }
     fence_async_smem();
     __syncthreads();
+    PHASE(7)
 
-    // ---- MMA 2: U = T~ V, W = T^ K ----------------------------------------
+    // ---- MMA 2: U_off = T~_off V, W = T^ K --------------------------------
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -416,41 +549,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(bar_mma);
     }
     if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    PHASE(8)
     tc_fence_after();
 
-    // ---- W -> bf16 K-major tile (rows t = 16*warp + lane for lane < 16) -----
+    // ---- W -> bf16 K-major tile; thread rows r_lo, r_lo+8, columns 64 hf + .. --
     {
-      const int t = warp * 16 + lane;
-      float v[16];
+      float w[32];
+      tmem_ld16x256_x8(tmem + lane_base + TM_W + 64 * hf, w);
+      tmem_wait_ld();
+      reg_fence(w);
+      const uint32_t tile = sb + OFF_AF + hf * 8192;
 #pragma unroll
-      for (int cb = 0; cb < 8; ++cb) {
-        tmem_ld16(tmem + lane_base + TM_W + cb * 16, v);
-        tmem_wait_ld();
-        if (lane < 16) {
-          write_bf16_row16(sb + OFF_AF + (cb >> 2) * 8192, t, cb, v);
-          if (dbg)
-            for (int i = 0; i < 16; ++i) p.debug[DBG_W + t * 128 + cb * 16 + i] = v[i];
-        }
+      for (int jg = 0; jg < 8; ++jg) {
+        sts32(tile + sw128_off(r_lo, jg) + 4 * tq, pack_bf16x2(w[4 * jg], w[4 * jg + 1]));
+        sts32(tile + sw128_off(r_lo + 8, jg) + 4 * tq, pack_bf16x2(w[4 * jg + 2], w[4 * jg + 3]));
       }
       if (dbg) {
-#pragma unroll
-        for (int cb = 0; cb < 8; ++cb) {
-          tmem_ld16(tmem + lane_base + TM_VN + cb * 16, v);
-          tmem_wait_ld();
-          if (lane < 16) {
-            float vrow[16];
-            read_bf16_row16(vsm, 8192, t, cb, vrow);
-            for (int i = 0; i < 16; ++i)
-              p.debug[DBG_U + t * 128 + cb * 16 + i] = fmaf(bet[t], vrow[i], v[i]);
+        for (int jg = 0; jg < 8; ++jg)
+          for (int e = 0; e < 2; ++e) {
+            const int col = 64 * hf + 8 * jg + 2 * tq + e;
+            p.debug[DBG_W + r_lo * 128 + col] = w[4 * jg + e];
+            p.debug[DBG_W + (r_lo + 8) * 128 + col] = w[4 * jg + 2 + e];
           }
-        }
+        float u[32];
+        tmem_ld16x256_x8(tmem + lane_base + TM_VN + 64 * hf, u);
+        tmem_wait_ld();
+        reg_fence(u);
+        for (int jg = 0; jg < 8; ++jg)
+          for (int rr = 0; rr < 2; ++rr) {
+            const int row = r_lo + 8 * rr;
+            const uint32_t vw = lds32(vsm + hf * 8192 + sw128_off(row, jg) + 4 * tq);
+            const int col = 64 * hf + 8 * jg + 2 * tq;
+            p.debug[DBG_U + row * 128 + col] = fmaf(bet[row], bf16_lo(vw), u[4 * jg + 2 * rr]);
+            p.debug[DBG_U + row * 128 + col + 1] = fmaf(bet[row], bf16_hi(vw), u[4 * jg + 2 * rr + 1]);
+          }
       }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    PHASE(9)
 
-    // ---- MMA 3: Vn = U - W S (accumulate on U), QS = Q S --------------------
+    // ---- MMA 3: Vn_part = U_off - W S (accumulate on U_off), QS = Q S ------
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -467,52 +607,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(bar_mma);
     }
+    if (warp == 0 && c + 1 < nchunks) {  // gates of the next chunk overlap MMA 3
+      compute_gates(c + 1);
+      if (c + 2 < nchunks) prefetch_gates(c + 2);
+    }
     if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    PHASE(10)
     tc_fence_after();
 
-    // ---- Vn -> bf16 (B of P Vn); Vd = e^{g63 - g_t} Vn -> hi/lo (A of state) --
+    // ---- Vn = beta V + Vn_part -> bf16 (B of P Vn);
+    //      Vd = e^{g63 - g_t} Vn -> hi/lo bf16 (A of the state update) --------
     {
-      const int t = warp * 16 + lane;
-      const bool valid = lane < 16 && t < L;
-      const float dec = valid ? __expf(gam[63] - gam[t]) : 0.f;
-      float v[16], hi[16], lo[16];
+      float v[32];
+      tmem_ld16x256_x8(tmem + lane_base + TM_VN + 64 * hf, v);
+      tmem_wait_ld();
+      reg_fence(v);
 #pragma unroll
-      for (int cb = 0; cb < 8; ++cb) {
-        tmem_ld16(tmem + lane_base + TM_VN + cb * 16, v);
-        tmem_wait_ld();
-        if (lane < 16) {
-          float vrow[16];
-          read_bf16_row16(vsm, 8192, t, cb, vrow);
-          const float bt = bet[t];
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = r_lo + 8 * rr;
+        const bool valid = row < L;
+        const float dec = valid ? ex2_ftz(gam[63] - gam[row]) : 0.f;
+        const float bt = bet[row];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float x = valid ? fmaf(bt, vrow[i], v[i]) : 0.f;
-            v[i] = x;
-            const float d = x * dec;
-            hi[i] = __bfloat162float(__float2bfloat16_rn(d));
-            lo[i] = d - hi[i];
+        for (int jg = 0; jg < 8; ++jg) {
+          const uint32_t off = hf * 8192 + sw128_off(row, jg) + 4 * tq;
+          const uint32_t vw = lds32(vsm + off);
+          const float x0 = valid ? fmaf(bt, bf16_lo(vw), v[4 * jg + 2 * rr]) : 0.f;
+          const float x1 = valid ? fmaf(bt, bf16_hi(vw), v[4 * jg + 2 * rr + 1]) : 0.f;
+          const float d0 = x0 * dec, d1 = x1 * dec;
+          const float h0 = __bfloat162float(__float2bfloat16_rn(d0));
+          const float h1 = __bfloat162float(__float2bfloat16_rn(d1));
+          sts32(sb + OFF_VN + off, pack_bf16x2(x0, x1));
+          sts32(sb + OFF_VH + off, pack_bf16x2(h0, h1));
+          sts32(sb + OFF_VL + off, pack_bf16x2(d0 - h0, d1 - h1));
+          if (dbg) {
+            const int col = 64 * hf + 8 * jg + 2 * tq;
+            p.debug[DBG_VN + row * 128 + col] = x0;
+            p.debug[DBG_VN + row * 128 + col + 1] = x1;
           }
-          const uint32_t blk = (cb >> 2) * 8192;
-          write_bf16_row16(sb + OFF_VN + blk, t, cb, v);
-          write_bf16_row16(sb + OFF_VH + blk, t, cb, hi);
-          write_bf16_row16(sb + OFF_VL + blk, t, cb, lo);
-          if (dbg)
-            for (int i = 0; i < 16; ++i) p.debug[DBG_VN + t * 128 + cb * 16 + i] = v[i];
         }
       }
       if (dbg) {
-#pragma unroll
-        for (int cb = 0; cb < 8; ++cb) {
-          tmem_ld16(tmem + lane_base + TM_W + cb * 16, v);
-          tmem_wait_ld();
-          if (lane < 16)
-            for (int i = 0; i < 16; ++i) p.debug[DBG_QS + t * 128 + cb * 16 + i] = v[i];
-        }
+        tmem_ld16x256_x8(tmem + lane_base + TM_W + 64 * hf, v);
+        tmem_wait_ld();
+        reg_fence(v);
+        for (int jg = 0; jg < 8; ++jg)
+          for (int rr = 0; rr < 2; ++rr)
+            for (int e = 0; e < 2; ++e)
+              p.debug[DBG_QS + (r_lo + 8 * rr) * 128 + 64 * hf + 8 * jg + 2 * tq + e] =
+                  v[4 * jg + 2 * rr + e];
       }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    PHASE(11)
 
     // ---- MMA 4: PV = P Vn (into the Vn columns); St += Vd_hi^T K + Vd_lo^T K --
     if (tid == 0) {
@@ -532,60 +681,65 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(bar_mma);
     }
     if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
+    PHASE(12)
     tc_fence_after();
 
     // ---- output rows: O = scale (e^{gamma_t} QS + PV) ------------------------
     {
-      const int t = warp * 16 + lane;
-      const bool valid = lane < 16 && t < L;
-      const float eg = valid ? __expf(gam[t]) : 0.f;
-      __nv_bfloat16* orow = p.out + ((t0 + (valid ? t : 0)) * p.Hv + h) * kHead;
-      float qs[16], pv[16];
+      float qs[32], pv[32];
+      tmem_ld16x256_x8(tmem + lane_base + TM_W + 64 * hf, qs);
+      tmem_ld16x256_x8(tmem + lane_base + TM_VN + 64 * hf, pv);
+      tmem_wait_ld();
+      reg_fence(qs);
+      reg_fence(pv);
 #pragma unroll
-      for (int cb = 0; cb < 8; ++cb) {
-        tmem_ld16(tmem + lane_base + TM_W + cb * 16, qs);
-        tmem_ld16(tmem + lane_base + TM_VN + cb * 16, pv);
-        tmem_wait_ld();
-        if (valid) {
-          float o[16];
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = r_lo + 8 * rr;
+        if (row < L) {
+          const float eg = p.scale * ex2_ftz(gam[row]);
+          uint32_t* orow = reinterpret_cast<uint32_t*>(p.out + ((t0 + row) * p.Hv + h) * kHead +
+                                                       64 * hf + 2 * tq);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = p.scale * fmaf(eg, qs[i], pv[i]);
-          uint4 w0 = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
-          uint4 w1 = make_uint4(pack_bf16x2(o[8], o[9]), pack_bf16x2(o[10], o[11]),
-                                pack_bf16x2(o[12], o[13]), pack_bf16x2(o[14], o[15]));
-          reinterpret_cast<uint4*>(orow + cb * 16)[0] = w0;
-          reinterpret_cast<uint4*>(orow + cb * 16)[1] = w1;
+          for (int jg = 0; jg < 8; ++jg) {
+            const float o0 = fmaf(eg, qs[4 * jg + 2 * rr], p.scale * pv[4 * jg + 2 * rr]);
+            const float o1 = fmaf(eg, qs[4 * jg + 2 * rr + 1], p.scale * pv[4 * jg + 2 * rr + 1]);
+            orow[4 * jg] = pack_bf16x2(o0, o1);
+          }
         }
-        if (dbg && lane < 16)
-          for (int i = 0; i < 16; ++i) p.debug[DBG_PV + t * 128 + cb * 16 + i] = pv[i];
+        if (dbg)
+          for (int jg = 0; jg < 8; ++jg)
+            for (int e = 0; e < 2; ++e)
+              p.debug[DBG_PV + row * 128 + 64 * hf + 8 * jg + 2 * tq + e] = pv[4 * jg + 2 * rr + e];
       }
       if (dbg) {
-        float v[16];
-#pragma unroll
-        for (int cb = 0; cb < 8; ++cb) {
-          tmem_ld16(tmem + lane_base + TM_ST + cb * 16, v);
-          tmem_wait_ld();
-          for (int i = 0; i < 16; ++i) p.debug[DBG_ST + tid * 128 + cb * 16 + i] = v[i];
-        }
+        float v[64];
+        tmem_ld32(tq_st, v);
+        tmem_ld32(tq_st + 32, v + 32);
+        tmem_wait_ld();
+        reg_fence(v);
+        for (int i = 0; i < 64; ++i) p.debug[DBG_ST + rowv * 128 + 64 * hf + i] = v[i];
       }
     }
+    PHASE(13)
   }
+  if constexpr (DEBUG) {
+    if (dbg_cta && tid == 0)
+      for (int i = 0; i < 16; ++i) p.debug[DBG_CLK + i] = static_cast<float>(clk_acc[i]);
+  }
+#undef PHASE
 
-  // ---- final state -> new_state (row v = tid) ---------------------------------
+  // ---- final state -> new_state (row rowv, columns of this half) -----------------
   if (!aborted) {
     tc_fence_after();
-    float* dst = ns_rows + tid * kHead;
+    float* dst = ns_rows + rowv * kHead + 64 * hf;
+    float v[64];
+    tmem_ld32(tq_st, v);
+    tmem_ld32(tq_st + 32, v + 32);
+    tmem_wait_ld();
+    reg_fence(v);
 #pragma unroll
-    for (int cb = 0; cb < 8; ++cb) {
-      float v[16];
-      tmem_ld16(tmem + lane_base + TM_ST + cb * 16, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4)
-        st_stream_f4(dst + cb * 16 + q4 * 4,
-                     make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
-    }
+    for (int q4 = 0; q4 < 16; ++q4)
+      st_stream_f4(dst + q4 * 4, make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
   } else {
     if (tid == 0) atomicOr(&g_gdn_status, kStatusPrefillTimeout);
     // let in-flight tensor-core work drain (bounded) before TMEM is released
