@@ -54,8 +54,14 @@ __device__ __forceinline__ float softplus_t20_fast(float x) {
   return x < -15.0f ? e : kLn2 * lg2_approx(1.0f + e);
 }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float sigmoid_fast(float x) {
-  return __frcp_rn(1.0f + ex2_ftz(-x * kLog2e));
+  return rcp_approx(1.0f + ex2_ftz(-x * kLog2e));
 }
 
 // ------------------------------------------------------------------ bf16

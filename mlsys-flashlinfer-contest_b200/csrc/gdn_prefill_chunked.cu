@@ -58,7 +58,8 @@ constexpr uint32_t OFF_VH = OFF_VN + 16384;        // Vd hi (MN-major A)
 constexpr uint32_t OFF_VL = OFF_VH + 16384;        // Vd lo; during the inverse: fp32 (A21 T11)^T [32][36]
 constexpr uint32_t OFF_MISC = OFF_VL + 16384;      // gamma[64], beta[64], barriers, tmem slot
 constexpr uint32_t kSmemBytes = OFF_MISC + 2048 + 1024;  // + slack for the 1024 alignment
-constexpr int kAPitch = 68;                        // fp32 row pitch of A / T^T
+constexpr int kAtPitch = 72;   // fp32 row pitch of A^T (72 = 8 mod 32: conflict-free tf32 A fragments)
+constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict-free B fragments)
 
 // ---- TMEM columns ----------------------------------------------------------
 constexpr uint32_t TM_ST = 0;     // St [v 128 lanes][k 128 cols]
@@ -144,8 +145,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + OFF_MISC + 1024);  // [2]
   uint64_t* bar_mma = bar_tma + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  // fp32 scratch of the inverse (A^T 18 KiB from OFF_AF into the Vn tile, T^T
+  // after it into the Vd_hi tile, products in the Vd_lo tile; all free then)
   float* At = reinterpret_cast<float*>(smem + OFF_AF);   // A column-major: At[k][i] = A[i][k]
-  float* Tcm = reinterpret_cast<float*>(smem + OFF_VN);  // T column-major: Tcm[j][i] = T[i][j]
+  float* Tcm = reinterpret_cast<float*>(smem + OFF_AF + 64 * kAtPitch * 4);  // Tcm[j][i] = T[i][j]
   float* Mcm = reinterpret_cast<float*>(smem + OFF_VL);  // (A21 T11) column-major, pitch 36
   float* Xcm = Mcm + 32 * 36;                            // 2 x [16][17] level-1 products
 
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return __syncthreads_or(ok ? 0 : 1) == 0;
   };
 
-  // Gates of one chunk from raw a/b values held by warp 0 (two tokens per lane):
+  // Gates of one chunk from raw a/b values held by warp 1 (two tokens per lane):
   // log-decay, its inclusive scan (gamma, stored in log2 units) and beta.
   float ga_raw[2] = {0.f, 0.f}, gb_raw[2] = {0.f, 0.f};
   auto prefetch_gates = [&](int cc) {
@@ -262,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   };
-  auto compute_gates = [&](int cc) {  // warp 0 only
+  auto compute_gates = [&](int cc) {  // warp 1 only
     const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
     const int Lc = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0c));
     float lg[2], bt[2];
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (tid == 0) issue_loads(0, 0);
-  if (warp == 0) {
+  if (warp == 1) {  // warp 1 owns the gates: warp 0's lane 0 is busy issuing MMAs
     prefetch_gates(0);
     compute_gates(0);
     if (Ltot > kChunk) prefetch_gates(1);
@@ -379,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * hf + jj;
           const float aij = (j < i) ? bi * v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
-          At[j * kAPitch + i] = aij;
+          At[j * kAtPitch + i] = aij;
           if (dbg) p.debug[DBG_A + i * 64 + j] = aij;
         }
       } else {
@@ -414,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int k = 0; k < 15; ++k) {
         const float xk = x[k];
-        const float* col = At + (b0 + k) * kAPitch + b0;  // A[b0 + i][b0 + k]
+        const float* col = At + (b0 + k) * kAtPitch + b0;  // A[b0 + i][b0 + k]
 #pragma unroll
         for (int q = (k + 1) / 4; q < 4; ++q) {
           const float4 a4 = *reinterpret_cast<const float4*>(col + 4 * q);
@@ -424,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (4 * q + 3 > k) x[4 * q + 3] = fmaf(-a4.w, xk, x[4 * q + 3]);
         }
       }
-      float* tcol = Tcm + (b0 + j) * kAPitch;
+      float* tcol = Tcm + (b0 + j) * kTcPitch;
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         *reinterpret_cast<float4*>(tcol + b0 + 4 * q) =
@@ -440,9 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       float x0 = 0.f, x1 = 0.f;
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
-        const float tkj = Tcm[(J0 + j) * kAPitch + J0 + k];   // T[J0+k][J0+j]
-        x0 = fmaf(At[(J0 + k) * kAPitch + I0 + r0], tkj, x0);     // A[I0+r0][J0+k]
-        x1 = fmaf(At[(J0 + k) * kAPitch + I0 + r0 + 1], tkj, x1);
+        const float tkj = Tcm[(J0 + j) * kTcPitch + J0 + k];   // T[J0+k][J0+j]
+        x0 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0], tkj, x0);     // A[I0+r0][J0+k]
+        x1 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0 + 1], tkj, x1);
       }
       Xcm[pr * 272 + j * 17 + r0] = x0;
       Xcm[pr * 272 + j * 17 + r0 + 1] = x1;
@@ -456,51 +459,50 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const float xkj = Xcm[pr * 272 + j * 17 + k];
-        t0_ = fmaf(Tcm[(I0 + k) * kAPitch + I0 + r0], xkj, t0_);   // T[I0+r0][I0+k]
-        t1_ = fmaf(Tcm[(I0 + k) * kAPitch + I0 + r0 + 1], xkj, t1_);
+        t0_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0], xkj, t0_);   // T[I0+r0][I0+k]
+        t1_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0 + 1], xkj, t1_);
       }
-      Tcm[(J0 + j) * kAPitch + I0 + r0] = -t0_;
-      Tcm[(J0 + j) * kAPitch + I0 + r0 + 1] = -t1_;
+      Tcm[(J0 + j) * kTcPitch + I0 + r0] = -t0_;
+      Tcm[(J0 + j) * kTcPitch + I0 + r0 + 1] = -t1_;
     }
     __syncthreads();
-    {  // level 2, step 1: M = A21' T11' (32x32): thread column j = lane, rows 4*warp..
-      const int j = lane, r0 = warp * 4;
-      float m[4] = {0.f, 0.f, 0.f, 0.f};
+    // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
+    // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after):
+    // warp w computes the 16x8 output tile (row tile w/4, column tile w%4).
+    {  // step 1: M = A21' T11' (32x32x32)
+      const int rt = warp >> 2, ct = warp & 3, t4 = tq;
+      float cacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int kq = 0; kq < 8; ++kq) {
-        const float4 t4 = *reinterpret_cast<const float4*>(Tcm + j * kAPitch + 4 * kq);
-        const float tk[4] = {t4.x, t4.y, t4.z, t4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float4 a = *reinterpret_cast<const float4*>(At + (4 * kq + e) * kAPitch + 32 + r0);
-          m[0] = fmaf(a.x, tk[e], m[0]);
-          m[1] = fmaf(a.y, tk[e], m[1]);
-          m[2] = fmaf(a.z, tk[e], m[2]);
-          m[3] = fmaf(a.w, tk[e], m[3]);
-        }
+      for (int ks = 0; ks < 4; ++ks) {
+        const int k0 = 8 * ks;
+        const float* ar = At + (k0 + t4) * kAtPitch + 32 + 16 * rt + g;  // A[32+16rt+g][k0+t]
+        const float* br = Tcm + (8 * ct + g) * kTcPitch + k0 + t4;       // T[k0+t][8ct+g]
+        mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
+                        to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
       }
-      *reinterpret_cast<float4*>(Mcm + j * 36 + r0) = make_float4(m[0], m[1], m[2], m[3]);
+      float* mc = Mcm + (8 * ct + 2 * t4) * 36 + 16 * rt + g;  // M[r][j] at Mcm[j*36 + r]
+      mc[0] = cacc[0];
+      mc[36] = cacc[1];
+      mc[8] = cacc[2];
+      mc[36 + 8] = cacc[3];
     }
     __syncthreads();
-    {  // level 2, step 2: T21' = -T22' M
-      const int j = lane, r0 = warp * 4;
-      float t[4] = {0.f, 0.f, 0.f, 0.f};
+    {  // step 2: T21' = -T22' M
+      const int rt = warp >> 2, ct = warp & 3, t4 = tq;
+      float cacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int kq = 0; kq < 8; ++kq) {
-        const float4 m4 = *reinterpret_cast<const float4*>(Mcm + j * 36 + 4 * kq);
-        const float mk[4] = {m4.x, m4.y, m4.z, m4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float4 a =
-              *reinterpret_cast<const float4*>(Tcm + (32 + 4 * kq + e) * kAPitch + 32 + r0);
-          t[0] = fmaf(a.x, mk[e], t[0]);
-          t[1] = fmaf(a.y, mk[e], t[1]);
-          t[2] = fmaf(a.z, mk[e], t[2]);
-          t[3] = fmaf(a.w, mk[e], t[3]);
-        }
+      for (int ks = 0; ks < 4; ++ks) {
+        const int k0 = 8 * ks;
+        const float* ar = Tcm + (32 + k0 + t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+16rt+g][32+k0+t]
+        const float* br = Mcm + (8 * ct + g) * 36 + k0 + t4;                  // M[k0+t][8ct+g]
+        mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kTcPitch]),
+                        to_tf32(ar[4 * kTcPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
       }
-      *reinterpret_cast<float4*>(Tcm + j * kAPitch + 32 + r0) =
-          make_float4(-t[0], -t[1], -t[2], -t[3]);
+      float* tc = Tcm + (8 * ct + 2 * t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+r][j] at Tcm[j][32+r]
+      tc[0] = -cacc[0];
+      tc[kTcPitch] = -cacc[1];
+      tc[8] = -cacc[2];
+      tc[kTcPitch + 8] = -cacc[3];
     }
     __syncthreads();
     PHASE(6)
@@ -514,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool hat = (tid >> 6) & 1;
       const int half = tid >> 7;
       const float sc = hat ? bet[j] * ex2_ftz(gam[j]) : bet[j];
-      const float* trow = Tcm + j * kAPitch;
+      const float* trow = Tcm + j * kTcPitch;
       const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
@@ -607,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(bar_mma);
     }
-    if (warp == 0 && c + 1 < nchunks) {  // gates of the next chunk overlap MMA 3
+    if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap MMA 3
       compute_gates(c + 1);
       if (c + 2 < nchunks) prefetch_gates(c + 2);
     }
