@@ -38,7 +38,7 @@ __device__ uint32_t g_gdn_status = 0;
 namespace {
 using namespace sm100;
 
-constexpr int kThreads = 256;  // 8 warps: two per TMEM lane quarter
+constexpr int kThreads = 512;  // 16 warps: four per TMEM lane quarter
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait, then give up
 
 // ---- shared memory map (offsets from a 1024-aligned base) -----------------
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-  const int hf = warp >> 2;      // column half handled by this warp
+  const int cq = warp >> 2;      // column quarter handled by this warp (32 of 128 columns)
   const int g = lane >> 2, tq = lane & 3;  // 16x256b fragment coordinates
   const int r_lo = 16 * quarter + g;       // rows of an M=64 accumulator held by this thread
   const int rowv = 32 * quarter + lane;    // row of an M=128 accumulator held by this thread
@@ -204,27 +204,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-  const uint32_t tq_st = tmem + lane_base + TM_ST + 64 * hf;  // this thread's St columns
+  const uint32_t tq_st = tmem + lane_base + TM_ST + 32 * cq;  // this thread's St columns
   const float neg_exp_A = -expf(p.A_log[h]);
   const float dt_bias_h = p.dt_bias[h];
 
-  // ---- initial state -> TMEM (row rowv, columns [64 hf, 64 hf + 64)) -------
+  // ---- initial state -> TMEM (row rowv, columns [32 cq, 32 cq + 32)) -------
   {
-    const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + rowv * kHead + 64 * hf
+    const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + rowv * kHead + 32 * cq
                                : nullptr;
+    float v[32];
 #pragma unroll
-    for (int cb = 0; cb < 2; ++cb) {
-      float v[32];
-#pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4) {
-        float4 x = src ? ld_stream_f4(src + cb * 32 + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[4 * q4] = x.x;
-        v[4 * q4 + 1] = x.y;
-        v[4 * q4 + 2] = x.z;
-        v[4 * q4 + 3] = x.w;
-      }
-      tmem_st32(tq_st + cb * 32, v);
+    for (int q4 = 0; q4 < 8; ++q4) {
+      float4 x = src ? ld_stream_f4(src + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * q4] = x.x;
+      v[4 * q4 + 1] = x.y;
+      v[4 * q4 + 2] = x.z;
+      v[4 * q4 + 3] = x.w;
     }
+    tmem_st32(tq_st, v);
     tmem_wait_st();
   }
 
@@ -329,21 +326,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- state pass: St -> bf16 operand tile; St *= e^{gamma_63} -----------
     {
       const float dec = ex2_ftz(gam[63]);
-      float v[64];
+      float v[32];
       tmem_ld32(tq_st, v);
-      tmem_ld32(tq_st + 32, v + 32);
       tmem_wait_ld();
       reg_fence(v);
-      const uint32_t tile = sb + OFF_ST + hf * 16384;
+      const uint32_t tile = sb + OFF_ST + (cq >> 1) * 16384;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        sts128(tile + sw128_off(rowv, ch), pack_bf16x2(v[8 * ch], v[8 * ch + 1]),
-               pack_bf16x2(v[8 * ch + 2], v[8 * ch + 3]), pack_bf16x2(v[8 * ch + 4], v[8 * ch + 5]),
-               pack_bf16x2(v[8 * ch + 6], v[8 * ch + 7]));
+      for (int c4 = 0; c4 < 4; ++c4)
+        sts128(tile + sw128_off(rowv, (cq & 1) * 4 + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
+               pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
+               pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
 #pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] *= dec;
+      for (int i = 0; i < 32; ++i) v[i] *= dec;
       tmem_st32(tq_st, v);
-      tmem_st32(tq_st + 32, v + 32);
       tmem_wait_st();
       fence_async_smem();
     }
@@ -371,33 +366,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       const int i = rowv & 63;
       const float gi = gam[i];
-      float v[32];
-      tmem_ld32(tmem + lane_base + TM_D1 + 32 * hf, v);
+      float v[16];
+      tmem_ld16(tmem + lane_base + TM_D1 + 16 * cq, v);
       tmem_wait_ld();
       reg_fence(v);
       PHASE(14)
       if (quarter < 2) {
         const float bi = bet[i];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * hf + jj;
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = 16 * cq + jj;
           const float aij = (j < i) ? bi * v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
           At[j * kAtPitch + i] = aij;
           if (dbg) p.debug[DBG_A + i * 64 + j] = aij;
         }
       } else {
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * hf + jj;
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = 16 * cq + jj;
           v[jj] = (j <= i) ? v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
         }
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-          sts128(sb + OFF_P + sw128_off(i, 4 * hf + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
-                 pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
-                 pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
+        for (int c2 = 0; c2 < 2; ++c2)
+          sts128(sb + OFF_P + sw128_off(i, 2 * cq + c2), pack_bf16x2(v[8 * c2], v[8 * c2 + 1]),
+                 pack_bf16x2(v[8 * c2 + 2], v[8 * c2 + 3]), pack_bf16x2(v[8 * c2 + 4], v[8 * c2 + 5]),
+                 pack_bf16x2(v[8 * c2 + 6], v[8 * c2 + 7]));
         if (dbg)
-          for (int jj = 0; jj < 32; ++jj) p.debug[DBG_P + i * 64 + 32 * hf + jj] = v[jj];
+          for (int jj = 0; jj < 16; ++jj) p.debug[DBG_P + i * 64 + 16 * cq + jj] = v[jj];
       }
     }
     PHASE(15)
@@ -436,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<float4*>(tcol + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncthreads();
-    {  // level 1, step 1: X = A_IJ T_JJ, (I, J) = (1, 0) for tid < 128, (3, 2) otherwise
+    if (tid < 256) {  // level 1, step 1: X = A_IJ T_JJ, (I, J) = (1, 0) for tid < 128, else (3, 2)
       const int pr = tid >> 7, u = tid & 127;
       const int J0 = 32 * pr, I0 = J0 + 16;
       const int j = u & 15, r0 = (u >> 4) * 2;
@@ -451,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       Xcm[pr * 272 + j * 17 + r0 + 1] = x1;
     }
     __syncthreads();
-    {  // level 1, step 2: T_IJ = -T_II X
+    if (tid < 256) {  // level 1, step 2: T_IJ = -T_II X
       const int pr = tid >> 7, u = tid & 127;
       const int J0 = 32 * pr, I0 = J0 + 16;
       const int j = u & 15, r0 = (u >> 4) * 2;
@@ -468,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
     // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after):
-    // warp w computes the 16x8 output tile (row tile w/4, column tile w%4).
-    {  // step 1: M = A21' T11' (32x32x32)
+    // warp w < 8 computes the 16x8 output tile (row tile w/4, column tile w%4).
+    if (warp < 8) {  // step 1: M = A21' T11' (32x32x32)
       const int rt = warp >> 2, ct = warp & 3, t4 = tq;
       float cacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -487,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mc[36 + 8] = cacc[3];
     }
     __syncthreads();
-    {  // step 2: T21' = -T22' M
+    if (warp < 8) {  // step 2: T21' = -T22' M
       const int rt = warp >> 2, ct = warp & 3, t4 = tq;
       float cacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -514,13 +509,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // error on all of U).
       const int j = tid & 63;
       const bool hat = (tid >> 6) & 1;
-      const int half = tid >> 7;
+      const int part = tid >> 7;  // 16-row quarter of the tile row (2 chunks)
       const float sc = hat ? bet[j] * ex2_ftz(gam[j]) : bet[j];
       const float* trow = Tcm + j * kTcPitch;
       const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const int ch = 4 * half + c4;
+      for (int c2 = 0; c2 < 2; ++c2) {
+        const int ch = 2 * part + c2;
         const float4 x0 = *reinterpret_cast<const float4*>(trow + ch * 8);
         const float4 x1 = *reinterpret_cast<const float4*>(trow + ch * 8 + 4);
         float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -530,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
       }
       if (dbg && !hat) {
-        for (int i = 32 * half; i < 32 * half + 32; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
+        for (int i = 16 * part; i < 16 * part + 16; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
       }
     }
     fence_async_smem();
@@ -554,34 +549,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     PHASE(8)
     tc_fence_after();
 
-    // ---- W -> bf16 K-major tile; thread rows r_lo, r_lo+8, columns 64 hf + .. --
+    // ---- W -> bf16 K-major tile; thread rows r_lo, r_lo+8, columns 32 cq + .. --
+    // (column group jg of this warp's 32 columns is chunk (cq&1)*4 + jg of block cq/2)
     {
-      float w[32];
-      tmem_ld16x256_x8(tmem + lane_base + TM_W + 64 * hf, w);
+      float w[16];
+      tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, w);
       tmem_wait_ld();
       reg_fence(w);
-      const uint32_t tile = sb + OFF_AF + hf * 8192;
+      const uint32_t tile = sb + OFF_AF + (cq >> 1) * 8192;
 #pragma unroll
-      for (int jg = 0; jg < 8; ++jg) {
-        sts32(tile + sw128_off(r_lo, jg) + 4 * tq, pack_bf16x2(w[4 * jg], w[4 * jg + 1]));
-        sts32(tile + sw128_off(r_lo + 8, jg) + 4 * tq, pack_bf16x2(w[4 * jg + 2], w[4 * jg + 3]));
+      for (int jg = 0; jg < 4; ++jg) {
+        const int ch = (cq & 1) * 4 + jg;
+        sts32(tile + sw128_off(r_lo, ch) + 4 * tq, pack_bf16x2(w[4 * jg], w[4 * jg + 1]));
+        sts32(tile + sw128_off(r_lo + 8, ch) + 4 * tq, pack_bf16x2(w[4 * jg + 2], w[4 * jg + 3]));
       }
       if (dbg) {
-        for (int jg = 0; jg < 8; ++jg)
+        for (int jg = 0; jg < 4; ++jg)
           for (int e = 0; e < 2; ++e) {
-            const int col = 64 * hf + 8 * jg + 2 * tq + e;
+            const int col = 32 * cq + 8 * jg + 2 * tq + e;
             p.debug[DBG_W + r_lo * 128 + col] = w[4 * jg + e];
             p.debug[DBG_W + (r_lo + 8) * 128 + col] = w[4 * jg + 2 + e];
           }
-        float u[32];
-        tmem_ld16x256_x8(tmem + lane_base + TM_VN + 64 * hf, u);
+        float u[16];
+        tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, u);
         tmem_wait_ld();
         reg_fence(u);
-        for (int jg = 0; jg < 8; ++jg)
+        for (int jg = 0; jg < 4; ++jg)
           for (int rr = 0; rr < 2; ++rr) {
             const int row = r_lo + 8 * rr;
-            const uint32_t vw = lds32(vsm + hf * 8192 + sw128_off(row, jg) + 4 * tq);
-            const int col = 64 * hf + 8 * jg + 2 * tq;
+            const uint32_t vw =
+                lds32(vsm + (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq);
+            const int col = 32 * cq + 8 * jg + 2 * tq;
             p.debug[DBG_U + row * 128 + col] = fmaf(bet[row], bf16_lo(vw), u[4 * jg + 2 * rr]);
             p.debug[DBG_U + row * 128 + col + 1] = fmaf(bet[row], bf16_hi(vw), u[4 * jg + 2 * rr + 1]);
           }
@@ -620,8 +618,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- Vn = beta V + Vn_part -> bf16 (B of P Vn);
     //      Vd = e^{g63 - g_t} Vn -> hi/lo bf16 (A of the state update) --------
     {
-      float v[32];
-      tmem_ld16x256_x8(tmem + lane_base + TM_VN + 64 * hf, v);
+      float v[16];
+      tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, v);
       tmem_wait_ld();
       reg_fence(v);
 #pragma unroll
@@ -631,8 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float dec = valid ? ex2_ftz(gam[63] - gam[row]) : 0.f;
         const float bt = bet[row];
 #pragma unroll
-        for (int jg = 0; jg < 8; ++jg) {
-          const uint32_t off = hf * 8192 + sw128_off(row, jg) + 4 * tq;
+        for (int jg = 0; jg < 4; ++jg) {
+          const uint32_t off = (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq;
           const uint32_t vw = lds32(vsm + off);
           const float x0 = valid ? fmaf(bt, bf16_lo(vw), v[4 * jg + 2 * rr]) : 0.f;
           const float x1 = valid ? fmaf(bt, bf16_hi(vw), v[4 * jg + 2 * rr + 1]) : 0.f;
@@ -643,20 +641,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           sts32(sb + OFF_VH + off, pack_bf16x2(h0, h1));
           sts32(sb + OFF_VL + off, pack_bf16x2(d0 - h0, d1 - h1));
           if (dbg) {
-            const int col = 64 * hf + 8 * jg + 2 * tq;
+            const int col = 32 * cq + 8 * jg + 2 * tq;
             p.debug[DBG_VN + row * 128 + col] = x0;
             p.debug[DBG_VN + row * 128 + col + 1] = x1;
           }
         }
       }
       if (dbg) {
-        tmem_ld16x256_x8(tmem + lane_base + TM_W + 64 * hf, v);
+        tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, v);
         tmem_wait_ld();
         reg_fence(v);
-        for (int jg = 0; jg < 8; ++jg)
+        for (int jg = 0; jg < 4; ++jg)
           for (int rr = 0; rr < 2; ++rr)
             for (int e = 0; e < 2; ++e)
-              p.debug[DBG_QS + (r_lo + 8 * rr) * 128 + 64 * hf + 8 * jg + 2 * tq + e] =
+              p.debug[DBG_QS + (r_lo + 8 * rr) * 128 + 32 * cq + 8 * jg + 2 * tq + e] =
                   v[4 * jg + 2 * rr + e];
       }
     }
@@ -688,9 +686,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- output rows: O = scale (e^{gamma_t} QS + PV) ------------------------
     {
-      float qs[32], pv[32];
-      tmem_ld16x256_x8(tmem + lane_base + TM_W + 64 * hf, qs);
-      tmem_ld16x256_x8(tmem + lane_base + TM_VN + 64 * hf, pv);
+      float qs[16], pv[16];
+      tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, qs);
+      tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, pv);
       tmem_wait_ld();
       reg_fence(qs);
       reg_fence(pv);
@@ -700,26 +698,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row < L) {
           const float eg = p.scale * ex2_ftz(gam[row]);
           uint32_t* orow = reinterpret_cast<uint32_t*>(p.out + ((t0 + row) * p.Hv + h) * kHead +
-                                                       64 * hf + 2 * tq);
+                                                       32 * cq + 2 * tq);
 #pragma unroll
-          for (int jg = 0; jg < 8; ++jg) {
+          for (int jg = 0; jg < 4; ++jg) {
             const float o0 = fmaf(eg, qs[4 * jg + 2 * rr], p.scale * pv[4 * jg + 2 * rr]);
             const float o1 = fmaf(eg, qs[4 * jg + 2 * rr + 1], p.scale * pv[4 * jg + 2 * rr + 1]);
             orow[4 * jg] = pack_bf16x2(o0, o1);
           }
         }
         if (dbg)
-          for (int jg = 0; jg < 8; ++jg)
+          for (int jg = 0; jg < 4; ++jg)
             for (int e = 0; e < 2; ++e)
-              p.debug[DBG_PV + row * 128 + 64 * hf + 8 * jg + 2 * tq + e] = pv[4 * jg + 2 * rr + e];
+              p.debug[DBG_PV + row * 128 + 32 * cq + 8 * jg + 2 * tq + e] = pv[4 * jg + 2 * rr + e];
       }
       if (dbg) {
-        float v[64];
+        float v[32];
         tmem_ld32(tq_st, v);
-        tmem_ld32(tq_st + 32, v + 32);
         tmem_wait_ld();
         reg_fence(v);
-        for (int i = 0; i < 64; ++i) p.debug[DBG_ST + rowv * 128 + 64 * hf + i] = v[i];
+        for (int i = 0; i < 32; ++i) p.debug[DBG_ST + rowv * 128 + 32 * cq + i] = v[i];
       }
     }
     PHASE(13)
@@ -730,17 +727,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 #undef PHASE
 
-  // ---- final state -> new_state (row rowv, columns of this half) -----------------
+  // ---- final state -> new_state (row rowv, this warp's 32 columns) --------------
   if (!aborted) {
     tc_fence_after();
-    float* dst = ns_rows + rowv * kHead + 64 * hf;
-    float v[64];
+    float* dst = ns_rows + rowv * kHead + 32 * cq;
+    float v[32];
     tmem_ld32(tq_st, v);
-    tmem_ld32(tq_st + 32, v + 32);
     tmem_wait_ld();
     reg_fence(v);
 #pragma unroll
-    for (int q4 = 0; q4 < 16; ++q4)
+    for (int q4 = 0; q4 < 8; ++q4)
       st_stream_f4(dst + q4 * 4, make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
   } else {
     if (tid == 0) atomicOr(&g_gdn_status, kStatusPrefillTimeout);
