@@ -20,6 +20,12 @@
 //           bf16 hi + lo (two MMAs) so the state update keeps ~16 mantissa bits.
 // Tokens past the end of the sequence get beta = 0 and log-decay 0, which
 // makes their Vn rows exactly zero and leaves gamma_63 = gamma_{L-1}.
+//
+// Warp roles: warps 0-15 do the CUDA-core work (four per TMEM lane quarter,
+// each on 32 of the 128 columns); warp 16 issues every TMA load and tcgen05
+// MMA.  The two sides hand off through mbarriers only, so the tensor pipe runs
+// Q S during the A/P/inverse phases, [K;Q]K^T of the next chunk during the Vn
+// drain and the state update during the output epilogue.
 // Math: same chunked algebra as cuda_kkt_inv_uw_v1.cu:1-20 (U, W, g_cu),
 // cuda_h_v2b.cu (state scan) and cuda_o_v1.cu (output); semantics as
 // definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md:62-142.
@@ -38,7 +44,10 @@ __device__ uint32_t g_gdn_status = 0;
 namespace {
 using namespace sm100;
 
-constexpr int kThreads = 512;  // 16 warps: four per TMEM lane quarter
+constexpr int kComputeWarps = 16;  // four per TMEM lane quarter
+constexpr int kComputeThreads = 32 * kComputeWarps;
+constexpr int kThreads = kComputeThreads + 32;  // + the TMA / MMA issue warp
+constexpr uint32_t kComputeBar = 1;             // named barrier of the compute warps
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait, then give up
 
 // ---- shared memory map (offsets from a 1024-aligned base) -----------------
@@ -51,7 +60,7 @@ constexpr uint32_t OFF_ST = OFF_V + 2 * kVStage;   // bf16 S: [kb 2][v 128][128 
 constexpr uint32_t OFF_P = OFF_ST + 32768;         // P: [t 64][128 B] (K-major A)
 constexpr uint32_t OFF_TB = OFF_P + 8192;          // T diag(beta): [s 64][t 128 B] (MN-major A)
 constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T diag(beta e^gamma)
-constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A^T [64][68]; later W [kb 2][t 64][128 B]
+constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A^T [64][72]; later W [kb 2][t 64][128 B]
 constexpr uint32_t OFF_VN = OFF_AF + 17408;        // Vn bf16 [vb 2][t 64][128 B] (MN-major B);
                                                    // during the inverse: fp32 T^T [64][68] (spills into VH)
 constexpr uint32_t OFF_VH = OFF_VN + 16384;        // Vd hi (MN-major A)
@@ -63,12 +72,19 @@ constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict
 
 // ---- TMEM columns ----------------------------------------------------------
 constexpr uint32_t TM_ST = 0;     // St [v 128 lanes][k 128 cols]
-constexpr uint32_t TM_D1 = 128;   // [K;Q]K^T [128 lanes][64 cols]
-constexpr uint32_t TM_VN = 192;   // U -> Vn, then P Vn   (M=64 layout)
-constexpr uint32_t TM_W = 320;    // W, then Q S          (M=64 layout)
+constexpr uint32_t TM_VN = 128;   // U -> Vn, then P Vn   (M=64 layout)
+constexpr uint32_t TM_W = 256;    // [K;Q]K^T ([128 lanes][64 cols]), then W (M=64 layout)
+constexpr uint32_t TM_QS = 384;   // Q S                  (M=64 layout)
 constexpr uint32_t kTmemCols = 512;
 
 constexpr uint32_t kTmaBytes = 2 * kKQStage / 2 + kVStage;  // K 16K + Q 16K + V 16K
+
+// mbarriers (OFF_MISC + 1024): TMA stages, tensor pipe -> compute warps (one
+// tcgen05.commit each), compute warps -> issue warp (one arrive per warp).
+enum : int {
+  BAR_TMA0 = 0, BAR_TMA1, BAR_M1, BAR_M2, BAR_M3, BAR_PV, BAR_ST,
+  RDY_S, RDY_T, RDY_W, RDY_V, BAR_END, kNumBars
+};
 
 struct ChunkParams {
   const float* state;
@@ -94,40 +110,6 @@ constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_
 // DBG_CLK: SM cycles thread 0 of the debug CTA spent in each phase, summed over
 // all chunks of its sequence (phases: see the PHASE() marks in the chunk loop).
 
-__device__ __forceinline__ void write_bf16_row16(uint32_t tile, uint32_t row, int cb,
-                                                 const float* v) {
-  // 16 consecutive columns [16*cb, 16*cb+16) of a 128-column bf16 row stored as
-  // two 64-column swizzled blocks of `rows` rows: block stride passed via tile.
-  const uint32_t c0 = (cb & 3) * 2;
-  sts128(tile + sw128_off(row, c0), pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-  sts128(tile + sw128_off(row, c0 + 1), pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
-         pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
-}
-
-// Reads columns [16*cb, 16*cb+16) of row `row` of a 128-column bf16 tile stored
-// as two swizzled 64-column blocks of `block_bytes` each, widened to fp32.
-__device__ __forceinline__ void read_bf16_row16(uint32_t tile, uint32_t block_bytes,
-                                                uint32_t row, int cb, float* v) {
-  const uint32_t base = tile + (cb >> 2) * block_bytes;
-  const uint32_t c0 = (cb & 3) * 2;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint32_t w0, w1, w2, w3;
-    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
-                 : "r"(base + sw128_off(row, c0 + h)));
-    v[8 * h + 0] = bf16_lo(w0);
-    v[8 * h + 1] = bf16_hi(w0);
-    v[8 * h + 2] = bf16_lo(w1);
-    v[8 * h + 3] = bf16_hi(w1);
-    v[8 * h + 4] = bf16_lo(w2);
-    v[8 * h + 5] = bf16_hi(w2);
-    v[8 * h + 6] = bf16_lo(w3);
-    v[8 * h + 7] = bf16_hi(w3);
-  }
-}
-
 template <bool DEBUG>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -142,9 +124,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // gamma * log2(e) and beta per token, double-buffered by chunk parity: the
   // gates of chunk c+1 are computed while chunk c's tensor-core work runs.
   float* gates_buf = reinterpret_cast<float*>(smem + OFF_MISC);  // [2][gamma 64 | beta 64]
-  uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + OFF_MISC + 1024);  // [2]
-  uint64_t* bar_mma = bar_tma + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_mma + 1);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_MISC + 1024);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   // fp32 scratch of the inverse (A^T 18 KiB from OFF_AF into the Vn tile, T^T
   // after it into the Vd_hi tile, products in the Vd_lo tile; all free then)
   float* At = reinterpret_cast<float*>(smem + OFF_AF);   // A column-major: At[k][i] = A[i][k]
@@ -154,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-  const int cq = warp >> 2;      // column quarter handled by this warp (32 of 128 columns)
+  const int cq = (warp >> 2) & 3;  // column quarter handled by this warp (32 of 128 columns)
   const int g = lane >> 2, tq = lane & 3;  // 16x256b fragment coordinates
   const int r_lo = 16 * quarter + g;       // rows of an M=64 accumulator held by this thread
   const int rowv = 32 * quarter + lane;    // row of an M=128 accumulator held by this thread
@@ -171,25 +152,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<float4*>(ns_rows)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     return;
   }
-  const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
-  long long clk_acc[16];
-  long long clk_last = 0;
-  if constexpr (DEBUG) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) clk_acc[i] = 0;
-    clk_last = clock64();
-  }
-#define PHASE(k)                              \
-  if constexpr (DEBUG) {                      \
-    const long long now_ = clock64();         \
-    clk_acc[k] += now_ - clk_last;            \
-    clk_last = now_;                          \
-  }
+  const int nchunks = static_cast<int>((Ltot + kChunk - 1) / kChunk);
 
   if (tid == 0) {
-    mbar_init(&bar_tma[0], 1);
-    mbar_init(&bar_tma[1], 1);
-    mbar_init(bar_mma, 1);
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(&bars[i], (i >= RDY_S && i <= RDY_V) ? kComputeWarps : 1);
     fence_mbar_init();
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
@@ -203,338 +170,540 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-  const uint32_t tq_st = tmem + lane_base + TM_ST + 32 * cq;  // this thread's St columns
-  const float neg_exp_A = -expf(p.A_log[h]);
-  const float dt_bias_h = p.dt_bias[h];
+  bool failed = false;  // this thread gave up on a wait
 
-  // ---- initial state -> TMEM (row rowv, columns [32 cq, 32 cq + 32)) -------
-  {
-    const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + rowv * kHead + 32 * cq
-                               : nullptr;
-    float v[32];
+  if (warp < kComputeWarps) {
+    // ======================= compute warps =================================
+    const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
+    long long clk_acc[16];
+    long long clk_last = 0;
+    if constexpr (DEBUG) {
 #pragma unroll
-    for (int q4 = 0; q4 < 8; ++q4) {
-      float4 x = src ? ld_stream_f4(src + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-      v[4 * q4] = x.x;
-      v[4 * q4 + 1] = x.y;
-      v[4 * q4 + 2] = x.z;
-      v[4 * q4 + 3] = x.w;
+      for (int i = 0; i < 16; ++i) clk_acc[i] = 0;
+      clk_last = clock64();
     }
-    tmem_st32(tq_st, v);
-    tmem_wait_st();
+#define PHASE(k)                              \
+  if constexpr (DEBUG) {                      \
+    const long long now_ = clock64();         \
+    clk_acc[k] += now_ - clk_last;            \
+    clk_last = now_;                          \
   }
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tq_st = tmem + lane_base + TM_ST + 32 * cq;  // this thread's St columns
+    const float neg_exp_A = -expf(p.A_log[h]);
+    const float dt_bias_h = p.dt_bias[h];
 
-  auto issue_loads = [&](int cc, int s) {
-    const int tok = static_cast<int>(bos + static_cast<int64_t>(cc) * kChunk);
-    uint64_t* bar = &bar_tma[s];
-    mbar_arrive_expect_tx(bar, kTmaBytes);
-    uint8_t* kq = smem + OFF_KQ + s * kKQStage;
-    uint8_t* vs = smem + OFF_V + s * kVStage;
-#pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
-      tma_load_3d(kq + kb * 16384, &tm_k, bar, kb * 64, qh, tok);
-      tma_load_3d(kq + kb * 16384 + 8192, &tm_q, bar, kb * 64, qh, tok);
-      tma_load_3d(vs + kb * 8192, &tm_v, bar, kb * 64, h, tok);
-    }
-  };
-
-  uint32_t tma_phase0 = 0, tma_phase1 = 0, mma_phase = 0;
-  bool aborted = false;
-  // All threads wait on the same barrier, then agree on the outcome.
-  auto wait_all = [&](uint64_t* bar, uint32_t& phase) -> bool {
-    const bool ok = mbar_wait(bar, phase, kTimeoutNs);
-    phase ^= 1u;
-    return __syncthreads_or(ok ? 0 : 1) == 0;
-  };
-
-  // Gates of one chunk from raw a/b values held by warp 1 (two tokens per lane):
-  // log-decay, its inclusive scan (gamma, stored in log2 units) and beta.
-  float ga_raw[2] = {0.f, 0.f}, gb_raw[2] = {0.f, 0.f};
-  auto prefetch_gates = [&](int cc) {
-    const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int64_t t = t0c + 2 * lane + e;
-      if (t < eos) {
-        ga_raw[e] = __bfloat162float(p.a[t * p.Hv + h]);
-        gb_raw[e] = __bfloat162float(p.b[t * p.Hv + h]);
-      }
-    }
-  };
-  auto compute_gates = [&](int cc) {  // warp 1 only
-    const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
-    const int Lc = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0c));
-    float lg[2], bt[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const bool valid = 2 * lane + e < Lc;
-      lg[e] = valid ? neg_exp_A * softplus_t20_fast(ga_raw[e] + dt_bias_h) : 0.f;
-      bt[e] = valid ? sigmoid_fast(gb_raw[e]) : 0.f;
-    }
-    const float pair = lg[0] + lg[1];
-    float incl = pair;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += y;
-    }
-    float* gb = gates_buf + (cc & 1) * 128;
-    gb[2 * lane] = (incl - pair + lg[0]) * kLog2e;
-    gb[2 * lane + 1] = incl * kLog2e;
-    gb[64 + 2 * lane] = bt[0];
-    gb[64 + 2 * lane + 1] = bt[1];
-  };
-
-  if (tid == 0) issue_loads(0, 0);
-  if (warp == 1) {  // warp 1 owns the gates: warp 0's lane 0 is busy issuing MMAs
-    prefetch_gates(0);
-    compute_gates(0);
-    if (Ltot > kChunk) prefetch_gates(1);
-  }
-  const int nchunks = static_cast<int>((Ltot + kChunk - 1) / kChunk);
-
-  const uint32_t idesc_d1 = idesc_bf16(128, 64, false, false);
-  const uint32_t idesc_tv = idesc_bf16(64, 128, true, true);
-  const uint32_t idesc_vn = idesc_bf16(64, 128, false, false, true);
-  const uint32_t idesc_qs = idesc_bf16(64, 128, false, false);
-  const uint32_t idesc_pv = idesc_bf16(64, 128, false, true);
-  const uint32_t idesc_st = idesc_bf16(128, 128, true, true);
-
-  for (int c = 0; c < nchunks; ++c) {
-    const int stage = c & 1;
-    const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
-    const int L = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0));
-    const bool dbg = dbg_cta && c == p.dbg_chunk;
-    const uint32_t kq = sb + OFF_KQ + stage * kKQStage;
-    const uint32_t vsm = sb + OFF_V + stage * kVStage;
-
-    tc_fence_before();
-    __syncthreads();  // previous chunk fully drained
-    tc_fence_after();
-    if (tid == 0 && c + 1 < nchunks) issue_loads(c + 1, stage ^ 1);
-    PHASE(0)
-
-    const float* gam = gates_buf + stage * 128;
-    const float* bet = gam + 64;
-    if (dbg && tid < 64) {
-      p.debug[DBG_GAM + tid] = gam[tid] / kLog2e;
-      p.debug[DBG_BET + tid] = bet[tid];
-    }
-    PHASE(1)
-
-    // ---- state pass: St -> bf16 operand tile; St *= e^{gamma_63} -----------
+    // ---- initial state -> TMEM (row rowv, columns [32 cq, 32 cq + 32)) -----
     {
-      const float dec = ex2_ftz(gam[63]);
+      const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + rowv * kHead + 32 * cq
+                                 : nullptr;
+      float v[32];
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4) {
+        float4 x = src ? ld_stream_f4(src + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[4 * q4] = x.x;
+        v[4 * q4 + 1] = x.y;
+        v[4 * q4 + 2] = x.z;
+        v[4 * q4 + 3] = x.w;
+      }
+      tmem_st32(tq_st, v);
+      tmem_wait_st();
+    }
+
+    // One arrival per warp on a compute -> issue-warp barrier, after this
+    // thread's operand writes (smem: fence to the async proxy; TMEM: ordered
+    // before the thread sync).
+    auto signal = [&](int b) {
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[b]);
+    };
+    // Bounded wait on a tensor-pipe commit.  After a timeout the thread stops
+    // waiting and runs on (its results are then garbage, the status word says
+    // so); the compute warps agree once per chunk to leave the loop.
+    auto wait_mma = [&](int b, uint32_t parity) {
+      if (!failed) failed = !mbar_wait(&bars[b], parity, kTimeoutNs);
+      tc_fence_after();
+    };
+
+    // Gates of one chunk from raw a/b values held by warp 1 (two tokens per lane):
+    // log-decay, its inclusive scan (gamma, stored in log2 units) and beta.
+    float ga_raw[2] = {0.f, 0.f}, gb_raw[2] = {0.f, 0.f};
+    auto prefetch_gates = [&](int cc) {
+      const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int64_t t = t0c + 2 * lane + e;
+        if (t < eos) {
+          ga_raw[e] = __bfloat162float(p.a[t * p.Hv + h]);
+          gb_raw[e] = __bfloat162float(p.b[t * p.Hv + h]);
+        }
+      }
+    };
+    auto compute_gates = [&](int cc) {  // warp 1 only
+      const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
+      const int Lc = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0c));
+      float lg[2], bt[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool valid = 2 * lane + e < Lc;
+        lg[e] = valid ? neg_exp_A * softplus_t20_fast(ga_raw[e] + dt_bias_h) : 0.f;
+        bt[e] = valid ? sigmoid_fast(gb_raw[e]) : 0.f;
+      }
+      const float pair = lg[0] + lg[1];
+      float incl = pair;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += y;
+      }
+      float* gb = gates_buf + (cc & 1) * 128;
+      gb[2 * lane] = (incl - pair + lg[0]) * kLog2e;
+      gb[2 * lane + 1] = incl * kLog2e;
+      gb[64 + 2 * lane] = bt[0];
+      gb[64 + 2 * lane + 1] = bt[1];
+    };
+    auto dump_state = [&]() {  // debug: St after the state update of the debug chunk
       float v[32];
       tmem_ld32(tq_st, v);
       tmem_wait_ld();
       reg_fence(v);
-      const uint32_t tile = sb + OFF_ST + (cq >> 1) * 16384;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4)
-        sts128(tile + sw128_off(rowv, (cq & 1) * 4 + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
-               pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
-               pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= dec;
-      tmem_st32(tq_st, v);
-      tmem_wait_st();
-      fence_async_smem();
-    }
-    PHASE(2)
-    tc_fence_before();
-    if (!wait_all(&bar_tma[stage], stage ? tma_phase1 : tma_phase0)) { aborted = true; break; }
-    PHASE(3)
+      for (int i = 0; i < 32; ++i) p.debug[DBG_ST + rowv * 128 + 32 * cq + i] = v[i];
+    };
 
-    // ---- MMA 1: [K;Q] K^T ---------------------------------------------------
-    if (tid == 0) {
+    if (warp == 1) {
+      prefetch_gates(0);
+      compute_gates(0);
+      if (Ltot > kChunk) prefetch_gates(1);
+    }
+    bool aborted = false;
+
+    for (int c = 0; c < nchunks; ++c) {
+      const int stage = c & 1;
+      const uint32_t par = static_cast<uint32_t>(c & 1);
+      const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
+      const int L = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0));
+      const bool dbg = dbg_cta && c == p.dbg_chunk;
+      const uint32_t vsm = sb + OFF_V + stage * kVStage;
+
+      // previous chunk's state update done: its operand tiles are free and St
+      // is final.  The barrier also publishes this chunk's gates (warp 1).
+      if (c > 0) wait_mma(BAR_ST, par ^ 1u);
+      if (named_any(kComputeBar, kComputeThreads, failed)) { aborted = true; break; }
+      if (dbg_cta && c - 1 == p.dbg_chunk) dump_state();
+      PHASE(0)
+
+      const float* gam = gates_buf + stage * 128;
+      const float* bet = gam + 64;
+      if (dbg && tid < 64) {
+        p.debug[DBG_GAM + tid] = gam[tid] / kLog2e;
+        p.debug[DBG_BET + tid] = bet[tid];
+      }
+      PHASE(1)
+
+      // ---- state pass: St -> bf16 operand tile; St *= e^{gamma_63} ---------
+      {
+        const float dec = ex2_ftz(gam[63]);
+        float v[32];
+        tmem_ld32(tq_st, v);
+        tmem_wait_ld();
+        reg_fence(v);
+        const uint32_t tile = sb + OFF_ST + (cq >> 1) * 16384;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+          sts128(tile + sw128_off(rowv, (cq & 1) * 4 + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
+                 pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
+                 pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= dec;
+        tmem_st32(tq_st, v);
+        tmem_wait_st();
+      }
+      signal(RDY_S);
+      PHASE(2)
+      wait_mma(BAR_M1, par);
+      PHASE(3)
+
+      // ---- A (quarters 0-1, stored column-major) and P (quarters 2-3) -------
+      {
+        const int i = rowv & 63;
+        const float gi = gam[i];
+        float v[16];
+        tmem_ld16(tmem + lane_base + TM_W + 16 * cq, v);
+        tmem_wait_ld();
+        reg_fence(v);
+        PHASE(4)
+        if (quarter < 2) {
+          const float bi = bet[i];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = 16 * cq + jj;
+            const float aij = (j < i) ? bi * v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
+            At[j * kAtPitch + i] = aij;
+            if (dbg) p.debug[DBG_A + i * 64 + j] = aij;
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = 16 * cq + jj;
+            v[jj] = (j <= i) ? v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
+          }
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2)
+            sts128(sb + OFF_P + sw128_off(i, 2 * cq + c2), pack_bf16x2(v[8 * c2], v[8 * c2 + 1]),
+                   pack_bf16x2(v[8 * c2 + 2], v[8 * c2 + 3]), pack_bf16x2(v[8 * c2 + 4], v[8 * c2 + 5]),
+                   pack_bf16x2(v[8 * c2 + 6], v[8 * c2 + 7]));
+          if (dbg)
+            for (int jj = 0; jj < 16; ++jj) p.debug[DBG_P + i * 64 + 16 * cq + jj] = v[jj];
+        }
+      }
+      PHASE(5)
+      named_sync(kComputeBar, kComputeThreads);
+      PHASE(6)
+
+      // ---- T = (I + A)^-1, fp32, blocks of 16:
+      //      level 0: the four diagonal blocks by right-looking elimination;
+      //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22;
+      //      level 2: [T20 T21; T30 T31] = -T22' (A21' T11'), primes = 32x32 halves.
+      if (tid < 64) {
+        const int b = tid >> 4, j = tid & 15, b0 = 16 * b;
+        float x[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) x[r] = (r == j) ? 1.f : 0.f;
+#pragma unroll
+        for (int k = 0; k < 15; ++k) {
+          const float xk = x[k];
+          const float* col = At + (b0 + k) * kAtPitch + b0;  // A[b0 + i][b0 + k]
+#pragma unroll
+          for (int q = (k + 1) / 4; q < 4; ++q) {
+            const float4 a4 = *reinterpret_cast<const float4*>(col + 4 * q);
+            if (4 * q + 0 > k) x[4 * q + 0] = fmaf(-a4.x, xk, x[4 * q + 0]);
+            if (4 * q + 1 > k) x[4 * q + 1] = fmaf(-a4.y, xk, x[4 * q + 1]);
+            if (4 * q + 2 > k) x[4 * q + 2] = fmaf(-a4.z, xk, x[4 * q + 2]);
+            if (4 * q + 3 > k) x[4 * q + 3] = fmaf(-a4.w, xk, x[4 * q + 3]);
+          }
+        }
+        float* tcol = Tcm + (b0 + j) * kTcPitch;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<float4*>(tcol + b0 + 4 * q) =
+              make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+        for (int q = 0; q < 4 * b; ++q)  // rows above the diagonal block are zero
+          *reinterpret_cast<float4*>(tcol + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      named_sync(kComputeBar, kComputeThreads);
+      if (tid < 256) {  // level 1, step 1: X = A_IJ T_JJ, (I, J) = (1, 0) for tid < 128, else (3, 2)
+        const int pr = tid >> 7, u = tid & 127;
+        const int J0 = 32 * pr, I0 = J0 + 16;
+        const int j = u & 15, r0 = (u >> 4) * 2;
+        float x0 = 0.f, x1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float tkj = Tcm[(J0 + j) * kTcPitch + J0 + k];   // T[J0+k][J0+j]
+          x0 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0], tkj, x0);     // A[I0+r0][J0+k]
+          x1 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0 + 1], tkj, x1);
+        }
+        Xcm[pr * 272 + j * 17 + r0] = x0;
+        Xcm[pr * 272 + j * 17 + r0 + 1] = x1;
+      }
+      named_sync(kComputeBar, kComputeThreads);
+      if (tid < 256) {  // level 1, step 2: T_IJ = -T_II X
+        const int pr = tid >> 7, u = tid & 127;
+        const int J0 = 32 * pr, I0 = J0 + 16;
+        const int j = u & 15, r0 = (u >> 4) * 2;
+        float t0_ = 0.f, t1_ = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float xkj = Xcm[pr * 272 + j * 17 + k];
+          t0_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0], xkj, t0_);   // T[I0+r0][I0+k]
+          t1_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0 + 1], xkj, t1_);
+        }
+        Tcm[(J0 + j) * kTcPitch + I0 + r0] = -t0_;
+        Tcm[(J0 + j) * kTcPitch + I0 + r0 + 1] = -t1_;
+      }
+      named_sync(kComputeBar, kComputeThreads);
+      // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
+      // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after):
+      // warp w < 8 computes the 16x8 output tile (row tile w/4, column tile w%4).
+      if (warp < 8) {  // step 1: M = A21' T11' (32x32x32)
+        const int rt = warp >> 2, ct = warp & 3, t4 = tq;
+        float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const int k0 = 8 * ks;
+          const float* ar = At + (k0 + t4) * kAtPitch + 32 + 16 * rt + g;  // A[32+16rt+g][k0+t]
+          const float* br = Tcm + (8 * ct + g) * kTcPitch + k0 + t4;       // T[k0+t][8ct+g]
+          mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
+                          to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+        }
+        float* mc = Mcm + (8 * ct + 2 * t4) * 36 + 16 * rt + g;  // M[r][j] at Mcm[j*36 + r]
+        mc[0] = cacc[0];
+        mc[36] = cacc[1];
+        mc[8] = cacc[2];
+        mc[36 + 8] = cacc[3];
+      }
+      named_sync(kComputeBar, kComputeThreads);
+      if (warp < 8) {  // step 2: T21' = -T22' M
+        const int rt = warp >> 2, ct = warp & 3, t4 = tq;
+        float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const int k0 = 8 * ks;
+          const float* ar = Tcm + (32 + k0 + t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+16rt+g][32+k0+t]
+          const float* br = Mcm + (8 * ct + g) * 36 + k0 + t4;                  // M[k0+t][8ct+g]
+          mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kTcPitch]),
+                          to_tf32(ar[4 * kTcPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+        }
+        float* tc = Tcm + (8 * ct + 2 * t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+r][j] at Tcm[j][32+r]
+        tc[0] = -cacc[0];
+        tc[kTcPitch] = -cacc[1];
+        tc[8] = -cacc[2];
+        tc[kTcPitch + 8] = -cacc[3];
+      }
+      named_sync(kComputeBar, kComputeThreads);
+      PHASE(7)
+      {
+        // T~ = T_off diag(beta) and T^ = T diag(beta e^gamma) as MN-major bf16
+        // tiles: row j of a tile holds column j of T.  T~ leaves out the unit
+        // diagonal: U = beta (.) V + T~_off V, and beta (.) V is added in fp32 when
+        // Vn is drained (a bf16 beta_j on the diagonal would cost ~2^-9 relative
+        // error on all of U).
+        const int j = tid & 63;
+        const bool hat = (tid >> 6) & 1;
+        const int part = tid >> 7;  // 16-row quarter of the tile row (2 chunks)
+        const float sc = hat ? bet[j] * ex2_ftz(gam[j]) : bet[j];
+        const float* trow = Tcm + j * kTcPitch;
+        const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int ch = 2 * part + c2;
+          const float4 x0 = *reinterpret_cast<const float4*>(trow + ch * 8);
+          const float4 x1 = *reinterpret_cast<const float4*>(trow + ch * 8 + 4);
+          float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = (!hat && ch * 8 + e == j) ? 0.f : x[e] * sc;
+          sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
+                 pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+        }
+        if (dbg && !hat) {
+          for (int i = 16 * part; i < 16 * part + 16; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
+        }
+      }
+      signal(RDY_T);
+      PHASE(8)
+      wait_mma(BAR_M2, par);
+      PHASE(9)
+
+      // ---- W -> bf16 K-major tile; thread rows r_lo, r_lo+8, columns 32 cq + .. --
+      // (column group jg of this warp's 32 columns is chunk (cq&1)*4 + jg of block cq/2)
+      {
+        float w[16];
+        tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, w);
+        tmem_wait_ld();
+        reg_fence(w);
+        const uint32_t tile = sb + OFF_AF + (cq >> 1) * 8192;
+#pragma unroll
+        for (int jg = 0; jg < 4; ++jg) {
+          const int ch = (cq & 1) * 4 + jg;
+          sts32(tile + sw128_off(r_lo, ch) + 4 * tq, pack_bf16x2(w[4 * jg], w[4 * jg + 1]));
+          sts32(tile + sw128_off(r_lo + 8, ch) + 4 * tq, pack_bf16x2(w[4 * jg + 2], w[4 * jg + 3]));
+        }
+        if (dbg) {
+          for (int jg = 0; jg < 4; ++jg)
+            for (int e = 0; e < 2; ++e) {
+              const int col = 32 * cq + 8 * jg + 2 * tq + e;
+              p.debug[DBG_W + r_lo * 128 + col] = w[4 * jg + e];
+              p.debug[DBG_W + (r_lo + 8) * 128 + col] = w[4 * jg + 2 + e];
+            }
+          float u[16];
+          tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, u);
+          tmem_wait_ld();
+          reg_fence(u);
+          for (int jg = 0; jg < 4; ++jg)
+            for (int rr = 0; rr < 2; ++rr) {
+              const int row = r_lo + 8 * rr;
+              const uint32_t vw =
+                  lds32(vsm + (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq);
+              const int col = 32 * cq + 8 * jg + 2 * tq;
+              p.debug[DBG_U + row * 128 + col] = fmaf(bet[row], bf16_lo(vw), u[4 * jg + 2 * rr]);
+              p.debug[DBG_U + row * 128 + col + 1] = fmaf(bet[row], bf16_hi(vw), u[4 * jg + 2 * rr + 1]);
+            }
+        }
+      }
+      signal(RDY_W);
+      PHASE(10)
+      if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap W S
+        compute_gates(c + 1);
+        if (c + 2 < nchunks) prefetch_gates(c + 2);
+      }
+      wait_mma(BAR_M3, par);
+      PHASE(11)
+
+      // ---- Vn = beta V + Vn_part -> bf16 (B of P Vn);
+      //      Vd = e^{g63 - g_t} Vn -> hi/lo bf16 (A of the state update) ------
+      {
+        float v[16];
+        tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, v);
+        tmem_wait_ld();
+        reg_fence(v);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int row = r_lo + 8 * rr;
+          const bool valid = row < L;
+          const float dec = valid ? ex2_ftz(gam[63] - gam[row]) : 0.f;
+          const float bt = bet[row];
+#pragma unroll
+          for (int jg = 0; jg < 4; ++jg) {
+            const uint32_t off = (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq;
+            const uint32_t vw = lds32(vsm + off);
+            const float x0 = valid ? fmaf(bt, bf16_lo(vw), v[4 * jg + 2 * rr]) : 0.f;
+            const float x1 = valid ? fmaf(bt, bf16_hi(vw), v[4 * jg + 2 * rr + 1]) : 0.f;
+            const float d0 = x0 * dec, d1 = x1 * dec;
+            const float h0 = __bfloat162float(__float2bfloat16_rn(d0));
+            const float h1 = __bfloat162float(__float2bfloat16_rn(d1));
+            sts32(sb + OFF_VN + off, pack_bf16x2(x0, x1));
+            sts32(sb + OFF_VH + off, pack_bf16x2(h0, h1));
+            sts32(sb + OFF_VL + off, pack_bf16x2(d0 - h0, d1 - h1));
+            if (dbg) {
+              const int col = 32 * cq + 8 * jg + 2 * tq;
+              p.debug[DBG_VN + row * 128 + col] = x0;
+              p.debug[DBG_VN + row * 128 + col + 1] = x1;
+            }
+          }
+        }
+        if (dbg) {
+          tmem_ld16x256_x4(tmem + lane_base + TM_QS + 32 * cq, v);
+          tmem_wait_ld();
+          reg_fence(v);
+          for (int jg = 0; jg < 4; ++jg)
+            for (int rr = 0; rr < 2; ++rr)
+              for (int e = 0; e < 2; ++e)
+                p.debug[DBG_QS + (r_lo + 8 * rr) * 128 + 32 * cq + 8 * jg + 2 * tq + e] =
+                    v[4 * jg + 2 * rr + e];
+        }
+      }
+      signal(RDY_V);
+      PHASE(12)
+      wait_mma(BAR_PV, par);
+      PHASE(13)
+
+      // ---- output rows: O = scale (e^{gamma_t} QS + PV) ----------------------
+      {
+        float qs[16], pv[16];
+        tmem_ld16x256_x4(tmem + lane_base + TM_QS + 32 * cq, qs);
+        tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, pv);
+        tmem_wait_ld();
+        reg_fence(qs);
+        reg_fence(pv);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int row = r_lo + 8 * rr;
+          if (row < L) {
+            const float eg = p.scale * ex2_ftz(gam[row]);
+            uint32_t* orow = reinterpret_cast<uint32_t*>(p.out + ((t0 + row) * p.Hv + h) * kHead +
+                                                         32 * cq + 2 * tq);
+#pragma unroll
+            for (int jg = 0; jg < 4; ++jg) {
+              const float o0 = fmaf(eg, qs[4 * jg + 2 * rr], p.scale * pv[4 * jg + 2 * rr]);
+              const float o1 = fmaf(eg, qs[4 * jg + 2 * rr + 1], p.scale * pv[4 * jg + 2 * rr + 1]);
+              orow[4 * jg] = pack_bf16x2(o0, o1);
+            }
+          }
+          if (dbg)
+            for (int jg = 0; jg < 4; ++jg)
+              for (int e = 0; e < 2; ++e)
+                p.debug[DBG_PV + row * 128 + 32 * cq + 8 * jg + 2 * tq + e] = pv[4 * jg + 2 * rr + e];
+        }
+      }
+      PHASE(14)
+    }
+    if constexpr (DEBUG) {
+      if (dbg_cta && tid == 0)
+        for (int i = 0; i < 16; ++i) p.debug[DBG_CLK + i] = static_cast<float>(clk_acc[i]);
+    }
+#undef PHASE
+
+    // ---- final state -> new_state (row rowv, this warp's 32 columns) --------
+    if (!aborted) {
+      wait_mma(BAR_ST, static_cast<uint32_t>((nchunks - 1) & 1));
+      if (!failed) {
+        if (dbg_cta && nchunks - 1 == p.dbg_chunk) dump_state();
+        float* dst = ns_rows + rowv * kHead + 32 * cq;
+        float v[32];
+        tmem_ld32(tq_st, v);
+        tmem_wait_ld();
+        reg_fence(v);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          st_stream_f4(dst + q4 * 4,
+                       make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
+      }
+    }
+  } else if (lane == 0) {
+    // ======================= TMA / MMA issue thread ========================
+    const uint32_t idesc_d1 = idesc_bf16(128, 64, false, false);
+    const uint32_t idesc_tv = idesc_bf16(64, 128, true, true);
+    const uint32_t idesc_vn = idesc_bf16(64, 128, false, false, true);
+    const uint32_t idesc_qs = idesc_bf16(64, 128, false, false);
+    const uint32_t idesc_pv = idesc_bf16(64, 128, false, true);
+    const uint32_t idesc_st = idesc_bf16(128, 128, true, true);
+
+    int tma_issued = 0, tma_done = 0;  // chunks whose loads were issued / have landed
+    auto issue_loads = [&](int cc) {
+      const int s = cc & 1;
+      const int tok = static_cast<int>(bos + static_cast<int64_t>(cc) * kChunk);
+      uint64_t* bar = &bars[BAR_TMA0 + s];
+      mbar_arrive_expect_tx(bar, kTmaBytes);
+      uint8_t* kq = smem + OFF_KQ + s * kKQStage;
+      uint8_t* vs = smem + OFF_V + s * kVStage;
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb) {
+        tma_load_3d(kq + kb * 16384, &tm_k, bar, kb * 64, qh, tok);
+        tma_load_3d(kq + kb * 16384 + 8192, &tm_q, bar, kb * 64, qh, tok);
+        tma_load_3d(vs + kb * 8192, &tm_v, bar, kb * 64, h, tok);
+      }
+      tma_issued = cc + 1;
+    };
+    auto wait_bar = [&](int b, uint32_t parity) -> bool {
+      if (!mbar_wait(&bars[b], parity, kTimeoutNs)) return false;
       tc_fence_after();
+      return true;
+    };
+    // MMA 1 of chunk cc: [K;Q] K^T -> TM_W (M=128, N=64)
+    auto mma1 = [&](int cc) -> bool {
+      const int s = cc & 1;
+      if (!wait_bar(BAR_TMA0 + s, static_cast<uint32_t>((cc >> 1) & 1))) return false;
+      tma_done = cc + 1;
+      const uint32_t kq = sb + OFF_KQ + s * kKQStage;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-        mma_bf16_ss(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
+        mma_bf16_ss(tmem + TM_W, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
                     idesc_d1, ks > 0);
       }
-      mma_commit(bar_mma);
-    }
-    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
-    PHASE(4)
-    tc_fence_after();
+      mma_commit(&bars[BAR_M1]);
+      return true;
+    };
 
-    // ---- A (quarters 0-1, stored column-major) and P (quarters 2-3) ---------
-    {
-      const int i = rowv & 63;
-      const float gi = gam[i];
-      float v[16];
-      tmem_ld16(tmem + lane_base + TM_D1 + 16 * cq, v);
-      tmem_wait_ld();
-      reg_fence(v);
-      PHASE(14)
-      if (quarter < 2) {
-        const float bi = bet[i];
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = 16 * cq + jj;
-          const float aij = (j < i) ? bi * v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
-          At[j * kAtPitch + i] = aij;
-          if (dbg) p.debug[DBG_A + i * 64 + j] = aij;
-        }
-      } else {
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = 16 * cq + jj;
-          v[jj] = (j <= i) ? v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
-        }
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2)
-          sts128(sb + OFF_P + sw128_off(i, 2 * cq + c2), pack_bf16x2(v[8 * c2], v[8 * c2 + 1]),
-                 pack_bf16x2(v[8 * c2 + 2], v[8 * c2 + 3]), pack_bf16x2(v[8 * c2 + 4], v[8 * c2 + 5]),
-                 pack_bf16x2(v[8 * c2 + 6], v[8 * c2 + 7]));
-        if (dbg)
-          for (int jj = 0; jj < 16; ++jj) p.debug[DBG_P + i * 64 + 16 * cq + jj] = v[jj];
-      }
-    }
-    PHASE(15)
-    fence_async_smem();
-    __syncthreads();
-    PHASE(5)
+    issue_loads(0);
+    if (nchunks > 1) issue_loads(1);
+    bool ok = mma1(0);
+    for (int c = 0; ok && c < nchunks; ++c) {
+      const uint32_t par = static_cast<uint32_t>(c & 1);
+      const uint32_t kq = sb + OFF_KQ + (c & 1) * kKQStage;
+      const uint32_t vsm = sb + OFF_V + (c & 1) * kVStage;
 
-    // ---- T = (I + A)^-1, fp32, blocks of 16:
-    //      level 0: the four diagonal blocks by right-looking elimination;
-    //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22;
-    //      level 2: [T20 T21; T30 T31] = -T22' (A21' T11'), primes = 32x32 halves.
-    if (tid < 64) {
-      const int b = tid >> 4, j = tid & 15, b0 = 16 * b;
-      float x[16];
+      // Q S (the S tile of this chunk) -> TM_QS
+      if (!(ok = wait_bar(RDY_S, par))) break;
 #pragma unroll
-      for (int r = 0; r < 16; ++r) x[r] = (r == j) ? 1.f : 0.f;
-#pragma unroll
-      for (int k = 0; k < 15; ++k) {
-        const float xk = x[k];
-        const float* col = At + (b0 + k) * kAtPitch + b0;  // A[b0 + i][b0 + k]
-#pragma unroll
-        for (int q = (k + 1) / 4; q < 4; ++q) {
-          const float4 a4 = *reinterpret_cast<const float4*>(col + 4 * q);
-          if (4 * q + 0 > k) x[4 * q + 0] = fmaf(-a4.x, xk, x[4 * q + 0]);
-          if (4 * q + 1 > k) x[4 * q + 1] = fmaf(-a4.y, xk, x[4 * q + 1]);
-          if (4 * q + 2 > k) x[4 * q + 2] = fmaf(-a4.z, xk, x[4 * q + 2]);
-          if (4 * q + 3 > k) x[4 * q + 3] = fmaf(-a4.w, xk, x[4 * q + 3]);
-        }
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
+        mma_bf16_ss(tmem + TM_QS, sdesc_sw128(kq + kb * 16384 + 8192 + kin, 16, 1024),
+                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_qs, ks > 0);
       }
-      float* tcol = Tcm + (b0 + j) * kTcPitch;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<float4*>(tcol + b0 + 4 * q) =
-            make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
-      for (int q = 0; q < 4 * b; ++q)  // rows above the diagonal block are zero
-        *reinterpret_cast<float4*>(tcol + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    __syncthreads();
-    if (tid < 256) {  // level 1, step 1: X = A_IJ T_JJ, (I, J) = (1, 0) for tid < 128, else (3, 2)
-      const int pr = tid >> 7, u = tid & 127;
-      const int J0 = 32 * pr, I0 = J0 + 16;
-      const int j = u & 15, r0 = (u >> 4) * 2;
-      float x0 = 0.f, x1 = 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float tkj = Tcm[(J0 + j) * kTcPitch + J0 + k];   // T[J0+k][J0+j]
-        x0 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0], tkj, x0);     // A[I0+r0][J0+k]
-        x1 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0 + 1], tkj, x1);
-      }
-      Xcm[pr * 272 + j * 17 + r0] = x0;
-      Xcm[pr * 272 + j * 17 + r0 + 1] = x1;
-    }
-    __syncthreads();
-    if (tid < 256) {  // level 1, step 2: T_IJ = -T_II X
-      const int pr = tid >> 7, u = tid & 127;
-      const int J0 = 32 * pr, I0 = J0 + 16;
-      const int j = u & 15, r0 = (u >> 4) * 2;
-      float t0_ = 0.f, t1_ = 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float xkj = Xcm[pr * 272 + j * 17 + k];
-        t0_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0], xkj, t0_);   // T[I0+r0][I0+k]
-        t1_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0 + 1], xkj, t1_);
-      }
-      Tcm[(J0 + j) * kTcPitch + I0 + r0] = -t0_;
-      Tcm[(J0 + j) * kTcPitch + I0 + r0 + 1] = -t1_;
-    }
-    __syncthreads();
-    // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
-    // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after):
-    // warp w < 8 computes the 16x8 output tile (row tile w/4, column tile w%4).
-    if (warp < 8) {  // step 1: M = A21' T11' (32x32x32)
-      const int rt = warp >> 2, ct = warp & 3, t4 = tq;
-      float cacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int k0 = 8 * ks;
-        const float* ar = At + (k0 + t4) * kAtPitch + 32 + 16 * rt + g;  // A[32+16rt+g][k0+t]
-        const float* br = Tcm + (8 * ct + g) * kTcPitch + k0 + t4;       // T[k0+t][8ct+g]
-        mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
-                        to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
-      }
-      float* mc = Mcm + (8 * ct + 2 * t4) * 36 + 16 * rt + g;  // M[r][j] at Mcm[j*36 + r]
-      mc[0] = cacc[0];
-      mc[36] = cacc[1];
-      mc[8] = cacc[2];
-      mc[36 + 8] = cacc[3];
-    }
-    __syncthreads();
-    if (warp < 8) {  // step 2: T21' = -T22' M
-      const int rt = warp >> 2, ct = warp & 3, t4 = tq;
-      float cacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int k0 = 8 * ks;
-        const float* ar = Tcm + (32 + k0 + t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+16rt+g][32+k0+t]
-        const float* br = Mcm + (8 * ct + g) * 36 + k0 + t4;                  // M[k0+t][8ct+g]
-        mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kTcPitch]),
-                        to_tf32(ar[4 * kTcPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
-      }
-      float* tc = Tcm + (8 * ct + 2 * t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+r][j] at Tcm[j][32+r]
-      tc[0] = -cacc[0];
-      tc[kTcPitch] = -cacc[1];
-      tc[8] = -cacc[2];
-      tc[kTcPitch + 8] = -cacc[3];
-    }
-    __syncthreads();
-    PHASE(6)
-    {
-      // T~ = T_off diag(beta) and T^ = T diag(beta e^gamma) as MN-major bf16
-      // tiles: row j of a tile holds column j of T.  T~ leaves out the unit
-      // diagonal: U = beta (.) V + T~_off V, and beta (.) V is added in fp32 when
-      // Vn is drained (a bf16 beta_j on the diagonal would cost ~2^-9 relative
-      // error on all of U).
-      const int j = tid & 63;
-      const bool hat = (tid >> 6) & 1;
-      const int part = tid >> 7;  // 16-row quarter of the tile row (2 chunks)
-      const float sc = hat ? bet[j] * ex2_ftz(gam[j]) : bet[j];
-      const float* trow = Tcm + j * kTcPitch;
-      const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
-#pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        const int ch = 2 * part + c2;
-        const float4 x0 = *reinterpret_cast<const float4*>(trow + ch * 8);
-        const float4 x1 = *reinterpret_cast<const float4*>(trow + ch * 8 + 4);
-        float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = (!hat && ch * 8 + e == j) ? 0.f : x[e] * sc;
-        sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
-               pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
-      }
-      if (dbg && !hat) {
-        for (int i = 16 * part; i < 16 * part + 16; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
-      }
-    }
-    fence_async_smem();
-    __syncthreads();
-    PHASE(7)
-
-    // ---- MMA 2: U_off = T~_off V, W = T^ K --------------------------------
-    if (tid == 0) {
-      tc_fence_after();
+      // MMA 2: U_off = T~_off V -> TM_VN, W = T^ K -> TM_W
+      if (!(ok = wait_bar(RDY_T, par))) break;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_TB + ks * 2048, 8192, 1024),
@@ -543,133 +712,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_W, sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024),
                     sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_tv, ks > 0);
-      mma_commit(bar_mma);
-    }
-    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
-    PHASE(8)
-    tc_fence_after();
-
-    // ---- W -> bf16 K-major tile; thread rows r_lo, r_lo+8, columns 32 cq + .. --
-    // (column group jg of this warp's 32 columns is chunk (cq&1)*4 + jg of block cq/2)
-    {
-      float w[16];
-      tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, w);
-      tmem_wait_ld();
-      reg_fence(w);
-      const uint32_t tile = sb + OFF_AF + (cq >> 1) * 8192;
-#pragma unroll
-      for (int jg = 0; jg < 4; ++jg) {
-        const int ch = (cq & 1) * 4 + jg;
-        sts32(tile + sw128_off(r_lo, ch) + 4 * tq, pack_bf16x2(w[4 * jg], w[4 * jg + 1]));
-        sts32(tile + sw128_off(r_lo + 8, ch) + 4 * tq, pack_bf16x2(w[4 * jg + 2], w[4 * jg + 3]));
-      }
-      if (dbg) {
-        for (int jg = 0; jg < 4; ++jg)
-          for (int e = 0; e < 2; ++e) {
-            const int col = 32 * cq + 8 * jg + 2 * tq + e;
-            p.debug[DBG_W + r_lo * 128 + col] = w[4 * jg + e];
-            p.debug[DBG_W + (r_lo + 8) * 128 + col] = w[4 * jg + 2 + e];
-          }
-        float u[16];
-        tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, u);
-        tmem_wait_ld();
-        reg_fence(u);
-        for (int jg = 0; jg < 4; ++jg)
-          for (int rr = 0; rr < 2; ++rr) {
-            const int row = r_lo + 8 * rr;
-            const uint32_t vw =
-                lds32(vsm + (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq);
-            const int col = 32 * cq + 8 * jg + 2 * tq;
-            p.debug[DBG_U + row * 128 + col] = fmaf(bet[row], bf16_lo(vw), u[4 * jg + 2 * rr]);
-            p.debug[DBG_U + row * 128 + col + 1] = fmaf(bet[row], bf16_hi(vw), u[4 * jg + 2 * rr + 1]);
-          }
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    PHASE(9)
-
-    // ---- MMA 3: Vn_part = U_off - W S (accumulate on U_off), QS = Q S ------
-    if (tid == 0) {
-      tc_fence_after();
+      mma_commit(&bars[BAR_M2]);
+      // MMA 3: Vn_part = U_off - W S (accumulate on U_off)
+      if (!(ok = wait_bar(RDY_W, par))) break;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_AF + kb * 8192 + kin, 16, 1024),
                     sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_vn, 1);
       }
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
-        mma_bf16_ss(tmem + TM_W, sdesc_sw128(kq + kb * 16384 + 8192 + kin, 16, 1024),
-                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_qs, ks > 0);
-      }
-      mma_commit(bar_mma);
-    }
-    if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap MMA 3
-      compute_gates(c + 1);
-      if (c + 2 < nchunks) prefetch_gates(c + 2);
-    }
-    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
-    PHASE(10)
-    tc_fence_after();
-
-    // ---- Vn = beta V + Vn_part -> bf16 (B of P Vn);
-    //      Vd = e^{g63 - g_t} Vn -> hi/lo bf16 (A of the state update) --------
-    {
-      float v[16];
-      tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, v);
-      tmem_wait_ld();
-      reg_fence(v);
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int row = r_lo + 8 * rr;
-        const bool valid = row < L;
-        const float dec = valid ? ex2_ftz(gam[63] - gam[row]) : 0.f;
-        const float bt = bet[row];
-#pragma unroll
-        for (int jg = 0; jg < 4; ++jg) {
-          const uint32_t off = (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq;
-          const uint32_t vw = lds32(vsm + off);
-          const float x0 = valid ? fmaf(bt, bf16_lo(vw), v[4 * jg + 2 * rr]) : 0.f;
-          const float x1 = valid ? fmaf(bt, bf16_hi(vw), v[4 * jg + 2 * rr + 1]) : 0.f;
-          const float d0 = x0 * dec, d1 = x1 * dec;
-          const float h0 = __bfloat162float(__float2bfloat16_rn(d0));
-          const float h1 = __bfloat162float(__float2bfloat16_rn(d1));
-          sts32(sb + OFF_VN + off, pack_bf16x2(x0, x1));
-          sts32(sb + OFF_VH + off, pack_bf16x2(h0, h1));
-          sts32(sb + OFF_VL + off, pack_bf16x2(d0 - h0, d1 - h1));
-          if (dbg) {
-            const int col = 32 * cq + 8 * jg + 2 * tq;
-            p.debug[DBG_VN + row * 128 + col] = x0;
-            p.debug[DBG_VN + row * 128 + col + 1] = x1;
-          }
-        }
-      }
-      if (dbg) {
-        tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, v);
-        tmem_wait_ld();
-        reg_fence(v);
-        for (int jg = 0; jg < 4; ++jg)
-          for (int rr = 0; rr < 2; ++rr)
-            for (int e = 0; e < 2; ++e)
-              p.debug[DBG_QS + (r_lo + 8 * rr) * 128 + 32 * cq + 8 * jg + 2 * tq + e] =
-                  v[4 * jg + 2 * rr + e];
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    PHASE(11)
-
-    // ---- MMA 4: PV = P Vn (into the Vn columns); St += Vd_hi^T K + Vd_lo^T K --
-    if (tid == 0) {
-      tc_fence_after();
+      mma_commit(&bars[BAR_M3]);
+      // [K;Q]K^T of the next chunk runs while the compute warps drain Vn (its
+      // TMEM columns held W, which the compute warps have already drained)
+      if (c + 1 < nchunks && !(ok = mma1(c + 1))) break;
+      // MMA 4: PV = P Vn -> TM_VN; St += Vd_hi^T K + Vd_lo^T K
+      if (!(ok = wait_bar(RDY_V, par))) break;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_P + ks * 32, 16, 1024),
                     sdesc_sw128(sb + OFF_VN + ks * 2048, 8192, 1024), idesc_pv, ks > 0);
+      mma_commit(&bars[BAR_PV]);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VH + ks * 2048, 8192, 1024),
@@ -678,74 +740,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VL + ks * 2048, 8192, 1024),
                     sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_st, 1);
-      mma_commit(bar_mma);
-    }
-    if (!wait_all(bar_mma, mma_phase)) { aborted = true; break; }
-    PHASE(12)
-    tc_fence_after();
-
-    // ---- output rows: O = scale (e^{gamma_t} QS + PV) ------------------------
-    {
-      float qs[16], pv[16];
-      tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, qs);
-      tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, pv);
-      tmem_wait_ld();
-      reg_fence(qs);
-      reg_fence(pv);
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int row = r_lo + 8 * rr;
-        if (row < L) {
-          const float eg = p.scale * ex2_ftz(gam[row]);
-          uint32_t* orow = reinterpret_cast<uint32_t*>(p.out + ((t0 + row) * p.Hv + h) * kHead +
-                                                       32 * cq + 2 * tq);
-#pragma unroll
-          for (int jg = 0; jg < 4; ++jg) {
-            const float o0 = fmaf(eg, qs[4 * jg + 2 * rr], p.scale * pv[4 * jg + 2 * rr]);
-            const float o1 = fmaf(eg, qs[4 * jg + 2 * rr + 1], p.scale * pv[4 * jg + 2 * rr + 1]);
-            orow[4 * jg] = pack_bf16x2(o0, o1);
-          }
-        }
-        if (dbg)
-          for (int jg = 0; jg < 4; ++jg)
-            for (int e = 0; e < 2; ++e)
-              p.debug[DBG_PV + row * 128 + 32 * cq + 8 * jg + 2 * tq + e] = pv[4 * jg + 2 * rr + e];
-      }
-      if (dbg) {
-        float v[32];
-        tmem_ld32(tq_st, v);
-        tmem_wait_ld();
-        reg_fence(v);
-        for (int i = 0; i < 32; ++i) p.debug[DBG_ST + rowv * 128 + 32 * cq + i] = v[i];
+      mma_commit(&bars[BAR_ST]);
+      // refill this chunk's stage once the state update has read K
+      if (c + 2 < nchunks) {
+        if (!(ok = wait_bar(BAR_ST, par))) break;
+        issue_loads(c + 2);
       }
     }
-    PHASE(13)
+    // drain the tensor pipe and any loads still in flight before the CTA exits
+    mma_commit(&bars[BAR_END]);
+    if (!mbar_wait(&bars[BAR_END], 0, kTimeoutNs)) ok = false;
+    for (int cc = tma_done; cc < tma_issued; ++cc)
+      if (!mbar_wait(&bars[BAR_TMA0 + (cc & 1)], static_cast<uint32_t>((cc >> 1) & 1), kTimeoutNs))
+        ok = false;
+    failed = !ok;
   }
-  if constexpr (DEBUG) {
-    if (dbg_cta && tid == 0)
-      for (int i = 0; i < 16; ++i) p.debug[DBG_CLK + i] = static_cast<float>(clk_acc[i]);
-  }
-#undef PHASE
-
-  // ---- final state -> new_state (row rowv, this warp's 32 columns) --------------
-  if (!aborted) {
-    tc_fence_after();
-    float* dst = ns_rows + rowv * kHead + 32 * cq;
-    float v[32];
-    tmem_ld32(tq_st, v);
-    tmem_wait_ld();
-    reg_fence(v);
-#pragma unroll
-    for (int q4 = 0; q4 < 8; ++q4)
-      st_stream_f4(dst + q4 * 4, make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
-  } else {
-    if (tid == 0) atomicOr(&g_gdn_status, kStatusPrefillTimeout);
-    // let in-flight tensor-core work drain (bounded) before TMEM is released
-    if (tid == 0) {
-      mma_commit(bar_mma);
-      mbar_wait(bar_mma, mma_phase, kTimeoutNs);
-    }
-  }
+  if (failed) atomicOr(&g_gdn_status, kStatusPrefillTimeout);
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

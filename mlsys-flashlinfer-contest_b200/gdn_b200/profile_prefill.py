@@ -19,9 +19,10 @@ from . import _native as N
 from . import workloads as W
 
 # order of the DBG_CLK slots written by the kernel
-PHASES = ["chunk top + TMA issue", "gates read", "state pass", "wait TMA", "MMA1 [K;Q]K^T",
-          "A/P sync", "inverse", "T tiles", "MMA2 U,W", "W drain", "MMA3 WS,QS (+next gates)",
-          "Vn drain", "MMA4 PV,state", "O epilogue", "A/P TMEM load", "A/P compute"]
+PHASES = ["wait state update (prev chunk)", "gates read", "state pass + signal", "wait MMA1",
+          "A/P TMEM load", "A/P compute", "A/P sync", "inverse", "T tiles + signal", "wait MMA2",
+          "W drain + signal", "next gates + wait MMA3", "Vn drain + signal", "wait PV",
+          "O epilogue", "(unused)"]
 DEBUG_TAIL = 16  # DBG_CLK is the last 16 floats of the dump
 
 
