@@ -32,6 +32,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
@@ -60,13 +61,24 @@ constexpr uint32_t OFF_ST = OFF_V + 2 * kVStage;   // bf16 S: [kb 2][v 128][128 
 constexpr uint32_t OFF_P = OFF_ST + 32768;         // P: [t 64][128 B] (K-major A)
 constexpr uint32_t OFF_TB = OFF_P + 8192;          // T diag(beta): [s 64][t 128 B] (MN-major A)
 constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T diag(beta e^gamma)
+constexpr uint32_t OFF_O = OFF_TB;                 // output tile [cb 2][t 64][128 B] (TMA store source),
+                                                   // between MMA 2 and the next chunk's T tiles
 constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A^T [64][72]; later W [kb 2][t 64][128 B]
 constexpr uint32_t OFF_VN = OFF_AF + 17408;        // Vn bf16 [vb 2][t 64][128 B] (MN-major B);
                                                    // during the inverse: fp32 T^T [64][68] (spills into VH)
 constexpr uint32_t OFF_VH = OFF_VN + 16384;        // Vd hi (MN-major A)
 constexpr uint32_t OFF_VL = OFF_VH + 16384;        // Vd lo; during the inverse: fp32 (A21 T11)^T [32][36]
-constexpr uint32_t OFF_MISC = OFF_VL + 16384;      // gamma[64], beta[64], barriers, tmem slot
-constexpr uint32_t kSmemBytes = OFF_MISC + 2048 + 1024;  // + slack for the 1024 alignment
+constexpr uint32_t OFF_MISC = OFF_VL + 16384;      // per-token gate tables, barriers, tmem slot
+// Per-token tables of one chunk (floats), double-buffered by chunk parity.
+constexpr int G_GAM = 0;     // gamma_t * log2(e) (cumulative log-decay)
+constexpr int G_BET = 64;    // beta_t (0 past the end of the sequence)
+constexpr int G_COLF = 128;  // 2^(gamma_{16 floor(t/16)} - gamma_t): column factor of e^{gamma_i - gamma_j}
+constexpr int G_DEC = 192;   // 2^(gamma_63 - gamma_t) for valid tokens, else 0
+constexpr int G_EG = 256;    // scale * 2^gamma_t
+constexpr int G_BE = 320;    // beta_t * 2^gamma_t
+constexpr int kGateFloats = 384;
+constexpr uint32_t kMiscBarOff = 2 * kGateFloats * 4;  // barriers after both table buffers
+constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBarOff + 256 + 1024;  // + slack for the 1024 alignment
 constexpr int kAtPitch = 72;   // fp32 row pitch of A^T (72 = 8 mod 32: conflict-free tf32 A fragments)
 constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict-free B fragments)
 
@@ -97,6 +109,7 @@ struct ChunkParams {
   float* new_state;
   float* debug;  // optional dump of one chunk's intermediates
   float scale;
+  int tma_out;   // output rows of full chunks go through a TMA store (out is 16-byte aligned)
   int64_t T, N;
   int Hq, Hv;
   int dbg_seq, dbg_head, dbg_chunk;
@@ -106,32 +119,34 @@ struct ChunkParams {
 constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_T = DBG_P + 4096,
               DBG_U = DBG_T + 4096, DBG_W = DBG_U + 8192, DBG_VN = DBG_W + 8192,
               DBG_QS = DBG_VN + 8192, DBG_PV = DBG_QS + 8192, DBG_ST = DBG_PV + 8192,
-              DBG_CLK = DBG_ST + 16384, DBG_SIZE = DBG_CLK + 16;
+              DBG_CLK = DBG_ST + 16384, DBG_MCLK = DBG_CLK + 32, DBG_SIZE = DBG_MCLK + 16;
 // DBG_CLK: SM cycles thread 0 of the debug CTA spent in each phase, summed over
-// all chunks of its sequence (phases: see the PHASE() marks in the chunk loop).
+// all chunks of its sequence (phases: see the PHASE() marks in the chunk loop);
+// DBG_MCLK: the same for the issue thread (MPHASE() marks).
 
 template <bool DEBUG>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                                const __grid_constant__ CUtensorMap tm_k,
-                               const __grid_constant__ CUtensorMap tm_v, const ChunkParams p) {
+                               const __grid_constant__ CUtensorMap tm_v,
+                               const __grid_constant__ CUtensorMap tm_o, const ChunkParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Align by offsetting the __shared__ array itself (not through an integer
   // cast), so every derived pointer stays in the shared state space and its
   // accesses compile to ld/st.shared rather than generic loads and stores.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sb = smem_u32(smem);
-  // gamma * log2(e) and beta per token, double-buffered by chunk parity: the
-  // gates of chunk c+1 are computed while chunk c's tensor-core work runs.
-  float* gates_buf = reinterpret_cast<float*>(smem + OFF_MISC);  // [2][gamma 64 | beta 64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_MISC + 1024);
+  // per-token gate tables (G_*), double-buffered by chunk parity: the tables
+  // of chunk c+1 are computed while chunk c's tensor-core work runs.
+  float* gates_buf = reinterpret_cast<float*>(smem + OFF_MISC);  // [2][kGateFloats]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_MISC + kMiscBarOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   // fp32 scratch of the inverse (A^T 18 KiB from OFF_AF into the Vn tile, T^T
   // after it into the Vd_hi tile, products in the Vd_lo tile; all free then)
   float* At = reinterpret_cast<float*>(smem + OFF_AF);   // A column-major: At[k][i] = A[i][k]
   float* Tcm = reinterpret_cast<float*>(smem + OFF_AF + 64 * kAtPitch * 4);  // Tcm[j][i] = T[i][j]
   float* Mcm = reinterpret_cast<float*>(smem + OFF_VL);  // (A21 T11) column-major, pitch 36
-  float* Xcm = Mcm + 32 * 36;                            // 2 x [16][17] level-1 products
+  float* Xcm = Mcm + 32 * 36;                            // 4 x [8][20] level-1 products
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3;  // TMEM lane quarter this warp may access
@@ -161,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
+    if (p.tma_out) prefetch_tmap(&tm_o);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -175,11 +191,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kComputeWarps) {
     // ======================= compute warps =================================
     const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
-    long long clk_acc[16];
+    long long clk_acc[20];
     long long clk_last = 0;
     if constexpr (DEBUG) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) clk_acc[i] = 0;
+      for (int i = 0; i < 20; ++i) clk_acc[i] = 0;
       clk_last = clock64();
     }
 #define PHASE(k)                              \
@@ -245,11 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
       const int Lc = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0c));
       float lg[2], bt[2];
+      bool valid[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const bool valid = 2 * lane + e < Lc;
-        lg[e] = valid ? neg_exp_A * softplus_t20_fast(ga_raw[e] + dt_bias_h) : 0.f;
-        bt[e] = valid ? sigmoid_fast(gb_raw[e]) : 0.f;
+        valid[e] = 2 * lane + e < Lc;
+        lg[e] = valid[e] ? neg_exp_A * softplus_t20_fast(ga_raw[e] + dt_bias_h) : 0.f;
+        bt[e] = valid[e] ? sigmoid_fast(gb_raw[e]) : 0.f;
       }
       const float pair = lg[0] + lg[1];
       float incl = pair;
@@ -258,11 +275,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float y = __shfl_up_sync(0xffffffffu, incl, d);
         if (lane >= d) incl += y;
       }
-      float* gb = gates_buf + (cc & 1) * 128;
-      gb[2 * lane] = (incl - pair + lg[0]) * kLog2e;
-      gb[2 * lane + 1] = incl * kLog2e;
-      gb[64 + 2 * lane] = bt[0];
-      gb[64 + 2 * lane + 1] = bt[1];
+      const float gt[2] = {(incl - pair + lg[0]) * kLog2e, incl * kLog2e};
+      const float g63 = __shfl_sync(0xffffffffu, gt[1], 31);
+      const float gref = __shfl_sync(0xffffffffu, gt[0], lane & ~7);  // token 16 floor(t/16)
+      float* gb = gates_buf + (cc & 1) * kGateFloats;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = 2 * lane + e;
+        const float eg = ex2_ftz(gt[e]);
+        gb[G_GAM + t] = gt[e];
+        gb[G_BET + t] = bt[e];
+        gb[G_COLF + t] = ex2_ftz(gref - gt[e]);
+        gb[G_DEC + t] = valid[e] ? ex2_ftz(g63 - gt[e]) : 0.f;
+        gb[G_EG + t] = p.scale * eg;
+        gb[G_BE + t] = bt[e] * eg;
+      }
     };
     auto dump_state = [&]() {  // debug: St after the state update of the debug chunk
       float v[32];
@@ -291,11 +318,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // is final.  The barrier also publishes this chunk's gates (warp 1).
       if (c > 0) wait_mma(BAR_ST, par ^ 1u);
       if (named_any(kComputeBar, kComputeThreads, failed)) { aborted = true; break; }
+      if (c > 0 && p.tma_out && tid == 0) {  // output tile of chunk c-1 (a full chunk)
+        tma_store_3d(&tm_o, smem + OFF_O, 0, h, static_cast<int>(t0 - kChunk));
+        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, static_cast<int>(t0 - kChunk));
+        bulk_commit();
+      }
       if (dbg_cta && c - 1 == p.dbg_chunk) dump_state();
       PHASE(0)
 
-      const float* gam = gates_buf + stage * 128;
-      const float* bet = gam + 64;
+      const float* gam = gates_buf + stage * kGateFloats + G_GAM;
+      const float* bet = gam + G_BET;
       if (dbg && tid < 64) {
         p.debug[DBG_GAM + tid] = gam[tid] / kLog2e;
         p.debug[DBG_BET + tid] = bet[tid];
@@ -334,20 +366,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(v);
         PHASE(4)
+        // e^{gamma_i - gamma_j} = rf_i * colf_j with the block's first column as
+        // reference (one ex2 per row instead of one per element), unless the
+        // decay across the 16-column block is too steep for the factors' range.
+        const int r0 = 16 * cq;
+        const bool factor = gam[r0] - gam[r0 + 15] <= 64.f;  // CTA-uniform per block
+        const float rf = ex2_ftz(gi - gam[r0]);               // <= 1 wherever unmasked
+        float ef[16];
+        if (factor) {
+          const float4* cf = reinterpret_cast<const float4*>(gam + G_COLF + r0);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 x = cf[q4];
+            ef[4 * q4] = rf * x.x;
+            ef[4 * q4 + 1] = rf * x.y;
+            ef[4 * q4 + 2] = rf * x.z;
+            ef[4 * q4 + 3] = rf * x.w;
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) ef[jj] = ex2_ftz(gi - gam[r0 + jj]);
+        }
         if (quarter < 2) {
           const float bi = bet[i];
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
-            const int j = 16 * cq + jj;
-            const float aij = (j < i) ? bi * v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
+            const int j = r0 + jj;
+            const float aij = (j < i) ? bi * v[jj] * ef[jj] : 0.f;
             At[j * kAtPitch + i] = aij;
             if (dbg) p.debug[DBG_A + i * 64 + j] = aij;
           }
         } else {
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
-            const int j = 16 * cq + jj;
-            v[jj] = (j <= i) ? v[jj] * ex2_ftz(gi - gam[j]) : 0.f;
+            const int j = r0 + jj;
+            v[jj] = (j <= i) ? v[jj] * ef[jj] : 0.f;
           }
 #pragma unroll
           for (int c2 = 0; c2 < 2; ++c2)
@@ -364,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- T = (I + A)^-1, fp32, blocks of 16:
       //      level 0: the four diagonal blocks by right-looking elimination;
-      //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22;
+      //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22 (mma.sync);
       //      level 2: [T20 T21; T30 T31] = -T22' (A21' T11'), primes = 32x32 halves.
       if (tid < 64) {
         const int b = tid >> 4, j = tid & 15, b0 = 16 * b;
@@ -393,36 +446,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(tcol + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
       named_sync(kComputeBar, kComputeThreads);
-      if (tid < 256) {  // level 1, step 1: X = A_IJ T_JJ, (I, J) = (1, 0) for tid < 128, else (3, 2)
-        const int pr = tid >> 7, u = tid & 127;
+      PHASE(15)
+      // level 1 on the tensor cores (mma.sync m16n8k8, tf32): warp w < 4 owns
+      // pair pr = w/2 ((I, J) = (1, 0) or (3, 2)) and 8-column tile nt = w%2 of
+      // T_IJ: X = A_IJ T_JJ[:, tile], then T_IJ[:, tile] = -T_II X.  X goes
+      // through warp-private smem for the fragment layout (__syncwarp only).
+      if (warp < 4) {
+        const int pr = warp >> 1, nt = warp & 1;
         const int J0 = 32 * pr, I0 = J0 + 16;
-        const int j = u & 15, r0 = (u >> 4) * 2;
-        float x0 = 0.f, x1 = 0.f;
+        float* xw = Xcm + warp * 160;  // X column-major: X[r][j] at xw[j * 20 + r]
+        float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+        auto l1a_step = [&](int k0) {
+          const float* ar = At + (J0 + k0 + tq) * kAtPitch + I0 + g;           // A[I0+g][J0+k0+t]
+          const float* br = Tcm + (J0 + 8 * nt + g) * kTcPitch + J0 + k0 + tq;  // T[J0+k0+t][J0+8nt+g]
+          mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
+                          to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+        };
+        if (nt == 0) l1a_step(0);  // T_JJ[k][n] = 0 for k < n: tile 1 needs k >= 8 only
+        l1a_step(8);
+        xw[(2 * tq) * 20 + g] = cacc[0];
+        xw[(2 * tq + 1) * 20 + g] = cacc[1];
+        xw[(2 * tq) * 20 + g + 8] = cacc[2];
+        xw[(2 * tq + 1) * 20 + g + 8] = cacc[3];
+        __syncwarp();
+        float dacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float tkj = Tcm[(J0 + j) * kTcPitch + J0 + k];   // T[J0+k][J0+j]
-          x0 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0], tkj, x0);     // A[I0+r0][J0+k]
-          x1 = fmaf(At[(J0 + k) * kAtPitch + I0 + r0 + 1], tkj, x1);
+        for (int k0 = 0; k0 < 16; k0 += 8) {
+          const float* ar = Tcm + (I0 + k0 + tq) * kTcPitch + I0 + g;  // T[I0+g][I0+k0+t]
+          const float* br = xw + g * 20 + k0 + tq;                     // X[k0+t][g]
+          mma_tf32_16x8x8(dacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kTcPitch]),
+                          to_tf32(ar[4 * kTcPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
         }
-        Xcm[pr * 272 + j * 17 + r0] = x0;
-        Xcm[pr * 272 + j * 17 + r0 + 1] = x1;
+        float* tc = Tcm + (J0 + 8 * nt + 2 * tq) * kTcPitch + I0 + g;  // T[I0+r][J0+8nt+j] at Tcm[col][row]
+        tc[0] = -dacc[0];
+        tc[kTcPitch] = -dacc[1];
+        tc[8] = -dacc[2];
+        tc[kTcPitch + 8] = -dacc[3];
       }
       named_sync(kComputeBar, kComputeThreads);
-      if (tid < 256) {  // level 1, step 2: T_IJ = -T_II X
-        const int pr = tid >> 7, u = tid & 127;
-        const int J0 = 32 * pr, I0 = J0 + 16;
-        const int j = u & 15, r0 = (u >> 4) * 2;
-        float t0_ = 0.f, t1_ = 0.f;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float xkj = Xcm[pr * 272 + j * 17 + k];
-          t0_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0], xkj, t0_);   // T[I0+r0][I0+k]
-          t1_ = fmaf(Tcm[(I0 + k) * kTcPitch + I0 + r0 + 1], xkj, t1_);
-        }
-        Tcm[(J0 + j) * kTcPitch + I0 + r0] = -t0_;
-        Tcm[(J0 + j) * kTcPitch + I0 + r0 + 1] = -t1_;
-      }
-      named_sync(kComputeBar, kComputeThreads);
+      PHASE(16)
       // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
       // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after):
       // warp w < 8 computes the 16x8 output tile (row tile w/4, column tile w%4).
@@ -444,6 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mc[36 + 8] = cacc[3];
       }
       named_sync(kComputeBar, kComputeThreads);
+      PHASE(18)
       if (warp < 8) {  // step 2: T21' = -T22' M
         const int rt = warp >> 2, ct = warp & 3, t4 = tq;
         float cacc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -461,6 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc[8] = -cacc[2];
         tc[kTcPitch + 8] = -cacc[3];
       }
+      if (tid == 0) bulk_wait_read_all();  // output tile read out before the T tiles reuse it
       named_sync(kComputeBar, kComputeThreads);
       PHASE(7)
       {
@@ -472,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = tid & 63;
         const bool hat = (tid >> 6) & 1;
         const int part = tid >> 7;  // 16-row quarter of the tile row (2 chunks)
-        const float sc = hat ? bet[j] * ex2_ftz(gam[j]) : bet[j];
+        const float sc = hat ? gam[G_BE + j] : bet[j];
         const float* trow = Tcm + j * kTcPitch;
         const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
 #pragma unroll
@@ -551,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int rr = 0; rr < 2; ++rr) {
           const int row = r_lo + 8 * rr;
           const bool valid = row < L;
-          const float dec = valid ? ex2_ftz(gam[63] - gam[row]) : 0.f;
+          const float dec = gam[G_DEC + row];  // 0 past the end of the sequence
           const float bt = bet[row];
 #pragma unroll
           for (int jg = 0; jg < 4; ++jg) {
@@ -596,33 +660,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(qs);
         reg_fence(pv);
+        // full chunks: bf16 rows into the swizzled output tile, stored by TMA
+        // at the top of the next chunk; a partial last chunk stores directly.
+        const bool via_tma = p.tma_out && L == kChunk;
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
           const int row = r_lo + 8 * rr;
-          if (row < L) {
-            const float eg = p.scale * ex2_ftz(gam[row]);
+          const float eg = gam[G_EG + row];
+          uint32_t w[4];
+#pragma unroll
+          for (int jg = 0; jg < 4; ++jg) {
+            const float o0 = fmaf(eg, qs[4 * jg + 2 * rr], p.scale * pv[4 * jg + 2 * rr]);
+            const float o1 = fmaf(eg, qs[4 * jg + 2 * rr + 1], p.scale * pv[4 * jg + 2 * rr + 1]);
+            w[jg] = pack_bf16x2(o0, o1);
+          }
+          if (via_tma) {
+#pragma unroll
+            for (int jg = 0; jg < 4; ++jg)
+              sts32(sb + OFF_O + (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq, w[jg]);
+          } else if (row < L) {
             uint32_t* orow = reinterpret_cast<uint32_t*>(p.out + ((t0 + row) * p.Hv + h) * kHead +
                                                          32 * cq + 2 * tq);
 #pragma unroll
-            for (int jg = 0; jg < 4; ++jg) {
-              const float o0 = fmaf(eg, qs[4 * jg + 2 * rr], p.scale * pv[4 * jg + 2 * rr]);
-              const float o1 = fmaf(eg, qs[4 * jg + 2 * rr + 1], p.scale * pv[4 * jg + 2 * rr + 1]);
-              orow[4 * jg] = pack_bf16x2(o0, o1);
-            }
+            for (int jg = 0; jg < 4; ++jg) orow[4 * jg] = w[jg];
           }
           if (dbg)
             for (int jg = 0; jg < 4; ++jg)
               for (int e = 0; e < 2; ++e)
                 p.debug[DBG_PV + row * 128 + 32 * cq + 8 * jg + 2 * tq + e] = pv[4 * jg + 2 * rr + e];
         }
+        if (via_tma) fence_async_smem();
       }
       PHASE(14)
     }
     if constexpr (DEBUG) {
       if (dbg_cta && tid == 0)
-        for (int i = 0; i < 16; ++i) p.debug[DBG_CLK + i] = static_cast<float>(clk_acc[i]);
+        for (int i = 0; i < 20; ++i) p.debug[DBG_CLK + i] = static_cast<float>(clk_acc[i]);
     }
 #undef PHASE
+
+    if (!aborted && p.tma_out) {  // output tile of the last chunk, if it is full
+      const int64_t tl = bos + static_cast<int64_t>(nchunks - 1) * kChunk;
+      if (eos - tl == kChunk) {
+        named_sync(kComputeBar, kComputeThreads);
+        if (tid == 0) {
+          tma_store_3d(&tm_o, smem + OFF_O, 0, h, static_cast<int>(tl));
+          tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, static_cast<int>(tl));
+          bulk_commit();
+        }
+      }
+    }
+    if (tid == 0) bulk_wait_all();  // stores complete before the CTA's shared memory goes away
 
     // ---- final state -> new_state (row rowv, this warp's 32 columns) --------
     if (!aborted) {
@@ -649,6 +737,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t idesc_pv = idesc_bf16(64, 128, false, true);
     const uint32_t idesc_st = idesc_bf16(128, 128, true, true);
 
+    const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
+    long long mclk[16];
+    long long mlast = 0;
+    if constexpr (DEBUG) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mclk[i] = 0;
+      mlast = clock64();
+    }
+#define MPHASE(k)                             \
+  if constexpr (DEBUG) {                      \
+    const long long now_ = clock64();         \
+    mclk[k] += now_ - mlast;                  \
+    mlast = now_;                             \
+  }
     int tma_issued = 0, tma_done = 0;  // chunks whose loads were issued / have landed
     auto issue_loads = [&](int cc) {
       const int s = cc & 1;
@@ -675,6 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = cc & 1;
       if (!wait_bar(BAR_TMA0 + s, static_cast<uint32_t>((cc >> 1) & 1))) return false;
       tma_done = cc + 1;
+      MPHASE(6)
       const uint32_t kq = sb + OFF_KQ + s * kKQStage;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
@@ -683,6 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     idesc_d1, ks > 0);
       }
       mma_commit(&bars[BAR_M1]);
+      MPHASE(7)
       return true;
     };
 
@@ -695,15 +799,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t vsm = sb + OFF_V + (c & 1) * kVStage;
 
       // Q S (the S tile of this chunk) -> TM_QS
+      MPHASE(12)
       if (!(ok = wait_bar(RDY_S, par))) break;
+      MPHASE(0)
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
         mma_bf16_ss(tmem + TM_QS, sdesc_sw128(kq + kb * 16384 + 8192 + kin, 16, 1024),
                     sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_qs, ks > 0);
       }
+      MPHASE(1)
       // MMA 2: U_off = T~_off V -> TM_VN, W = T^ K -> TM_W
       if (!(ok = wait_bar(RDY_T, par))) break;
+      MPHASE(2)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_TB + ks * 2048, 8192, 1024),
@@ -713,8 +821,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_bf16_ss(tmem + TM_W, sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024),
                     sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_tv, ks > 0);
       mma_commit(&bars[BAR_M2]);
+      MPHASE(3)
       // MMA 3: Vn_part = U_off - W S (accumulate on U_off)
       if (!(ok = wait_bar(RDY_W, par))) break;
+      MPHASE(4)
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
@@ -722,16 +832,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_vn, 1);
       }
       mma_commit(&bars[BAR_M3]);
+      MPHASE(5)
       // [K;Q]K^T of the next chunk runs while the compute warps drain Vn (its
       // TMEM columns held W, which the compute warps have already drained)
       if (c + 1 < nchunks && !(ok = mma1(c + 1))) break;
       // MMA 4: PV = P Vn -> TM_VN; St += Vd_hi^T K + Vd_lo^T K
       if (!(ok = wait_bar(RDY_V, par))) break;
+      MPHASE(8)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_P + ks * 32, 16, 1024),
                     sdesc_sw128(sb + OFF_VN + ks * 2048, 8192, 1024), idesc_pv, ks > 0);
       mma_commit(&bars[BAR_PV]);
+      MPHASE(9)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VH + ks * 2048, 8192, 1024),
@@ -741,12 +854,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VL + ks * 2048, 8192, 1024),
                     sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_st, 1);
       mma_commit(&bars[BAR_ST]);
+      MPHASE(10)
       // refill this chunk's stage once the state update has read K
       if (c + 2 < nchunks) {
         if (!(ok = wait_bar(BAR_ST, par))) break;
+        MPHASE(11)
         issue_loads(c + 2);
       }
     }
+    if constexpr (DEBUG) {
+      if (dbg_cta)
+        for (int i = 0; i < 16; ++i) p.debug[DBG_MCLK + i] = static_cast<float>(mclk[i]);
+    }
+#undef MPHASE
     // drain the tensor pipe and any loads still in flight before the CTA exits
     mma_commit(&bars[BAR_END]);
     if (!mbar_wait(&bars[BAR_END], 0, kTimeoutNs)) ok = false;
@@ -819,11 +939,15 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
     return cudaMemsetAsync(a.new_state, 0,
                            static_cast<size_t>(a.N) * a.Hv * kHead * kHead * sizeof(float), s);
   }
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   cudaError_t e;
   if ((e = make_head_map(&mq, a.q, a.Hq, a.T)) != cudaSuccess) return e;
   if ((e = make_head_map(&mk, a.k, a.Hq, a.T)) != cudaSuccess) return e;
   if ((e = make_head_map(&mv, a.v, a.Hv, a.T)) != cudaSuccess) return e;
+  // full-chunk output rows go out by TMA store when the output allows a tensor map
+  const int tma_out = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) ? 1 : 0;
+  memset(&mo, 0, sizeof(mo));
+  if (tma_out && (e = make_head_map(&mo, a.out, a.Hv, a.T)) != cudaSuccess) return e;
   static bool attr_set = false;
   if (!attr_set) {
     e = cudaFuncSetAttribute(gdn_prefill_chunked_kernel<DEBUG>,
@@ -834,12 +958,12 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   ChunkParams p{a.state, a.A_log, a.dt_bias,
                 static_cast<const __nv_bfloat16*>(a.a), static_cast<const __nv_bfloat16*>(a.b),
                 a.cu_seqlens, static_cast<__nv_bfloat16*>(a.out), a.new_state, debug, a.scale,
-                a.T, a.N, static_cast<int>(a.Hq), static_cast<int>(a.Hv), dbg_seq, dbg_head,
+                tma_out, a.T, a.N, static_cast<int>(a.Hq), static_cast<int>(a.Hv), dbg_seq, dbg_head,
                 dbg_chunk};
   const int64_t ctas = a.N * a.Hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
   gdn_prefill_chunked_kernel<DEBUG><<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(
-      mq, mk, mv, p);
+      mq, mk, mv, mo, p);
   return cudaGetLastError();
 }
 

@@ -20,10 +20,15 @@ from . import workloads as W
 
 # order of the DBG_CLK slots written by the kernel
 PHASES = ["wait state update (prev chunk)", "gates read", "state pass + signal", "wait MMA1",
-          "A/P TMEM load", "A/P compute", "A/P sync", "inverse", "T tiles + signal", "wait MMA2",
+          "A/P TMEM load", "A/P compute", "A/P sync", "inverse level 2b", "T tiles + signal", "wait MMA2",
           "W drain + signal", "next gates + wait MMA3", "Vn drain + signal", "wait PV",
-          "O epilogue", "(unused)"]
-DEBUG_TAIL = 16  # DBG_CLK is the last 16 floats of the dump
+          "O epilogue", "inverse level 0", "inverse level 1", "(unused)",
+          "inverse level 2a"]
+# issue thread (warp 16): waits on the compute warps / TMA, and MMA issue
+MMA_PHASES = ["wait S tile", "issue QS", "wait T tiles", "issue MMA2", "wait W tile", "issue WS",
+              "wait next K/Q/V", "issue next MMA1", "wait Vn tiles", "issue PV", "issue state update",
+              "wait state update", "issue TMA", "(unused)", "(unused)", "(unused)"]
+DEBUG_TAIL = 48  # DBG_CLK (32 floats), DBG_MCLK (16): the end of the dump
 
 
 def phase_cycles(L: int, Hq: int, Hv: int, head: int, seed: int = 3):
@@ -43,7 +48,9 @@ def phase_cycles(L: int, Hq: int, Hv: int, head: int, seed: int = 3):
     torch.cuda.synchronize()
     clk = dbg[nf - DEBUG_TAIL:].cpu().tolist()
     nch = (L + 63) // 64
-    return {name: clk[i] / nch for i, name in enumerate(PHASES)}
+    comp = {name: clk[i] / nch for i, name in enumerate(PHASES)}
+    issue = {name: clk[32 + i] / nch for i, name in enumerate(MMA_PHASES)}
+    return comp, issue
 
 
 def main():
@@ -54,15 +61,19 @@ def main():
     ap.add_argument("--head", type=int, default=5)
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args()
-    per = phase_cycles(a.len, a.hq, a.hv, a.head)
-    tot = sum(per.values())
+    comp, issue = phase_cycles(a.len, a.hq, a.hv, a.head)
+    tot = sum(comp.values())
     if a.json:
-        print(json.dumps({"len": a.len, "cycles_per_chunk": per, "total": tot}))
+        print(json.dumps({"len": a.len, "cycles_per_chunk": comp, "issue_thread": issue,
+                          "total": tot}))
         return
     print(f"sequence length {a.len}, Hq={a.hq}, Hv={a.hv}: {tot:.0f} SM cycles per chunk")
-    for name, v in per.items():
-        print(f"  {name:28s} {v:8.0f}  {100 * v / tot:5.1f}%")
-
+    print("compute warps (thread 0):")
+    for name, v in comp.items():
+        print(f"  {name:32s} {v:8.0f}  {100 * v / tot:5.1f}%")
+    print("issue thread (warp 16):")
+    for name, v in issue.items():
+        print(f"  {name:32s} {v:8.0f}  {100 * v / tot:5.1f}%")
 
 if __name__ == "__main__":
     main()

@@ -17,7 +17,7 @@ from gdn_b200 import _native as N, prefill, workloads as W
 pytestmark = pytest.mark.gpu
 
 DBG_NAMES = [("gam", 64), ("bet", 64), ("A", 4096), ("P", 4096), ("T", 4096), ("U", 8192),
-             ("W", 8192), ("Vn", 8192), ("QS", 8192), ("PV", 8192), ("St", 16384), ("clk", 16)]
+             ("W", 8192), ("Vn", 8192), ("QS", 8192), ("PV", 8192), ("St", 16384), ("clk", 32), ("mclk", 16)]
 
 
 def chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
