@@ -12,9 +12,11 @@
 //   G|QK  = [K;Q] K^T                          (tcgen05, M=128: rows 0-63 KK^T, 64-127 QK^T)
 //   A     = strict_tril(beta_t G e^{gamma_t - gamma_s}),  P = tril(QK e^{gamma_t - gamma_s})
 //   T     = (I + A)^-1                         (fp32, CUDA cores, blocks of 16)
-//   U     = beta (.) V + T_off diag(beta) V,  W = T diag(beta e^gamma) K
-//           (tcgen05; the unit diagonal of T is applied exactly in fp32)
-//   Vn    = U - W S,         QS = Q S                            (tcgen05, S as bf16)
+//   KS|QS = [K;Q] S                            (tcgen05, M=128, S as bf16; right after the
+//           state is read, so it overlaps the CUDA-core phases below)
+//   Vn    = U - W S  with  U = beta (.) V + T_off diag(beta) V  and  W S = T^ (K S),
+//           T^ = T diag(beta e^gamma): one tcgen05 group T~ V - T^ (KS) once T is known
+//           (T~ = T_off diag(beta); the unit diagonal is applied exactly in fp32)
 //   O     = scale (e^{gamma_t} QS + P Vn)      (tcgen05 for P Vn)
 //   St   <- e^{gamma_63} St + Vd^T K,  Vd = e^{gamma_63 - gamma_t} Vn split into
 //           bf16 hi + lo (two MMAs) so the state update keeps ~16 mantissa bits.
@@ -24,8 +26,9 @@
 // Warp roles: warps 0-15 do the CUDA-core work (four per TMEM lane quarter,
 // each on 32 of the 128 columns); warp 16 issues every TMA load and tcgen05
 // MMA.  The two sides hand off through mbarriers only, so the tensor pipe runs
-// Q S during the A/P/inverse phases, [K;Q]K^T of the next chunk during the Vn
-// drain and the state update during the output epilogue.
+// [K;Q] S during the A/P phase, [K;Q]K^T of the next chunk during the Vn drain
+// and the state update during the output epilogue.  The only MMAs between the
+// triangular inverse and the next chunk are T~ V - T^ (KS) and P Vn.
 // Math: same chunked algebra as cuda_kkt_inv_uw_v1.cu:1-20 (U, W, g_cu),
 // cuda_h_v2b.cu (state scan) and cuda_o_v1.cu (output); semantics as
 // definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md:62-142.
@@ -49,6 +52,7 @@ constexpr int kComputeWarps = 16;  // four per TMEM lane quarter
 constexpr int kComputeThreads = 32 * kComputeWarps;
 constexpr int kThreads = kComputeThreads + 32;  // + the TMA / MMA issue warp
 constexpr uint32_t kComputeBar = 1;             // named barrier of the compute warps
+constexpr int kStoreTid = 256;  // issues the output TMA stores: warp 8 is idle in the inverse
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait, then give up
 
 // ---- shared memory map (offsets from a 1024-aligned base) -----------------
@@ -57,13 +61,14 @@ constexpr uint32_t kKQStage = 32768;  // [kb 2][row 128: K rows 0-63, Q rows 64-
 constexpr uint32_t kVStage = 16384;   // [vb 2][t 64][128 B]
 constexpr uint32_t OFF_KQ = 0;                     // 2 stages
 constexpr uint32_t OFF_V = OFF_KQ + 2 * kKQStage;  // 2 stages
-constexpr uint32_t OFF_ST = OFF_V + 2 * kVStage;   // bf16 S: [kb 2][v 128][128 B] (K-major B)
-constexpr uint32_t OFF_P = OFF_ST + 32768;         // P: [t 64][128 B] (K-major A)
+constexpr uint32_t OFF_ST = OFF_V + 2 * kVStage;   // bf16 S: [kb 2][v 128][128 B] (K-major B);
+                                                   // once [K;Q] S is done: K S [vb 2][s 64][128 B] (MN-major B)
+constexpr uint32_t OFF_P = OFF_ST + 32768;         // P: [t 64][128 B] (K-major A rows 64-127 of P Vn)
 constexpr uint32_t OFF_TB = OFF_P + 8192;          // T diag(beta): [s 64][t 128 B] (MN-major A)
 constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T diag(beta e^gamma)
 constexpr uint32_t OFF_O = OFF_TB;                 // output tile [cb 2][t 64][128 B] (TMA store source),
-                                                   // between MMA 2 and the next chunk's T tiles
-constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A^T [64][72]; later W [kb 2][t 64][128 B]
+                                                   // between the Vn MMAs and the next chunk's T tiles
+constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A^T [64][72] (spills 1 KiB into VN)
 constexpr uint32_t OFF_VN = OFF_AF + 17408;        // Vn bf16 [vb 2][t 64][128 B] (MN-major B);
                                                    // during the inverse: fp32 T^T [64][68] (spills into VH)
 constexpr uint32_t OFF_VH = OFF_VN + 16384;        // Vd hi (MN-major A)
@@ -84,9 +89,9 @@ constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict
 
 // ---- TMEM columns ----------------------------------------------------------
 constexpr uint32_t TM_ST = 0;     // St [v 128 lanes][k 128 cols]
-constexpr uint32_t TM_VN = 128;   // U -> Vn, then P Vn   (M=64 layout)
-constexpr uint32_t TM_W = 256;    // [K;Q]K^T ([128 lanes][64 cols]), then W (M=64 layout)
-constexpr uint32_t TM_QS = 384;   // Q S                  (M=64 layout)
+constexpr uint32_t TM_KQS = 128;  // [K;Q] S: lanes 0-63 K S, lanes 64-127 Q S (M=128)
+constexpr uint32_t TM_D1 = 256;   // [K;Q] K^T [128 lanes][64 cols]
+constexpr uint32_t TM_VN = 320;   // T~ V - T^ KS -> Vn (M=64 layout); then P Vn in lanes 64-127 (M=128)
 constexpr uint32_t kTmemCols = 512;
 
 constexpr uint32_t kTmaBytes = 2 * kKQStage / 2 + kVStage;  // K 16K + Q 16K + V 16K
@@ -94,8 +99,8 @@ constexpr uint32_t kTmaBytes = 2 * kKQStage / 2 + kVStage;  // K 16K + Q 16K + V
 // mbarriers (OFF_MISC + 1024): TMA stages, tensor pipe -> compute warps (one
 // tcgen05.commit each), compute warps -> issue warp (one arrive per warp).
 enum : int {
-  BAR_TMA0 = 0, BAR_TMA1, BAR_M1, BAR_M2, BAR_M3, BAR_PV, BAR_ST,
-  RDY_S, RDY_T, RDY_W, RDY_V, BAR_END, kNumBars
+  BAR_TMA0 = 0, BAR_TMA1, BAR_M1, BAR_KQS, BAR_M3, BAR_PV, BAR_ST,
+  RDY_S, RDY_T, RDY_V, BAR_END, kNumBars
 };
 
 struct ChunkParams {
@@ -115,14 +120,20 @@ struct ChunkParams {
   int dbg_seq, dbg_head, dbg_chunk;
 };
 
-// Debug dump layout (floats)
+constexpr int kClkSlots = 20;  // phase clock slots per compute warp (debug build)
+// Debug dump layout (floats); the DBG_U block is not written (U is never formed
+// on its own: the kernel computes T~ V - T^ (K S) in one accumulator).
 constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_T = DBG_P + 4096,
-              DBG_U = DBG_T + 4096, DBG_W = DBG_U + 8192, DBG_VN = DBG_W + 8192,
+              DBG_U = DBG_T + 4096, DBG_KS = DBG_U + 8192, DBG_VN = DBG_KS + 8192,
               DBG_QS = DBG_VN + 8192, DBG_PV = DBG_QS + 8192, DBG_ST = DBG_PV + 8192,
-              DBG_CLK = DBG_ST + 16384, DBG_MCLK = DBG_CLK + 32, DBG_SIZE = DBG_MCLK + 16;
-// DBG_CLK: SM cycles thread 0 of the debug CTA spent in each phase, summed over
-// all chunks of its sequence (phases: see the PHASE() marks in the chunk loop);
-// DBG_MCLK: the same for the issue thread (MPHASE() marks).
+              DBG_CLK = DBG_ST + 16384, DBG_MCLK = DBG_CLK + 16 * kClkSlots, DBG_EV = DBG_MCLK + 16,
+              DBG_SIZE = DBG_EV + 96;
+// DBG_CLK: [warp 16][kClkSlots] SM cycles lane 0 of each compute warp of the
+// debug CTA spent in each phase, summed over all chunks of its sequence
+// (phases: the PHASE() marks in the chunk loop); DBG_MCLK: the same for the
+// issue thread (MPHASE() marks).  DBG_EV: SM-clock timestamps (from a common
+// base) of handoff events around the debug chunk: [warp 16][5] for the compute
+// warps, then 8 for the issue thread.
 
 template <bool DEBUG>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -186,16 +197,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const long long t_base = DEBUG ? clock64() : 0;
   bool failed = false;  // this thread gave up on a wait
 
   if (warp < kComputeWarps) {
     // ======================= compute warps =================================
     const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
-    long long clk_acc[20];
+    long long clk_acc[kClkSlots];
     long long clk_last = 0;
     if constexpr (DEBUG) {
 #pragma unroll
-      for (int i = 0; i < 20; ++i) clk_acc[i] = 0;
+      for (int i = 0; i < kClkSlots; ++i) clk_acc[i] = 0;
       clk_last = clock64();
     }
 #define PHASE(k)                              \
@@ -317,8 +329,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // previous chunk's state update done: its operand tiles are free and St
       // is final.  The barrier also publishes this chunk's gates (warp 1).
       if (c > 0) wait_mma(BAR_ST, par ^ 1u);
+      PHASE(17)
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 1 && lane == 0)
+        p.debug[DBG_EV + warp * 5 + 3] = float(clock64() - t_base);
       if (named_any(kComputeBar, kComputeThreads, failed)) { aborted = true; break; }
-      if (c > 0 && p.tma_out && tid == 0) {  // output tile of chunk c-1 (a full chunk)
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 1 && lane == 0)
+        p.debug[DBG_EV + warp * 5 + 4] = float(clock64() - t_base);
+      if (c > 0 && p.tma_out && tid == kStoreTid) {  // output tile of chunk c-1 (a full chunk)
         tma_store_3d(&tm_o, smem + OFF_O, 0, h, static_cast<int>(t0 - kChunk));
         tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, static_cast<int>(t0 - kChunk));
         bulk_commit();
@@ -362,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = rowv & 63;
         const float gi = gam[i];
         float v[16];
-        tmem_ld16(tmem + lane_base + TM_W + 16 * cq, v);
+        tmem_ld16(tmem + lane_base + TM_D1 + 16 * cq, v);
         tmem_wait_ld();
         reg_fence(v);
         PHASE(4)
@@ -419,8 +436,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       //      level 0: the four diagonal blocks by right-looking elimination;
       //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22 (mma.sync);
       //      level 2: [T20 T21; T30 T31] = -T22' (A21' T11'), primes = 32x32 halves.
-      if (tid < 64) {
-        const int b = tid >> 4, j = tid & 15, b0 = 16 * b;
+      if (quarter < 2) {
+        // K S rows (tokens, lanes 0-63 of the [K;Q] S accumulator) -> bf16 K S
+        // tile over the S tile (Q S and K S are both done): the B operand of
+        // T^ (K S).  Runs beside the level-0 inverse (warps 2 and 3).
+        wait_mma(BAR_KQS, par);
+        float v[32];
+        tmem_ld32(tmem + lane_base + TM_KQS + 32 * cq, v);
+        tmem_wait_ld();
+        reg_fence(v);
+        const uint32_t tile = sb + OFF_ST + (cq >> 1) * 8192;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+          sts128(tile + sw128_off(rowv, (cq & 1) * 4 + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
+                 pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
+                 pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
+        if (dbg)
+          for (int i = 0; i < 32; ++i) p.debug[DBG_KS + rowv * 128 + 32 * cq + i] = v[i];
+      } else if (warp == 2 || warp == 3) {
+        const int u = tid - 64;
+        const int b = u >> 4, j = u & 15, b0 = 16 * b;
         float x[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) x[r] = (r == j) ? 1.f : 0.f;
@@ -524,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc[8] = -cacc[2];
         tc[kTcPitch + 8] = -cacc[3];
       }
-      if (tid == 0) bulk_wait_read_all();  // output tile read out before the T tiles reuse it
+      if (tid == kStoreTid) bulk_wait_read_all();  // output tile read out before the T tiles reuse it
       named_sync(kComputeBar, kComputeThreads);
       PHASE(7)
       {
@@ -556,48 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       signal(RDY_T);
       PHASE(8)
-      wait_mma(BAR_M2, par);
-      PHASE(9)
-
-      // ---- W -> bf16 K-major tile; thread rows r_lo, r_lo+8, columns 32 cq + .. --
-      // (column group jg of this warp's 32 columns is chunk (cq&1)*4 + jg of block cq/2)
-      {
-        float w[16];
-        tmem_ld16x256_x4(tmem + lane_base + TM_W + 32 * cq, w);
-        tmem_wait_ld();
-        reg_fence(w);
-        const uint32_t tile = sb + OFF_AF + (cq >> 1) * 8192;
-#pragma unroll
-        for (int jg = 0; jg < 4; ++jg) {
-          const int ch = (cq & 1) * 4 + jg;
-          sts32(tile + sw128_off(r_lo, ch) + 4 * tq, pack_bf16x2(w[4 * jg], w[4 * jg + 1]));
-          sts32(tile + sw128_off(r_lo + 8, ch) + 4 * tq, pack_bf16x2(w[4 * jg + 2], w[4 * jg + 3]));
-        }
-        if (dbg) {
-          for (int jg = 0; jg < 4; ++jg)
-            for (int e = 0; e < 2; ++e) {
-              const int col = 32 * cq + 8 * jg + 2 * tq + e;
-              p.debug[DBG_W + r_lo * 128 + col] = w[4 * jg + e];
-              p.debug[DBG_W + (r_lo + 8) * 128 + col] = w[4 * jg + 2 + e];
-            }
-          float u[16];
-          tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, u);
-          tmem_wait_ld();
-          reg_fence(u);
-          for (int jg = 0; jg < 4; ++jg)
-            for (int rr = 0; rr < 2; ++rr) {
-              const int row = r_lo + 8 * rr;
-              const uint32_t vw =
-                  lds32(vsm + (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq);
-              const int col = 32 * cq + 8 * jg + 2 * tq;
-              p.debug[DBG_U + row * 128 + col] = fmaf(bet[row], bf16_lo(vw), u[4 * jg + 2 * rr]);
-              p.debug[DBG_U + row * 128 + col + 1] = fmaf(bet[row], bf16_hi(vw), u[4 * jg + 2 * rr + 1]);
-            }
-        }
-      }
-      signal(RDY_W);
-      PHASE(10)
-      if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap W S
+      if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap the Vn MMAs
         compute_gates(c + 1);
         if (c + 2 < nchunks) prefetch_gates(c + 2);
       }
@@ -636,66 +630,69 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (dbg) {
-          tmem_ld16x256_x4(tmem + lane_base + TM_QS + 32 * cq, v);
-          tmem_wait_ld();
-          reg_fence(v);
-          for (int jg = 0; jg < 4; ++jg)
-            for (int rr = 0; rr < 2; ++rr)
-              for (int e = 0; e < 2; ++e)
-                p.debug[DBG_QS + (r_lo + 8 * rr) * 128 + 32 * cq + 8 * jg + 2 * tq + e] =
-                    v[4 * jg + 2 * rr + e];
-        }
       }
       signal(RDY_V);
       PHASE(12)
+      if (DEBUG && dbg && lane == 0) p.debug[DBG_EV + warp * 5 + 0] = float(clock64() - t_base);
       wait_mma(BAR_PV, par);
       PHASE(13)
+      if (DEBUG && dbg && lane == 0) p.debug[DBG_EV + warp * 5 + 1] = float(clock64() - t_base);
 
-      // ---- output rows: O = scale (e^{gamma_t} QS + PV) ----------------------
-      {
-        float qs[16], pv[16];
-        tmem_ld16x256_x4(tmem + lane_base + TM_QS + 32 * cq, qs);
-        tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, pv);
-        tmem_wait_ld();
-        reg_fence(qs);
-        reg_fence(pv);
+      // ---- output rows, quarters 2-3 (token t = rowv - 64 of the M=128 Q S and
+      //      P Vn accumulators): O = scale (e^{gamma_t} QS + PV) ---------------
+      if (quarter >= 2) {
+        const int t = rowv - 64;
+        const float eg = gam[G_EG + t];
         // full chunks: bf16 rows into the swizzled output tile, stored by TMA
         // at the top of the next chunk; a partial last chunk stores directly.
         const bool via_tma = p.tma_out && L == kChunk;
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int row = r_lo + 8 * rr;
-          const float eg = gam[G_EG + row];
-          uint32_t w[4];
+        for (int hf = 0; hf < 2; ++hf) {  // 16 of this warp's 32 columns at a time
+          float qs[16], pv[16];
+          tmem_ld16(tmem + lane_base + TM_KQS + 32 * cq + 16 * hf, qs);
+          tmem_ld16(tmem + lane_base + TM_VN + 32 * cq + 16 * hf, pv);
+          tmem_wait_ld();
+          reg_fence(qs);
+          reg_fence(pv);
+          uint32_t w[8];
 #pragma unroll
-          for (int jg = 0; jg < 4; ++jg) {
-            const float o0 = fmaf(eg, qs[4 * jg + 2 * rr], p.scale * pv[4 * jg + 2 * rr]);
-            const float o1 = fmaf(eg, qs[4 * jg + 2 * rr + 1], p.scale * pv[4 * jg + 2 * rr + 1]);
-            w[jg] = pack_bf16x2(o0, o1);
-          }
+          for (int e = 0; e < 8; ++e)
+            w[e] = pack_bf16x2(fmaf(eg, qs[2 * e], p.scale * pv[2 * e]),
+                               fmaf(eg, qs[2 * e + 1], p.scale * pv[2 * e + 1]));
+          const int col = 32 * cq + 16 * hf;  // first of these 16 output columns
           if (via_tma) {
+            const uint32_t base = sb + OFF_O + (cq >> 1) * 8192;
+            const int ch = (cq & 1) * 4 + 2 * hf;
+            sts128(base + sw128_off(t, ch), w[0], w[1], w[2], w[3]);
+            sts128(base + sw128_off(t, ch + 1), w[4], w[5], w[6], w[7]);
+          } else if (t < L) {
+            __nv_bfloat16* orow = p.out + ((t0 + t) * p.Hv + h) * kHead + col;
+            if (p.tma_out) {  // 16-byte aligned output
+              reinterpret_cast<uint4*>(orow)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              reinterpret_cast<uint4*>(orow)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
 #pragma unroll
-            for (int jg = 0; jg < 4; ++jg)
-              sts32(sb + OFF_O + (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq, w[jg]);
-          } else if (row < L) {
-            uint32_t* orow = reinterpret_cast<uint32_t*>(p.out + ((t0 + row) * p.Hv + h) * kHead +
-                                                         32 * cq + 2 * tq);
-#pragma unroll
-            for (int jg = 0; jg < 4; ++jg) orow[4 * jg] = w[jg];
+              for (int e = 0; e < 8; ++e) {
+                orow[2 * e] = __ushort_as_bfloat16(static_cast<unsigned short>(w[e] & 0xffffu));
+                orow[2 * e + 1] = __ushort_as_bfloat16(static_cast<unsigned short>(w[e] >> 16));
+              }
+            }
           }
           if (dbg)
-            for (int jg = 0; jg < 4; ++jg)
-              for (int e = 0; e < 2; ++e)
-                p.debug[DBG_PV + row * 128 + 32 * cq + 8 * jg + 2 * tq + e] = pv[4 * jg + 2 * rr + e];
+            for (int e = 0; e < 16; ++e) {
+              p.debug[DBG_QS + t * 128 + col + e] = qs[e];
+              p.debug[DBG_PV + t * 128 + col + e] = pv[e];
+            }
         }
         if (via_tma) fence_async_smem();
       }
       PHASE(14)
+      if (DEBUG && dbg && lane == 0) p.debug[DBG_EV + warp * 5 + 2] = float(clock64() - t_base);
     }
     if constexpr (DEBUG) {
-      if (dbg_cta && tid == 0)
-        for (int i = 0; i < 20; ++i) p.debug[DBG_CLK + i] = static_cast<float>(clk_acc[i]);
+      if (dbg_cta && lane == 0)
+        for (int i = 0; i < kClkSlots; ++i)
+          p.debug[DBG_CLK + warp * kClkSlots + i] = static_cast<float>(clk_acc[i]);
     }
 #undef PHASE
 
@@ -703,14 +700,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t tl = bos + static_cast<int64_t>(nchunks - 1) * kChunk;
       if (eos - tl == kChunk) {
         named_sync(kComputeBar, kComputeThreads);
-        if (tid == 0) {
+        if (tid == kStoreTid) {
           tma_store_3d(&tm_o, smem + OFF_O, 0, h, static_cast<int>(tl));
           tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, static_cast<int>(tl));
           bulk_commit();
         }
       }
     }
-    if (tid == 0) bulk_wait_all();  // stores complete before the CTA's shared memory goes away
+    if (tid == kStoreTid) bulk_wait_all();  // stores complete before the CTA's shared memory goes away
 
     // ---- final state -> new_state (row rowv, this warp's 32 columns) --------
     if (!aborted) {
@@ -731,10 +728,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (lane == 0) {
     // ======================= TMA / MMA issue thread ========================
     const uint32_t idesc_d1 = idesc_bf16(128, 64, false, false);
+    const uint32_t idesc_kqs = idesc_bf16(128, 128, false, false);
     const uint32_t idesc_tv = idesc_bf16(64, 128, true, true);
-    const uint32_t idesc_vn = idesc_bf16(64, 128, false, false, true);
-    const uint32_t idesc_qs = idesc_bf16(64, 128, false, false);
-    const uint32_t idesc_pv = idesc_bf16(64, 128, false, true);
+    const uint32_t idesc_tks = idesc_bf16(64, 128, true, true, true);  // -T^ (K S)
+    const uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
     const uint32_t idesc_st = idesc_bf16(128, 128, true, true);
 
     const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
@@ -772,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       return true;
     };
-    // MMA 1 of chunk cc: [K;Q] K^T -> TM_W (M=128, N=64)
+    // MMA 1 of chunk cc: [K;Q] K^T -> TM_D1 (M=128, N=64)
     auto mma1 = [&](int cc) -> bool {
       const int s = cc & 1;
       if (!wait_bar(BAR_TMA0 + s, static_cast<uint32_t>((cc >> 1) & 1))) return false;
@@ -782,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-        mma_bf16_ss(tmem + TM_W, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
+        mma_bf16_ss(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
                     idesc_d1, ks > 0);
       }
       mma_commit(&bars[BAR_M1]);
@@ -798,18 +795,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kq = sb + OFF_KQ + (c & 1) * kKQStage;
       const uint32_t vsm = sb + OFF_V + (c & 1) * kVStage;
 
-      // Q S (the S tile of this chunk) -> TM_QS
+      // [K;Q] S -> TM_KQS (K S in lanes 0-63, Q S in lanes 64-127)
       MPHASE(12)
       if (!(ok = wait_bar(RDY_S, par))) break;
       MPHASE(0)
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 1) p.debug[DBG_EV + 85] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
-        mma_bf16_ss(tmem + TM_QS, sdesc_sw128(kq + kb * 16384 + 8192 + kin, 16, 1024),
-                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_qs, ks > 0);
+        mma_bf16_ss(tmem + TM_KQS, sdesc_sw128(kq + kb * 16384 + kin, 16, 1024),
+                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_kqs, ks > 0);
       }
+      mma_commit(&bars[BAR_KQS]);
       MPHASE(1)
-      // MMA 2: U_off = T~_off V -> TM_VN, W = T^ K -> TM_W
+      // Vn_part = T~ V - T^ (K S) -> TM_VN (the compute warps have replaced the
+      // S tile by the bf16 K S tile)
       if (!(ok = wait_bar(RDY_T, par))) break;
       MPHASE(2)
 #pragma unroll
@@ -818,33 +818,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sdesc_sw128(vsm + ks * 2048, 8192, 1024), idesc_tv, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_W, sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024),
-                    sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_tv, ks > 0);
-      mma_commit(&bars[BAR_M2]);
-      MPHASE(3)
-      // MMA 3: Vn_part = U_off - W S (accumulate on U_off)
-      if (!(ok = wait_bar(RDY_W, par))) break;
-      MPHASE(4)
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_AF + kb * 8192 + kin, 16, 1024),
-                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_vn, 1);
-      }
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024),
+                    sdesc_sw128(sb + OFF_ST + ks * 2048, 8192, 1024), idesc_tks, 1);
       mma_commit(&bars[BAR_M3]);
-      MPHASE(5)
-      // [K;Q]K^T of the next chunk runs while the compute warps drain Vn (its
-      // TMEM columns held W, which the compute warps have already drained)
+      MPHASE(3)
+      // [K;Q]K^T of the next chunk runs while the compute warps drain Vn
       if (c + 1 < nchunks && !(ok = mma1(c + 1))) break;
-      // MMA 4: PV = P Vn -> TM_VN; St += Vd_hi^T K + Vd_lo^T K
+      // P Vn -> lanes 64-127 of TM_VN (M=128 with P as A rows 64-127; rows
+      // 0-63 read don't-care bytes below the P tile, their results are unused);
+      // St += Vd_hi^T K + Vd_lo^T K
       if (!(ok = wait_bar(RDY_V, par))) break;
       MPHASE(8)
+      const bool ev = DEBUG && dbg_cta && c == p.dbg_chunk;
+      if (ev) p.debug[DBG_EV + 80] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_P + ks * 32, 16, 1024),
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_P - 8192 + ks * 32, 16, 1024),
                     sdesc_sw128(sb + OFF_VN + ks * 2048, 8192, 1024), idesc_pv, ks > 0);
       mma_commit(&bars[BAR_PV]);
       MPHASE(9)
+      if (ev) p.debug[DBG_EV + 81] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VH + ks * 2048, 8192, 1024),
@@ -855,11 +848,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_st, 1);
       mma_commit(&bars[BAR_ST]);
       MPHASE(10)
+      if (ev) p.debug[DBG_EV + 82] = float(clock64() - t_base);
       // refill this chunk's stage once the state update has read K
       if (c + 2 < nchunks) {
         if (!(ok = wait_bar(BAR_ST, par))) break;
         MPHASE(11)
+        if (ev) p.debug[DBG_EV + 83] = float(clock64() - t_base);
         issue_loads(c + 2);
+        if (ev) p.debug[DBG_EV + 84] = float(clock64() - t_base);
       }
     }
     if constexpr (DEBUG) {

@@ -295,8 +295,9 @@ def rel_err(x, ref) -> float:
 def chunk_intermediates(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, n, h, c, chunk=CHUNK):
     """fp64 intermediates of chunk ``c`` of sequence ``n``, v-head ``h``, in the
     definitions the fused tensor-core kernel uses (it dumps the same names):
-    gam, bet (zero log-decay and beta past the sequence end), A, P, T, U, W, Vn,
-    QS, PV and the k-last state after the chunk.  Rows past the sequence end hold
+    gam, bet (zero log-decay and beta past the sequence end), A, P, T, U, W, KS
+    (K times the chunk-start state, the kernel's form of W S = T^ (K S)), Vn, QS,
+    PV and the k-last state after the chunk.  Rows past the sequence end hold
     the packed neighbours' data (or zeros past T), as the kernel's tile loads do.
     The state at the chunk start comes from the token recurrence in fp64."""
     T_, Hq, K = np.asarray(q).shape
@@ -336,7 +337,8 @@ def chunk_intermediates(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, n, h, 
     Vn = U - W @ S
     Vn[~valid] = 0.0
     QS = Qc @ S
+    KS = Kc @ S
     PV = P @ Vn
     S_after = np.exp(gam[-1]) * S + Kc.T @ (np.exp(gam[-1] - gam)[:, None] * Vn)
-    return dict(gam=gam, bet=bet, A=A, P=P, T=Tm, U=U, W=W, Vn=Vn, QS=QS, PV=PV,
+    return dict(gam=gam, bet=bet, A=A, P=P, T=Tm, U=U, W=W, KS=KS, Vn=Vn, QS=QS, PV=PV,
                 St=S_after.T, L=L, valid=valid)

@@ -17,7 +17,7 @@ from gdn_b200 import _native as N, prefill, workloads as W
 pytestmark = pytest.mark.gpu
 
 DBG_NAMES = [("gam", 64), ("bet", 64), ("A", 4096), ("P", 4096), ("T", 4096), ("U", 8192),
-             ("W", 8192), ("Vn", 8192), ("QS", 8192), ("PV", 8192), ("St", 16384), ("clk", 32), ("mclk", 16)]
+             ("KS", 8192), ("Vn", 8192), ("QS", 8192), ("PV", 8192), ("St", 16384), ("clk", 320), ("mclk", 16), ("ev", 96)]
 
 
 def chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
@@ -54,7 +54,7 @@ def debug_dump(inp, n, h, c):
     for name, size in DBG_NAMES:
         res[name] = x[off:off + size]
         off += size
-    shapes = dict(A=(64, 64), P=(64, 64), T=(64, 64), U=(64, 128), W=(64, 128), Vn=(64, 128),
+    shapes = dict(A=(64, 64), P=(64, 64), T=(64, 64), U=(64, 128), KS=(64, 128), Vn=(64, 128),
                   QS=(64, 128), PV=(64, 128), St=(128, 128))
     for k_, s in shapes.items():
         res[k_] = res[k_].reshape(s)
@@ -78,9 +78,9 @@ def test_chunk_intermediates(lengths, n, h, c):
     assert np.abs(got["A"] - ref["A"]).max() < 1e-4
     assert _rel(got["P"], ref["P"], v) < 1e-5          # fp32 values before bf16 packing
     assert _rel(got["T"], ref["T"]) < 1e-4
-    errs = {k_: _rel(got[k_], ref[k_], v) for k_ in ("U", "W", "Vn", "QS", "PV")}
+    errs = {k_: _rel(got[k_], ref[k_], v) for k_ in ("KS", "Vn", "QS", "PV")}
     errs["St"] = _rel(got["St"], ref["St"])
-    assert errs["U"] < 1e-2 and errs["W"] < 1e-2, errs   # bf16 T operands
+    assert errs["KS"] < 1e-2, errs                       # bf16 S operand
     assert errs["QS"] < 1e-2 and errs["Vn"] < 2e-2, errs  # bf16 S operand
     assert errs["PV"] < 2e-2, errs
     assert errs["St"] < 1e-3, errs
