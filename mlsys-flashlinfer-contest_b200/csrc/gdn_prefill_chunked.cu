@@ -11,24 +11,27 @@
 // S = [K,V] state at the chunk start, St = S^T = k-last [V,K] in TMEM):
 //   G|QK  = [K;Q] K^T                          (tcgen05, M=128: rows 0-63 KK^T, 64-127 QK^T)
 //   A     = strict_tril(beta_t G e^{gamma_t - gamma_s}),  P = tril(QK e^{gamma_t - gamma_s})
-//   T     = (I + A)^-1                         (fp32, CUDA cores, blocks of 16)
-//   KS|QS = [K;Q] S                            (tcgen05, M=128, S as bf16; right after the
-//           state is read, so it overlaps the CUDA-core phases below)
-//   Vn    = U - W S  with  U = beta (.) V + T_off diag(beta) V  and  W S = T^ (K S),
-//           T^ = T diag(beta e^gamma): one tcgen05 group T~ V - T^ (KS) once T is known
-//           (T~ = T_off diag(beta); the unit diagonal is applied exactly in fp32)
-//   O     = scale (e^{gamma_t} QS + P Vn)      (tcgen05 for P Vn)
-//   St   <- e^{gamma_63} St + Vd^T K,  Vd = e^{gamma_63 - gamma_t} Vn split into
-//           bf16 hi + lo (two MMAs) so the state update keeps ~16 mantissa bits.
+//   T     = (I + A)^-1                         (fp32, CUDA cores + mma.sync, blocks of 16)
+//   (KS|QS)^T = St [K;Q]^T                     (tcgen05, A = bf16 St from TMEM, right after
+//                                               the state is read: overlaps A/P and the inverse)
+//   Vn^T  = V^T T~^T - (KS)^T T^^T + beta (.) V^T    (U - W S with W S = T^ (K S);
+//           T~ = T_off diag(beta), T^ = T diag(beta e^gamma); the unit diagonal of T is
+//           applied exactly in fp32 as beta (.) V when Vn is drained)
+//   O^T   = scale (e^{gamma_t} (QS)^T + Vn^T P^T)   (tcgen05, A = bf16 Vn^T from TMEM)
+//   St   <- e^{gamma_63} St + Vd^T K,  Vd = e^{gamma_63 - gamma_t} Vn as bf16 hi + lo (two
+//           MMAs with A from TMEM) so the state update keeps ~16 mantissa bits.
+// Everything after the state read works on transposed ([v][t]) accumulators,
+// so every TMEM lane is a v row: each thread owns one v row of every
+// accumulator, and the operands the threads produce (bf16 St, K S, Vn, Vd)
+// go back to TMEM as tcgen05 A operands instead of through shared memory.
 // Tokens past the end of the sequence get beta = 0 and log-decay 0, which
 // makes their Vn rows exactly zero and leaves gamma_63 = gamma_{L-1}.
 //
 // Warp roles: warps 0-15 do the CUDA-core work (four per TMEM lane quarter,
-// each on 32 of the 128 columns); warp 16 issues every TMA load and tcgen05
+// each on a quarter of the columns); warp 16 issues every TMA load and tcgen05
 // MMA.  The two sides hand off through mbarriers only, so the tensor pipe runs
-// [K;Q] S during the A/P phase, [K;Q]K^T of the next chunk during the Vn drain
-// and the state update during the output epilogue.  The only MMAs between the
-// triangular inverse and the next chunk are T~ V - T^ (KS) and P Vn.
+// St [K;Q]^T during the A/P phase, [K;Q]K^T of the next chunk during the Vn
+// drain and the state update during the output epilogue.
 // Math: same chunked algebra as cuda_kkt_inv_uw_v1.cu:1-20 (U, W, g_cu),
 // cuda_h_v2b.cu (state scan) and cuda_o_v1.cu (output); semantics as
 // definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md:62-142.
@@ -52,28 +55,28 @@ constexpr int kComputeWarps = 16;  // four per TMEM lane quarter
 constexpr int kComputeThreads = 32 * kComputeWarps;
 constexpr int kThreads = kComputeThreads + 32;  // + the TMA / MMA issue warp
 constexpr uint32_t kComputeBar = 1;             // named barrier of the compute warps
-constexpr int kStoreTid = 256;  // issues the output TMA stores: warp 8 is idle in the inverse
+constexpr int kL0Warp = 14;                     // warps 14-15 run the level-0 inverse
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait, then give up
 
 // ---- shared memory map (offsets from a 1024-aligned base) -----------------
-// Every operand tile is a stack of 128-byte rows in the SWIZZLE_128B pattern.
+// Operand tiles are stacks of 128-byte rows in the SWIZZLE_128B pattern.
 constexpr uint32_t kKQStage = 32768;  // [kb 2][row 128: K rows 0-63, Q rows 64-127][128 B]
 constexpr uint32_t kVStage = 16384;   // [vb 2][t 64][128 B]
 constexpr uint32_t OFF_KQ = 0;                     // 2 stages
 constexpr uint32_t OFF_V = OFF_KQ + 2 * kKQStage;  // 2 stages
-constexpr uint32_t OFF_ST = OFF_V + 2 * kVStage;   // bf16 S: [kb 2][v 128][128 B] (K-major B);
-                                                   // once [K;Q] S is done: K S [vb 2][s 64][128 B] (MN-major B)
-constexpr uint32_t OFF_P = OFF_ST + 32768;         // P: [t 64][128 B] (K-major A rows 64-127 of P Vn)
-constexpr uint32_t OFF_TB = OFF_P + 8192;          // T diag(beta): [s 64][t 128 B] (MN-major A)
-constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T diag(beta e^gamma)
-constexpr uint32_t OFF_O = OFF_TB;                 // output tile [cb 2][t 64][128 B] (TMA store source),
-                                                   // between the Vn MMAs and the next chunk's T tiles
-constexpr uint32_t OFF_AF = OFF_TG + 8192;         // fp32 A^T [64][72] (spills 1 KiB into VN)
-constexpr uint32_t OFF_VN = OFF_AF + 17408;        // Vn bf16 [vb 2][t 64][128 B] (MN-major B);
-                                                   // during the inverse: fp32 T^T [64][68] (spills into VH)
-constexpr uint32_t OFF_VH = OFF_VN + 16384;        // Vd hi (MN-major A)
-constexpr uint32_t OFF_VL = OFF_VH + 16384;        // Vd lo; during the inverse: fp32 (A21 T11)^T [32][36]
-constexpr uint32_t OFF_MISC = OFF_VL + 16384;      // per-token gate tables, barriers, tmem slot
+constexpr uint32_t OFF_P = OFF_V + 2 * kVStage;    // P: [t 64][128 B] (K-major B of Vn^T P^T)
+constexpr uint32_t OFF_TB = OFF_P + 8192;          // T~ = T_off diag(beta): row s = column s (MN-major B)
+constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T^ = T diag(beta e^gamma), same layout
+constexpr int kAtPitch = 72;   // fp32 row pitch of A^T (72 = 8 mod 32: conflict-free tf32 A fragments)
+constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict-free B fragments)
+constexpr uint32_t OFF_AT = OFF_TG + 8192;                // fp32 A^T [64][72]
+constexpr uint32_t OFF_TC = OFF_AT + 64 * kAtPitch * 4;   // fp32 T^T [64][68]
+constexpr uint32_t OFF_MC = OFF_TC + 64 * kTcPitch * 4;   // fp32 (A21 T11)^T [32][36]
+constexpr uint32_t OFF_XC = OFF_MC + 32 * 36 * 4;         // fp32 level-1 products, 4 x [8][20]
+constexpr uint32_t OFF_O = (OFF_XC + 4 * 160 * 4 + 1023) / 1024 * 1024;  // output tile
+// [cb 2][t 64][128 B] (TMA store source; written by the output epilogue, stored
+// by the issue thread once the next chunk's T tiles are signalled)
+constexpr uint32_t OFF_MISC = OFF_O + 16384;
 // Per-token tables of one chunk (floats), double-buffered by chunk parity.
 constexpr int G_GAM = 0;     // gamma_t * log2(e) (cumulative log-decay)
 constexpr int G_BET = 64;    // beta_t (0 past the end of the sequence)
@@ -84,20 +87,23 @@ constexpr int G_BE = 320;    // beta_t * 2^gamma_t
 constexpr int kGateFloats = 384;
 constexpr uint32_t kMiscBarOff = 2 * kGateFloats * 4;  // barriers after both table buffers
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBarOff + 256 + 1024;  // + slack for the 1024 alignment
-constexpr int kAtPitch = 72;   // fp32 row pitch of A^T (72 = 8 mod 32: conflict-free tf32 A fragments)
-constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict-free B fragments)
 
-// ---- TMEM columns ----------------------------------------------------------
-constexpr uint32_t TM_ST = 0;     // St [v 128 lanes][k 128 cols]
-constexpr uint32_t TM_KQS = 128;  // [K;Q] S: lanes 0-63 K S, lanes 64-127 Q S (M=128)
-constexpr uint32_t TM_D1 = 256;   // [K;Q] K^T [128 lanes][64 cols]
-constexpr uint32_t TM_VN = 320;   // T~ V - T^ KS -> Vn (M=64 layout); then P Vn in lanes 64-127 (M=128)
+// ---- TMEM columns (every accumulator has lanes = v, except D1) -------------
+constexpr uint32_t TM_ST = 0;     // St [v][k] fp32
+constexpr uint32_t TM_KQS = 128;  // [K S | Q S]^T fp32: cols 0-63 (KS)^T[v][s], 64-127 (QS)^T[v][t]
+constexpr uint32_t TM_D1 = 256;   // [K;Q] K^T fp32 [128 rows][64]
+constexpr uint32_t TM_VN = 320;   // Vn^T (without beta V) fp32 [v][t], then (P Vn)^T [v][t]
+constexpr uint32_t TM_SB = 384;   // A operand: St as bf16 [v][k] (64 cols), then
+constexpr uint32_t TM_VDH = 384;  //   Vd_hi^T bf16 [v][t] (32 cols)
+constexpr uint32_t TM_VDL = 416;  //   Vd_lo^T bf16 [v][t] (32 cols)
+constexpr uint32_t TM_KSB = 448;  // A operand: (KS)^T bf16 [v][s] (32 cols), then
+constexpr uint32_t TM_VNB = 448;  //   Vn^T bf16 [v][s] (32 cols)
 constexpr uint32_t kTmemCols = 512;
 
 constexpr uint32_t kTmaBytes = 2 * kKQStage / 2 + kVStage;  // K 16K + Q 16K + V 16K
 
-// mbarriers (OFF_MISC + 1024): TMA stages, tensor pipe -> compute warps (one
-// tcgen05.commit each), compute warps -> issue warp (one arrive per warp).
+// mbarriers (OFF_MISC + kMiscBarOff): TMA stages, tensor pipe -> compute warps
+// (one tcgen05.commit each), compute warps -> issue warp (one arrive per warp).
 enum : int {
   BAR_TMA0 = 0, BAR_TMA1, BAR_M1, BAR_KQS, BAR_M3, BAR_PV, BAR_ST,
   RDY_S, RDY_T, RDY_V, BAR_END, kNumBars
@@ -122,7 +128,7 @@ struct ChunkParams {
 
 constexpr int kClkSlots = 20;  // phase clock slots per compute warp (debug build)
 // Debug dump layout (floats); the DBG_U block is not written (U is never formed
-// on its own: the kernel computes T~ V - T^ (K S) in one accumulator).
+// on its own: the kernel computes V^T T~^T - (KS)^T T^^T in one accumulator).
 constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_T = DBG_P + 4096,
               DBG_U = DBG_T + 4096, DBG_KS = DBG_U + 8192, DBG_VN = DBG_KS + 8192,
               DBG_QS = DBG_VN + 8192, DBG_PV = DBG_QS + 8192, DBG_ST = DBG_PV + 8192,
@@ -132,8 +138,20 @@ constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_
 // debug CTA spent in each phase, summed over all chunks of its sequence
 // (phases: the PHASE() marks in the chunk loop); DBG_MCLK: the same for the
 // issue thread (MPHASE() marks).  DBG_EV: SM-clock timestamps (from a common
-// base) of handoff events around the debug chunk: [warp 16][5] for the compute
-// warps, then 8 for the issue thread.
+// base) of handoff events around chunk dbg_chunk + 2 (away from the dump's own
+// stores): [warp 16][5] for the compute warps, then 8 for the issue thread.
+
+// 16 consecutive floats of a per-token table (16-byte aligned) as four vector loads
+__device__ __forceinline__ void load_table16(const float* src, float* v) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 x = reinterpret_cast<const float4*>(src)[q];
+    v[4 * q] = x.x;
+    v[4 * q + 1] = x.y;
+    v[4 * q + 2] = x.z;
+    v[4 * q + 3] = x.w;
+  }
+}
 
 template <bool DEBUG>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -152,19 +170,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* gates_buf = reinterpret_cast<float*>(smem + OFF_MISC);  // [2][kGateFloats]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_MISC + kMiscBarOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  // fp32 scratch of the inverse (A^T 18 KiB from OFF_AF into the Vn tile, T^T
-  // after it into the Vd_hi tile, products in the Vd_lo tile; all free then)
-  float* At = reinterpret_cast<float*>(smem + OFF_AF);   // A column-major: At[k][i] = A[i][k]
-  float* Tcm = reinterpret_cast<float*>(smem + OFF_AF + 64 * kAtPitch * 4);  // Tcm[j][i] = T[i][j]
-  float* Mcm = reinterpret_cast<float*>(smem + OFF_VL);  // (A21 T11) column-major, pitch 36
-  float* Xcm = Mcm + 32 * 36;                            // 4 x [8][20] level-1 products
+  float* At = reinterpret_cast<float*>(smem + OFF_AT);   // A column-major: At[k][i] = A[i][k]
+  float* Tcm = reinterpret_cast<float*>(smem + OFF_TC);  // Tcm[j][i] = T[i][j]
+  float* Mcm = reinterpret_cast<float*>(smem + OFF_MC);  // (A21 T11) column-major, pitch 36
+  float* Xcm = reinterpret_cast<float*>(smem + OFF_XC);  // 4 x [8][20] level-1 products
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-  const int cq = (warp >> 2) & 3;  // column quarter handled by this warp (32 of 128 columns)
-  const int g = lane >> 2, tq = lane & 3;  // 16x256b fragment coordinates
-  const int r_lo = 16 * quarter + g;       // rows of an M=64 accumulator held by this thread
-  const int rowv = 32 * quarter + lane;    // row of an M=128 accumulator held by this thread
+  const int quarter = warp & 3;    // TMEM lane quarter this warp may access
+  const int cq = (warp >> 2) & 3;  // column quarter handled by this warp
+  const int g = lane >> 2, tq = lane & 3;  // mma.sync fragment coordinates
+  const int rowv = 32 * quarter + lane;    // TMEM lane (accumulator row) of this thread
   const int h = static_cast<int>(blockIdx.x % p.Hv);
   const int64_t n = blockIdx.x / p.Hv;
   const int qh = h / (p.Hv / p.Hq);
@@ -238,11 +253,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
     }
 
-    // One arrival per warp on a compute -> issue-warp barrier, after this
-    // thread's operand writes (smem: fence to the async proxy; TMEM: ordered
-    // before the thread sync).
-    auto signal = [&](int b) {
-      fence_async_smem();
+    // One arrival per warp on a compute -> issue-warp barrier after this
+    // thread's TMEM operand stores (waited), optionally with its shared-memory
+    // operand writes made visible to the async proxy first.
+    auto signal = [&](int b, bool smem_written) {
+      if (smem_written) fence_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[b]);
@@ -256,7 +271,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     // Gates of one chunk from raw a/b values held by warp 1 (two tokens per lane):
-    // log-decay, its inclusive scan (gamma, stored in log2 units) and beta.
+    // log-decay, its inclusive scan (gamma, stored in log2 units), beta and the
+    // derived per-token tables.
     float ga_raw[2] = {0.f, 0.f}, gb_raw[2] = {0.f, 0.f};
     auto prefetch_gates = [&](int cc) {
       const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
@@ -326,20 +342,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool dbg = dbg_cta && c == p.dbg_chunk;
       const uint32_t vsm = sb + OFF_V + stage * kVStage;
 
-      // previous chunk's state update done: its operand tiles are free and St
-      // is final.  The barrier also publishes this chunk's gates (warp 1).
+      // previous chunk's state update done: St is final and its TMEM operands
+      // are free.  The barrier also publishes this chunk's gates (warp 1).
       if (c > 0) wait_mma(BAR_ST, par ^ 1u);
       PHASE(17)
-      if (DEBUG && dbg_cta && c == p.dbg_chunk + 1 && lane == 0)
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 3 && lane == 0)
         p.debug[DBG_EV + warp * 5 + 3] = float(clock64() - t_base);
       if (named_any(kComputeBar, kComputeThreads, failed)) { aborted = true; break; }
-      if (DEBUG && dbg_cta && c == p.dbg_chunk + 1 && lane == 0)
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 3 && lane == 0)
         p.debug[DBG_EV + warp * 5 + 4] = float(clock64() - t_base);
-      if (c > 0 && p.tma_out && tid == kStoreTid) {  // output tile of chunk c-1 (a full chunk)
-        tma_store_3d(&tm_o, smem + OFF_O, 0, h, static_cast<int>(t0 - kChunk));
-        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, static_cast<int>(t0 - kChunk));
-        bulk_commit();
-      }
       if (dbg_cta && c - 1 == p.dbg_chunk) dump_state();
       PHASE(0)
 
@@ -351,30 +362,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       PHASE(1)
 
-      // ---- state pass: St -> bf16 operand tile; St *= e^{gamma_63} ---------
+      // ---- state pass: St -> bf16 A operand in TMEM; St *= e^{gamma_63} ----
       {
         const float dec = ex2_ftz(gam[63]);
         float v[32];
         tmem_ld32(tq_st, v);
         tmem_wait_ld();
         reg_fence(v);
-        const uint32_t tile = sb + OFF_ST + (cq >> 1) * 16384;
+        uint32_t w[16];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-          sts128(tile + sw128_off(rowv, (cq & 1) * 4 + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
-                 pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
-                 pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
+        for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+        tmem_st16u(tmem + lane_base + TM_SB + 16 * cq, w);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= dec;
         tmem_st32(tq_st, v);
         tmem_wait_st();
       }
-      signal(RDY_S);
+      signal(RDY_S, false);
       PHASE(2)
       wait_mma(BAR_M1, par);
       PHASE(3)
 
-      // ---- A (quarters 0-1, stored column-major) and P (quarters 2-3) -------
+      // ---- A (rows 0-63 of D1: quarters 0-1, stored column-major) and
+      //      P (rows 64-127: quarters 2-3) -----------------------------------
       {
         const int i = rowv & 63;
         const float gi = gam[i];
@@ -425,36 +435,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                    pack_bf16x2(v[8 * c2 + 2], v[8 * c2 + 3]), pack_bf16x2(v[8 * c2 + 4], v[8 * c2 + 5]),
                    pack_bf16x2(v[8 * c2 + 6], v[8 * c2 + 7]));
           if (dbg)
-            for (int jj = 0; jj < 16; ++jj) p.debug[DBG_P + i * 64 + 16 * cq + jj] = v[jj];
+            for (int jj = 0; jj < 16; ++jj) p.debug[DBG_P + i * 64 + r0 + jj] = v[jj];
         }
       }
       PHASE(5)
       named_sync(kComputeBar, kComputeThreads);
       PHASE(6)
 
+      // ---- (KS)^T -> bf16 A operand of the Vn MMAs: lanes v, tokens s in
+      //      [16 cq, 16 cq + 16); warps 14-15 convert after the level-0 inverse.
+      auto convert_ks = [&]() {
+        wait_mma(BAR_KQS, par);
+        float v[16];
+        tmem_ld16(tmem + lane_base + TM_KQS + 16 * cq, v);
+        tmem_wait_ld();
+        reg_fence(v);
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+        tmem_st8u(tmem + lane_base + TM_KSB + 8 * cq, w);
+        tmem_wait_st();
+        if (dbg)
+          for (int i = 0; i < 16; ++i) p.debug[DBG_KS + (16 * cq + i) * 128 + rowv] = v[i];
+      };
+
       // ---- T = (I + A)^-1, fp32, blocks of 16:
       //      level 0: the four diagonal blocks by right-looking elimination;
       //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22 (mma.sync);
       //      level 2: [T20 T21; T30 T31] = -T22' (A21' T11'), primes = 32x32 halves.
-      if (quarter < 2) {
-        // K S rows (tokens, lanes 0-63 of the [K;Q] S accumulator) -> bf16 K S
-        // tile over the S tile (Q S and K S are both done): the B operand of
-        // T^ (K S).  Runs beside the level-0 inverse (warps 2 and 3).
-        wait_mma(BAR_KQS, par);
-        float v[32];
-        tmem_ld32(tmem + lane_base + TM_KQS + 32 * cq, v);
-        tmem_wait_ld();
-        reg_fence(v);
-        const uint32_t tile = sb + OFF_ST + (cq >> 1) * 8192;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-          sts128(tile + sw128_off(rowv, (cq & 1) * 4 + c4), pack_bf16x2(v[8 * c4], v[8 * c4 + 1]),
-                 pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]), pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]),
-                 pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
-        if (dbg)
-          for (int i = 0; i < 32; ++i) p.debug[DBG_KS + rowv * 128 + 32 * cq + i] = v[i];
-      } else if (warp == 2 || warp == 3) {
-        const int u = tid - 64;
+      if (warp < kL0Warp) {
+        convert_ks();
+      } else {
+        const int u = tid - 32 * kL0Warp;
         const int b = u >> 4, j = u & 15, b0 = 16 * b;
         float x[16];
 #pragma unroll
@@ -517,6 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc[kTcPitch] = -dacc[1];
         tc[8] = -dacc[2];
         tc[kTcPitch + 8] = -dacc[3];
+      } else if (warp >= kL0Warp) {
+        convert_ks();
       }
       named_sync(kComputeBar, kComputeThreads);
       PHASE(16)
@@ -559,15 +573,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc[8] = -cacc[2];
         tc[kTcPitch + 8] = -cacc[3];
       }
-      if (tid == kStoreTid) bulk_wait_read_all();  // output tile read out before the T tiles reuse it
       named_sync(kComputeBar, kComputeThreads);
       PHASE(7)
       {
-        // T~ = T_off diag(beta) and T^ = T diag(beta e^gamma) as MN-major bf16
-        // tiles: row j of a tile holds column j of T.  T~ leaves out the unit
-        // diagonal: U = beta (.) V + T~_off V, and beta (.) V is added in fp32 when
-        // Vn is drained (a bf16 beta_j on the diagonal would cost ~2^-9 relative
-        // error on all of U).
+        // T~ = T_off diag(beta) and T^ = T diag(beta e^gamma) as bf16 tiles in
+        // which row j holds column j of T: MN-major B operands (K = s rows, N = t
+        // contiguous) of V^T T~^T and (KS)^T T^^T.  T~ leaves out the unit
+        // diagonal: beta (.) V is added in fp32 when Vn is drained (a bf16 beta_j
+        // on the diagonal would cost ~2^-9 relative error on all of U).
         const int j = tid & 63;
         const bool hat = (tid >> 6) & 1;
         const int part = tid >> 7;  // 16-row quarter of the tile row (2 chunks)
@@ -589,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 16 * part; i < 16 * part + 16; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
         }
       }
-      signal(RDY_T);
+      signal(RDY_T, true);  // T tiles and the P tile are read by the tensor pipe
       PHASE(8)
       if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap the Vn MMAs
         compute_gates(c + 1);
@@ -598,96 +611,104 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_mma(BAR_M3, par);
       PHASE(11)
 
-      // ---- Vn = beta V + Vn_part -> bf16 (B of P Vn);
-      //      Vd = e^{g63 - g_t} Vn -> hi/lo bf16 (A of the state update) ------
+      // ---- Vn^T = (V^T T~^T - (KS)^T T^^T) + beta (.) V^T -> bf16 A operand
+      //      of (P Vn)^T; Vd^T = e^{g63 - g_t} Vn^T -> hi/lo bf16 A operands
+      //      of the state update.  Lane v, tokens t in [16 cq, 16 cq + 16). ---
       {
-        float v[16];
-        tmem_ld16x256_x4(tmem + lane_base + TM_VN + 32 * cq, v);
+        float x[16];
+        tmem_ld16(tmem + lane_base + TM_VN + 16 * cq, x);
         tmem_wait_ld();
-        reg_fence(v);
+        reg_fence(x);
+        // V[t][v] in the V tile: block v/64, row t, 16-byte chunk (v%64)/8 ^ (t%8);
+        // read as the 32-bit word of the (even, odd) v pair (16-bit shared
+        // accesses are much slower), this lane's half selected
+        const uint32_t vrow = vsm + (rowv >> 6) * 8192 + 4 * ((rowv & 7) >> 1);
+        const uint32_t vshift = (rowv & 1) ? 0u : 16u;
+        const int vch = (rowv & 63) >> 3;
+        float bt[16], dc[16];  // beta_t and 2^(g63 - g_t) of this warp's 16 tokens
+        load_table16(bet + 16 * cq, bt);
+        load_table16(gam + G_DEC + 16 * cq, dc);
+        uint32_t wn[8], wh[8], wl[8];
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const int row = r_lo + 8 * rr;
-          const bool valid = row < L;
-          const float dec = gam[G_DEC + row];  // 0 past the end of the sequence
-          const float bt = bet[row];
+        for (int e = 0; e < 8; ++e) {
+          float xv[2], d[2];
 #pragma unroll
-          for (int jg = 0; jg < 4; ++jg) {
-            const uint32_t off = (cq >> 1) * 8192 + sw128_off(row, (cq & 1) * 4 + jg) + 4 * tq;
-            const uint32_t vw = lds32(vsm + off);
-            const float x0 = valid ? fmaf(bt, bf16_lo(vw), v[4 * jg + 2 * rr]) : 0.f;
-            const float x1 = valid ? fmaf(bt, bf16_hi(vw), v[4 * jg + 2 * rr + 1]) : 0.f;
-            const float d0 = x0 * dec, d1 = x1 * dec;
-            const float h0 = __bfloat162float(__float2bfloat16_rn(d0));
-            const float h1 = __bfloat162float(__float2bfloat16_rn(d1));
-            sts32(sb + OFF_VN + off, pack_bf16x2(x0, x1));
-            sts32(sb + OFF_VH + off, pack_bf16x2(h0, h1));
-            sts32(sb + OFF_VL + off, pack_bf16x2(d0 - h0, d1 - h1));
-            if (dbg) {
-              const int col = 32 * cq + 8 * jg + 2 * tq;
-              p.debug[DBG_VN + row * 128 + col] = x0;
-              p.debug[DBG_VN + row * 128 + col + 1] = x1;
-            }
+          for (int f = 0; f < 2; ++f) {
+            const int t = 16 * cq + 2 * e + f;
+            const float vt =
+                __uint_as_float((lds32(vrow + t * 128 + ((vch ^ (t & 7)) << 4)) << vshift) & 0xFFFF0000u);
+            xv[f] = (t < L) ? fmaf(bt[2 * e + f], vt, x[2 * e + f]) : 0.f;
+            d[f] = xv[f] * dc[2 * e + f];
+          }
+          wn[e] = pack_bf16x2(xv[0], xv[1]);
+          const uint32_t hp = pack_bf16x2(d[0], d[1]);  // round-to-nearest hi parts
+          wh[e] = hp;
+          wl[e] = pack_bf16x2(d[0] - bf16_lo(hp), d[1] - bf16_hi(hp));
+          if (dbg) {
+            p.debug[DBG_VN + (16 * cq + 2 * e) * 128 + rowv] = xv[0];
+            p.debug[DBG_VN + (16 * cq + 2 * e + 1) * 128 + rowv] = xv[1];
           }
         }
+        tmem_st8u(tmem + lane_base + TM_VNB + 8 * cq, wn);
+        tmem_st8u(tmem + lane_base + TM_VDH + 8 * cq, wh);
+        tmem_st8u(tmem + lane_base + TM_VDL + 8 * cq, wl);
+        tmem_wait_st();
       }
-      signal(RDY_V);
+      signal(RDY_V, false);
       PHASE(12)
-      if (DEBUG && dbg && lane == 0) p.debug[DBG_EV + warp * 5 + 0] = float(clock64() - t_base);
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 2 && lane == 0) p.debug[DBG_EV + warp * 5 + 0] = float(clock64() - t_base);
       wait_mma(BAR_PV, par);
       PHASE(13)
-      if (DEBUG && dbg && lane == 0) p.debug[DBG_EV + warp * 5 + 1] = float(clock64() - t_base);
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 2 && lane == 0) p.debug[DBG_EV + warp * 5 + 1] = float(clock64() - t_base);
 
-      // ---- output rows, quarters 2-3 (token t = rowv - 64 of the M=128 Q S and
-      //      P Vn accumulators): O = scale (e^{gamma_t} QS + PV) ---------------
-      if (quarter >= 2) {
-        const int t = rowv - 64;
-        const float eg = gam[G_EG + t];
-        // full chunks: bf16 rows into the swizzled output tile, stored by TMA
-        // at the top of the next chunk; a partial last chunk stores directly.
+      // ---- output: O[t][v] = scale (e^{gamma_t} (QS)^T[v][t] + (P Vn)^T[v][t]),
+      //      lane v, tokens t in [16 cq, 16 cq + 16).  Full chunks go to the
+      //      swizzled output tile (each warp store: 64 contiguous bytes of row
+      //      t), stored by TMA from the issue thread; a partial chunk stores
+      //      directly. ---------------------------------------------------
+      {
         const bool via_tma = p.tma_out && L == kChunk;
+        // lanes pair up (v even, v + 1): the even lane stores the bf16x2 words
+        // of tokens 0-7 of this warp's 16, the odd lane those of tokens 8-15
+        const bool odd = rowv & 1;
+        const uint32_t ocol = sb + OFF_O + (rowv >> 6) * 8192 + 4 * ((rowv & 7) >> 1);
+        const int och = (rowv & 63) >> 3;
+        float qs[16], pv[16];
+        tmem_ld16(tmem + lane_base + TM_KQS + 64 + 16 * cq, qs);
+        tmem_ld16(tmem + lane_base + TM_VN + 16 * cq, pv);
+        tmem_wait_ld();
+        reg_fence(qs);
+        reg_fence(pv);
+        const int64_t tstride = static_cast<int64_t>(p.Hv) * kHead;
+        float eg[16];  // scale * 2^g_t of this warp's 16 tokens
+        load_table16(gam + G_EG + 16 * cq, eg);
+        __nv_bfloat16* orow = p.out + (t0 * p.Hv + h) * kHead + rowv;
+        float o[16];
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {  // 16 of this warp's 32 columns at a time
-          float qs[16], pv[16];
-          tmem_ld16(tmem + lane_base + TM_KQS + 32 * cq + 16 * hf, qs);
-          tmem_ld16(tmem + lane_base + TM_VN + 32 * cq + 16 * hf, pv);
-          tmem_wait_ld();
-          reg_fence(qs);
-          reg_fence(pv);
-          uint32_t w[8];
+        for (int i = 0; i < 16; ++i) o[i] = fmaf(eg[i], qs[i], p.scale * pv[i]);
+        if (via_tma) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            w[e] = pack_bf16x2(fmaf(eg, qs[2 * e], p.scale * pv[2 * e]),
-                               fmaf(eg, qs[2 * e + 1], p.scale * pv[2 * e + 1]));
-          const int col = 32 * cq + 16 * hf;  // first of these 16 output columns
-          if (via_tma) {
-            const uint32_t base = sb + OFF_O + (cq >> 1) * 8192;
-            const int ch = (cq & 1) * 4 + 2 * hf;
-            sts128(base + sw128_off(t, ch), w[0], w[1], w[2], w[3]);
-            sts128(base + sw128_off(t, ch + 1), w[4], w[5], w[6], w[7]);
-          } else if (t < L) {
-            __nv_bfloat16* orow = p.out + ((t0 + t) * p.Hv + h) * kHead + col;
-            if (p.tma_out) {  // 16-byte aligned output
-              reinterpret_cast<uint4*>(orow)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-              reinterpret_cast<uint4*>(orow)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                orow[2 * e] = __ushort_as_bfloat16(static_cast<unsigned short>(w[e] & 0xffffu));
-                orow[2 * e + 1] = __ushort_as_bfloat16(static_cast<unsigned short>(w[e] >> 16));
-              }
-            }
+          for (int i = 0; i < 8; ++i) {
+            // send what the partner keeps, receive the partner's value for ours
+            const float mine = odd ? o[8 + i] : o[i];
+            const float theirs = __shfl_xor_sync(0xffffffffu, odd ? o[i] : o[8 + i], 1);
+            const int t = 16 * cq + (odd ? 8 : 0) + i;
+            const uint32_t w = odd ? pack_bf16x2(theirs, mine) : pack_bf16x2(mine, theirs);
+            sts32(ocol + t * 128 + ((och ^ (t & 7)) << 4), w);
           }
-          if (dbg)
-            for (int e = 0; e < 16; ++e) {
-              p.debug[DBG_QS + t * 128 + col + e] = qs[e];
-              p.debug[DBG_PV + t * 128 + col + e] = pv[e];
-            }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (16 * cq + i < L) orow[(16 * cq + i) * tstride] = __float2bfloat16_rn(o[i]);
         }
-        if (via_tma) fence_async_smem();
+        if (dbg)
+          for (int i = 0; i < 16; ++i) {
+            p.debug[DBG_QS + (16 * cq + i) * 128 + rowv] = qs[i];
+            p.debug[DBG_PV + (16 * cq + i) * 128 + rowv] = pv[i];
+          }
       }
       PHASE(14)
-      if (DEBUG && dbg && lane == 0) p.debug[DBG_EV + warp * 5 + 2] = float(clock64() - t_base);
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 2 && lane == 0) p.debug[DBG_EV + warp * 5 + 2] = float(clock64() - t_base);
     }
     if constexpr (DEBUG) {
       if (dbg_cta && lane == 0)
@@ -696,18 +717,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 #undef PHASE
 
-    if (!aborted && p.tma_out) {  // output tile of the last chunk, if it is full
-      const int64_t tl = bos + static_cast<int64_t>(nchunks - 1) * kChunk;
-      if (eos - tl == kChunk) {
-        named_sync(kComputeBar, kComputeThreads);
-        if (tid == kStoreTid) {
-          tma_store_3d(&tm_o, smem + OFF_O, 0, h, static_cast<int>(tl));
-          tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, static_cast<int>(tl));
-          bulk_commit();
-        }
+    if (!aborted && p.tma_out && eos - (bos + static_cast<int64_t>(nchunks - 1) * kChunk) == kChunk) {
+      // output tile of the last (full) chunk
+      fence_async_smem();
+      named_sync(kComputeBar, kComputeThreads);
+      if (tid == 0) {
+        const int tl = static_cast<int>(bos + static_cast<int64_t>(nchunks - 1) * kChunk);
+        tma_store_3d(&tm_o, smem + OFF_O, 0, h, tl);
+        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, tl);
+        bulk_commit();
+        bulk_wait_all();
       }
     }
-    if (tid == kStoreTid) bulk_wait_all();  // stores complete before the CTA's shared memory goes away
 
     // ---- final state -> new_state (row rowv, this warp's 32 columns) --------
     if (!aborted) {
@@ -728,11 +749,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (lane == 0) {
     // ======================= TMA / MMA issue thread ========================
     const uint32_t idesc_d1 = idesc_bf16(128, 64, false, false);
-    const uint32_t idesc_kqs = idesc_bf16(128, 128, false, false);
-    const uint32_t idesc_tv = idesc_bf16(64, 128, true, true);
-    const uint32_t idesc_tks = idesc_bf16(64, 128, true, true, true);  // -T^ (K S)
-    const uint32_t idesc_pv = idesc_bf16(128, 128, false, true);
-    const uint32_t idesc_st = idesc_bf16(128, 128, true, true);
+    const uint32_t idesc_kqs = idesc_bf16(128, 128, false, false);   // St (TMEM) x [K;Q]^T
+    const uint32_t idesc_vt = idesc_bf16(128, 64, true, true);       // V^T (smem, MN) x T~^T
+    const uint32_t idesc_kst = idesc_bf16(128, 64, false, true, true);  // -(KS)^T (TMEM) x T^^T
+    const uint32_t idesc_pv = idesc_bf16(128, 64, false, false);     // Vn^T (TMEM) x P^T
+    const uint32_t idesc_st = idesc_bf16(128, 128, false, true);     // Vd^T (TMEM) x K
 
     const bool dbg_cta = DEBUG && p.debug && n == p.dbg_seq && h == p.dbg_head;
     long long mclk[16];
@@ -795,57 +816,64 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kq = sb + OFF_KQ + (c & 1) * kKQStage;
       const uint32_t vsm = sb + OFF_V + (c & 1) * kVStage;
 
-      // [K;Q] S -> TM_KQS (K S in lanes 0-63, Q S in lanes 64-127)
+      // (KS|QS)^T = St [K;Q]^T -> TM_KQS: A = bf16 St from TMEM (8 columns per
+      // K=16 step), B = the [K;Q] rows of the stage (K-major)
       MPHASE(12)
       if (!(ok = wait_bar(RDY_S, par))) break;
       MPHASE(0)
-      if (DEBUG && dbg_cta && c == p.dbg_chunk + 1) p.debug[DBG_EV + 85] = float(clock64() - t_base);
+      if (DEBUG && dbg_cta && c == p.dbg_chunk + 3) p.debug[DBG_EV + 85] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
-        mma_bf16_ss(tmem + TM_KQS, sdesc_sw128(kq + kb * 16384 + kin, 16, 1024),
-                    sdesc_sw128(sb + OFF_ST + kb * 16384 + kin, 16, 1024), idesc_kqs, ks > 0);
+        mma_bf16_ts(tmem + TM_KQS, tmem + TM_SB + 8 * ks,
+                    sdesc_sw128(kq + kb * 16384 + kin, 16, 1024), idesc_kqs, ks > 0);
       }
       mma_commit(&bars[BAR_KQS]);
       MPHASE(1)
-      // Vn_part = T~ V - T^ (K S) -> TM_VN (the compute warps have replaced the
-      // S tile by the bf16 K S tile)
+      // Vn^T (without beta V) = V^T T~^T - (KS)^T T^^T -> TM_VN
       if (!(ok = wait_bar(RDY_T, par))) break;
       MPHASE(2)
+      // the output tile of chunk c-1 (full: only a sequence's last chunk can be
+      // partial) is complete and fenced by every compute thread before RDY_T
+      if (c > 0 && p.tma_out) {
+        const int tp = static_cast<int>(bos + static_cast<int64_t>(c - 1) * kChunk);
+        tma_store_3d(&tm_o, smem + OFF_O, 0, h, tp);
+        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, tp);
+        bulk_commit();
+      }
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_TB + ks * 2048, 8192, 1024),
-                    sdesc_sw128(vsm + ks * 2048, 8192, 1024), idesc_tv, ks > 0);
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(vsm + ks * 2048, 8192, 1024),
+                    sdesc_sw128(sb + OFF_TB + ks * 2048, 8192, 1024), idesc_vt, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024),
-                    sdesc_sw128(sb + OFF_ST + ks * 2048, 8192, 1024), idesc_tks, 1);
+        mma_bf16_ts(tmem + TM_VN, tmem + TM_KSB + 8 * ks,
+                    sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024), idesc_kst, 1);
       mma_commit(&bars[BAR_M3]);
       MPHASE(3)
       // [K;Q]K^T of the next chunk runs while the compute warps drain Vn
       if (c + 1 < nchunks && !(ok = mma1(c + 1))) break;
-      // P Vn -> lanes 64-127 of TM_VN (M=128 with P as A rows 64-127; rows
-      // 0-63 read don't-care bytes below the P tile, their results are unused);
-      // St += Vd_hi^T K + Vd_lo^T K
+      // (P Vn)^T = Vn^T P^T -> TM_VN; St += Vd_hi^T K + Vd_lo^T K
       if (!(ok = wait_bar(RDY_V, par))) break;
       MPHASE(8)
-      const bool ev = DEBUG && dbg_cta && c == p.dbg_chunk;
+      const bool ev = DEBUG && dbg_cta && c == p.dbg_chunk + 2;
       if (ev) p.debug[DBG_EV + 80] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(sb + OFF_P - 8192 + ks * 32, 16, 1024),
-                    sdesc_sw128(sb + OFF_VN + ks * 2048, 8192, 1024), idesc_pv, ks > 0);
+        mma_bf16_ts(tmem + TM_VN, tmem + TM_VNB + 8 * ks, sdesc_sw128(sb + OFF_P + ks * 32, 16, 1024),
+                    idesc_pv, ks > 0);
+      bulk_wait_read_all();  // output tile read out before BAR_PV lets the epilogue rewrite it
       mma_commit(&bars[BAR_PV]);
       MPHASE(9)
       if (ev) p.debug[DBG_EV + 81] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VH + ks * 2048, 8192, 1024),
-                    sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_st, 1);
+        mma_bf16_ts(tmem + TM_ST, tmem + TM_VDH + 8 * ks, sdesc_sw128(kq + ks * 2048, 16384, 1024),
+                    idesc_st, 1);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_ST, sdesc_sw128(sb + OFF_VL + ks * 2048, 8192, 1024),
-                    sdesc_sw128(kq + ks * 2048, 16384, 1024), idesc_st, 1);
+        mma_bf16_ts(tmem + TM_ST, tmem + TM_VDL + 8 * ks, sdesc_sw128(kq + ks * 2048, 16384, 1024),
+                    idesc_st, 1);
       mma_commit(&bars[BAR_ST]);
       MPHASE(10)
       if (ev) p.debug[DBG_EV + 82] = float(clock64() - t_base);
@@ -863,7 +891,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) p.debug[DBG_MCLK + i] = static_cast<float>(mclk[i]);
     }
 #undef MPHASE
-    // drain the tensor pipe and any loads still in flight before the CTA exits
+    // drain the tensor pipe, the output stores and any loads still in flight
+    // before the CTA exits
+    bulk_wait_all();
     mma_commit(&bars[BAR_END]);
     if (!mbar_wait(&bars[BAR_END], 0, kTimeoutNs)) ok = false;
     for (int cc = tma_done; cc < tma_issued; ++cc)

@@ -84,7 +84,7 @@ def main():
         print(f"  {name:32s} {v:8.0f}  {100 * v / tot:5.1f}%")
     iv = events["issue"]
     t0 = iv[0]
-    print(f"handoff timestamps around chunk {a.chunk} (cycles after the issue thread saw the Vn tiles):")
+    print(f"handoff timestamps around chunk {a.chunk + 2} (cycles after the issue thread saw the Vn tiles):")
     for name, v in zip(["PV committed", "state update committed", "state update seen done",
                         "next loads issued", "next S tile seen"], iv[1:]):
         print(f"  issue: {name:28s} {v - t0:8.0f}")
