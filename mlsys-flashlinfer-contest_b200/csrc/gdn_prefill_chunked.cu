@@ -80,7 +80,7 @@ constexpr uint32_t OFF_MISC = OFF_O + 16384;
 // Per-token tables of one chunk (floats), double-buffered by chunk parity.
 constexpr int G_GAM = 0;     // gamma_t * log2(e) (cumulative log-decay)
 constexpr int G_BET = 64;    // beta_t (0 past the end of the sequence)
-constexpr int G_COLF = 128;  // 2^(gamma_{16 floor(t/16)} - gamma_t): column factor of e^{gamma_i - gamma_j}
+constexpr int G_D = 128;     // 2^(gamma_t - gamma_{t-1}): per-token decay factor (1 past the end)
 constexpr int G_DEC = 192;   // 2^(gamma_63 - gamma_t) for valid tokens, else 0
 constexpr int G_EG = 256;    // scale * 2^gamma_t
 constexpr int G_BE = 320;    // beta_t * 2^gamma_t
@@ -305,7 +305,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float gt[2] = {(incl - pair + lg[0]) * kLog2e, incl * kLog2e};
       const float g63 = __shfl_sync(0xffffffffu, gt[1], 31);
-      const float gref = __shfl_sync(0xffffffffu, gt[0], lane & ~7);  // token 16 floor(t/16)
       float* gb = gates_buf + (cc & 1) * kGateFloats;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -313,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float eg = ex2_ftz(gt[e]);
         gb[G_GAM + t] = gt[e];
         gb[G_BET + t] = bt[e];
-        gb[G_COLF + t] = ex2_ftz(gref - gt[e]);
+        gb[G_D + t] = ex2_ftz(lg[e] * kLog2e);
         gb[G_DEC + t] = valid[e] ? ex2_ftz(g63 - gt[e]) : 0.f;
         gb[G_EG + t] = p.scale * eg;
         gb[G_BE + t] = bt[e] * eg;
@@ -393,26 +392,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(v);
         PHASE(4)
-        // e^{gamma_i - gamma_j} = rf_i * colf_j with the block's first column as
-        // reference (one ex2 per row instead of one per element), unless the
-        // decay across the 16-column block is too steep for the factors' range.
+        // e^{gamma_i - gamma_j} for this block's 16 columns, walking down from
+        // the highest column j <= i with e(j-1) = e(j) d_j, d_j = e^{gamma_j -
+        // gamma_{j-1}} <= 1: one ex2 per row, the rest on the FMA pipe, and no
+        // overflow whatever the decay (columns above the diagonal are masked).
         const int r0 = 16 * cq;
-        const bool factor = gam[r0] - gam[r0 + 15] <= 64.f;  // CTA-uniform per block
-        const float rf = ex2_ftz(gi - gam[r0]);               // <= 1 wherever unmasked
+        float dd[16];
+        load_table16(gam + G_D + r0, dd);
+        float e = (r0 + 15 <= i) ? ex2_ftz(gi - gam[r0 + 15]) : 1.f;
         float ef[16];
-        if (factor) {
-          const float4* cf = reinterpret_cast<const float4*>(gam + G_COLF + r0);
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const float4 x = cf[q4];
-            ef[4 * q4] = rf * x.x;
-            ef[4 * q4 + 1] = rf * x.y;
-            ef[4 * q4 + 2] = rf * x.z;
-            ef[4 * q4 + 3] = rf * x.w;
-          }
-        } else {
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) ef[jj] = ex2_ftz(gi - gam[r0 + jj]);
+        for (int jj = 15; jj >= 0; --jj) {
+          ef[jj] = e;
+          e = (r0 + jj > i) ? 1.f : e * dd[jj];
         }
         if (quarter < 2) {
           const float bi = bet[i];
