@@ -14,9 +14,10 @@
 //   T     = (I + A)^-1                         (fp32, CUDA cores + mma.sync, blocks of 16)
 //   (KS|QS)^T = St [K;Q]^T                     (tcgen05, A = bf16 St from TMEM, right after
 //                                               the state is read: overlaps A/P and the inverse)
-//   Vn^T  = V^T T~^T - (KS)^T T^^T + beta (.) V^T    (U - W S with W S = T^ (K S);
-//           T~ = T_off diag(beta), T^ = T diag(beta e^gamma); the unit diagonal of T is
-//           applied exactly in fp32 as beta (.) V when Vn is drained)
+//   Vn^T  = V^T T~^T + V^T Bl - (KS)^T T^^T    (U - W S with W S = T^ (K S), one tcgen05
+//           accumulator; T~ = T diag(beta) with the diagonal beta rounded to bf16, Bl =
+//           diag(beta - bf16(beta)), so beta V enters with ~2^-17 relative error;
+//           T^ = T diag(beta e^gamma))
 //   O^T   = scale (e^{gamma_t} (QS)^T + Vn^T P^T)   (tcgen05, A = bf16 Vn^T from TMEM)
 //   St   <- e^{gamma_63} St + Vd^T K,  Vd = e^{gamma_63 - gamma_t} Vn as bf16 hi + lo (two
 //           MMAs with A from TMEM) so the state update keeps ~16 mantissa bits.
@@ -67,9 +68,11 @@ constexpr uint32_t OFF_V = OFF_KQ + 2 * kKQStage;  // 2 stages
 constexpr uint32_t OFF_P = OFF_V + 2 * kVStage;    // P: [t 64][128 B] (K-major B of Vn^T P^T)
 constexpr uint32_t OFF_TB = OFF_P + 8192;          // T~ = T_off diag(beta): row s = column s (MN-major B)
 constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T^ = T diag(beta e^gamma), same layout
+constexpr uint32_t OFF_BL = OFF_TG + 8192;         // diag(beta - bf16(beta)), same layout (zero
+                                                   // off the diagonal: cleared once per CTA)
 constexpr int kAtPitch = 72;   // fp32 row pitch of A^T (72 = 8 mod 32: conflict-free tf32 A fragments)
 constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict-free B fragments)
-constexpr uint32_t OFF_AT = OFF_TG + 8192;                // fp32 A^T [64][72]
+constexpr uint32_t OFF_AT = OFF_BL + 8192;                // fp32 A^T [64][72]
 constexpr uint32_t OFF_TC = OFF_AT + 64 * kAtPitch * 4;   // fp32 T^T [64][68]
 constexpr uint32_t OFF_MC = OFF_TC + 64 * kTcPitch * 4;   // fp32 (A21 T11)^T [32][36]
 constexpr uint32_t OFF_XC = OFF_MC + 32 * 36 * 4;         // fp32 level-1 products, 4 x [8][20]
@@ -92,7 +95,7 @@ constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBarOff + 256 + 1024;  // + slack
 constexpr uint32_t TM_ST = 0;     // St [v][k] fp32
 constexpr uint32_t TM_KQS = 128;  // [K S | Q S]^T fp32: cols 0-63 (KS)^T[v][s], 64-127 (QS)^T[v][t]
 constexpr uint32_t TM_D1 = 256;   // [K;Q] K^T fp32 [128 rows][64]
-constexpr uint32_t TM_VN = 320;   // Vn^T (without beta V) fp32 [v][t], then (P Vn)^T [v][t]
+constexpr uint32_t TM_VN = 320;   // Vn^T fp32 [v][t], then (P Vn)^T [v][t]
 constexpr uint32_t TM_SB = 384;   // A operand: St as bf16 [v][k] (64 cols), then
 constexpr uint32_t TM_VDH = 384;  //   Vd_hi^T bf16 [v][t] (32 cols)
 constexpr uint32_t TM_VDL = 416;  //   Vd_lo^T bf16 [v][t] (32 cols)
@@ -331,6 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       compute_gates(0);
       if (Ltot > kChunk) prefetch_gates(1);
     }
+    for (int i = tid; i < 8192 / 16; i += kComputeThreads)  // Bl: zero off the diagonal
+      sts128(sb + OFF_BL + 16 * i, 0u, 0u, 0u, 0u);
     bool aborted = false;
 
     for (int c = 0; c < nchunks; ++c) {
@@ -568,11 +573,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_sync(kComputeBar, kComputeThreads);
       PHASE(7)
       {
-        // T~ = T_off diag(beta) and T^ = T diag(beta e^gamma) as bf16 tiles in
-        // which row j holds column j of T: MN-major B operands (K = s rows, N = t
-        // contiguous) of V^T T~^T and (KS)^T T^^T.  T~ leaves out the unit
-        // diagonal: beta (.) V is added in fp32 when Vn is drained (a bf16 beta_j
-        // on the diagonal would cost ~2^-9 relative error on all of U).
+        // T~ = T diag(beta) and T^ = T diag(beta e^gamma) as bf16 tiles in which
+        // row j holds column j of T: MN-major B operands (K = s rows, N = t
+        // contiguous) of V^T T~^T and (KS)^T T^^T.  The diagonal of T~ is beta_j
+        // rounded to bf16; the rounding remainder goes on the diagonal of Bl.
         const int j = tid & 63;
         const bool hat = (tid >> 6) & 1;
         const int part = tid >> 7;  // 16-row quarter of the tile row (2 chunks)
@@ -586,9 +590,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float4 x1 = *reinterpret_cast<const float4*>(trow + ch * 8 + 4);
           float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = (!hat && ch * 8 + e == j) ? 0.f : x[e] * sc;
+          for (int e = 0; e < 8; ++e) x[e] *= sc;
           sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
                  pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+        }
+        if (!hat && part == (j >> 4)) {  // the thread holding the diagonal element
+          const float blo = bet[j] - bf16_lo(pack_bf16x2(bet[j], 0.f));
+          const uint32_t w = pack_bf16x2(blo, 0.f);  // bf16(blo) in the low half
+          sts32(sb + OFF_BL + sw128_off(j, j >> 3) + 4 * ((j & 7) >> 1), (j & 1) ? (w << 16) : w);
         }
         if (dbg && !hat) {
           for (int i = 16 * part; i < 16 * part + 16; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
@@ -603,22 +612,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_mma(BAR_M3, par);
       PHASE(11)
 
-      // ---- Vn^T = (V^T T~^T - (KS)^T T^^T) + beta (.) V^T -> bf16 A operand
-      //      of (P Vn)^T; Vd^T = e^{g63 - g_t} Vn^T -> hi/lo bf16 A operands
-      //      of the state update.  Lane v, tokens t in [16 cq, 16 cq + 16). ---
+      // ---- Vn^T -> bf16 A operand of (P Vn)^T; Vd^T = e^{g63 - g_t} Vn^T ->
+      //      hi/lo bf16 A operands of the state update.  Lane v, tokens t in
+      //      [16 cq, 16 cq + 16). ---------------------------------------------
       {
         float x[16];
         tmem_ld16(tmem + lane_base + TM_VN + 16 * cq, x);
         tmem_wait_ld();
         reg_fence(x);
-        // V[t][v] in the V tile: block v/64, row t, 16-byte chunk (v%64)/8 ^ (t%8);
-        // read as the 32-bit word of the (even, odd) v pair (16-bit shared
-        // accesses are much slower), this lane's half selected
-        const uint32_t vrow = vsm + (rowv >> 6) * 8192 + 4 * ((rowv & 7) >> 1);
-        const uint32_t vshift = (rowv & 1) ? 0u : 16u;
-        const int vch = (rowv & 63) >> 3;
-        float bt[16], dc[16];  // beta_t and 2^(g63 - g_t) of this warp's 16 tokens
-        load_table16(bet + 16 * cq, bt);
+        float dc[16];  // 2^(g63 - g_t) of this warp's 16 tokens (0 past the end)
         load_table16(gam + G_DEC + 16 * cq, dc);
         uint32_t wn[8], wh[8], wl[8];
 #pragma unroll
@@ -627,9 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int f = 0; f < 2; ++f) {
             const int t = 16 * cq + 2 * e + f;
-            const float vt =
-                __uint_as_float((lds32(vrow + t * 128 + ((vch ^ (t & 7)) << 4)) << vshift) & 0xFFFF0000u);
-            xv[f] = (t < L) ? fmaf(bt[2 * e + f], vt, x[2 * e + f]) : 0.f;
+            xv[f] = (t < L) ? x[2 * e + f] : 0.f;
             d[f] = xv[f] * dc[2 * e + f];
           }
           wn[e] = pack_bf16x2(xv[0], xv[1]);
@@ -822,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(&bars[BAR_KQS]);
       MPHASE(1)
-      // Vn^T (without beta V) = V^T T~^T - (KS)^T T^^T -> TM_VN
+      // Vn^T = V^T T~^T + V^T Bl - (KS)^T T^^T -> TM_VN
       if (!(ok = wait_bar(RDY_T, par))) break;
       MPHASE(2)
       // the output tile of chunk c-1 (full: only a sequence's last chunk can be
@@ -837,6 +837,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128(vsm + ks * 2048, 8192, 1024),
                     sdesc_sw128(sb + OFF_TB + ks * 2048, 8192, 1024), idesc_vt, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(vsm + ks * 2048, 8192, 1024),
+                    sdesc_sw128(sb + OFF_BL + ks * 2048, 8192, 1024), idesc_vt, 1);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ts(tmem + TM_VN, tmem + TM_KSB + 8 * ks,
