@@ -397,6 +397,9 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
                         "hbm_peak_GBps": hbm_peak, "tc_peak_TFLOPs": tc_burst,
                         "roofline_ms": round(max(t_hbm, t_tc) * 1e3, 4),
                         "frac": round(max(t_hbm, t_tc) * 1e3 / ms, 4), "peak_source": peak_src}}
+    full = profiled_traffic("gdn_prefill_chunked_config3.md")  # ncu, 1-GPU config-3 launch
+    if full is not None and args.prefill_seqs == 4 and args.prefill_len == 16384:
+        res["roofline"]["traffic"] = int(full * hv / HV)  # this rank's heads
     if dist and world > 1:
         from gdn_b200.sharding import all_gather_heads
         for _ in range(2):
