@@ -276,15 +276,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Gates of one chunk from raw a/b values held by warp 1 (two tokens per lane):
     // log-decay, its inclusive scan (gamma, stored in log2 units), beta and the
     // derived per-token tables.
-    float ga_raw[2] = {0.f, 0.f}, gb_raw[2] = {0.f, 0.f};
+    // raw bf16 bits: nothing consumes a prefetched value until the next
+    // compute_gates, so the global loads stay in flight meanwhile
+    unsigned short ga_raw[2] = {0, 0}, gb_raw[2] = {0, 0};
     auto prefetch_gates = [&](int cc) {
       const int64_t t0c = bos + static_cast<int64_t>(cc) * kChunk;
+      const unsigned short* pa = reinterpret_cast<const unsigned short*>(p.a);
+      const unsigned short* pb = reinterpret_cast<const unsigned short*>(p.b);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int64_t t = t0c + 2 * lane + e;
         if (t < eos) {
-          ga_raw[e] = __bfloat162float(p.a[t * p.Hv + h]);
-          gb_raw[e] = __bfloat162float(p.b[t * p.Hv + h]);
+          ga_raw[e] = pa[t * p.Hv + h];
+          gb_raw[e] = pb[t * p.Hv + h];
         }
       }
     };
@@ -296,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         valid[e] = 2 * lane + e < Lc;
-        lg[e] = valid[e] ? neg_exp_A * softplus_t20_fast(ga_raw[e] + dt_bias_h) : 0.f;
-        bt[e] = valid[e] ? sigmoid_fast(gb_raw[e]) : 0.f;
+        lg[e] = valid[e] ? neg_exp_A * softplus_t20_fast(bf16_bits_to_f32(ga_raw[e]) + dt_bias_h) : 0.f;
+        bt[e] = valid[e] ? sigmoid_fast(bf16_bits_to_f32(gb_raw[e])) : 0.f;
       }
       const float pair = lg[0] + lg[1];
       float incl = pair;
@@ -788,12 +792,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!wait_bar(BAR_TMA0 + s, static_cast<uint32_t>((cc >> 1) & 1))) return false;
       tma_done = cc + 1;
       MPHASE(6)
-      const uint32_t kq = sb + OFF_KQ + s * kKQStage;
+      const uint32_t kq16 = (sb + OFF_KQ + s * kKQStage) >> 4;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-        mma_bf16_ss(tmem + TM_D1, sdesc_sw128(kq + off, 16, 1024), sdesc_sw128(kq + off, 16, 1024),
-                    idesc_d1, ks > 0);
+        const uint64_t d = sdesc_sw128_f(kq16 + ((ks >> 2) * 16384 + (ks & 3) * 32) / 16, 16, 1024);
+        mma_bf16_ss(tmem + TM_D1, d, d, idesc_d1, ks > 0);
       }
       mma_commit(&bars[BAR_M1]);
       MPHASE(7)
@@ -805,8 +808,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = mma1(0);
     for (int c = 0; ok && c < nchunks; ++c) {
       const uint32_t par = static_cast<uint32_t>(c & 1);
-      const uint32_t kq = sb + OFF_KQ + (c & 1) * kKQStage;
-      const uint32_t vsm = sb + OFF_V + (c & 1) * kVStage;
+      // descriptor start fields (address / 16) of this chunk's operands
+      const uint32_t kq16 = (sb + OFF_KQ + (c & 1) * kKQStage) >> 4;
+      const uint32_t v16 = (sb + OFF_V + (c & 1) * kVStage) >> 4;
+      const uint32_t sb16 = sb >> 4;
 
       // (KS|QS)^T = St [K;Q]^T -> TM_KQS: A = bf16 St from TMEM (8 columns per
       // K=16 step), B = the [K;Q] rows of the stage (K-major)
@@ -818,7 +823,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < 8; ++ks) {
         const uint32_t kb = ks >> 2, kin = (ks & 3) * 32;
         mma_bf16_ts(tmem + TM_KQS, tmem + TM_SB + 8 * ks,
-                    sdesc_sw128(kq + kb * 16384 + kin, 16, 1024), idesc_kqs, ks > 0);
+                    sdesc_sw128_f(kq16 + (kb * 16384 + kin) / 16, 16, 1024), idesc_kqs, ks > 0);
       }
       mma_commit(&bars[BAR_KQS]);
       MPHASE(1)
@@ -835,16 +840,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(vsm + ks * 2048, 8192, 1024),
-                    sdesc_sw128(sb + OFF_TB + ks * 2048, 8192, 1024), idesc_vt, ks > 0);
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
+                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_vt, ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128(vsm + ks * 2048, 8192, 1024),
-                    sdesc_sw128(sb + OFF_BL + ks * 2048, 8192, 1024), idesc_vt, 1);
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
+                    sdesc_sw128_f(sb16 + (OFF_BL + ks * 2048) / 16, 8192, 1024), idesc_vt, 1);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ts(tmem + TM_VN, tmem + TM_KSB + 8 * ks,
-                    sdesc_sw128(sb + OFF_TG + ks * 2048, 8192, 1024), idesc_kst, 1);
+                    sdesc_sw128_f(sb16 + (OFF_TG + ks * 2048) / 16, 8192, 1024), idesc_kst, 1);
       mma_commit(&bars[BAR_M3]);
       MPHASE(3)
       // [K;Q]K^T of the next chunk runs while the compute warps drain Vn
@@ -856,19 +861,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ev) p.debug[DBG_EV + 80] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ts(tmem + TM_VN, tmem + TM_VNB + 8 * ks, sdesc_sw128(sb + OFF_P + ks * 32, 16, 1024),
-                    idesc_pv, ks > 0);
+        mma_bf16_ts(tmem + TM_VN, tmem + TM_VNB + 8 * ks,
+                    sdesc_sw128_f(sb16 + (OFF_P + ks * 32) / 16, 16, 1024), idesc_pv, ks > 0);
       bulk_wait_read_all();  // output tile read out before BAR_PV lets the epilogue rewrite it
       mma_commit(&bars[BAR_PV]);
       MPHASE(9)
       if (ev) p.debug[DBG_EV + 81] = float(clock64() - t_base);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ts(tmem + TM_ST, tmem + TM_VDH + 8 * ks, sdesc_sw128(kq + ks * 2048, 16384, 1024),
+        mma_bf16_ts(tmem + TM_ST, tmem + TM_VDH + 8 * ks, sdesc_sw128_f(kq16 + ks * 128, 16384, 1024),
                     idesc_st, 1);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ts(tmem + TM_ST, tmem + TM_VDL + 8 * ks, sdesc_sw128(kq + ks * 2048, 16384, 1024),
+        mma_bf16_ts(tmem + TM_ST, tmem + TM_VDL + 8 * ks, sdesc_sw128_f(kq16 + ks * 128, 16384, 1024),
                     idesc_st, 1);
       mma_commit(&bars[BAR_ST]);
       MPHASE(10)

@@ -164,6 +164,15 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
+// The same descriptor from a precomputed start field (saddr >> 4, a 16-byte
+// aligned address below 256 KiB): the high word and the LBO bits are constants,
+// so a k-step offset costs one 32-bit add.
+__device__ __forceinline__ uint64_t sdesc_sw128_f(uint32_t start16, uint32_t lbo, uint32_t sbo) {
+  const uint32_t lo = start16 | (((lbo >> 4) & 0x3FFFu) << 16);
+  const uint32_t hi = ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
 // Instruction descriptor, kind::f16 with bf16 A/B and fp32 accumulation.
 //   [4,6) D fmt=1 (f32), [7,10) A fmt=1 (bf16), [10,13) B fmt=1 (bf16),
 //   13 negate A, 15 A MN-major, 16 B MN-major, [17,23) N>>3, [24,29) M>>4.
