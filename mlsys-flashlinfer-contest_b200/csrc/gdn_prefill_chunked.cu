@@ -75,7 +75,7 @@ constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict
 constexpr uint32_t OFF_AT = OFF_BL + 8192;                // fp32 A^T [64][72]
 constexpr uint32_t OFF_TC = OFF_AT + 64 * kAtPitch * 4;   // fp32 T^T [64][68]
 constexpr uint32_t OFF_MC = OFF_TC + 64 * kTcPitch * 4;   // fp32 (A21 T11)^T [32][36]
-constexpr uint32_t OFF_XC = OFF_MC + 32 * 36 * 4;         // fp32 level-1 products, 4 x [8][20]
+constexpr uint32_t OFF_XC = OFF_MC + 32 * 36 * 4;         // fp32 level-1 products, 2 x [16][20]
 constexpr uint32_t OFF_O = (OFF_XC + 4 * 160 * 4 + 1023) / 1024 * 1024;  // output tile
 // [cb 2][t 64][128 B] (TMA store source; written by the output epilogue, stored
 // by the issue thread once the next chunk's T tiles are signalled)
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* At = reinterpret_cast<float*>(smem + OFF_AT);   // A column-major: At[k][i] = A[i][k]
   float* Tcm = reinterpret_cast<float*>(smem + OFF_TC);  // Tcm[j][i] = T[i][j]
   float* Mcm = reinterpret_cast<float*>(smem + OFF_MC);  // (A21 T11) column-major, pitch 36
-  float* Xcm = reinterpret_cast<float*>(smem + OFF_XC);  // 4 x [8][20] level-1 products
+  float* Xcm = reinterpret_cast<float*>(smem + OFF_XC);  // 2 x [16][20] level-1 products
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3;    // TMEM lane quarter this warp may access
@@ -348,7 +348,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t t0 = bos + static_cast<int64_t>(c) * kChunk;
       const int L = static_cast<int>(min(static_cast<int64_t>(kChunk), eos - t0));
       const bool dbg = dbg_cta && c == p.dbg_chunk;
-      const uint32_t vsm = sb + OFF_V + stage * kVStage;
 
       // previous chunk's state update done: St is final and its TMEM operands
       // are free.  The barrier also publishes this chunk's gates (warp 1).
@@ -443,29 +442,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_sync(kComputeBar, kComputeThreads);
       PHASE(6)
 
-      // ---- (KS)^T -> bf16 A operand of the Vn MMAs: lanes v, tokens s in
-      //      [16 cq, 16 cq + 16); warps 14-15 convert after the level-0 inverse.
-      auto convert_ks = [&]() {
-        wait_mma(BAR_KQS, par);
+      // ---- (KS)^T -> bf16 A operand of the Vn MMAs: lanes v, 16-token column
+      //      groups; warps 10-11 also convert the groups of warps 14-15, which
+      //      run the level-0/1 inverse meanwhile.
+      auto convert_ks = [&](int grp) {
         float v[16];
-        tmem_ld16(tmem + lane_base + TM_KQS + 16 * cq, v);
+        tmem_ld16(tmem + lane_base + TM_KQS + 16 * grp, v);
         tmem_wait_ld();
         reg_fence(v);
         uint32_t w[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
-        tmem_st8u(tmem + lane_base + TM_KSB + 8 * cq, w);
-        tmem_wait_st();
+        tmem_st8u(tmem + lane_base + TM_KSB + 8 * grp, w);
         if (dbg)
-          for (int i = 0; i < 16; ++i) p.debug[DBG_KS + (16 * cq + i) * 128 + rowv] = v[i];
+          for (int i = 0; i < 16; ++i) p.debug[DBG_KS + (16 * grp + i) * 128 + rowv] = v[i];
       };
 
       // ---- T = (I + A)^-1, fp32, blocks of 16:
-      //      level 0: the four diagonal blocks by right-looking elimination;
-      //      level 1: T10 = -T11 A10 T00, T32 = -T33 A32 T22 (mma.sync);
+      //      level 0: the four diagonal blocks by right-looking elimination and
+      //      level 1: T10 = -T11 A10 T00 (warp 14), T32 = -T33 A32 T22 (warp 15),
+      //      each warp on its own blocks (mma.sync, warp-local);
       //      level 2: [T20 T21; T30 T31] = -T22' (A21' T11'), primes = 32x32 halves.
       if (warp < kL0Warp) {
-        convert_ks();
+        wait_mma(BAR_KQS, par);
+        convert_ks(cq);
+        if (cq == 2 && quarter >= 2) convert_ks(3);
+        tmem_wait_st();
       } else {
         const int u = tid - 32 * kL0Warp;
         const int b = u >> 4, j = u & 15, b0 = 16 * b;
@@ -492,49 +494,51 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
         for (int q = 0; q < 4 * b; ++q)  // rows above the diagonal block are zero
           *reinterpret_cast<float4*>(tcol + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
+              __syncwarp();
+        // level 1 of this warp's pair: X = A_IJ T_JJ, then T_IJ = -T_II X
+        // (mma.sync m16n8k8, tf32; X through warp-private smem for the
+        // fragment layout)
+        const int pr = warp - kL0Warp;
+        const int J0 = 32 * pr, I0 = J0 + 16;
+        float* xw = Xcm + pr * 320;  // X column-major: X[r][j] at xw[j * 20 + r]
+        float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+        auto l1a_step = [&](float* acc, int nt, int k0) {
+          const float* ar = At + (J0 + k0 + tq) * kAtPitch + I0 + g;           // A[I0+g][J0+k0+t]
+          const float* br = Tcm + (J0 + 8 * nt + g) * kTcPitch + J0 + k0 + tq;  // T[J0+k0+t][J0+8nt+g]
+          mma_tf32_16x8x8(acc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
+                          to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+        };
+        l1a_step(c0, 0, 0);
+        l1a_step(c0, 0, 8);
+        l1a_step(c1, 1, 8);  // T_JJ[k][n] = 0 for k < n: columns 8-15 need k >= 8 only
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float* cc = nt ? c1 : c0;
+          xw[(8 * nt + 2 * tq) * 20 + g] = cc[0];
+          xw[(8 * nt + 2 * tq + 1) * 20 + g] = cc[1];
+          xw[(8 * nt + 2 * tq) * 20 + g + 8] = cc[2];
+          xw[(8 * nt + 2 * tq + 1) * 20 + g + 8] = cc[3];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          float dacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int k0 = 0; k0 < 16; k0 += 8) {
+            const float* ar = Tcm + (I0 + k0 + tq) * kTcPitch + I0 + g;  // T[I0+g][I0+k0+t]
+            const float* br = xw + (8 * nt + g) * 20 + k0 + tq;          // X[k0+t][8nt+g]
+            mma_tf32_16x8x8(dacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kTcPitch]),
+                            to_tf32(ar[4 * kTcPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+          }
+          float* tc = Tcm + (J0 + 8 * nt + 2 * tq) * kTcPitch + I0 + g;  // T[I0+r][J0+8nt+j]
+          tc[0] = -dacc[0];
+          tc[kTcPitch] = -dacc[1];
+          tc[8] = -dacc[2];
+          tc[kTcPitch + 8] = -dacc[3];
+        }
       }
       named_sync(kComputeBar, kComputeThreads);
       PHASE(15)
-      // level 1 on the tensor cores (mma.sync m16n8k8, tf32): warp w < 4 owns
-      // pair pr = w/2 ((I, J) = (1, 0) or (3, 2)) and 8-column tile nt = w%2 of
-      // T_IJ: X = A_IJ T_JJ[:, tile], then T_IJ[:, tile] = -T_II X.  X goes
-      // through warp-private smem for the fragment layout (__syncwarp only).
-      if (warp < 4) {
-        const int pr = warp >> 1, nt = warp & 1;
-        const int J0 = 32 * pr, I0 = J0 + 16;
-        float* xw = Xcm + warp * 160;  // X column-major: X[r][j] at xw[j * 20 + r]
-        float cacc[4] = {0.f, 0.f, 0.f, 0.f};
-        auto l1a_step = [&](int k0) {
-          const float* ar = At + (J0 + k0 + tq) * kAtPitch + I0 + g;           // A[I0+g][J0+k0+t]
-          const float* br = Tcm + (J0 + 8 * nt + g) * kTcPitch + J0 + k0 + tq;  // T[J0+k0+t][J0+8nt+g]
-          mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
-                          to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
-        };
-        if (nt == 0) l1a_step(0);  // T_JJ[k][n] = 0 for k < n: tile 1 needs k >= 8 only
-        l1a_step(8);
-        xw[(2 * tq) * 20 + g] = cacc[0];
-        xw[(2 * tq + 1) * 20 + g] = cacc[1];
-        xw[(2 * tq) * 20 + g + 8] = cacc[2];
-        xw[(2 * tq + 1) * 20 + g + 8] = cacc[3];
-        __syncwarp();
-        float dacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k0 = 0; k0 < 16; k0 += 8) {
-          const float* ar = Tcm + (I0 + k0 + tq) * kTcPitch + I0 + g;  // T[I0+g][I0+k0+t]
-          const float* br = xw + g * 20 + k0 + tq;                     // X[k0+t][g]
-          mma_tf32_16x8x8(dacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kTcPitch]),
-                          to_tf32(ar[4 * kTcPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
-        }
-        float* tc = Tcm + (J0 + 8 * nt + 2 * tq) * kTcPitch + I0 + g;  // T[I0+r][J0+8nt+j] at Tcm[col][row]
-        tc[0] = -dacc[0];
-        tc[kTcPitch] = -dacc[1];
-        tc[8] = -dacc[2];
-        tc[kTcPitch + 8] = -dacc[3];
-      } else if (warp >= kL0Warp) {
-        convert_ks();
-      }
-      named_sync(kComputeBar, kComputeThreads);
-      PHASE(16)
       // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
       // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after):
       // warp w < 8 computes the 16x8 output tile (row tile w/4, column tile w%4).
