@@ -400,19 +400,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(v);
         PHASE(4)
-        // e^{gamma_i - gamma_j} for this block's 16 columns, walking down from
-        // the highest column j <= i with e(j-1) = e(j) d_j, d_j = e^{gamma_j -
-        // gamma_{j-1}} <= 1: one ex2 per row, the rest on the FMA pipe, and no
-        // overflow whatever the decay (columns above the diagonal are masked).
+        // e^{gamma_i - gamma_j} for this block's 16 columns, walking down each
+        // group of 4 from its highest column j <= i with e(j-1) = e(j) d_j,
+        // d_j = e^{gamma_j - gamma_{j-1}} <= 1: one ex2 per group, the rest on
+        // the FMA pipe, and no overflow whatever the decay (columns above the
+        // diagonal are masked).
         const int r0 = 16 * cq;
         float dd[16];
         load_table16(gam + G_D + r0, dd);
-        float e = (r0 + 15 <= i) ? ex2_ftz(gi - gam[r0 + 15]) : 1.f;
         float ef[16];
 #pragma unroll
-        for (int jj = 15; jj >= 0; --jj) {
-          ef[jj] = e;
-          e = (r0 + jj > i) ? 1.f : e * dd[jj];
+        for (int q = 0; q < 4; ++q) {  // four independent 4-column chains
+          const int top = r0 + 4 * q + 3;
+          float e = (top <= i) ? ex2_ftz(gi - gam[top]) : 1.f;
+#pragma unroll
+          for (int jj = 4 * q + 3; jj >= 4 * q; --jj) {
+            ef[jj] = e;
+            e = (r0 + jj > i) ? 1.f : e * dd[jj];
+          }
         }
         if (quarter < 2) {
           const float bi = bet[i];
