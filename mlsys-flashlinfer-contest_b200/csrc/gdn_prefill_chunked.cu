@@ -14,10 +14,11 @@
 //   T     = (I + A)^-1                         (fp32, CUDA cores + mma.sync, blocks of 16)
 //   (KS|QS)^T = St [K;Q]^T                     (tcgen05, A = bf16 St from TMEM, right after
 //                                               the state is read: overlaps A/P and the inverse)
-//   Vn^T  = V^T T~^T + V^T Bl - (KS)^T T^^T    (U - W S with W S = T^ (K S), one tcgen05
-//           accumulator; T~ = T diag(beta) with the diagonal beta rounded to bf16, Bl =
-//           diag(beta - bf16(beta)), so beta V enters with ~2^-17 relative error;
-//           T^ = T diag(beta e^gamma))
+//   Vn^T  = V^T T~^T + V^T Bl - (KS e^gamma)^T T~^T   (U - W S with W S =
+//           T diag(beta e^gamma) (K S) = T~ diag(e^gamma) (K S), one tcgen05 accumulator;
+//           T~ = T diag(beta) with the diagonal beta rounded to bf16, Bl = diag(beta -
+//           bf16(beta)), so beta V enters with ~2^-17 relative error; the e^gamma row
+//           scaling of K S is applied while K S is converted to a bf16 operand)
 //   O^T   = scale (e^{gamma_t} (QS)^T + Vn^T P^T)   (tcgen05, A = bf16 Vn^T from TMEM)
 //   St   <- e^{gamma_63} St + Vd^T K,  Vd = e^{gamma_63 - gamma_t} Vn as bf16 hi + lo (two
 //           MMAs with A from TMEM) so the state update keeps ~16 mantissa bits.
@@ -67,8 +68,7 @@ constexpr uint32_t OFF_KQ = 0;                     // 2 stages
 constexpr uint32_t OFF_V = OFF_KQ + 2 * kKQStage;  // 2 stages
 constexpr uint32_t OFF_P = OFF_V + 2 * kVStage;    // P: [t 64][128 B] (K-major B of Vn^T P^T)
 constexpr uint32_t OFF_TB = OFF_P + 8192;          // T~ = T_off diag(beta): row s = column s (MN-major B)
-constexpr uint32_t OFF_TG = OFF_TB + 8192;         // T^ = T diag(beta e^gamma), same layout
-constexpr uint32_t OFF_BL = OFF_TG + 8192;         // diag(beta - bf16(beta)), same layout (zero
+constexpr uint32_t OFF_BL = OFF_TB + 8192;         // diag(beta - bf16(beta)), same layout (zero
                                                    // off the diagonal: cleared once per CTA)
 constexpr int kAtPitch = 72;   // fp32 row pitch of A^T (72 = 8 mod 32: conflict-free tf32 A fragments)
 constexpr int kTcPitch = 68;   // fp32 row pitch of T^T (68 = 4 mod 32: conflict-free B fragments)
@@ -86,7 +86,7 @@ constexpr int G_BET = 64;    // beta_t (0 past the end of the sequence)
 constexpr int G_D = 128;     // 2^(gamma_t - gamma_{t-1}): per-token decay factor (1 past the end)
 constexpr int G_DEC = 192;   // 2^(gamma_63 - gamma_t) for valid tokens, else 0
 constexpr int G_EG = 256;    // scale * 2^gamma_t
-constexpr int G_BE = 320;    // beta_t * 2^gamma_t
+constexpr int G_E2 = 320;    // 2^gamma_t
 constexpr int kGateFloats = 384;
 constexpr uint32_t kMiscBarOff = 2 * kGateFloats * 4;  // barriers after both table buffers
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBarOff + 256 + 1024;  // + slack for the 1024 alignment
@@ -131,7 +131,7 @@ struct ChunkParams {
 
 constexpr int kClkSlots = 20;  // phase clock slots per compute warp (debug build)
 // Debug dump layout (floats); the DBG_U block is not written (U is never formed
-// on its own: the kernel computes V^T T~^T - (KS)^T T^^T in one accumulator).
+// on its own: the kernel computes V^T T~^T - (KS e^gamma)^T T~^T in one accumulator).
 constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_T = DBG_P + 4096,
               DBG_U = DBG_T + 4096, DBG_KS = DBG_U + 8192, DBG_VN = DBG_KS + 8192,
               DBG_QS = DBG_VN + 8192, DBG_PV = DBG_QS + 8192, DBG_ST = DBG_PV + 8192,
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         gb[G_D + t] = ex2_ftz(lg[e] * kLog2e);
         gb[G_DEC + t] = valid[e] ? ex2_ftz(g63 - gt[e]) : 0.f;
         gb[G_EG + t] = p.scale * eg;
-        gb[G_BE + t] = bt[e] * eg;
+        gb[G_E2 + t] = eg;
       }
     };
     auto dump_state = [&]() {  // debug: St after the state update of the debug chunk
@@ -453,11 +453,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto convert_ks = [&](int grp) {
         float v[16];
         tmem_ld16(tmem + lane_base + TM_KQS + 16 * grp, v);
+        float e2[16];  // 2^g_s of these 16 tokens
+        load_table16(gam + G_E2 + 16 * grp, e2);
         tmem_wait_ld();
         reg_fence(v);
         uint32_t w[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+        for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2(v[2 * e] * e2[2 * e], v[2 * e + 1] * e2[2 * e + 1]);
         tmem_st8u(tmem + lane_base + TM_KSB + 8 * grp, w);
         if (dbg)
           for (int i = 0; i < 16; ++i) p.debug[DBG_KS + (16 * grp + i) * 128 + rowv] = v[i];
@@ -586,35 +588,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_sync(kComputeBar, kComputeThreads);
       PHASE(7)
       {
-        // T~ = T diag(beta) and T^ = T diag(beta e^gamma) as bf16 tiles in which
-        // row j holds column j of T: MN-major B operands (K = s rows, N = t
-        // contiguous) of V^T T~^T and (KS)^T T^^T.  The diagonal of T~ is beta_j
-        // rounded to bf16; the rounding remainder goes on the diagonal of Bl.
-        const int j = tid & 63;
-        const bool hat = (tid >> 6) & 1;
-        const int part = tid >> 7;  // 16-row quarter of the tile row (2 chunks)
-        const float sc = hat ? gam[G_BE + j] : bet[j];
-        const float* trow = Tcm + j * kTcPitch;
-        const uint32_t dst = sb + (hat ? OFF_TG : OFF_TB);
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          const int ch = 2 * part + c2;
-          const float4 x0 = *reinterpret_cast<const float4*>(trow + ch * 8);
-          const float4 x1 = *reinterpret_cast<const float4*>(trow + ch * 8 + 4);
-          float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] *= sc;
-          sts128(dst + sw128_off(j, ch), pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]),
-                 pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
-        }
-        if (!hat && part == (j >> 4)) {  // the thread holding the diagonal element
+        // T~ = T diag(beta) as a bf16 tile in which row j holds column j of T:
+        // the MN-major B operand (K = s rows, N = t contiguous) of both V^T T~^T
+        // and (KS e^gamma)^T T~^T.  Its diagonal is beta_j rounded to bf16; the
+        // rounding remainder goes on the diagonal of Bl.  Thread: row j, chunk ch.
+        const int j = tid & 63, ch = tid >> 6;
+        const float sc = bet[j];
+        const float* src = Tcm + j * kTcPitch + ch * 8;
+        const float4 x0 = *reinterpret_cast<const float4*>(src);
+        const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+        sts128(sb + OFF_TB + sw128_off(j, ch), pack_bf16x2(x0.x * sc, x0.y * sc),
+               pack_bf16x2(x0.z * sc, x0.w * sc), pack_bf16x2(x1.x * sc, x1.y * sc),
+               pack_bf16x2(x1.z * sc, x1.w * sc));
+        if (ch == (j >> 3)) {  // the thread holding the diagonal element
           const float blo = bet[j] - bf16_lo(pack_bf16x2(bet[j], 0.f));
           const uint32_t w = pack_bf16x2(blo, 0.f);  // bf16(blo) in the low half
           sts32(sb + OFF_BL + sw128_off(j, j >> 3) + 4 * ((j & 7) >> 1), (j & 1) ? (w << 16) : w);
         }
-        if (dbg && !hat) {
-          for (int i = 16 * part; i < 16 * part + 16; ++i) p.debug[DBG_T + i * 64 + j] = trow[i];
-        }
+        if (dbg && ch == 0)
+          for (int i = 0; i < 64; ++i) p.debug[DBG_T + i * 64 + j] = Tcm[j * kTcPitch + i];
       }
       signal(RDY_T, true);  // T tiles and the P tile are read by the tensor pipe
       PHASE(8)
@@ -756,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t idesc_d1 = idesc_bf16(128, 64, false, false);
     const uint32_t idesc_kqs = idesc_bf16(128, 128, false, false);   // St (TMEM) x [K;Q]^T
     const uint32_t idesc_vt = idesc_bf16(128, 64, true, true);       // V^T (smem, MN) x T~^T
-    const uint32_t idesc_kst = idesc_bf16(128, 64, false, true, true);  // -(KS)^T (TMEM) x T^^T
+    const uint32_t idesc_kst = idesc_bf16(128, 64, false, true, true);  // -(KS e^g)^T (TMEM) x T~^T
     const uint32_t idesc_pv = idesc_bf16(128, 64, false, false);     // Vn^T (TMEM) x P^T
     const uint32_t idesc_st = idesc_bf16(128, 128, false, true);     // Vd^T (TMEM) x K
 
@@ -836,7 +828,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(&bars[BAR_KQS]);
       MPHASE(1)
-      // Vn^T = V^T T~^T + V^T Bl - (KS)^T T^^T -> TM_VN
+      // Vn^T = V^T T~^T + V^T Bl - (KS e^gamma)^T T~^T -> TM_VN
       if (!(ok = wait_bar(RDY_T, par))) break;
       MPHASE(2)
       // the output tile of chunk c-1 (full: only a sequence's last chunk can be
@@ -858,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ts(tmem + TM_VN, tmem + TM_KSB + 8 * ks,
-                    sdesc_sw128_f(sb16 + (OFF_TG + ks * 2048) / 16, 8192, 1024), idesc_kst, 1);
+                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_kst, 1);
       mma_commit(&bars[BAR_M3]);
       MPHASE(3)
       // [K;Q]K^T of the next chunk runs while the compute warps drain Vn
