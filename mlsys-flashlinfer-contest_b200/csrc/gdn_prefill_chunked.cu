@@ -76,7 +76,9 @@ constexpr uint32_t OFF_AT = OFF_BL + 8192;                // fp32 A^T [64][72]
 constexpr uint32_t OFF_TC = OFF_AT + 64 * kAtPitch * 4;   // fp32 T^T [64][68]
 constexpr uint32_t OFF_MC = OFF_TC + 64 * kTcPitch * 4;   // fp32 (A21 T11)^T [32][36]
 constexpr uint32_t OFF_XC = OFF_MC + 32 * 36 * 4;         // fp32 level-1 products, 2 x [16][20]
-constexpr uint32_t OFF_O = (OFF_XC + 4 * 160 * 4 + 1023) / 1024 * 1024;  // output tile
+constexpr uint32_t OFF_MC2 = OFF_XC + 2 * 320 * 4;        // second K-half of (A21 T11), columns 0-15
+constexpr uint32_t OFF_TC2 = OFF_MC2 + 32 * 36 * 4;       // second K-half of T rows 48-63, cols 0-31 [32][20]
+constexpr uint32_t OFF_O = (OFF_TC2 + 32 * 20 * 4 + 1023) / 1024 * 1024;  // output tile
 // [cb 2][t 64][128 B] (TMA store source; written by the output epilogue, stored
 // by the issue thread once the next chunk's T tiles are signalled)
 constexpr uint32_t OFF_MISC = OFF_O + 16384;
@@ -177,6 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* Tcm = reinterpret_cast<float*>(smem + OFF_TC);  // Tcm[j][i] = T[i][j]
   float* Mcm = reinterpret_cast<float*>(smem + OFF_MC);  // (A21 T11) column-major, pitch 36
   float* Xcm = reinterpret_cast<float*>(smem + OFF_XC);  // 2 x [16][20] level-1 products
+  float* Mcm2 = reinterpret_cast<float*>(smem + OFF_MC2);  // second K-half of M (columns 0-15)
+  float* Tcm2 = reinterpret_cast<float*>(smem + OFF_TC2);  // second K-half of T[48:64][0:32]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3;    // TMEM lane quarter this warp may access
@@ -547,20 +551,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_sync(kComputeBar, kComputeThreads);
       PHASE(15)
       // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
-      // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after):
-      // warp w < 8 computes the 16x8 output tile (row tile w/4, column tile w%4).
-      if (warp < 8) {  // step 1: M = A21' T11' (32x32x32)
-        const int rt = warp >> 2, ct = warp & 3, t4 = tq;
+      // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after).
+      // Zero k-steps of the triangular factors are skipped and the longer
+      // 16x8 output tiles are split over two warps by K half (at most two
+      // dependent MMAs per warp); the second halves land in Mcm2 / Tcm2 and
+      // are added where they are read.
+      if (warp < 12) {  // step 1: M = A21' T11' (32x32x32), T11'[k][n] = 0 for k < n
+        const int rt = warp / 6, u = warp % 6, t4 = tq;
+        // (column tile, first k-step, k-steps, second half?) for u = 0..5
+        const int ct = u < 2 ? 0 : u < 4 ? 1 : u - 2;
+        const int ks0 = u == 0 ? 0 : u == 2 ? 1 : u == 5 ? 3 : 2;
+        const int nks = (u == 2 || u == 5) ? 1 : 2;
+        const bool second = (u == 1 || u == 3);
         float cacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const int k0 = 8 * ks;
-          const float* ar = At + (k0 + t4) * kAtPitch + 32 + 16 * rt + g;  // A[32+16rt+g][k0+t]
-          const float* br = Tcm + (8 * ct + g) * kTcPitch + k0 + t4;       // T[k0+t][8ct+g]
-          mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
-                          to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+        for (int s2 = 0; s2 < 2; ++s2) {
+          if (s2 < nks) {
+            const int k0 = 8 * (ks0 + s2);
+            const float* ar = At + (k0 + t4) * kAtPitch + 32 + 16 * rt + g;  // A[32+16rt+g][k0+t]
+            const float* br = Tcm + (8 * ct + g) * kTcPitch + k0 + t4;       // T[k0+t][8ct+g]
+            mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kAtPitch]),
+                            to_tf32(ar[4 * kAtPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+          }
         }
-        float* mc = Mcm + (8 * ct + 2 * t4) * 36 + 16 * rt + g;  // M[r][j] at Mcm[j*36 + r]
+        float* mc = (second ? Mcm2 : Mcm) + (8 * ct + 2 * t4) * 36 + 16 * rt + g;  // M[r][j] at [j*36 + r]
         mc[0] = cacc[0];
         mc[36] = cacc[1];
         mc[8] = cacc[2];
@@ -568,22 +582,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_sync(kComputeBar, kComputeThreads);
       PHASE(18)
-      if (warp < 8) {  // step 2: T21' = -T22' M
-        const int rt = warp >> 2, ct = warp & 3, t4 = tq;
+      if (warp < 12) {  // step 2: T21' = -T22' M, T22'[r][k] = 0 for k > r
+        const int t4 = tq;
+        const int rt = warp < 4 ? 0 : 1;
+        const int ct = warp < 4 ? warp : (warp - 4) >> 1;
+        const int half = warp < 4 ? 0 : (warp - 4) & 1;  // rows 16-31 of T22': k-steps {0,1} or {2,3}
         float cacc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const int k0 = 8 * ks;
+        for (int s2 = 0; s2 < 2; ++s2) {
+          const int k0 = 8 * (2 * half + s2);
           const float* ar = Tcm + (32 + k0 + t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+16rt+g][32+k0+t]
-          const float* br = Mcm + (8 * ct + g) * 36 + k0 + t4;                  // M[k0+t][8ct+g]
+          const int mo = (8 * ct + g) * 36 + k0 + t4;                           // M[k0+t][8ct+g]
+          float b0 = Mcm[mo], b1 = Mcm[mo + 4];
+          if (ct < 2) {
+            b0 += Mcm2[mo];
+            b1 += Mcm2[mo + 4];
+          }
           mma_tf32_16x8x8(cacc, to_tf32(ar[0]), to_tf32(ar[8]), to_tf32(ar[4 * kTcPitch]),
-                          to_tf32(ar[4 * kTcPitch + 8]), to_tf32(br[0]), to_tf32(br[4]));
+                          to_tf32(ar[4 * kTcPitch + 8]), to_tf32(b0), to_tf32(b1));
         }
-        float* tc = Tcm + (8 * ct + 2 * t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+r][j] at Tcm[j][32+r]
-        tc[0] = -cacc[0];
-        tc[kTcPitch] = -cacc[1];
-        tc[8] = -cacc[2];
-        tc[kTcPitch + 8] = -cacc[3];
+        if (half == 0) {
+          float* tc = Tcm + (8 * ct + 2 * t4) * kTcPitch + 32 + 16 * rt + g;  // T[32+r][j] at Tcm[j][32+r]
+          tc[0] = -cacc[0];
+          tc[kTcPitch] = -cacc[1];
+          tc[8] = -cacc[2];
+          tc[kTcPitch + 8] = -cacc[3];
+        } else {
+          float* tc = Tcm2 + (8 * ct + 2 * t4) * 20 + g;  // T[48+r][j] at Tcm2[j*20 + r]
+          tc[0] = -cacc[0];
+          tc[20] = -cacc[1];
+          tc[8] = -cacc[2];
+          tc[28] = -cacc[3];
+        }
       }
       named_sync(kComputeBar, kComputeThreads);
       PHASE(7)
@@ -595,8 +625,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = tid & 63, ch = tid >> 6;
         const float sc = bet[j];
         const float* src = Tcm + j * kTcPitch + ch * 8;
-        const float4 x0 = *reinterpret_cast<const float4*>(src);
-        const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+        float4 x0 = *reinterpret_cast<const float4*>(src);
+        float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+        if (j < 32 && ch >= 6) {  // T rows 48-63 of columns 0-31: add level 2's second K half
+          const float* s2 = Tcm2 + j * 20 + 8 * (ch - 6);
+          const float4 y0 = *reinterpret_cast<const float4*>(s2);
+          const float4 y1 = *reinterpret_cast<const float4*>(s2 + 4);
+          x0 = make_float4(x0.x + y0.x, x0.y + y0.y, x0.z + y0.z, x0.w + y0.w);
+          x1 = make_float4(x1.x + y1.x, x1.y + y1.y, x1.z + y1.z, x1.w + y1.w);
+        }
         sts128(sb + OFF_TB + sw128_off(j, ch), pack_bf16x2(x0.x * sc, x0.y * sc),
                pack_bf16x2(x0.z * sc, x0.w * sc), pack_bf16x2(x1.x * sc, x1.y * sc),
                pack_bf16x2(x1.z * sc, x1.w * sc));
@@ -606,7 +643,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           sts32(sb + OFF_BL + sw128_off(j, j >> 3) + 4 * ((j & 7) >> 1), (j & 1) ? (w << 16) : w);
         }
         if (dbg && ch == 0)
-          for (int i = 0; i < 64; ++i) p.debug[DBG_T + i * 64 + j] = Tcm[j * kTcPitch + i];
+          for (int i = 0; i < 64; ++i)
+            p.debug[DBG_T + i * 64 + j] =
+                Tcm[j * kTcPitch + i] + ((j < 32 && i >= 48) ? Tcm2[j * 20 + i - 48] : 0.f);
       }
       signal(RDY_T, true);  // T tiles and the P tile are read by the tensor pipe
       PHASE(8)
