@@ -389,7 +389,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st32(tq_st, v);
         tmem_wait_st();
       }
-      signal(RDY_S, false);
+      if (tid < 64) {  // Bl: beta_j - bf16(beta_j) on the diagonal (row j, column j)
+        const int j = tid;
+        const float blo = bet[j] - bf16_lo(pack_bf16x2(bet[j], 0.f));
+        const uint32_t w = pack_bf16x2(blo, 0.f);  // bf16(blo) in the low half
+        sts32(sb + OFF_BL + sw128_off(j, j >> 3) + 4 * ((j & 7) >> 1), (j & 1) ? (w << 16) : w);
+      }
+      signal(RDY_S, tid < 64);  // the tensor pipe reads Bl right after the state
       PHASE(2)
       wait_mma(BAR_M1, par);
       PHASE(3)
@@ -621,7 +627,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // T~ = T diag(beta) as a bf16 tile in which row j holds column j of T:
         // the MN-major B operand (K = s rows, N = t contiguous) of both V^T T~^T
         // and (KS e^gamma)^T T~^T.  Its diagonal is beta_j rounded to bf16; the
-        // rounding remainder goes on the diagonal of Bl.  Thread: row j, chunk ch.
+        // rounding remainder is on the diagonal of Bl (written with the state
+        // pass).  Thread: row j, chunk ch.
         const int j = tid & 63, ch = tid >> 6;
         const float sc = bet[j];
         const float* src = Tcm + j * kTcPitch + ch * 8;
@@ -637,11 +644,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         sts128(sb + OFF_TB + sw128_off(j, ch), pack_bf16x2(x0.x * sc, x0.y * sc),
                pack_bf16x2(x0.z * sc, x0.w * sc), pack_bf16x2(x1.x * sc, x1.y * sc),
                pack_bf16x2(x1.z * sc, x1.w * sc));
-        if (ch == (j >> 3)) {  // the thread holding the diagonal element
-          const float blo = bet[j] - bf16_lo(pack_bf16x2(bet[j], 0.f));
-          const uint32_t w = pack_bf16x2(blo, 0.f);  // bf16(blo) in the low half
-          sts32(sb + OFF_BL + sw128_off(j, j >> 3) + 4 * ((j & 7) >> 1), (j & 1) ? (w << 16) : w);
-        }
         if (dbg && ch == 0)
           for (int i = 0; i < 64; ++i)
             p.debug[DBG_T + i * 64 + j] =
@@ -866,8 +868,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sdesc_sw128_f(kq16 + (kb * 16384 + kin) / 16, 16, 1024), idesc_kqs, ks > 0);
       }
       mma_commit(&bars[BAR_KQS]);
+      // V^T Bl (the beta remainder) starts the Vn accumulator: it needs only
+      // the gates, so it runs before the inverse is done
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
+                    sdesc_sw128_f(sb16 + (OFF_BL + ks * 2048) / 16, 8192, 1024), idesc_vt, ks > 0);
       MPHASE(1)
-      // Vn^T = V^T T~^T + V^T Bl - (KS e^gamma)^T T~^T -> TM_VN
+      // Vn^T += V^T T~^T - (KS e^gamma)^T T~^T -> TM_VN
       if (!(ok = wait_bar(RDY_T, par))) break;
       MPHASE(2)
       // the output tile of chunk c-1 (full: only a sequence's last chunk can be
@@ -881,11 +889,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
-                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_vt, ks > 0);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
-                    sdesc_sw128_f(sb16 + (OFF_BL + ks * 2048) / 16, 8192, 1024), idesc_vt, 1);
+                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_vt, 1);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_bf16_ts(tmem + TM_VN, tmem + TM_KSB + 8 * ks,
