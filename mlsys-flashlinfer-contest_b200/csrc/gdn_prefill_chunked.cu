@@ -108,10 +108,11 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmaBytes = 2 * kKQStage / 2 + kVStage;  // K 16K + Q 16K + V 16K
 
 // mbarriers (OFF_MISC + kMiscBarOff): TMA stages, tensor pipe -> compute warps
-// (one tcgen05.commit each), compute warps -> issue warp (one arrive per warp).
+// (one tcgen05.commit each), compute warps -> issue warp (one arrive per warp;
+// RDY_T1: warps 12-15, once the T~ rows 32-63 are written).
 enum : int {
   BAR_TMA0 = 0, BAR_TMA1, BAR_M1, BAR_KQS, BAR_M3, BAR_PV, BAR_ST,
-  RDY_S, RDY_T, RDY_V, BAR_END, kNumBars
+  RDY_S, RDY_T, RDY_V, BAR_END, RDY_T1, kNumBars
 };
 
 struct ChunkParams {
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(&bars[i], (i >= RDY_S && i <= RDY_V) ? kComputeWarps : 1);
+      mbar_init(&bars[i], (i >= RDY_S && i <= RDY_V) ? kComputeWarps : i == RDY_T1 ? 4 : 1);
     fence_mbar_init();
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
@@ -485,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         convert_ks(cq);
         if (cq == 2 && quarter >= 2) convert_ks(3);
         tmem_wait_st();
+        tc_fence_before();  // read by the Vn MMAs after the next barrier
       } else {
         const int u = tid - 32 * kL0Warp;
         const int b = u >> 4, j = u & 15, b0 = 16 * b;
@@ -556,6 +558,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_sync(kComputeBar, kComputeThreads);
       PHASE(15)
+      // T~ = T diag(beta) as a bf16 tile in which row j holds column j of T: the
+      // MN-major B operand (K = s rows, N = t contiguous) of both V^T T~^T and
+      // (KS e^gamma)^T T~^T.  Its diagonal is beta_j rounded to bf16; the
+      // rounding remainder is on the diagonal of Bl (written with the state
+      // pass).  One call writes the 16-byte chunk ch (T rows 8 ch .. 8 ch + 7)
+      // of tile row j.  Rows 32-63 (columns 32-63 of T) are final after level
+      // 1: warps 12-15 write them during level 2 and the tensor pipe takes the
+      // Vn MMAs of those K rows early; rows 0-31 follow the last barrier.
+      auto t_chunk = [&](int j, int ch) {
+        const float sc = bet[j];
+        const float* src = Tcm + j * kTcPitch + ch * 8;
+        float4 x0 = *reinterpret_cast<const float4*>(src);
+        float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+        if (j < 32 && ch >= 6) {  // T rows 48-63 of columns 0-31: add level 2's second K half
+          const float* s2 = Tcm2 + j * 20 + 8 * (ch - 6);
+          const float4 y0 = *reinterpret_cast<const float4*>(s2);
+          const float4 y1 = *reinterpret_cast<const float4*>(s2 + 4);
+          x0 = make_float4(x0.x + y0.x, x0.y + y0.y, x0.z + y0.z, x0.w + y0.w);
+          x1 = make_float4(x1.x + y1.x, x1.y + y1.y, x1.z + y1.z, x1.w + y1.w);
+        }
+        sts128(sb + OFF_TB + sw128_off(j, ch), pack_bf16x2(x0.x * sc, x0.y * sc),
+               pack_bf16x2(x0.z * sc, x0.w * sc), pack_bf16x2(x1.x * sc, x1.y * sc),
+               pack_bf16x2(x1.z * sc, x1.w * sc));
+      };
+      if (warp >= 12) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int k = tid - 384 + 128 * r;  // 256 chunks of rows 32-63
+          t_chunk(32 + (k >> 3), k & 7);
+        }
+        signal(RDY_T1, true);
+      }
       // level 2 on the tensor cores (mma.sync m16n8k8, tf32 in, fp32 accumulate;
       // tf32 rounding, 2^-11, is below the bf16 rounding T gets right after).
       // Zero k-steps of the triangular factors are skipped and the longer
@@ -623,32 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_sync(kComputeBar, kComputeThreads);
       PHASE(7)
-      {
-        // T~ = T diag(beta) as a bf16 tile in which row j holds column j of T:
-        // the MN-major B operand (K = s rows, N = t contiguous) of both V^T T~^T
-        // and (KS e^gamma)^T T~^T.  Its diagonal is beta_j rounded to bf16; the
-        // rounding remainder is on the diagonal of Bl (written with the state
-        // pass).  Thread: row j, chunk ch.
-        const int j = tid & 63, ch = tid >> 6;
-        const float sc = bet[j];
-        const float* src = Tcm + j * kTcPitch + ch * 8;
-        float4 x0 = *reinterpret_cast<const float4*>(src);
-        float4 x1 = *reinterpret_cast<const float4*>(src + 4);
-        if (j < 32 && ch >= 6) {  // T rows 48-63 of columns 0-31: add level 2's second K half
-          const float* s2 = Tcm2 + j * 20 + 8 * (ch - 6);
-          const float4 y0 = *reinterpret_cast<const float4*>(s2);
-          const float4 y1 = *reinterpret_cast<const float4*>(s2 + 4);
-          x0 = make_float4(x0.x + y0.x, x0.y + y0.y, x0.z + y0.z, x0.w + y0.w);
-          x1 = make_float4(x1.x + y1.x, x1.y + y1.y, x1.z + y1.z, x1.w + y1.w);
-        }
-        sts128(sb + OFF_TB + sw128_off(j, ch), pack_bf16x2(x0.x * sc, x0.y * sc),
-               pack_bf16x2(x0.z * sc, x0.w * sc), pack_bf16x2(x1.x * sc, x1.y * sc),
-               pack_bf16x2(x1.z * sc, x1.w * sc));
-        if (dbg && ch == 0)
-          for (int i = 0; i < 64; ++i)
-            p.debug[DBG_T + i * 64 + j] =
-                Tcm[j * kTcPitch + i] + ((j < 32 && i >= 48) ? Tcm2[j * 20 + i - 48] : 0.f);
-      }
+      if (tid < 256) t_chunk(tid & 31, tid >> 5);  // T~ rows 0-31
+      if (dbg && tid < 64)
+        for (int i = 0; i < 64; ++i)
+          p.debug[DBG_T + i * 64 + tid] =
+              Tcm[tid * kTcPitch + i] + ((tid < 32 && i >= 48) ? Tcm2[tid * 20 + i - 48] : 0.f);
       signal(RDY_T, true);  // T tiles and the P tile are read by the tensor pipe
       PHASE(8)
       if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap the Vn MMAs
@@ -875,7 +888,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
                     sdesc_sw128_f(sb16 + (OFF_BL + ks * 2048) / 16, 8192, 1024), idesc_vt, ks > 0);
       MPHASE(1)
-      // Vn^T += V^T T~^T - (KS e^gamma)^T T~^T -> TM_VN
+      // Vn^T += V^T T~^T - (KS e^gamma)^T T~^T -> TM_VN, first over the K rows
+      // 32-63 of T~ (final after level 1 of the inverse), then rows 0-31
+      auto vn_mmas = [&](int ks) {
+        mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
+                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_vt, 1);
+        mma_bf16_ts(tmem + TM_VN, tmem + TM_KSB + 8 * ks,
+                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_kst, 1);
+      };
+      if (!(ok = wait_bar(RDY_T1, par))) break;
+      vn_mmas(2);
+      vn_mmas(3);
       if (!(ok = wait_bar(RDY_T, par))) break;
       MPHASE(2)
       // the output tile of chunk c-1 (full: only a sequence's last chunk can be
@@ -886,14 +909,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, tp);
         bulk_commit();
       }
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ss(tmem + TM_VN, sdesc_sw128_f(v16 + ks * 128, 8192, 1024),
-                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_vt, 1);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        mma_bf16_ts(tmem + TM_VN, tmem + TM_KSB + 8 * ks,
-                    sdesc_sw128_f(sb16 + (OFF_TB + ks * 2048) / 16, 8192, 1024), idesc_kst, 1);
+      vn_mmas(0);
+      vn_mmas(1);
       mma_commit(&bars[BAR_M3]);
       MPHASE(3)
       // [K;Q]K^T of the next chunk runs while the compute warps drain Vn
