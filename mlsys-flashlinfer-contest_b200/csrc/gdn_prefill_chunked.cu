@@ -148,6 +148,12 @@ constexpr int DBG_GAM = 0, DBG_BET = 64, DBG_A = 128, DBG_P = DBG_A + 4096, DBG_
 // stores): [warp 16][5] for the compute warps, then 8 for the issue thread.
 
 // 16 consecutive floats of a per-token table (16-byte aligned) as four vector loads
+// Two fp32 lanes per instruction (sm_100 packed FMUL2 / FFMA2 / FADD2); each
+// lane rounds exactly like the scalar operation.
+__device__ __forceinline__ float2 mul2(float a0, float a1, float b0, float b1) {
+  return __fmul2_rn(make_float2(a0, a1), make_float2(b0, b1));
+}
+
 __device__ __forceinline__ void load_table16(const float* src, float* v) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -386,7 +392,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
         tmem_st16u(tmem + lane_base + TM_SB + 16 * cq, w);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= dec;
+        for (int i = 0; i < 32; i += 2) {
+          const float2 r = mul2(v[i], v[i + 1], dec, dec);
+          v[i] = r.x;
+          v[i + 1] = r.y;
+        }
         tmem_st32(tq_st, v);
         tmem_wait_st();
       }
@@ -470,7 +480,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         reg_fence(v);
         uint32_t w[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2(v[2 * e] * e2[2 * e], v[2 * e + 1] * e2[2 * e + 1]);
+        for (int e = 0; e < 8; ++e) {
+          const float2 r = mul2(v[2 * e], v[2 * e + 1], e2[2 * e], e2[2 * e + 1]);
+          w[e] = pack_bf16x2(r.x, r.y);
+        }
         tmem_st8u(tmem + lane_base + TM_KSB + 8 * grp, w);
         if (dbg)
           for (int i = 0; i < 16; ++i) p.debug[DBG_KS + (16 * grp + i) * 128 + rowv] = v[i];
@@ -578,9 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           x0 = make_float4(x0.x + y0.x, x0.y + y0.y, x0.z + y0.z, x0.w + y0.w);
           x1 = make_float4(x1.x + y1.x, x1.y + y1.y, x1.z + y1.z, x1.w + y1.w);
         }
-        sts128(sb + OFF_TB + sw128_off(j, ch), pack_bf16x2(x0.x * sc, x0.y * sc),
-               pack_bf16x2(x0.z * sc, x0.w * sc), pack_bf16x2(x1.x * sc, x1.y * sc),
-               pack_bf16x2(x1.z * sc, x1.w * sc));
+        const float2 r0 = mul2(x0.x, x0.y, sc, sc), r1 = mul2(x0.z, x0.w, sc, sc);
+        const float2 r2 = mul2(x1.x, x1.y, sc, sc), r3 = mul2(x1.z, x1.w, sc, sc);
+        sts128(sb + OFF_TB + sw128_off(j, ch), pack_bf16x2(r0.x, r0.y), pack_bf16x2(r1.x, r1.y),
+               pack_bf16x2(r2.x, r2.y), pack_bf16x2(r3.x, r3.y));
       };
       if (warp >= 12) {
 #pragma unroll
@@ -681,20 +695,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         reg_fence(x);
         float dc[16];  // 2^(g63 - g_t) of this warp's 16 tokens (0 past the end)
         load_table16(gam + G_DEC + 16 * cq, dc);
+        if (L < kChunk) {  // partial chunk: tokens past the end contribute nothing
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (16 * cq + i >= L) x[i] = 0.f;
+        }
         uint32_t wn[8], wh[8], wl[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          float xv[2], d[2];
-#pragma unroll
-          for (int f = 0; f < 2; ++f) {
-            const int t = 16 * cq + 2 * e + f;
-            xv[f] = (t < L) ? x[2 * e + f] : 0.f;
-            d[f] = xv[f] * dc[2 * e + f];
-          }
+          const float xv[2] = {x[2 * e], x[2 * e + 1]};
+          const float2 d = mul2(xv[0], xv[1], dc[2 * e], dc[2 * e + 1]);
           wn[e] = pack_bf16x2(xv[0], xv[1]);
-          const uint32_t hp = pack_bf16x2(d[0], d[1]);  // round-to-nearest hi parts
+          const uint32_t hp = pack_bf16x2(d.x, d.y);  // round-to-nearest hi parts
           wh[e] = hp;
-          wl[e] = pack_bf16x2(d[0] - bf16_lo(hp), d[1] - bf16_hi(hp));
+          const float2 lo = __fadd2_rn(d, make_float2(-bf16_lo(hp), -bf16_hi(hp)));
+          wl[e] = pack_bf16x2(lo.x, lo.y);
           if (dbg) {
             p.debug[DBG_VN + (16 * cq + 2 * e) * 128 + rowv] = xv[0];
             p.debug[DBG_VN + (16 * cq + 2 * e + 1) * 128 + rowv] = xv[1];
@@ -736,7 +751,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         __nv_bfloat16* orow = p.out + (t0 * p.Hv + h) * kHead + rowv;
         float o[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = fmaf(eg[i], qs[i], p.scale * pv[i]);
+        for (int i = 0; i < 16; i += 2) {  // (P Vn)^T already carries the scale (P tile)
+          const float2 r = __ffma2_rn(make_float2(eg[i], eg[i + 1]), make_float2(qs[i], qs[i + 1]),
+                                      mul2(pv[i], pv[i + 1], p.scale, p.scale));
+          o[i] = r.x;
+          o[i + 1] = r.y;
+        }
         if (via_tma) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {

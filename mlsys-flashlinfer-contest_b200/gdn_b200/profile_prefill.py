@@ -66,6 +66,7 @@ def main():
     ap.add_argument("--head", type=int, default=5)
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--chunk", type=int, default=100, help="chunk whose handoff timestamps print")
+    ap.add_argument("--warps", action="store_true", help="also print every warp's phase cycles")
     a = ap.parse_args()
     comp, issue, per_warp, events = phase_cycles(a.len, a.hq, a.hv, a.head, chunk=a.chunk)
     tot = sum(comp.values())
@@ -79,6 +80,10 @@ def main():
         col = [per_warp[w][i] for w in range(16)]
         print(f"  {name:32s} {v:8.0f}  {100 * v / tot:5.1f}%   min {min(col):6.0f}  max {max(col):6.0f}"
               f"  (argmax warp {col.index(max(col))})")
+    if a.warps:
+        print("  " + " " * 32 + "".join(f"{w:6d}" for w in range(16)))
+        for i, name in enumerate(comp):
+            print(f"  {name:32s}" + "".join(f"{per_warp[w][i]:6.0f}" for w in range(16)))
     print("issue thread (warp 16):")
     for name, v in issue.items():
         print(f"  {name:32s} {v:8.0f}  {100 * v / tot:5.1f}%")
