@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // waiting and runs on (its results are then garbage, the status word says
     // so); the compute warps agree once per chunk to leave the loop.
     auto wait_mma = [&](int b, uint32_t parity) {
-      if (!failed) failed = !mbar_wait(&bars[b], parity, kTimeoutNs);
+      if (!failed) failed = !mbar_wait_nap(&bars[b], parity, kTimeoutNs);
       tc_fence_after();
     };
 

@@ -90,6 +90,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// The same wait with a short nanosleep between tests: a warp that waits long
+// leaves more issue slots to the warps that are working.
+__device__ __forceinline__ bool mbar_wait_nap(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 63u) == 0 && globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y, int z) {
