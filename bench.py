@@ -447,6 +447,76 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_replay(args):
+    """Contest-shape replay (qk4_v8 geometry: Hq = Hk = 4, Hv = 8): latency of the
+    public ``run`` entry points over seeded synthetic shapes spanning the contest
+    workloads' axes, next to the C restatement of the reference on the host cores.
+    Back-to-back calls with inputs resident on the device, as a Solution harness
+    calls them; per case: median of 5 batches of 20 calls (CUDA events)."""
+    from gdn_b200 import decode, prefill, workloads as W
+    from oracle import c_oracle
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hq, hv = W.CONTEST_HQ, W.CONTEST_HV
+    cpu_left = args.cpu_budget * 6
+
+    def gpu_us(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) / 20 * 1e3)
+        return sorted(ts)[2]
+
+    def cpu_us(fn):
+        nonlocal cpu_left
+        if cpu_left <= 0:
+            return None
+        t0 = time.perf_counter()
+        fn()
+        dt = time.perf_counter() - t0
+        cpu_left -= dt
+        return dt * 1e6
+
+    rows_d, rows_p, ratios = [], [], []
+    for B in W.CONTEST_DECODE_BATCHES:
+        inp = W.make_decode_inputs(B, hq, hv, seed=500 + B)
+        c_us = cpu_us(lambda: c_oracle.decode(*inp.args()))
+        dinp = W.make_decode_inputs(B, hq, hv, seed=500 + B, device=dev)
+        g_us = gpu_us(lambda: decode.run(*dinp.args()))
+        r = None if c_us is None else c_us / g_us
+        if r:
+            ratios.append(r)
+        rows_d.append({"batch": B, "us": round(g_us, 2), "cpu_us": c_us and round(c_us, 1),
+                       "speedup_vs_cpu": r and round(r, 1)})
+    for i, lengths in enumerate(W.contest_prefill_cases()):
+        inp = W.make_prefill_inputs(lengths, hq, hv, seed=700 + i)
+        c_us = cpu_us(lambda: c_oracle.prefill(*inp.args()))
+        dinp = W.make_prefill_inputs(lengths, hq, hv, seed=700 + i, device=dev)
+        g_us = gpu_us(lambda: prefill.run(*dinp.args()))
+        r = None if c_us is None else c_us / g_us
+        if r:
+            ratios.append(r)
+        rows_p.append({"num_seqs": len(lengths), "total_seq_len": sum(lengths), "us": round(g_us, 2),
+                       "cpu_us": c_us and round(c_us, 1), "speedup_vs_cpu": r and round(r, 1)})
+    geo = math.exp(sum(math.log(r) for r in ratios) / len(ratios)) if ratios else None
+    print(json.dumps({
+        "metric": "contest-shape replay latency (qk4_v8: Hq=Hk=4, Hv=8, d=128)", "unit": "us",
+        "data": "synthetic (seeded shapes spanning the contest workload axes)",
+        "api": "gdn_b200.decode.run / gdn_b200.prefill.run, device-resident inputs",
+        "cpu": {"impl": "oracle/gdn_oracle.c (C restatement of the reference definitions)",
+                "cores": c_oracle.max_threads()},
+        "geomean_speedup_vs_cpu": geo and round(geo, 1),
+        "decode": rows_d, "prefill": rows_p}), flush=True)
+
+
 def main():
     global B_PER_RANK
     ap = argparse.ArgumentParser()
@@ -465,6 +535,8 @@ def main():
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the prefill leg and print its JSON (profiling runs)")
+    ap.add_argument("--replay", action="store_true",
+                    help="contest-shape replay (qk4_v8 geometry) instead of the headline line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     B_PER_RANK = args.batch_per_rank
@@ -472,6 +544,10 @@ def main():
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
     local_rank = env_int("LOCAL_RANK", 0)
+    if args.replay:
+        if rank == 0:
+            run_replay(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -7,6 +7,10 @@ Each csrc/*.cu compiles to _build/<name>.o with
 link into gdn_b200/libgdn_b200.so (static CUDA runtime, no other dependency).
 A source is recompiled when it or any csrc header is newer than its object.
 nvcc cross-compiles, so no GPU is needed to build.
+
+csrc/gdn_torch.cpp, the torch-tensor binding of that C ABI, compiles with g++
+against the installed torch headers into gdn_b200/_gdn_torch.so (linked to
+libgdn_b200.so through an $ORIGIN rpath).
 """
 from __future__ import annotations
 
@@ -22,6 +26,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB = HERE / "gdn_b200" / "libgdn_b200.so"
+TORCH_EXT = HERE / "gdn_b200" / "_gdn_torch.so"
 REPO = HERE.parent
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -69,7 +74,37 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False, extra=()) -
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
+    build_torch_ext(force=force, verbose=verbose)
     return LIB
+
+
+def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
+    """g++ build of the torch-tensor binding (a CPython extension module)."""
+    src = CSRC / "gdn_torch.cpp"
+    deps = [src, REPO / "include" / "gdn_b200.h", LIB]
+    if not force and TORCH_EXT.exists() and TORCH_EXT.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return TORCH_EXT
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension as ce
+    torch_lib = Path(torch.__file__).resolve().parent / "lib"
+    cuda_inc = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+    incs = [p for p in ce.include_paths("cpu")] + [str(cuda_inc), sysconfig.get_paths()["include"],
+                                                  str(REPO / "include")]
+    tmp = TORCH_EXT.with_suffix(".so.tmp")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           "-DTORCH_EXTENSION_NAME=_gdn_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           *[f"-I{p}" for p in incs], str(src), "-o", str(tmp),
+           f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+           f"-L{LIB.parent}", "-lgdn_b200", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch binding build failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, TORCH_EXT)
+    return TORCH_EXT
 
 
 if __name__ == "__main__":

@@ -1,0 +1,234 @@
+// Native Python binding of the C ABI (include/gdn_b200.h) for torch tensors: the
+// role TVM-FFI plays for the reference (gdn_decode/solution/python/gdn_decode_utils.h,
+// gdn_prefill/solution/python/cuda_utils.h).  Each entry point checks the tensors'
+// device, layout, rank and dtype, allocates the outputs the caller did not pass
+// from the torch caching allocator, and makes one C-ABI call on the tensors'
+// current CUDA stream.  Checks raise the same exception types as the Python
+// checks in gdn_b200/_checks.py (ValueError for device/layout/shape, TypeError for
+// dtypes); C-ABI error codes map GDN_ERR_VALUE -> ValueError, GDN_ERR_TYPE ->
+// TypeError, GDN_ERR_CUDA -> RuntimeError.  Doing this in C++ takes the host cost
+// of a call from ~30 us (Python checks + ctypes) to a few microseconds, which is
+// most of the latency of a small decode or prefill call.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include "gdn_b200.h"
+
+namespace {
+
+constexpr int64_t kHead = 128;
+
+void cuda_contig(const at::Tensor& t, const char* name) {
+  TORCH_CHECK_VALUE(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK_VALUE(t.is_contiguous(), name, " must be contiguous");
+}
+
+void rank(const at::Tensor& t, const char* name, int64_t d) {
+  TORCH_CHECK_VALUE(t.dim() == d, name, " must be a ", d, "D tensor");
+}
+
+void dtype(const at::Tensor& t, const char* name, at::ScalarType s) {
+  TORCH_CHECK_TYPE(t.scalar_type() == s, name, " must be ",
+                   s == at::kBFloat16 ? "bfloat16" : s == at::kFloat ? "float32" : "int64");
+}
+
+void same_device(const at::Tensor& ref, const at::Tensor& t, const char* name) {
+  TORCH_CHECK_VALUE(t.device() == ref.device(), "q and ", name, " must be on the same device");
+}
+
+void check_rc(int rc, const char* what) {
+  if (rc == GDN_OK) return;
+  const char* msg = gdn_last_error();
+  TORCH_CHECK_VALUE(rc != GDN_ERR_VALUE, what, ": ", msg);
+  TORCH_CHECK_TYPE(rc != GDN_ERR_TYPE, what, ": ", msg);
+  TORCH_CHECK(false, what, ": ", msg);
+}
+
+const float* state_ptr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() ? t->data_ptr<float>() : nullptr;
+}
+
+// decode: q, k [B,1,Hq,128] bf16; v [B,1,Hv,128] bf16; state [B,Hv,128,128] fp32 or
+// None; A_log, dt_bias [Hv] fp32; a, b [B,1,Hv] bf16 -> (output, new_state).
+// output / new_state: destinations (new_state may be state itself: in place).
+std::tuple<at::Tensor, at::Tensor> decode(const at::Tensor& q, const at::Tensor& k,
+                                          const at::Tensor& v,
+                                          const c10::optional<at::Tensor>& state,
+                                          const at::Tensor& A_log, const at::Tensor& a,
+                                          const at::Tensor& dt_bias, const at::Tensor& b,
+                                          double scale, c10::optional<at::Tensor> output,
+                                          c10::optional<at::Tensor> new_state) {
+  const std::pair<const at::Tensor*, const char*> ins[] = {
+      {&q, "q"}, {&k, "k"}, {&v, "v"}, {&A_log, "A_log"}, {&a, "a"}, {&dt_bias, "dt_bias"}, {&b, "b"}};
+  for (const auto& [t, n] : ins) cuda_contig(*t, n);
+  rank(q, "q", 4);
+  rank(k, "k", 4);
+  rank(v, "v", 4);
+  rank(A_log, "A_log", 1);
+  rank(a, "a", 3);
+  rank(dt_bias, "dt_bias", 1);
+  rank(b, "b", 3);
+  for (const auto& [t, n] : ins) same_device(q, *t, n);
+  dtype(q, "q", at::kBFloat16);
+  dtype(k, "k", at::kBFloat16);
+  dtype(v, "v", at::kBFloat16);
+  dtype(a, "a", at::kBFloat16);
+  dtype(b, "b", at::kBFloat16);
+  dtype(A_log, "A_log", at::kFloat);
+  dtype(dt_bias, "dt_bias", at::kFloat);
+  const int64_t B = q.size(0), T = q.size(1), Hq = q.size(2), Hk = k.size(2), Hv = v.size(2);
+  TORCH_CHECK_VALUE(k.size(0) == B && v.size(0) == B, "batch mismatch among q/k/v");
+  TORCH_CHECK_VALUE(k.size(1) == T && v.size(1) == T, "sequence length mismatch among q/k/v");
+  TORCH_CHECK_VALUE(T == 1, "decode requires T=1");
+  TORCH_CHECK_VALUE(q.size(3) == kHead && k.size(3) == kHead && v.size(3) == kHead,
+                    "head size must be 128");
+  TORCH_CHECK_VALUE(Hk == Hq, "num_k_heads must equal num_q_heads");
+  TORCH_CHECK_VALUE(Hq > 0 && Hv % Hq == 0, "HV must be divisible by Hq");
+  TORCH_CHECK_VALUE(a.sizes() == at::IntArrayRef({B, T, Hv}), "a must have shape [B, T, HV]");
+  TORCH_CHECK_VALUE(b.sizes() == at::IntArrayRef({B, T, Hv}), "b must have shape [B, T, HV]");
+  TORCH_CHECK_VALUE(A_log.size(0) == Hv, "A_log must have shape [HV]");
+  TORCH_CHECK_VALUE(dt_bias.size(0) == Hv, "dt_bias must have shape [HV]");
+  if (state.has_value()) {
+    cuda_contig(*state, "state");
+    rank(*state, "state", 4);
+    dtype(*state, "state", at::kFloat);
+    same_device(q, *state, "state");
+    TORCH_CHECK_VALUE(state->sizes() == at::IntArrayRef({B, Hv, kHead, kHead}),
+                      "state must have shape [B, HV, V, K]");
+  }
+  if (output.has_value()) {
+    cuda_contig(*output, "output");
+    rank(*output, "output", 4);
+    dtype(*output, "output", at::kBFloat16);
+    same_device(q, *output, "output");
+    TORCH_CHECK_VALUE(output->sizes() == at::IntArrayRef({B, T, Hv, kHead}),
+                      "output must have shape [B, T, HV, V]");
+  } else {
+    output = at::empty_like(v);
+  }
+  if (new_state.has_value()) {
+    cuda_contig(*new_state, "new_state");
+    rank(*new_state, "new_state", 4);
+    dtype(*new_state, "new_state", at::kFloat);
+    same_device(q, *new_state, "new_state");
+    TORCH_CHECK_VALUE(new_state->sizes() == at::IntArrayRef({B, Hv, kHead, kHead}),
+                      "new_state must have shape [B, HV, V, K]");
+  } else {
+    new_state = at::empty({B, Hv, kHead, kHead}, v.options().dtype(at::kFloat));
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  check_rc(gdn_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state), A_log.data_ptr<float>(),
+                      a.data_ptr(), dt_bias.data_ptr<float>(), b.data_ptr(), static_cast<float>(scale),
+                      output->data_ptr(), new_state->data_ptr<float>(), B, Hq, Hk, Hv, kHead, stream),
+           "gdn_decode");
+  return {*output, *new_state};
+}
+
+// prefill: q, k [T,Hq,128] bf16; v [T,Hv,128] bf16; state [N,Hv,128,128] fp32 or
+// None; a, b [T,Hv] bf16; cu_seqlens [N+1] int64 -> (output, new_state).
+// path: 0 = the default dispatch (gdn_prefill), 1 = token-recurrent kernel.
+std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor& k,
+                                           const at::Tensor& v,
+                                           const c10::optional<at::Tensor>& state,
+                                           const at::Tensor& A_log, const at::Tensor& a,
+                                           const at::Tensor& dt_bias, const at::Tensor& b,
+                                           const at::Tensor& cu_seqlens, double scale,
+                                           c10::optional<at::Tensor> output,
+                                           c10::optional<at::Tensor> new_state, int64_t path) {
+  const std::pair<const at::Tensor*, const char*> ins[] = {
+      {&q, "q"}, {&k, "k"},           {&v, "v"}, {&A_log, "A_log"}, {&a, "a"}, {&dt_bias, "dt_bias"},
+      {&b, "b"}, {&cu_seqlens, "cu_seqlens"}};
+  for (const auto& [t, n] : ins) cuda_contig(*t, n);
+  rank(q, "q", 3);
+  rank(k, "k", 3);
+  rank(v, "v", 3);
+  rank(A_log, "A_log", 1);
+  rank(a, "a", 2);
+  rank(dt_bias, "dt_bias", 1);
+  rank(b, "b", 2);
+  rank(cu_seqlens, "cu_seqlens", 1);
+  const int64_t T = q.size(0), Hq = q.size(1), Nseq = cu_seqlens.size(0) - 1;
+  const int64_t Hk = k.size(1), Hv = v.size(1);
+  TORCH_CHECK_VALUE(Nseq > 0, "must have at least one sequence");
+  TORCH_CHECK_VALUE(q.size(2) == kHead && k.size(2) == kHead && v.size(2) == kHead,
+                    "head size must be 128");
+  TORCH_CHECK_VALUE(k.size(0) == T && v.size(0) == T, "k/v shape mismatch");
+  TORCH_CHECK_VALUE(Hk == Hq, "num_k_heads must equal num_q_heads");
+  TORCH_CHECK_VALUE(Hq > 0 && Hv % Hq == 0, "num_v_heads must be divisible by num_q_heads");
+  TORCH_CHECK_VALUE(a.sizes() == at::IntArrayRef({T, Hv}), "a shape mismatch");
+  TORCH_CHECK_VALUE(b.sizes() == at::IntArrayRef({T, Hv}), "b shape mismatch");
+  TORCH_CHECK_VALUE(A_log.size(0) == Hv && dt_bias.size(0) == Hv,
+                    "A_log / dt_bias must have shape [HV]");
+  dtype(q, "q", at::kBFloat16);
+  dtype(k, "k", at::kBFloat16);
+  dtype(v, "v", at::kBFloat16);
+  dtype(a, "a", at::kBFloat16);
+  dtype(b, "b", at::kBFloat16);
+  dtype(A_log, "A_log", at::kFloat);
+  dtype(dt_bias, "dt_bias", at::kFloat);
+  dtype(cu_seqlens, "cu_seqlens", at::kLong);
+  for (const auto& [t, n] : ins) same_device(q, *t, n);
+  if (state.has_value()) {
+    cuda_contig(*state, "state");
+    rank(*state, "state", 4);
+    dtype(*state, "state", at::kFloat);
+    same_device(q, *state, "state");
+    TORCH_CHECK_VALUE(state->sizes() == at::IntArrayRef({Nseq, Hv, kHead, kHead}),
+                      "state shape mismatch");
+  }
+  if (output.has_value()) {
+    cuda_contig(*output, "output");
+    rank(*output, "output", 3);
+    dtype(*output, "output", at::kBFloat16);
+    same_device(q, *output, "output");
+    TORCH_CHECK_VALUE(output->sizes() == at::IntArrayRef({T, Hv, kHead}), "output shape mismatch");
+  } else {
+    output = at::empty_like(v);
+  }
+  if (new_state.has_value()) {
+    cuda_contig(*new_state, "new_state");
+    rank(*new_state, "new_state", 4);
+    dtype(*new_state, "new_state", at::kFloat);
+    same_device(q, *new_state, "new_state");
+    TORCH_CHECK_VALUE(new_state->sizes() == at::IntArrayRef({Nseq, Hv, kHead, kHead}),
+                      "new_state shape mismatch");
+  } else {
+    new_state = at::empty({Nseq, Hv, kHead, kHead}, v.options().dtype(at::kFloat));
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  const float sc = static_cast<float>(scale);
+  if (path == 1) {
+    check_rc(gdn_prefill_recurrent(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
+                                   A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
+                                   b.data_ptr(), cu_seqlens.data_ptr<int64_t>(), sc,
+                                   output->data_ptr(), new_state->data_ptr<float>(), T, Nseq, Hq,
+                                   Hk, Hv, kHead, stream),
+             "gdn_prefill_recurrent");
+  } else {
+    TORCH_CHECK_VALUE(gdn_prefill_workspace_bytes(T, Nseq, Hq, Hv) == 0,
+                      "gdn_prefill needs a workspace: call the Python launch()");
+    check_rc(gdn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
+                         A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
+                         b.data_ptr(), cu_seqlens.data_ptr<int64_t>(), sc, output->data_ptr(),
+                         new_state->data_ptr<float>(), T, Nseq, Hq, Hk, Hv, kHead, nullptr, 0,
+                         stream),
+             "gdn_prefill");
+  }
+  return {*output, *new_state};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "torch-tensor binding of the gdn_b200 C ABI";
+  m.def("decode", &decode, "GDN decode (C ABI gdn_decode)", py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("state"), py::arg("A_log"), py::arg("a"), py::arg("dt_bias"), py::arg("b"),
+        py::arg("scale"), py::arg("output") = py::none(), py::arg("new_state") = py::none());
+  m.def("prefill", &prefill, "GDN prefill (C ABI gdn_prefill / gdn_prefill_recurrent)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("state"), py::arg("A_log"), py::arg("a"),
+        py::arg("dt_bias"), py::arg("b"), py::arg("cu_seqlens"), py::arg("scale"),
+        py::arg("output") = py::none(), py::arg("new_state") = py::none(), py::arg("path") = 0);
+}

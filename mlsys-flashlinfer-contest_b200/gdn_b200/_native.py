@@ -57,6 +57,24 @@ def lib():
     return L
 
 
+_ext = False
+
+
+def torch_ext():
+    """The torch-tensor binding (gdn_b200/_gdn_torch.so, built from
+    csrc/gdn_torch.cpp), or None when it was not built: the entry points then
+    make the same C-ABI calls through ctypes (same kernels, more host time)."""
+    global _ext
+    if _ext is False:
+        lib()  # the binding links libgdn_b200.so; load and version-check it first
+        try:
+            from . import _gdn_torch as ext
+        except ImportError:
+            ext = None
+        _ext = ext
+    return _ext
+
+
 def check(rc: int, what: str = "") -> None:
     if rc == GDN_OK:
         return

@@ -8,7 +8,9 @@ B < 8 and updates ``state`` in place for B >= 8
 (gdn_decode_kernel_large_batch.py:348,405-406); here ``run`` is out-of-place for
 every B (definition-exact) and ``run_inplace`` is the explicit in-place form.
 Both launch the single fused sm_100a decode kernel through the C ABI
-(``gdn_decode`` in include/gdn_b200.h) on the current CUDA stream.
+(``gdn_decode`` in include/gdn_b200.h) on the current CUDA stream, by way of the
+torch-tensor binding ``_gdn_torch`` (checks and output allocation in C++) when it
+is built, else through ctypes after the Python checks below.
 """
 from __future__ import annotations
 
@@ -70,6 +72,10 @@ def _validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state):
 def launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
     """Destination-passing form: writes ``output`` and ``new_state`` (which may be
     ``state`` itself) and returns them."""
+    ext = N.torch_ext()
+    if ext is not None:
+        return ext.decode(q, k, v, state, A_log, a, dt_bias, b, resolve_scale(scale), output,
+                          new_state)
     B, Hq, Hk, Hv = _validate(q, k, v, state, A_log, a, dt_bias, b, output, new_state)
     with torch.cuda.device(q.device):
         rc = N.lib().gdn_decode(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(state), N.ptr(A_log), N.ptr(a),
@@ -81,6 +87,9 @@ def launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
 
 def run(q, k, v, state, A_log, a, dt_bias, b, scale):
     """Out-of-place decode: returns (output [B,1,Hv,128] bf16, new_state [B,Hv,128,128] fp32)."""
+    ext = N.torch_ext()
+    if ext is not None:
+        return ext.decode(q, k, v, state, A_log, a, dt_bias, b, resolve_scale(scale))
     output = torch.empty_like(v)
     B, Hv = v.shape[0], v.shape[2]
     new_state = torch.empty((B, Hv, HEAD, HEAD), dtype=torch.float32, device=v.device)

@@ -6,7 +6,9 @@ same argument order and meaning, ``state`` optional (None = zero initial states)
 ``cu_seqlens`` int64 as in the definition (int32 is accepted and widened).
 The call allocates the outputs and the workspace from the torch caching
 allocator, then makes one C-ABI call (``gdn_prefill``, include/gdn_b200.h) that
-enqueues every kernel on the current stream.  No host synchronisation: the
+enqueues every kernel on the current stream; the torch-tensor binding
+``_gdn_torch`` does the checks, the allocation and the call in C++ when it is
+built, else ctypes does the call after the Python checks below.  No host synchronisation: the
 chunk layout is derived on the device from ``cu_seqlens``.
 """
 from __future__ import annotations
@@ -81,6 +83,10 @@ def launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_
     """Destination-passing form.  ``recurrent=True`` forces the token-recurrent
     CUDA-core kernel (the reference's path for tiny inputs)."""
     cu_seqlens = _widen(cu_seqlens)
+    ext = N.torch_ext()
+    if ext is not None and workspace is None:
+        return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, resolve_scale(scale),
+                           output, new_state, 1 if recurrent else 0)
     T, Nseq, Hq, Hk, Hv = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output,
                                     new_state)
     L = N.lib()
@@ -108,6 +114,10 @@ def launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_
 
 def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
     """Returns (output [T,Hv,128] bf16, new_state [N,Hv,128,128] fp32)."""
+    ext = N.torch_ext()
+    if ext is not None:
+        return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, _widen(cu_seqlens),
+                           resolve_scale(scale))
     Nseq = cu_seqlens.shape[0] - 1
     Hv = v.shape[1]
     output = torch.empty_like(v)
@@ -117,6 +127,10 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
 
 def run_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
     """Token-recurrent prefill (no workspace)."""
+    ext = N.torch_ext()
+    if ext is not None:
+        return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, _widen(cu_seqlens),
+                           resolve_scale(scale), None, None, 1)
     Nseq = cu_seqlens.shape[0] - 1
     output = torch.empty_like(v)
     new_state = torch.empty((max(Nseq, 0), v.shape[1], HEAD, HEAD), dtype=torch.float32,

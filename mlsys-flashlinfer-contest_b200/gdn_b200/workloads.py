@@ -161,3 +161,49 @@ def config_lengths(name: str) -> list:
     if name == "prefill_long":        # config 3: 4 x 16384
         return [16384] * 4
     raise KeyError(name)
+
+
+# ---- contest-shape replay ---------------------------------------------------
+# The contest scores solutions on workloads of the qk4_v8 definitions (Hq = Hk = 4,
+# Hv = 8).  Their axes, as listed in the reference's workloads/gdn/*.md, span:
+# decode batch_size 1..64 (values 1, 4, 8, 16, 32, 48, 64); prefill total_seq_len
+# 6..8192 over num_seqs 1..57, most batches holding 1-4 sequences.  The tensors
+# themselves are not available, so the replay draws seeded synthetic shapes over
+# the same ranges (both extremes included) and feeds them the usual distributions.
+CONTEST_HQ, CONTEST_HV = 4, 8
+CONTEST_DECODE_BATCHES = (1, 4, 8, 16, 32, 48, 64)
+CONTEST_MAX_TOKENS, CONTEST_MAX_SEQS, CONTEST_MIN_TOKENS = 8192, 57, 6
+
+
+def split_lengths(total: int, n: int, gen: torch.Generator) -> list:
+    """Ragged split of ``total`` tokens into ``n`` sequences of length >= 1."""
+    if n <= 1:
+        return [int(total)]
+    cuts = torch.randperm(total - 1, generator=gen)[: n - 1] + 1
+    cuts = sorted(int(c) for c in cuts)
+    edges = [0] + cuts + [int(total)]
+    return [edges[i + 1] - edges[i] for i in range(n)]
+
+
+def contest_prefill_cases(n_random: int = 20, seed: int = 26) -> list:
+    """Seeded lists of sequence lengths spanning the contest prefill axes: the
+    four corners (fewest/most tokens with one sequence and with the most
+    sequences), then ``n_random`` draws with num_seqs mostly in 1..4 (a tail up
+    to 57) and total_seq_len log-uniform over [max(6, num_seqs), 8192]."""
+    gen = _gen("cpu", seed)
+    cases = [[CONTEST_MIN_TOKENS], [CONTEST_MAX_TOKENS],
+             split_lengths(CONTEST_MAX_SEQS * 2, CONTEST_MAX_SEQS, gen),
+             split_lengths(CONTEST_MAX_TOKENS, CONTEST_MAX_SEQS, gen)]
+    for _ in range(n_random):
+        u = float(torch.rand((), generator=gen))
+        if u < 0.65:
+            n = 1 + int(torch.randint(0, 4, (), generator=gen))
+        else:
+            n = int(round(math.exp(math.log(5) + float(torch.rand((), generator=gen))
+                                   * (math.log(CONTEST_MAX_SEQS) - math.log(5)))))
+        lo = math.log(max(CONTEST_MIN_TOKENS, n))
+        hi = math.log(CONTEST_MAX_TOKENS)
+        total = int(round(math.exp(lo + float(torch.rand((), generator=gen)) * (hi - lo))))
+        cases.append(split_lengths(max(total, n), n, gen))
+    return cases
+

@@ -144,3 +144,16 @@ def test_chunk_intermediates_match_recurrence(lengths, n, h, c):
     o_chunk = O.resolve_scale(None) * (np.exp(ref["gam"])[:, None] * ref["QS"] + ref["PV"])
     L = ref["L"]
     assert O.rel_err(o_chunk[:L], O.bf16_to_f32(o_rec[t0:t0 + L, h])) < 5e-3
+
+
+def test_contest_shapes_span_the_axes():
+    """The replay shapes are deterministic and cover the contest axis ranges."""
+    cases = W.contest_prefill_cases()
+    assert cases == W.contest_prefill_cases()
+    totals = [sum(c) for c in cases]
+    seqs = [len(c) for c in cases]
+    assert min(totals) == W.CONTEST_MIN_TOKENS and max(totals) == W.CONTEST_MAX_TOKENS
+    assert min(seqs) == 1 and max(seqs) == W.CONTEST_MAX_SEQS
+    assert all(min(c) >= 1 for c in cases)
+    assert sum(1 for n in seqs if n <= 4) >= len(cases) // 2
+    assert W.CONTEST_DECODE_BATCHES[0] == 1 and W.CONTEST_DECODE_BATCHES[-1] == 64
