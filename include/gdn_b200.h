@@ -65,6 +65,41 @@ int gdn_decode(const void *q, const void *k, const void *v, const float *state,
                int64_t num_q_heads, int64_t num_k_heads, int64_t num_v_heads,
                int64_t head_size, void *stream);
 
+/* Storage type of a pooled state (gdn_decode_pool). */
+enum gdn_state_dtype { GDN_STATE_F32 = 0, GDN_STATE_BF16 = 1 };
+/* gdn_decode_pool flags */
+#define GDN_POOL_QK_L2NORM 1        /* L2-normalise q and k per head: x / sqrt(sum x^2 + 1e-6) */
+#define GDN_POOL_NO_STATE_UPDATE 2  /* leave the pool untouched (outputs / cache only) */
+
+/*
+ * Pooled multi-token decode: the serving form of gdn_decode.  No reference
+ * counterpart: the reference workspace decodes one token per sequence with a
+ * dense fp32 state batch (gdn_decode_final.py:23-36); this entry is the adjacent
+ * "next" variant (bf16 state, multi-token, in-kernel q/k L2 norm) that installed
+ * FlashInfer ships as gdn_decode_bf16_state / gdn_decode_mtp.
+ *
+ *   q, k      [B, T, Hq, 128] bf16        v        [B, T, Hv, 128] bf16
+ *   A_log, dt_bias [Hv] fp32              a, b     [B, T, Hv] bf16
+ *   state_pool [pool_size, Hv, 128, 128] in state_dtype (k-last)
+ *   in_slots  [B] int32 device: pool slot each sequence starts from; a negative
+ *             or out-of-range slot means a zero initial state
+ *   out_slots [B] int32 device or NULL (= in_slots): slot each final state is
+ *             written to; negative or out-of-range: not written
+ *   intermediate NULL or [B, T, Hv, 128, 128] in state_dtype: state after each token
+ *   output    [B, T, Hv, 128] bf16
+ * Tokens of a sequence are applied in order t = 0..T-1 (T >= 1), the state kept
+ * in fp32 registers between them and rounded to state_dtype once per store.  The
+ * pool is updated in place; two sequences writing the same slot, or one reading a
+ * slot another writes, race.  All buffers need 16-byte alignment.
+ */
+int gdn_decode_pool(const void *q, const void *k, const void *v, const float *A_log,
+                    const void *a, const float *dt_bias, const void *b, float scale,
+                    void *state_pool, int state_dtype, int64_t pool_size,
+                    const int32_t *in_slots, const int32_t *out_slots, void *intermediate,
+                    int flags, void *output, int64_t batch_size, int64_t seq_len,
+                    int64_t num_q_heads, int64_t num_k_heads, int64_t num_v_heads,
+                    int64_t head_size, void *stream);
+
 /*
  * Prefill packed variable-length sequences.
  * Replaces the solution entry gdn_prefill/solution/python/gdn_prefill_mix.py:13-38

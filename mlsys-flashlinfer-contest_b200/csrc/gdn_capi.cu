@@ -87,6 +87,36 @@ int gdn_decode(const void* q, const void* k, const void* v, const float* state, 
   return cuda_status(gdn::launch_decode(p, 0, static_cast<cudaStream_t>(stream)), "gdn_decode launch");
 }
 
+int gdn_decode_pool(const void* q, const void* k, const void* v, const float* A_log, const void* a,
+                    const float* dt_bias, const void* b, float scale, void* pool, int state_dtype,
+                    int64_t pool_size, const int32_t* in_slots, const int32_t* out_slots,
+                    void* intermediate, int flags, void* output, int64_t B, int64_t T, int64_t Hq,
+                    int64_t Hk, int64_t Hv, int64_t D, void* stream) {
+  if (int e = check_heads(Hq, Hk, Hv, D)) return e;
+  if (B < 0) return fail(GDN_ERR_VALUE, "batch_size must be non-negative");
+  if (T < 1) return fail(GDN_ERR_VALUE, "seq_len must be at least 1");
+  if (pool_size < 0) return fail(GDN_ERR_VALUE, "pool_size must be non-negative");
+  if (pool_size > INT32_MAX) return fail(GDN_ERR_VALUE, "pool_size must fit int32 slot indices");
+  if (state_dtype != GDN_STATE_F32 && state_dtype != GDN_STATE_BF16)
+    return fail(GDN_ERR_TYPE, "state_dtype must be GDN_STATE_F32 or GDN_STATE_BF16");
+  if (flags & ~(GDN_POOL_QK_L2NORM | GDN_POOL_NO_STATE_UPDATE))
+    return fail(GDN_ERR_VALUE, "unknown flags");
+  if (B == 0) return ok();
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !in_slots)
+    return fail(GDN_ERR_VALUE, "null pointer argument");
+  if (pool_size > 0 && !pool) return fail(GDN_ERR_VALUE, "null pointer argument");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(pool, 16) || !aligned(intermediate, 16))
+    return fail(GDN_ERR_VALUE, "q, k, state_pool and intermediate must be 16-byte aligned");
+  if (!aligned(in_slots, 4) || !aligned(out_slots, 4))
+    return fail(GDN_ERR_VALUE, "slot arrays must be 4-byte aligned");
+  gdn::DecodePoolArgs p{q, k, v, A_log, a, dt_bias, b, scale == 0.0f ? 0.08838834764831845f : scale,
+                        pool, in_slots, out_slots, intermediate, output, B, T, Hq, Hv, pool_size,
+                        state_dtype == GDN_STATE_BF16, (flags & GDN_POOL_QK_L2NORM) != 0,
+                        (flags & GDN_POOL_NO_STATE_UPDATE) != 0};
+  return cuda_status(gdn::launch_decode_pool(p, static_cast<cudaStream_t>(stream)),
+                     "gdn_decode_pool launch");
+}
+
 static int check_prefill(const void* q, const void* k, const void* v, const float* state,
                          const float* A_log, const void* a, const float* dt_bias, const void* b,
                          const int64_t* cu, void* out, float* new_state, int64_t T, int64_t N,

@@ -1,0 +1,237 @@
+// GDN pooled multi-token decode (serving form), sm_100a.
+//
+// The reference workspace decodes one token per sequence with a dense fp32 state
+// batch (gdn_decode_final.py:23-36).  Serving stacks add three things around the
+// same recurrence, and this kernel carries them in one pass over the state:
+//   * a state pool: sequence b reads slot in_slots[b] of a [pool, Hv, 128, 128]
+//     pool and writes slot out_slots[b] (in place when they match); a negative or
+//     out-of-range read slot means a zero initial state, such a write slot means
+//     no write-back;
+//   * T >= 1 tokens per sequence applied in order (multi-token / speculative
+//     decode), the state held in registers between tokens, optionally with the
+//     state after every token written to a [B, T, Hv, 128, 128] cache;
+//   * fp32 or bf16 state storage (bf16 halves the HBM bytes of the stream; the
+//     arithmetic stays fp32 and the state is rounded once per store), and an
+//     optional L2 normalisation of q and k per head inside the kernel
+//     (x / sqrt(sum x^2 + 1e-6)).
+// Per token the math is that of definitions/gdn/gdn_decode_qk4_v8_d128_k_last.md:91-132
+// (as in gdn_decode.cu): g = exp(-exp(A_log) softplus(a + dt_bias)), beta = sigmoid(b),
+// old_v = k . (g S[v]), S'[v] = g S[v] + beta k (v[v] - old_v), o[v] = scale q . S'[v].
+//
+// Mapping: a CTA of 256 threads owns 32*U consecutive state rows of one (b, h);
+// each aligned octet of 8 lanes owns one row at a time and lane j of the octet
+// holds the 16 contiguous elements k in [16 j, 16 j + 16) (64 bytes in fp32, 32 in
+// bf16: whole 128-byte segments per octet).  All state loads of a thread are
+// issued before any use.
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+
+namespace gdn {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cs.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void st_stream_u4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// 16 contiguous bf16 through the read-only path, widened to fp32.
+__device__ __forceinline__ void ld_bf16x16(const __nv_bfloat16* p, float* out) {
+  uint4 w[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[h].x), "=r"(w[h].y), "=r"(w[h].z), "=r"(w[h].w)
+                 : "l"(p + 8 * h));
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    out[8 * h + 0] = bf16_lo(w[h].x);
+    out[8 * h + 1] = bf16_hi(w[h].x);
+    out[8 * h + 2] = bf16_lo(w[h].y);
+    out[8 * h + 3] = bf16_hi(w[h].y);
+    out[8 * h + 4] = bf16_lo(w[h].z);
+    out[8 * h + 5] = bf16_hi(w[h].z);
+    out[8 * h + 6] = bf16_lo(w[h].w);
+    out[8 * h + 7] = bf16_hi(w[h].w);
+  }
+}
+
+// One lane's 16 state elements of a row: load from / store to fp32 or bf16 storage.
+template <bool BF16>
+__device__ __forceinline__ void load_row16(const void* base, int64_t elem, float* s) {
+  if constexpr (BF16) {
+    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(base) + elem;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 w = ld_stream_u4(p + 8 * h);
+      s[8 * h + 0] = bf16_lo(w.x);
+      s[8 * h + 1] = bf16_hi(w.x);
+      s[8 * h + 2] = bf16_lo(w.y);
+      s[8 * h + 3] = bf16_hi(w.y);
+      s[8 * h + 4] = bf16_lo(w.z);
+      s[8 * h + 5] = bf16_hi(w.z);
+      s[8 * h + 6] = bf16_lo(w.w);
+      s[8 * h + 7] = bf16_hi(w.w);
+    }
+  } else {
+    const float* p = static_cast<const float*>(base) + elem;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 x = ld_stream_f4(p + 4 * i);
+      s[4 * i + 0] = x.x;
+      s[4 * i + 1] = x.y;
+      s[4 * i + 2] = x.z;
+      s[4 * i + 3] = x.w;
+    }
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ void store_row16(void* base, int64_t elem, const float* s) {
+  if constexpr (BF16) {
+    __nv_bfloat16* p = static_cast<__nv_bfloat16*>(base) + elem;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      st_stream_u4(p + 8 * h, make_uint4(pack_bf16x2(s[8 * h + 0], s[8 * h + 1]),
+                                         pack_bf16x2(s[8 * h + 2], s[8 * h + 3]),
+                                         pack_bf16x2(s[8 * h + 4], s[8 * h + 5]),
+                                         pack_bf16x2(s[8 * h + 6], s[8 * h + 7])));
+  } else {
+    float* p = static_cast<float*>(base) + elem;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      st_stream_f4(p + 4 * i, make_float4(s[4 * i + 0], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]));
+  }
+}
+
+template <int U, bool BF16, bool L2NORM>
+__global__ void __launch_bounds__(kThreads) gdn_decode_pool_kernel(DecodePoolArgs p) {
+  constexpr int kRows = 32 * U;
+  constexpr int kTilesPerHead = kHead / kRows;
+  const int64_t cta = blockIdx.x;
+  const int64_t bh = cta / kTilesPerHead;  // b * Hv + h
+  const int tile = static_cast<int>(cta % kTilesPerHead);
+  const int64_t bidx = bh / p.Hv;
+  const int h = static_cast<int>(bh % p.Hv);
+  const int qh = h / static_cast<int>(p.Hv / p.Hq);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int oct = lane >> 3;
+  const int j = lane & 7;
+  const int row0 = tile * kRows + warp * (4 * U) + oct;  // rows row0 + 4u
+  constexpr int64_t kTile = kHead * kHead;
+
+  const int32_t sin = p.in_slots[bidx];
+  const int32_t sout = p.out_slots ? p.out_slots[bidx] : sin;
+  const bool has_in = sin >= 0 && sin < p.pool_size;
+  const bool write_back = !p.no_state_update && sout >= 0 && sout < p.pool_size;
+
+  float s[U][16];
+  if (has_in) {
+    const int64_t base = (static_cast<int64_t>(sin) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 16 * j;
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_row16<BF16>(p.pool, base + u * 4 * kHead, s[u]);
+  } else {
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int c = 0; c < 16; ++c) s[u][c] = 0.0f;
+  }
+
+  const __nv_bfloat16* a_ptr = static_cast<const __nv_bfloat16*>(p.a);
+  const __nv_bfloat16* b_ptr = static_cast<const __nv_bfloat16*>(p.b);
+  const float A_log = p.A_log[h], dt_bias = p.dt_bias[h];
+  for (int t = 0; t < p.T; ++t) {
+    const int64_t bt = bidx * p.T + t;
+    const float g = expf(log_decay(A_log, __bfloat162float(a_ptr[bt * p.Hv + h]), dt_bias));
+    const float beta = sigmoidf_acc(__bfloat162float(b_ptr[bt * p.Hv + h]));
+    float kf[16], qf[16];
+    ld_bf16x16(static_cast<const __nv_bfloat16*>(p.k) + (bt * p.Hq + qh) * kHead + 16 * j, kf);
+    ld_bf16x16(static_cast<const __nv_bfloat16*>(p.q) + (bt * p.Hq + qh) * kHead + 16 * j, qf);
+    if constexpr (L2NORM) {
+      float sk = 0.0f, sq = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        sk = fmaf(kf[c], kf[c], sk);
+        sq = fmaf(qf[c], qf[c], sq);
+      }
+      const float rk = rsqrtf(octet_sum(sk) + 1e-6f), rq = rsqrtf(octet_sum(sq) + 1e-6f);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        kf[c] *= rk;
+        qf[c] *= rq;
+      }
+    }
+    const __nv_bfloat16* vrow = static_cast<const __nv_bfloat16*>(p.v) + (bt * p.Hv + h) * kHead;
+    __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (bt * p.Hv + h) * kHead;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int row = row0 + 4 * u;
+      const float vv = __bfloat162float(vrow[row]);
+      float dot = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        s[u][c] *= g;
+        dot = fmaf(kf[c], s[u][c], dot);
+      }
+      const float delta = beta * (vv - octet_sum(dot));
+      float ov = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        s[u][c] = fmaf(kf[c], delta, s[u][c]);
+        ov = fmaf(qf[c], s[u][c], ov);
+      }
+      ov = octet_sum(ov);
+      if (j == 0) orow[row] = __float2bfloat16_rn(p.scale * ov);
+      if (p.intermediate)
+        store_row16<BF16>(p.intermediate, (bt * p.Hv + h) * kTile + static_cast<int64_t>(row) * kHead + 16 * j,
+                          s[u]);
+    }
+  }
+
+  if (write_back) {
+    const int64_t base = (static_cast<int64_t>(sout) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 16 * j;
+#pragma unroll
+    for (int u = 0; u < U; ++u) store_row16<BF16>(p.pool, base + u * 4 * kHead, s[u]);
+  }
+}
+
+template <int U, bool BF16>
+cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
+  const int64_t ctas = a.B * a.Hv * (kHead / (32 * U));
+  if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (a.qk_l2norm)
+    gdn_decode_pool_kernel<U, BF16, true><<<static_cast<unsigned>(ctas), kThreads, 0, s>>>(a);
+  else
+    gdn_decode_pool_kernel<U, BF16, false><<<static_cast<unsigned>(ctas), kThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <bool BF16>
+cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
+  // enough CTAs to fill the 148 SMs several times before the tile grows
+  const int64_t tiles = a.B * a.Hv;
+  if (tiles >= 4 * 148) return launch_u<4, BF16>(a, s);
+  if (tiles >= 2 * 148) return launch_u<2, BF16>(a, s);
+  return launch_u<1, BF16>(a, s);
+}
+
+}  // namespace
+
+cudaError_t launch_decode_pool(const DecodePoolArgs& a, cudaStream_t s) {
+  if (a.B == 0 || a.T == 0) return cudaSuccess;
+  return a.state_bf16 ? launch_dtype<true>(a, s) : launch_dtype<false>(a, s);
+}
+
+}  // namespace gdn

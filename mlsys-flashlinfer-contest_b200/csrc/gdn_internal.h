@@ -32,6 +32,26 @@ struct DecodeArgs {
 // rows_per_cta: 0 = choose from the problem size, else 32, 64 or 128.
 cudaError_t launch_decode(const DecodeArgs& a, int rows_per_cta, cudaStream_t s);
 
+struct DecodePoolArgs {
+  const void* q;           // [B,T,Hq,128] bf16
+  const void* k;           // [B,T,Hk,128] bf16
+  const void* v;           // [B,T,Hv,128] bf16
+  const float* A_log;      // [Hv]
+  const void* a;           // [B,T,Hv] bf16
+  const float* dt_bias;    // [Hv]
+  const void* b;           // [B,T,Hv] bf16
+  float scale;             // already resolved
+  void* pool;              // [pool_size,Hv,128,128] fp32 or bf16 (state_bf16)
+  const int32_t* in_slots;   // [B] device
+  const int32_t* out_slots;  // [B] device, or nullptr (= in_slots)
+  void* intermediate;      // [B,T,Hv,128,128] in the pool's dtype, or nullptr
+  void* out;               // [B,T,Hv,128] bf16
+  int64_t B, T, Hq, Hv, pool_size;
+  bool state_bf16, qk_l2norm, no_state_update;
+};
+
+cudaError_t launch_decode_pool(const DecodePoolArgs& a, cudaStream_t s);
+
 struct PrefillArgs {
   const void* q;           // [T,Hq,128] bf16
   const void* k;           // [T,Hk,128] bf16

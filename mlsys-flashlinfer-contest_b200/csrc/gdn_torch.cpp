@@ -220,6 +220,95 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
   return {*output, *new_state};
 }
 
+// pooled multi-token decode: q, k [B,T,Hq,128] bf16; v [B,T,Hv,128] bf16; a, b
+// [B,T,Hv] bf16; state_pool [P,Hv,128,128] fp32 or bf16 (updated in place);
+// in_slots / out_slots [B] int32; intermediate: None or [B,T,Hv,128,128] in the
+// pool's dtype -> output [B,T,Hv,128] bf16.
+at::Tensor decode_pool(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                       const at::Tensor& A_log, const at::Tensor& a, const at::Tensor& dt_bias,
+                       const at::Tensor& b, double scale, const at::Tensor& state_pool,
+                       const at::Tensor& in_slots, const c10::optional<at::Tensor>& out_slots,
+                       const c10::optional<at::Tensor>& intermediate, bool qk_l2norm,
+                       bool no_state_update, c10::optional<at::Tensor> output) {
+  const std::pair<const at::Tensor*, const char*> ins[] = {
+      {&q, "q"}, {&k, "k"}, {&v, "v"}, {&A_log, "A_log"}, {&a, "a"}, {&dt_bias, "dt_bias"},
+      {&b, "b"}, {&state_pool, "state_pool"}, {&in_slots, "in_slots"}};
+  for (const auto& [t, n] : ins) cuda_contig(*t, n);
+  rank(q, "q", 4);
+  rank(k, "k", 4);
+  rank(v, "v", 4);
+  rank(A_log, "A_log", 1);
+  rank(a, "a", 3);
+  rank(dt_bias, "dt_bias", 1);
+  rank(b, "b", 3);
+  rank(state_pool, "state_pool", 4);
+  rank(in_slots, "in_slots", 1);
+  for (const auto& [t, n] : ins) same_device(q, *t, n);
+  dtype(q, "q", at::kBFloat16);
+  dtype(k, "k", at::kBFloat16);
+  dtype(v, "v", at::kBFloat16);
+  dtype(a, "a", at::kBFloat16);
+  dtype(b, "b", at::kBFloat16);
+  dtype(A_log, "A_log", at::kFloat);
+  dtype(dt_bias, "dt_bias", at::kFloat);
+  TORCH_CHECK_TYPE(state_pool.scalar_type() == at::kFloat || state_pool.scalar_type() == at::kBFloat16,
+                   "state_pool must be float32 or bfloat16");
+  TORCH_CHECK_TYPE(in_slots.scalar_type() == at::kInt, "in_slots must be int32");
+  const int64_t B = q.size(0), T = q.size(1), Hq = q.size(2), Hk = k.size(2), Hv = v.size(2);
+  const int64_t P = state_pool.size(0);
+  TORCH_CHECK_VALUE(k.size(0) == B && v.size(0) == B, "batch mismatch among q/k/v");
+  TORCH_CHECK_VALUE(k.size(1) == T && v.size(1) == T, "sequence length mismatch among q/k/v");
+  TORCH_CHECK_VALUE(T >= 1, "need at least one token per sequence");
+  TORCH_CHECK_VALUE(q.size(3) == kHead && k.size(3) == kHead && v.size(3) == kHead,
+                    "head size must be 128");
+  TORCH_CHECK_VALUE(Hk == Hq, "num_k_heads must equal num_q_heads");
+  TORCH_CHECK_VALUE(Hq > 0 && Hv % Hq == 0, "HV must be divisible by Hq");
+  TORCH_CHECK_VALUE(a.sizes() == at::IntArrayRef({B, T, Hv}), "a must have shape [B, T, HV]");
+  TORCH_CHECK_VALUE(b.sizes() == at::IntArrayRef({B, T, Hv}), "b must have shape [B, T, HV]");
+  TORCH_CHECK_VALUE(A_log.size(0) == Hv && dt_bias.size(0) == Hv,
+                    "A_log / dt_bias must have shape [HV]");
+  TORCH_CHECK_VALUE(state_pool.sizes() == at::IntArrayRef({P, Hv, kHead, kHead}),
+                    "state_pool must have shape [pool_size, HV, V, K]");
+  TORCH_CHECK_VALUE(in_slots.size(0) == B, "in_slots must have shape [B]");
+  if (out_slots.has_value()) {
+    cuda_contig(*out_slots, "out_slots");
+    rank(*out_slots, "out_slots", 1);
+    same_device(q, *out_slots, "out_slots");
+    TORCH_CHECK_TYPE(out_slots->scalar_type() == at::kInt, "out_slots must be int32");
+    TORCH_CHECK_VALUE(out_slots->size(0) == B, "out_slots must have shape [B]");
+  }
+  if (intermediate.has_value()) {
+    cuda_contig(*intermediate, "intermediate");
+    same_device(q, *intermediate, "intermediate");
+    TORCH_CHECK_TYPE(intermediate->scalar_type() == state_pool.scalar_type(),
+                     "intermediate must have the state_pool dtype");
+    TORCH_CHECK_VALUE(intermediate->sizes() == at::IntArrayRef({B, T, Hv, kHead, kHead}),
+                      "intermediate must have shape [B, T, HV, V, K]");
+  }
+  if (output.has_value()) {
+    cuda_contig(*output, "output");
+    dtype(*output, "output", at::kBFloat16);
+    same_device(q, *output, "output");
+    TORCH_CHECK_VALUE(output->sizes() == at::IntArrayRef({B, T, Hv, kHead}),
+                      "output must have shape [B, T, HV, V]");
+  } else {
+    output = at::empty_like(v);
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  const int flags = (qk_l2norm ? GDN_POOL_QK_L2NORM : 0) | (no_state_update ? GDN_POOL_NO_STATE_UPDATE : 0);
+  check_rc(gdn_decode_pool(q.data_ptr(), k.data_ptr(), v.data_ptr(), A_log.data_ptr<float>(), a.data_ptr(),
+                           dt_bias.data_ptr<float>(), b.data_ptr(), static_cast<float>(scale),
+                           state_pool.data_ptr(),
+                           state_pool.scalar_type() == at::kBFloat16 ? GDN_STATE_BF16 : GDN_STATE_F32, P,
+                           in_slots.data_ptr<int32_t>(),
+                           out_slots.has_value() ? out_slots->data_ptr<int32_t>() : nullptr,
+                           intermediate.has_value() ? intermediate->data_ptr() : nullptr, flags,
+                           output->data_ptr(), B, T, Hq, Hk, Hv, kHead, stream),
+           "gdn_decode_pool");
+  return *output;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -231,4 +320,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("state"), py::arg("A_log"), py::arg("a"),
         py::arg("dt_bias"), py::arg("b"), py::arg("cu_seqlens"), py::arg("scale"),
         py::arg("output") = py::none(), py::arg("new_state") = py::none(), py::arg("path") = 0);
+  m.def("decode_pool", &decode_pool, "pooled multi-token GDN decode (C ABI gdn_decode_pool)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("A_log"), py::arg("a"), py::arg("dt_bias"),
+        py::arg("b"), py::arg("scale"), py::arg("state_pool"), py::arg("in_slots"),
+        py::arg("out_slots") = py::none(), py::arg("intermediate") = py::none(),
+        py::arg("qk_l2norm") = false, py::arg("no_state_update") = false,
+        py::arg("output") = py::none());
 }

@@ -21,6 +21,8 @@ SIGNATURES = {
     "gdn_abi_version": (I, []),
     "gdn_last_error": (ctypes.c_char_p, []),
     "gdn_decode": (I, [P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, P]),
+    "gdn_decode_pool": (I, [P, P, P, P, P, P, P, F, P, I, I64, P, P, P, I, P, I64, I64, I64, I64,
+                            I64, I64, P]),
     "gdn_prefill": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P, SZ, P]),
     "gdn_prefill_workspace_bytes": (SZ, [I64, I64, I64, I64]),
     "gdn_prefill_recurrent": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P]),

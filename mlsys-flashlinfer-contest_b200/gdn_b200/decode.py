@@ -103,3 +103,43 @@ def run_inplace(q, k, v, state, A_log, a, dt_bias, b, scale):
         raise ValueError("run_inplace needs a state tensor")
     output = torch.empty_like(v)
     return launch(q, k, v, state, A_log, a, dt_bias, b, scale, output, state)
+
+
+def run_pool(q, k, v, A_log, a, dt_bias, b, scale, state_pool, in_slots, out_slots=None,
+             intermediate=None, qk_l2norm: bool = False, no_state_update: bool = False,
+             output=None):
+    """Pooled multi-token decode (the serving form; C ABI ``gdn_decode_pool``).
+
+    q, k [B,T,Hq,128] bf16; v [B,T,Hv,128] bf16; a, b [B,T,Hv] bf16;
+    state_pool [P,Hv,128,128] fp32 or bf16, updated in place: sequence i starts
+    from slot in_slots[i] (int32 [B]; negative or >= P = zero state) and its final
+    state goes to out_slots[i] (default in_slots; negative or >= P = not written).
+    intermediate: optional [B,T,Hv,128,128] tensor of the pool's dtype that gets
+    the state after every token.  qk_l2norm normalises q and k per head in the
+    kernel.  Returns output [B,T,Hv,128] bf16."""
+    ext = N.torch_ext()
+    if ext is not None:
+        return ext.decode_pool(q, k, v, A_log, a, dt_bias, b, resolve_scale(scale), state_pool,
+                               in_slots, out_slots, intermediate, qk_l2norm, no_state_update,
+                               output)
+    for name, t in (("q", q), ("k", k), ("v", v), ("A_log", A_log), ("a", a), ("dt_bias", dt_bias),
+                    ("b", b), ("state_pool", state_pool), ("in_slots", in_slots)):
+        cuda_contig(name, t)
+    if state_pool.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("state_pool must be float32 or bfloat16")
+    if in_slots.dtype != torch.int32 or (out_slots is not None and out_slots.dtype != torch.int32):
+        raise TypeError("slot indices must be int32")
+    B, T, Hq, _ = q.shape
+    Hv = v.shape[2]
+    if output is None:
+        output = torch.empty_like(v)
+    flags = (1 if qk_l2norm else 0) | (2 if no_state_update else 0)
+    with torch.cuda.device(q.device):
+        rc = N.lib().gdn_decode_pool(
+            N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(A_log), N.ptr(a), N.ptr(dt_bias), N.ptr(b),
+            resolve_scale(scale), N.ptr(state_pool), 1 if state_pool.dtype == torch.bfloat16 else 0,
+            state_pool.shape[0], N.ptr(in_slots), N.ptr(out_slots), N.ptr(intermediate), flags,
+            N.ptr(output), B, T, Hq, k.shape[2], Hv, HEAD, N.stream_handle(q.device))
+    N.check(rc, "gdn_decode_pool")
+    return output
+

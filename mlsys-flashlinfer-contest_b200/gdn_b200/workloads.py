@@ -103,6 +103,58 @@ def make_decode_inputs(B: int, Hq: int = 16, Hv: int = 32, seed: int = 0,
     return DecodeInputs(q, k, v, state, A_log, a, dt_bias, b, 1.0 / math.sqrt(d))
 
 
+@dataclass
+class DecodePoolInputs:
+    q: torch.Tensor       # [B,T,Hq,128] bf16
+    k: torch.Tensor
+    v: torch.Tensor       # [B,T,Hv,128] bf16
+    A_log: torch.Tensor
+    a: torch.Tensor       # [B,T,Hv] bf16
+    dt_bias: torch.Tensor
+    b: torch.Tensor
+    scale: float
+    pool: torch.Tensor    # [P,Hv,128,128] fp32 or bf16
+    in_slots: torch.Tensor   # [B] int32
+    out_slots: torch.Tensor  # [B] int32
+
+
+def make_decode_pool_inputs(B: int, T: int, Hq: int, Hv: int, pool_size: int, seed: int = 0,
+                            device="cpu", state_bf16: bool = False, normalized_qk: bool = True,
+                            state_std: float = 0.05) -> DecodePoolInputs:
+    """Pooled multi-token decode inputs: T tokens per sequence, a state pool of
+    ``pool_size`` slots, read slots a seeded choice of distinct slots (the first
+    sequence reads slot -1: zero state).  Sequences write back in place, except
+    that every third one writes to a slot nobody reads (while free slots last) and
+    the last one writes slot -1 (no write-back): no slot is both read and written
+    by different sequences, which would race.  ``normalized_qk=False`` leaves q, k
+    un-normalised (for the in-kernel L2 norm)."""
+    assert pool_size >= B
+    gen = _gen(device, seed)
+    d = HEAD_SIZE
+    q = _normal((B, T, Hq, d), gen, device)
+    k = _normal((B, T, Hq, d), gen, device)
+    q = _l2norm_bf16(q) if normalized_qk else q.to(torch.bfloat16)
+    k = _l2norm_bf16(k) if normalized_qk else k.to(torch.bfloat16)
+    v = _normal((B, T, Hv, d), gen, device).to(torch.bfloat16)
+    A_log, dt_bias = head_params(Hv, gen, device)
+    a = _normal((B, T, Hv), gen, device).to(torch.bfloat16)
+    b = _normal((B, T, Hv), gen, device).to(torch.bfloat16)
+    pool = _normal((pool_size, Hv, d, d), gen, device, state_std)
+    if state_bf16:
+        pool = pool.to(torch.bfloat16)
+    cpu_gen = _gen("cpu", seed + 1)
+    perm = torch.randperm(pool_size, generator=cpu_gen).to(torch.int32)
+    ins, free = perm[:B].clone(), [int(x) for x in perm[B:]]
+    outs = ins.clone()
+    for i in range(0, B, 3):
+        if free:
+            outs[i] = free.pop()
+    ins[0] = -1
+    outs[-1] = -1
+    return DecodePoolInputs(q, k, v, A_log, a, dt_bias, b, 1.0 / math.sqrt(d), pool,
+                            ins.to(device), outs.to(device))
+
+
 def varlen_lengths(n: int, lo: int, hi: int, seed: int) -> list:
     """n sequence lengths ~ U[lo, hi] (inclusive), seeded."""
     gen = _gen("cpu", seed)

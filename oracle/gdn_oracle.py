@@ -144,6 +144,56 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale):
     return f32_to_bf16(o[:, None].astype(np.float32)), new_state
 
 
+def l2norm_heads(x):
+    """x / sqrt(sum x^2 + 1e-6) over the last axis, in fp32 (the in-kernel q/k
+    normalisation of the pooled decode)."""
+    x = np.asarray(x, np.float32)
+    return x / np.sqrt(np.sum(x * x, axis=-1, keepdims=True, dtype=np.float32) + np.float32(1e-6))
+
+
+def decode_pool(q, k, v, A_log, a, dt_bias, b, scale, pool, in_slots, out_slots=None,
+                state_bf16=False, qk_l2norm=False, no_state_update=False, cache=False):
+    """Pooled multi-token decode (the serving form; no reference counterpart).
+
+    q, k [B,T,Hq,128]; v [B,T,Hv,128]; a, b [B,T,Hv] (float32 arrays holding the
+    bf16 values); pool [P,Hv,V,K] (fp32 values; with state_bf16 they are bf16
+    values and every stored state is rounded to bf16).  Sequence i starts from
+    pool[in_slots[i]] (zero if the slot is negative or >= P), applies its T tokens
+    in order with the decode step of definitions/gdn/gdn_decode_qk4_v8_d128_k_last.md:96-132
+    (the ``decode`` above, one token at a time), and writes its final state to
+    pool[out_slots[i]] (default in_slots; skipped if negative, >= P or
+    no_state_update).  Returns (o as bf16 bits [B,T,Hv,128], new pool,
+    per-token states [B,T,Hv,V,K] or None)."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    B, T, Hq, _ = q.shape
+    Hv = v.shape[2]
+    P = pool.shape[0]
+    if qk_l2norm:
+        q, k = l2norm_heads(q), l2norm_heads(k)
+    rnd = round_bf16 if state_bf16 else (lambda x: np.asarray(x, np.float32))
+    new_pool = np.array(pool, np.float32, copy=True)
+    o = np.zeros((B, T, Hv, HEAD), np.uint16)
+    inter = np.zeros((B, T, Hv, HEAD, HEAD), np.float32) if cache else None
+    ins = [int(x) for x in np.asarray(in_slots).reshape(-1)]
+    outs = ins if out_slots is None else [int(x) for x in np.asarray(out_slots).reshape(-1)]
+    finals = []
+    for i in range(B):
+        S = pool[ins[i]][None] if 0 <= ins[i] < P else None
+        for t in range(T):
+            ob, S = decode(q[i:i + 1, t:t + 1], k[i:i + 1, t:t + 1], v[i:i + 1, t:t + 1], S, A_log,
+                           a[i:i + 1, t:t + 1], dt_bias, b[i:i + 1, t:t + 1], scale)
+            o[i, t] = ob[0, 0]
+            if cache:
+                inter[i, t] = rnd(S[0])
+        finals.append(S[0])
+    if not no_state_update:
+        for i in range(B):
+            if 0 <= outs[i] < P:
+                new_pool[outs[i]] = rnd(finals[i])
+    return o, new_pool, inter
+
+
 # ---------------------------------------------------------------- prefill
 def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
     """GDN prefill over packed variable-length sequences.  q, k [T,Hq,128];

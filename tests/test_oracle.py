@@ -157,3 +157,31 @@ def test_contest_shapes_span_the_axes():
     assert all(min(c) >= 1 for c in cases)
     assert sum(1 for n in seqs if n <= 4) >= len(cases) // 2
     assert W.CONTEST_DECODE_BATCHES[0] == 1 and W.CONTEST_DECODE_BATCHES[-1] == 64
+
+
+def test_oracle_decode_pool_reduces_to_decode():
+    """One token, identity slots, fp32: the pooled oracle is the definition's decode."""
+    inp = W.make_decode_inputs(3, 4, 8, seed=4)
+    a = O.to_numpy
+    o_ref, s_ref = O.decode(*[a(x) if hasattr(x, "numpy") else x for x in inp.args()])
+    o, pool, inter = O.decode_pool(a(inp.q), a(inp.k), a(inp.v), a(inp.A_log), a(inp.a),
+                                   a(inp.dt_bias), a(inp.b), inp.scale, a(inp.state),
+                                   np.arange(3), cache=True)
+    assert (o == o_ref).all()
+    assert np.array_equal(pool, s_ref) and np.array_equal(inter[:, 0], s_ref)
+
+
+def test_oracle_decode_pool_slots_and_l2norm():
+    """Slot -1 reads a zero state and is never written; T tokens equal T single steps."""
+    inp = W.make_decode_pool_inputs(3, 2, 4, 8, 4, seed=5, normalized_qk=False)
+    a = O.to_numpy
+    args = (a(inp.q), a(inp.k), a(inp.v), a(inp.A_log), a(inp.a), a(inp.dt_bias), a(inp.b),
+            inp.scale)
+    o, pool, _ = O.decode_pool(*args, a(inp.pool), a(inp.in_slots), a(inp.out_slots),
+                               qk_l2norm=True)
+    written = set(int(x) for x in a(inp.out_slots) if x >= 0)
+    for s in range(4):
+        if s not in written:
+            assert np.array_equal(pool[s], a(inp.pool)[s])
+    qn = O.l2norm_heads(args[0])
+    assert np.allclose(np.sum(qn * qn, axis=-1), 1.0, atol=1e-5)
