@@ -269,6 +269,10 @@ def run_ours(args, rank, world, local_rank, dist):
     if not args.no_prefill:
         prefill = run_prefill_bench(args, rank, world, local_rank, dev, dist)
 
+    pool = None
+    if world == 1 and not args.no_pool:
+        pool = run_pool_bench(args, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = time_cpu_decode(args.cpu_budget)
@@ -294,6 +298,7 @@ def run_ours(args, rank, world, local_rank, dist):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "decode_pool": pool,
         }
         print(json.dumps(line), flush=True)
 
@@ -337,6 +342,47 @@ def run_e2e(args, inp, dev, stream, dist, world):
     return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps, "us_per_step": round(ms / steps * 1e3, 2),
             "api": "gdn_b200.decode.run", "state": "resident in HBM across steps"}
+
+
+def run_pool_bench(args, dev):
+    """Pooled decode (C ABI gdn_decode_pool) at the config-1 batch: B = 256 sequences
+    x Hv = 32 heads, pool of 256 slots updated in place, fp32 and bf16 state, one
+    token and four tokens per sequence.  Algorithmic bytes per (sequence, v-head):
+    the state read and written once (2 x 64 KiB fp32, 2 x 32 KiB bf16) plus, per
+    token, v, o (256 B each), q, k (256 B, shared by the GVA pair) and a, b."""
+    from gdn_b200 import decode, workloads as W
+    hbm_peak, _, _, _ = measured_peaks()
+    res = {}
+    for name, bf16, T in (("f32_t1", False, 1), ("bf16_t1", True, 1), ("bf16_t4", True, 4)):
+        inp = W.make_decode_pool_inputs(B_PER_RANK, T, HQ, HV, B_PER_RANK, seed=4242, device=dev,
+                                        state_bf16=bf16)
+        slots = torch.arange(B_PER_RANK, dtype=torch.int32, device=dev)
+        out = torch.empty_like(inp.v)
+
+        def step():
+            decode.run_pool(inp.q, inp.k, inp.v, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                            inp.pool, slots, output=out)
+
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        steps = max(args.steps // 5, 20)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / steps * 1e3
+        unit = 2 * D * D * (2 if bf16 else 4) + T * (256 + 256 + 256 + 4)
+        gbs = B_PER_RANK * HV * unit / (us / 1e6) / 1e9
+        res[name] = {"state_dtype": "bf16" if bf16 else "f32", "tokens_per_seq": T,
+                     "us_per_step": round(us, 2), "tokens_per_s": round(B_PER_RANK * T / (us / 1e6), 1),
+                     "GB_per_s": round(gbs, 1), "roofline_frac": round(gbs / hbm_peak, 4),
+                     "algorithmic_bytes_per_step": B_PER_RANK * HV * unit}
+    return {"api": "gdn_b200.decode.run_pool (C ABI gdn_decode_pool)", "batch": B_PER_RANK,
+            "num_v_heads": HV, "pool": "256 slots, in place; larger than L2 in every case",
+            "results": res}
 
 
 def run_prefill_bench(args, rank, world, local_rank, dev, dist):
@@ -527,6 +573,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-pool", action="store_true", help="skip the pooled-decode leg")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--batch-per-rank", type=int, default=256,
                     help="sequences per rank (default 256 = BASELINE config 1; smaller only for profiling)")

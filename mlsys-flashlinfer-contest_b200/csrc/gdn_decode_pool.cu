@@ -19,10 +19,12 @@
 // old_v = k . (g S[v]), S'[v] = g S[v] + beta k (v[v] - old_v), o[v] = scale q . S'[v].
 //
 // Mapping: a CTA of 256 threads owns 32*U consecutive state rows of one (b, h);
-// each aligned octet of 8 lanes owns one row at a time and lane j of the octet
-// holds the 16 contiguous elements k in [16 j, 16 j + 16) (64 bytes in fp32, 32 in
-// bf16: whole 128-byte segments per octet).  All state loads of a thread are
-// issued before any use.
+// each aligned octet of 8 lanes owns one row at a time.  Lane j of the octet holds
+// 16 of the row's elements such that every 16-byte load of the octet covers one
+// contiguous 128-byte segment: k = 32 i + 4 j + c (i < 4, c < 4) for fp32 storage,
+// k = 64 i + 8 j + c (i < 2, c < 8) for bf16; q and k are read in the same
+// pattern.  All state loads of a thread are issued before any use, and the
+// inputs of token t+1 are loaded while token t is applied.
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 
@@ -45,35 +47,41 @@ __device__ __forceinline__ void st_stream_u4(void* p, uint4 v) {
                : "memory");
 }
 
-// 16 contiguous bf16 through the read-only path, widened to fp32.
-__device__ __forceinline__ void ld_bf16x16(const __nv_bfloat16* p, float* out) {
-  uint4 w[2];
+// This lane's 16 elements of a bf16 vector of 128 (q or k), widened to fp32, in
+// the lane pattern of the state storage (see the mapping above).
+template <bool BF16>
+__device__ __forceinline__ void ld_vec16(const __nv_bfloat16* row, int j, float* out) {
+  if constexpr (BF16) {
 #pragma unroll
-  for (int h = 0; h < 2; ++h)
-    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(w[h].x), "=r"(w[h].y), "=r"(w[h].z), "=r"(w[h].w)
-                 : "l"(p + 8 * h));
+    for (int i = 0; i < 2; ++i) {
+      uint4 w;
+      asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                   : "l"(row + 64 * i + 8 * j));
+      out[8 * i + 0] = bf16_lo(w.x);
+      out[8 * i + 1] = bf16_hi(w.x);
+      out[8 * i + 2] = bf16_lo(w.y);
+      out[8 * i + 3] = bf16_hi(w.y);
+      out[8 * i + 4] = bf16_lo(w.z);
+      out[8 * i + 5] = bf16_hi(w.z);
+      out[8 * i + 6] = bf16_lo(w.w);
+      out[8 * i + 7] = bf16_hi(w.w);
+    }
+  } else {
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    out[8 * h + 0] = bf16_lo(w[h].x);
-    out[8 * h + 1] = bf16_hi(w[h].x);
-    out[8 * h + 2] = bf16_lo(w[h].y);
-    out[8 * h + 3] = bf16_hi(w[h].y);
-    out[8 * h + 4] = bf16_lo(w[h].z);
-    out[8 * h + 5] = bf16_hi(w[h].z);
-    out[8 * h + 6] = bf16_lo(w[h].w);
-    out[8 * h + 7] = bf16_hi(w[h].w);
+    for (int i = 0; i < 4; ++i) ld_bf16x4(row + 32 * i + 4 * j, out + 4 * i);
   }
 }
 
-// One lane's 16 state elements of a row: load from / store to fp32 or bf16 storage.
+// One lane's 16 state elements of a row (row start at element offset `elem`):
+// load from / store to fp32 or bf16 storage.
 template <bool BF16>
-__device__ __forceinline__ void load_row16(const void* base, int64_t elem, float* s) {
+__device__ __forceinline__ void load_row16(const void* base, int64_t elem, int j, float* s) {
   if constexpr (BF16) {
-    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(base) + elem;
+    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(base) + elem + 8 * j;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const uint4 w = ld_stream_u4(p + 8 * h);
+      const uint4 w = ld_stream_u4(p + 64 * h);
       s[8 * h + 0] = bf16_lo(w.x);
       s[8 * h + 1] = bf16_hi(w.x);
       s[8 * h + 2] = bf16_lo(w.y);
@@ -84,10 +92,10 @@ __device__ __forceinline__ void load_row16(const void* base, int64_t elem, float
       s[8 * h + 7] = bf16_hi(w.w);
     }
   } else {
-    const float* p = static_cast<const float*>(base) + elem;
+    const float* p = static_cast<const float*>(base) + elem + 4 * j;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float4 x = ld_stream_f4(p + 4 * i);
+      const float4 x = ld_stream_f4(p + 32 * i);
       s[4 * i + 0] = x.x;
       s[4 * i + 1] = x.y;
       s[4 * i + 2] = x.z;
@@ -97,25 +105,27 @@ __device__ __forceinline__ void load_row16(const void* base, int64_t elem, float
 }
 
 template <bool BF16>
-__device__ __forceinline__ void store_row16(void* base, int64_t elem, const float* s) {
+__device__ __forceinline__ void store_row16(void* base, int64_t elem, int j, const float* s) {
   if constexpr (BF16) {
-    __nv_bfloat16* p = static_cast<__nv_bfloat16*>(base) + elem;
+    __nv_bfloat16* p = static_cast<__nv_bfloat16*>(base) + elem + 8 * j;
 #pragma unroll
     for (int h = 0; h < 2; ++h)
-      st_stream_u4(p + 8 * h, make_uint4(pack_bf16x2(s[8 * h + 0], s[8 * h + 1]),
+      st_stream_u4(p + 64 * h, make_uint4(pack_bf16x2(s[8 * h + 0], s[8 * h + 1]),
                                          pack_bf16x2(s[8 * h + 2], s[8 * h + 3]),
                                          pack_bf16x2(s[8 * h + 4], s[8 * h + 5]),
                                          pack_bf16x2(s[8 * h + 6], s[8 * h + 7])));
   } else {
-    float* p = static_cast<float*>(base) + elem;
+    float* p = static_cast<float*>(base) + elem + 4 * j;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      st_stream_f4(p + 4 * i, make_float4(s[4 * i + 0], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]));
+      st_stream_f4(p + 32 * i, make_float4(s[4 * i + 0], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]));
   }
 }
 
-template <int U, bool BF16, bool L2NORM>
-__global__ void __launch_bounds__(kThreads) gdn_decode_pool_kernel(DecodePoolArgs p) {
+// MTP: T > 1 (the next token's inputs are prefetched); two CTAs per SM keep the
+// slot lookup, a dependent load in front of every state stream, overlapped.
+template <int U, bool BF16, bool L2NORM, bool MTP>
+__global__ void __launch_bounds__(kThreads, 2) gdn_decode_pool_kernel(DecodePoolArgs p) {
   constexpr int kRows = 32 * U;
   constexpr int kTilesPerHead = kHead / kRows;
   const int64_t cta = blockIdx.x;
@@ -139,9 +149,9 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_pool_kernel(DecodePoolArg
 
   float s[U][16];
   if (has_in) {
-    const int64_t base = (static_cast<int64_t>(sin) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 16 * j;
+    const int64_t base = (static_cast<int64_t>(sin) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead;
 #pragma unroll
-    for (int u = 0; u < U; ++u) load_row16<BF16>(p.pool, base + u * 4 * kHead, s[u]);
+    for (int u = 0; u < U; ++u) load_row16<BF16>(p.pool, base + u * 4 * kHead, j, s[u]);
   } else {
 #pragma unroll
     for (int u = 0; u < U; ++u)
@@ -151,59 +161,75 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_pool_kernel(DecodePoolArg
 
   const __nv_bfloat16* a_ptr = static_cast<const __nv_bfloat16*>(p.a);
   const __nv_bfloat16* b_ptr = static_cast<const __nv_bfloat16*>(p.b);
+  const __nv_bfloat16* q_ptr = static_cast<const __nv_bfloat16*>(p.q);
+  const __nv_bfloat16* k_ptr = static_cast<const __nv_bfloat16*>(p.k);
+  const __nv_bfloat16* v_ptr = static_cast<const __nv_bfloat16*>(p.v);
   const float A_log = p.A_log[h], dt_bias = p.dt_bias[h];
-  for (int t = 0; t < p.T; ++t) {
+  // inputs of one token: raw gates, q, k (this lane's 16 elements), v of this
+  // thread's rows
+  struct Tok {
+    float ga, gb, kf[16], qf[16], vv[U];
+  };
+  auto load_tok = [&](int t, Tok& x) {
     const int64_t bt = bidx * p.T + t;
-    const float g = expf(log_decay(A_log, __bfloat162float(a_ptr[bt * p.Hv + h]), dt_bias));
-    const float beta = sigmoidf_acc(__bfloat162float(b_ptr[bt * p.Hv + h]));
-    float kf[16], qf[16];
-    ld_bf16x16(static_cast<const __nv_bfloat16*>(p.k) + (bt * p.Hq + qh) * kHead + 16 * j, kf);
-    ld_bf16x16(static_cast<const __nv_bfloat16*>(p.q) + (bt * p.Hq + qh) * kHead + 16 * j, qf);
+    x.ga = __bfloat162float(a_ptr[bt * p.Hv + h]);
+    x.gb = __bfloat162float(b_ptr[bt * p.Hv + h]);
+    ld_vec16<BF16>(k_ptr + (bt * p.Hq + qh) * kHead, j, x.kf);
+    ld_vec16<BF16>(q_ptr + (bt * p.Hq + qh) * kHead, j, x.qf);
+#pragma unroll
+    for (int u = 0; u < U; ++u) x.vv[u] = __bfloat162float(v_ptr[(bt * p.Hv + h) * kHead + row0 + 4 * u]);
+  };
+  Tok cur;
+  load_tok(0, cur);
+  for (int t = 0; t < p.T; ++t) {
+    Tok nxt;
+    if (MTP && t + 1 < p.T) load_tok(t + 1, nxt);
+    const int64_t bt = bidx * p.T + t;
+    const float g = expf(log_decay(A_log, cur.ga, dt_bias));
+    const float beta = sigmoidf_acc(cur.gb);
     if constexpr (L2NORM) {
       float sk = 0.0f, sq = 0.0f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        sk = fmaf(kf[c], kf[c], sk);
-        sq = fmaf(qf[c], qf[c], sq);
+        sk = fmaf(cur.kf[c], cur.kf[c], sk);
+        sq = fmaf(cur.qf[c], cur.qf[c], sq);
       }
       const float rk = rsqrtf(octet_sum(sk) + 1e-6f), rq = rsqrtf(octet_sum(sq) + 1e-6f);
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        kf[c] *= rk;
-        qf[c] *= rq;
+        cur.kf[c] *= rk;
+        cur.qf[c] *= rq;
       }
     }
-    const __nv_bfloat16* vrow = static_cast<const __nv_bfloat16*>(p.v) + (bt * p.Hv + h) * kHead;
     __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (bt * p.Hv + h) * kHead;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int row = row0 + 4 * u;
-      const float vv = __bfloat162float(vrow[row]);
       float dot = 0.0f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         s[u][c] *= g;
-        dot = fmaf(kf[c], s[u][c], dot);
+        dot = fmaf(cur.kf[c], s[u][c], dot);
       }
-      const float delta = beta * (vv - octet_sum(dot));
+      const float delta = beta * (cur.vv[u] - octet_sum(dot));
       float ov = 0.0f;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        s[u][c] = fmaf(kf[c], delta, s[u][c]);
-        ov = fmaf(qf[c], s[u][c], ov);
+        s[u][c] = fmaf(cur.kf[c], delta, s[u][c]);
+        ov = fmaf(cur.qf[c], s[u][c], ov);
       }
       ov = octet_sum(ov);
       if (j == 0) orow[row] = __float2bfloat16_rn(p.scale * ov);
       if (p.intermediate)
-        store_row16<BF16>(p.intermediate, (bt * p.Hv + h) * kTile + static_cast<int64_t>(row) * kHead + 16 * j,
-                          s[u]);
+        store_row16<BF16>(p.intermediate, (bt * p.Hv + h) * kTile + static_cast<int64_t>(row) * kHead, j, s[u]);
     }
+    if (MTP && t + 1 < p.T) cur = nxt;
   }
 
   if (write_back) {
-    const int64_t base = (static_cast<int64_t>(sout) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 16 * j;
+    const int64_t base = (static_cast<int64_t>(sout) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead;
 #pragma unroll
-    for (int u = 0; u < U; ++u) store_row16<BF16>(p.pool, base + u * 4 * kHead, s[u]);
+    for (int u = 0; u < U; ++u) store_row16<BF16>(p.pool, base + u * 4 * kHead, j, s[u]);
   }
 }
 
@@ -211,10 +237,18 @@ template <int U, bool BF16>
 cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
   const int64_t ctas = a.B * a.Hv * (kHead / (32 * U));
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (a.qk_l2norm)
-    gdn_decode_pool_kernel<U, BF16, true><<<static_cast<unsigned>(ctas), kThreads, 0, s>>>(a);
-  else
-    gdn_decode_pool_kernel<U, BF16, false><<<static_cast<unsigned>(ctas), kThreads, 0, s>>>(a);
+  const unsigned grid = static_cast<unsigned>(ctas);
+  if (a.T > 1) {
+    if (a.qk_l2norm)
+      gdn_decode_pool_kernel<U, BF16, true, true><<<grid, kThreads, 0, s>>>(a);
+    else
+      gdn_decode_pool_kernel<U, BF16, false, true><<<grid, kThreads, 0, s>>>(a);
+  } else {
+    if (a.qk_l2norm)
+      gdn_decode_pool_kernel<U, BF16, true, false><<<grid, kThreads, 0, s>>>(a);
+    else
+      gdn_decode_pool_kernel<U, BF16, false, false><<<grid, kThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 
@@ -222,7 +256,9 @@ template <bool BF16>
 cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
   // enough CTAs to fill the 148 SMs several times before the tile grows
   const int64_t tiles = a.B * a.Hv;
-  if (tiles >= 4 * 148) return launch_u<4, BF16>(a, s);
+  // (multi-token: at most 64 rows per thread block, whose registers also hold
+  // the next token's inputs)
+  if (tiles >= 4 * 148 && a.T == 1) return launch_u<4, BF16>(a, s);
   if (tiles >= 2 * 148) return launch_u<2, BF16>(a, s);
   return launch_u<1, BF16>(a, s);
 }
