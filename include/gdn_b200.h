@@ -140,6 +140,27 @@ int gdn_prefill_recurrent(const void *q, const void *k, const void *v, const flo
                           int64_t num_k_heads, int64_t num_v_heads, int64_t head_size,
                           void *stream);
 
+/* gdn_prefill_ex flags and paths */
+#define GDN_PREFILL_QK_L2NORM 1   /* L2-normalise q and k per head: x / sqrt(sum x^2 + 1e-6) */
+#define GDN_PREFILL_PATH_AUTO 0   /* the dispatch of gdn_prefill */
+#define GDN_PREFILL_PATH_RECURRENT 1
+#define GDN_PREFILL_PATH_CHUNKED 2
+
+/*
+ * gdn_prefill with options (no workspace: none of the kernels needs one).  The
+ * reference's prefill entry has no flags; GDN_PREFILL_QK_L2NORM is the in-kernel
+ * q/k normalisation that FlashInfer's chunk_gated_delta_rule exposes as
+ * use_qk_l2norm_in_kernel (rejected by the reference's baseline wrapper,
+ * reference_solutions/.../flashinfer_wrapper_123ca6.md:271-273).  The chunked path
+ * folds 1/|k_t| and 1/|q_t| into per-token factors instead of rescaling q and k.
+ */
+int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *state,
+                   const float *A_log, const void *a, const float *dt_bias, const void *b,
+                   const int64_t *cu_seqlens, float scale, void *output, float *new_state,
+                   int64_t total_seq_len, int64_t num_seqs, int64_t num_q_heads,
+                   int64_t num_k_heads, int64_t num_v_heads, int64_t head_size, int flags,
+                   int path, void *stream);
+
 /*
  * Chunk metadata (chunk size 64) for packed sequences.
  * Replaces prep_meta_v2 (gdn_prefill/solution/python/cuda_prep_meta_v2.cu:72-94),

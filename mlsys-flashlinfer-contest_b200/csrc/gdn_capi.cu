@@ -193,6 +193,28 @@ int gdn_prefill(const void* q, const void* k, const void* v, const float* state,
                              new_state, T, N, Hq, Hk, Hv, D, stream);
 }
 
+int gdn_prefill_ex(const void* q, const void* k, const void* v, const float* state,
+                   const float* A_log, const void* a, const float* dt_bias, const void* b,
+                   const int64_t* cu_seqlens, float scale, void* output, float* new_state, int64_t T,
+                   int64_t N, int64_t Hq, int64_t Hk, int64_t Hv, int64_t D, int flags, int path,
+                   void* stream) {
+  if (flags & ~GDN_PREFILL_QK_L2NORM) return fail(GDN_ERR_VALUE, "unknown flags");
+  if (path < GDN_PREFILL_PATH_AUTO || path > GDN_PREFILL_PATH_CHUNKED)
+    return fail(GDN_ERR_VALUE, "unknown path");
+  if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
+                            N, Hq, Hk, Hv, D))
+    return e;
+  if (T > 0x7fffffffLL - 64) return fail(GDN_ERR_VALUE, "total_seq_len too large");
+  gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                     scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv,
+                     (flags & GDN_PREFILL_QK_L2NORM) != 0};
+  const bool recurrent =
+      path == GDN_PREFILL_PATH_RECURRENT || (path == GDN_PREFILL_PATH_AUTO && use_recurrent(T, N));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return recurrent ? cuda_status(gdn::launch_prefill_recurrent(p, st), "gdn_prefill_recurrent launch")
+                   : cuda_status(gdn::launch_prefill_chunked(p, st), "gdn_prefill_chunked launch");
+}
+
 int gdn_prefill_chunked_debug(const void* q, const void* k, const void* v, const float* state,
                               const float* A_log, const void* a, const float* dt_bias,
                               const void* b, const int64_t* cu_seqlens, float scale, void* output,

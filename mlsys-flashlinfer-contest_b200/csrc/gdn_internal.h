@@ -66,6 +66,7 @@ struct PrefillArgs {
   void* out;               // [T,Hv,128] bf16
   float* new_state;        // [N,Hv,128,128] fp32
   int64_t T, N, Hq, Hv;
+  bool qk_l2norm = false;  // L2-normalise q and k per head: x / sqrt(sum x^2 + 1e-6)
 };
 
 cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);

@@ -89,7 +89,9 @@ constexpr int G_D = 128;     // 2^(gamma_t - gamma_{t-1}): per-token decay facto
 constexpr int G_DEC = 192;   // 2^(gamma_63 - gamma_t) for valid tokens, else 0
 constexpr int G_EG = 256;    // scale * 2^gamma_t
 constexpr int G_E2 = 320;    // 2^gamma_t
-constexpr int kGateFloats = 384;
+constexpr int G_RK = 384;    // 1 / |k_t| (q/k L2 norm only)
+constexpr int G_RQ = 448;    // 1 / |q_t| (q/k L2 norm only)
+constexpr int kGateFloats = 512;
 constexpr uint32_t kMiscBarOff = 2 * kGateFloats * 4;  // barriers after both table buffers
 constexpr uint32_t kSmemBytes = OFF_MISC + kMiscBarOff + 256 + 1024;  // + slack for the 1024 alignment
 
@@ -165,7 +167,9 @@ __device__ __forceinline__ void load_table16(const float* src, float* v) {
   }
 }
 
-template <bool DEBUG>
+// L2: q/k L2 norm folded in as per-token factors (a separate instantiation so the
+// plain kernel carries none of it).
+template <bool DEBUG, bool L2>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                                const __grid_constant__ CUtensorMap tm_k,
@@ -344,6 +348,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 32; ++i) p.debug[DBG_ST + rowv * 128 + 32 * cq + i] = v[i];
     };
 
+    // q/k L2 norm: 1 / sqrt(sum x^2 + 1e-6) of every K and Q row of chunk cc's
+    // stage (rows 0-63 K, 64-127 Q; a row's 64 elements of a 128-byte line are
+    // permuted by the swizzle, which a sum of squares ignores), four threads per
+    // row.  The factors scale A/P columns and rows, K S columns, Vd rows and the
+    // Q S columns of the output instead of the operands themselves.
+    auto qk_norms = [&](int cc) {
+      const int r = tid >> 2, part = tid & 3;
+      const uint32_t base = sb + OFF_KQ + (cc & 1) * kKQStage + r * 128 + part * 32;
+      float acc = 0.f;
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint4 w = lds128(base + kb * 16384 + hh * 16);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float lo = bf16_lo(ws[e]), hi = bf16_hi(ws[e]);
+            acc = fmaf(lo, lo, fmaf(hi, hi, acc));
+          }
+        }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (part == 0) gates_buf[(cc & 1) * kGateFloats + (r < 64 ? G_RK + r : G_RQ + r - 64)] = rsqrtf(acc + 1e-6f);
+    };
+
     if (warp == 1) {
       prefetch_gates(0);
       compute_gates(0);
@@ -351,6 +381,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = tid; i < 8192 / 16; i += kComputeThreads)  // Bl: zero off the diagonal
       sts128(sb + OFF_BL + 16 * i, 0u, 0u, 0u, 0u);
+    if constexpr (L2) {  // chunk 0's factors, published by the first loop-top barrier
+      wait_mma(BAR_M1, 0u);
+      qk_norms(0);
+    }
     bool aborted = false;
 
     for (int c = 0; c < nchunks; ++c) {
@@ -421,6 +455,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         reg_fence(v);
         PHASE(4)
+        if constexpr (L2) {  // A[i][j] / (|k_i| |k_j|), P[i][j] / (|q_i| |k_j|)
+          float rc[16];
+          load_table16(gam + G_RK + 16 * cq, rc);
+          const float rr = quarter < 2 ? gam[G_RK + i] : gam[G_RQ + i];
+#pragma unroll
+          for (int jj = 0; jj < 16; jj += 2) {
+            const float2 x = mul2(v[jj], v[jj + 1], rc[jj] * rr, rc[jj + 1] * rr);
+            v[jj] = x.x;
+            v[jj + 1] = x.y;
+          }
+        }
         // e^{gamma_i - gamma_j} for this block's 16 columns, walking down each
         // group of 4 from its highest column j <= i with e(j-1) = e(j) d_j,
         // d_j = e^{gamma_j - gamma_{j-1}} <= 1: one ex2 per group, the rest on
@@ -476,6 +521,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem + lane_base + TM_KQS + 16 * grp, v);
         float e2[16];  // 2^g_s of these 16 tokens
         load_table16(gam + G_E2 + 16 * grp, e2);
+        if constexpr (L2) {  // K S columns / |k_s|
+          float rk[16];
+          load_table16(gam + G_RK + 16 * grp, rk);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) e2[e] *= rk[e];
+        }
         tmem_wait_ld();
         reg_fence(v);
         uint32_t w[8];
@@ -695,6 +746,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         reg_fence(x);
         float dc[16];  // 2^(g63 - g_t) of this warp's 16 tokens (0 past the end)
         load_table16(gam + G_DEC + 16 * cq, dc);
+        if constexpr (L2) {  // Vd rows / |k_t|: the state update with normalised K
+          float rk[16];
+          load_table16(gam + G_RK + 16 * cq, rk);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) dc[e] *= rk[e];
+        }
         if (L < kChunk) {  // partial chunk: tokens past the end contribute nothing
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -721,6 +778,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
       }
       signal(RDY_V, false);
+      if (L2 && c + 1 < nchunks) {  // next chunk's factors, in the PV wait
+        wait_mma(BAR_M1, par ^ 1u);
+        qk_norms(c + 1);
+      }
       PHASE(12)
       if (DEBUG && dbg_cta && c == p.dbg_chunk + 2 && lane == 0) p.debug[DBG_EV + warp * 5 + 0] = float(clock64() - t_base);
       wait_mma(BAR_PV, par);
@@ -748,6 +809,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t tstride = static_cast<int64_t>(p.Hv) * kHead;
         float eg[16];  // scale * 2^g_t of this warp's 16 tokens
         load_table16(gam + G_EG + 16 * cq, eg);
+        if constexpr (L2) {  // Q S columns / |q_t|
+          float rq[16];
+          load_table16(gam + G_RQ + 16 * cq, rq);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) eg[e] *= rq[e];
+        }
         __nv_bfloat16* orow = p.out + (t0 * p.Hv + h) * kHead + rowv;
         float o[16];
 #pragma unroll
@@ -1056,12 +1123,15 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   const int tma_out = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) ? 1 : 0;
   memset(&mo, 0, sizeof(mo));
   if (tma_out && (e = make_head_map(&mo, a.out, a.Hv, a.T)) != cudaSuccess) return e;
-  static bool attr_set = false;
-  if (!attr_set) {
-    e = cudaFuncSetAttribute(gdn_prefill_chunked_kernel<DEBUG>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  auto kernel = gdn_prefill_chunked_kernel<DEBUG, false>;
+  if constexpr (!DEBUG) {
+    if (a.qk_l2norm) kernel = gdn_prefill_chunked_kernel<false, true>;
+  }
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[a.qk_l2norm ? 1 : 0]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set[a.qk_l2norm ? 1 : 0] = true;
   }
   ChunkParams p{a.state, a.A_log, a.dt_bias,
                 static_cast<const __nv_bfloat16*>(a.a), static_cast<const __nv_bfloat16*>(a.b),
@@ -1070,8 +1140,7 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
                 dbg_chunk};
   const int64_t ctas = a.N * a.Hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  gdn_prefill_chunked_kernel<DEBUG><<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(
-      mq, mk, mv, mo, p);
+  kernel<<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, p);
   return cudaGetLastError();
 }
 

@@ -8,6 +8,7 @@
 // and it is written to new_state once at the end.  The next token's q/k/v/a/b
 // are fetched while the current token is processed.
 //
+// With qk_l2norm, q and k are L2-normalised per head first (x / sqrt(sum x^2 + 1e-6)).
 // Semantics follow definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md:108-142:
 // state == nullptr means a zero initial state, and a sequence of length 0 ends
 // with a zero final state (the definition skips it and new_state starts at 0).
@@ -81,6 +82,20 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_recurrent_kernel(Prefill
     if (t + 1 < t1) load_token(p, t + 1, h, qh, row, j, nxt);
     const float g = expf(log_decay(A_log, cur.a, dt_bias));
     const float beta = sigmoidf_acc(cur.b);
+    if (p.qk_l2norm) {  // x / sqrt(sum x^2 + 1e-6), the sum over the octet
+      float sk = 0.0f, sq = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        sk = fmaf(cur.k[c], cur.k[c], sk);
+        sq = fmaf(cur.q[c], cur.q[c], sq);
+      }
+      const float rk = rsqrtf(octet_sum(sk) + 1e-6f), rq = rsqrtf(octet_sum(sq) + 1e-6f);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        cur.k[c] *= rk;
+        cur.q[c] *= rq;
+      }
+    }
     float dot = 0.0f;
 #pragma unroll
     for (int c = 0; c < 16; ++c) {

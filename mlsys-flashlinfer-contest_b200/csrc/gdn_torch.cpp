@@ -128,7 +128,8 @@ std::tuple<at::Tensor, at::Tensor> decode(const at::Tensor& q, const at::Tensor&
 
 // prefill: q, k [T,Hq,128] bf16; v [T,Hv,128] bf16; state [N,Hv,128,128] fp32 or
 // None; a, b [T,Hv] bf16; cu_seqlens [N+1] int64 -> (output, new_state).
-// path: 0 = the default dispatch (gdn_prefill), 1 = token-recurrent kernel.
+// path: 0 = the default dispatch (gdn_prefill), 1 = token-recurrent kernel,
+// 2 = chunked kernel; qk_l2norm: in-kernel q/k L2 normalisation.
 std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor& k,
                                            const at::Tensor& v,
                                            const c10::optional<at::Tensor>& state,
@@ -136,7 +137,8 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
                                            const at::Tensor& dt_bias, const at::Tensor& b,
                                            const at::Tensor& cu_seqlens, double scale,
                                            c10::optional<at::Tensor> output,
-                                           c10::optional<at::Tensor> new_state, int64_t path) {
+                                           c10::optional<at::Tensor> new_state, int64_t path,
+                                           bool qk_l2norm) {
   const std::pair<const at::Tensor*, const char*> ins[] = {
       {&q, "q"}, {&k, "k"},           {&v, "v"}, {&A_log, "A_log"}, {&a, "a"}, {&dt_bias, "dt_bias"},
       {&b, "b"}, {&cu_seqlens, "cu_seqlens"}};
@@ -152,6 +154,7 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
   const int64_t T = q.size(0), Hq = q.size(1), Nseq = cu_seqlens.size(0) - 1;
   const int64_t Hk = k.size(1), Hv = v.size(1);
   TORCH_CHECK_VALUE(Nseq > 0, "must have at least one sequence");
+  TORCH_CHECK_VALUE(path >= 0 && path <= 2, "path must be 0 (auto), 1 (recurrent) or 2 (chunked)");
   TORCH_CHECK_VALUE(q.size(2) == kHead && k.size(2) == kHead && v.size(2) == kHead,
                     "head size must be 128");
   TORCH_CHECK_VALUE(k.size(0) == T && v.size(0) == T, "k/v shape mismatch");
@@ -199,24 +202,13 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
   }
   const c10::cuda::CUDAGuard guard(q.device());
   const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
-  const float sc = static_cast<float>(scale);
-  if (path == 1) {
-    check_rc(gdn_prefill_recurrent(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
-                                   A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
-                                   b.data_ptr(), cu_seqlens.data_ptr<int64_t>(), sc,
-                                   output->data_ptr(), new_state->data_ptr<float>(), T, Nseq, Hq,
-                                   Hk, Hv, kHead, stream),
-             "gdn_prefill_recurrent");
-  } else {
-    TORCH_CHECK_VALUE(gdn_prefill_workspace_bytes(T, Nseq, Hq, Hv) == 0,
-                      "gdn_prefill needs a workspace: call the Python launch()");
-    check_rc(gdn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
-                         A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
-                         b.data_ptr(), cu_seqlens.data_ptr<int64_t>(), sc, output->data_ptr(),
-                         new_state->data_ptr<float>(), T, Nseq, Hq, Hk, Hv, kHead, nullptr, 0,
-                         stream),
-             "gdn_prefill");
-  }
+  check_rc(gdn_prefill_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
+                          A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
+                          b.data_ptr(), cu_seqlens.data_ptr<int64_t>(), static_cast<float>(scale),
+                          output->data_ptr(), new_state->data_ptr<float>(), T, Nseq, Hq, Hk, Hv,
+                          kHead, qk_l2norm ? GDN_PREFILL_QK_L2NORM : 0, static_cast<int>(path),
+                          stream),
+           "gdn_prefill_ex");
   return {*output, *new_state};
 }
 
@@ -319,7 +311,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill", &prefill, "GDN prefill (C ABI gdn_prefill / gdn_prefill_recurrent)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("state"), py::arg("A_log"), py::arg("a"),
         py::arg("dt_bias"), py::arg("b"), py::arg("cu_seqlens"), py::arg("scale"),
-        py::arg("output") = py::none(), py::arg("new_state") = py::none(), py::arg("path") = 0);
+        py::arg("output") = py::none(), py::arg("new_state") = py::none(), py::arg("path") = 0,
+        py::arg("qk_l2norm") = false);
   m.def("decode_pool", &decode_pool, "pooled multi-token GDN decode (C ABI gdn_decode_pool)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("A_log"), py::arg("a"), py::arg("dt_bias"),
         py::arg("b"), py::arg("scale"), py::arg("state_pool"), py::arg("in_slots"),

@@ -25,6 +25,7 @@ SIGNATURES = {
                             I64, I64, P]),
     "gdn_prefill": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P, SZ, P]),
     "gdn_prefill_workspace_bytes": (SZ, [I64, I64, I64, I64]),
+    "gdn_prefill_ex": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, I, I, P]),
     "gdn_prefill_recurrent": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P]),
     "gdn_prep_meta": (I, [P, I64, P, P, I64, P]),
     "gdn_chunk_upper_bound": (I64, [I64, I64]),

@@ -79,19 +79,30 @@ def _widen(cu_seqlens):
 
 
 def launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
-           workspace=None, recurrent: bool = False):
+           workspace=None, recurrent: bool = False, use_qk_l2norm: bool = False,
+           chunked: bool = False):
     """Destination-passing form.  ``recurrent=True`` forces the token-recurrent
-    CUDA-core kernel (the reference's path for tiny inputs)."""
+    CUDA-core kernel (the reference's path for tiny inputs), ``chunked=True`` the
+    fused chunked kernel; ``use_qk_l2norm`` L2-normalises q and k per head in the
+    kernels (x / sqrt(sum x^2 + 1e-6); C ABI gdn_prefill_ex)."""
     cu_seqlens = _widen(cu_seqlens)
+    path = 1 if recurrent else (2 if chunked else 0)
     ext = N.torch_ext()
     if ext is not None and workspace is None:
         return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, resolve_scale(scale),
-                           output, new_state, 1 if recurrent else 0)
+                           output, new_state, path, use_qk_l2norm)
     T, Nseq, Hq, Hk, Hv = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output,
                                     new_state)
     L = N.lib()
     with torch.cuda.device(q.device):
         stream = N.stream_handle(q.device)
+        if use_qk_l2norm or chunked:
+            rc = L.gdn_prefill_ex(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(state), N.ptr(A_log),
+                                  N.ptr(a), N.ptr(dt_bias), N.ptr(b), N.ptr(cu_seqlens),
+                                  resolve_scale(scale), N.ptr(output), N.ptr(new_state), T, Nseq,
+                                  Hq, Hk, Hv, HEAD, 1 if use_qk_l2norm else 0, path, stream)
+            N.check(rc, "gdn_prefill_ex")
+            return output, new_state
         if recurrent:
             rc = L.gdn_prefill_recurrent(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(state), N.ptr(A_log),
                                          N.ptr(a), N.ptr(dt_bias), N.ptr(b), N.ptr(cu_seqlens),
@@ -112,28 +123,44 @@ def launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_
     return output, new_state
 
 
-def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
-    """Returns (output [T,Hv,128] bf16, new_state [N,Hv,128,128] fp32)."""
+def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, use_qk_l2norm: bool = False):
+    """Returns (output [T,Hv,128] bf16, new_state [N,Hv,128,128] fp32).
+    ``use_qk_l2norm`` (not in the reference's signature; keyword only in practice)
+    L2-normalises q and k per head inside the kernels."""
     ext = N.torch_ext()
     if ext is not None:
         return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, _widen(cu_seqlens),
-                           resolve_scale(scale))
+                           resolve_scale(scale), None, None, 0, use_qk_l2norm)
     Nseq = cu_seqlens.shape[0] - 1
     Hv = v.shape[1]
     output = torch.empty_like(v)
     new_state = torch.empty((max(Nseq, 0), Hv, HEAD, HEAD), dtype=torch.float32, device=v.device)
-    return launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+    return launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                  use_qk_l2norm=use_qk_l2norm)
 
 
-def run_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+def run_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
+                  use_qk_l2norm: bool = False):
     """Token-recurrent prefill (no workspace)."""
     ext = N.torch_ext()
     if ext is not None:
         return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, _widen(cu_seqlens),
-                           resolve_scale(scale), None, None, 1)
+                           resolve_scale(scale), None, None, 1, use_qk_l2norm)
     Nseq = cu_seqlens.shape[0] - 1
     output = torch.empty_like(v)
     new_state = torch.empty((max(Nseq, 0), v.shape[1], HEAD, HEAD), dtype=torch.float32,
                             device=v.device)
     return launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
-                  recurrent=True)
+                  recurrent=True, use_qk_l2norm=use_qk_l2norm)
+
+
+def run_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
+                use_qk_l2norm: bool = False):
+    """The fused chunked kernel whatever the size (the default dispatch sends
+    tiny inputs to the recurrent kernel)."""
+    Nseq = cu_seqlens.shape[0] - 1
+    output = torch.empty_like(v)
+    new_state = torch.empty((max(Nseq, 0), v.shape[1], HEAD, HEAD), dtype=torch.float32,
+                            device=v.device)
+    return launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                  chunked=True, use_qk_l2norm=use_qk_l2norm)

@@ -179,17 +179,20 @@ def uneven_lengths(total: int, n: int) -> list:
 def make_prefill_inputs(lengths: Sequence[int], Hq: int = 16, Hv: int = 32, seed: int = 0,
                         device="cpu", with_state=True, state_std: float = 0.05,
                         zero_state_every_other: bool = False,
-                        cu_dtype=torch.int64) -> PrefillInputs:
+                        cu_dtype=torch.int64, normalized_qk: bool = True) -> PrefillInputs:
     """Packed varlen prefill inputs (BASELINE configs 2/3).
 
     ``zero_state_every_other`` zeroes the initial state of every second sequence
-    (config 2: "initial state is zero for half the sequences")."""
+    (config 2: "initial state is zero for half the sequences");
+    ``normalized_qk=False`` leaves q, k un-normalised (for the in-kernel L2 norm)."""
     gen = _gen(device, seed)
     d = HEAD_SIZE
     N = len(lengths)
     T = int(sum(lengths))
-    q = _l2norm_bf16(_normal((T, Hq, d), gen, device))
-    k = _l2norm_bf16(_normal((T, Hq, d), gen, device))
+    q = _normal((T, Hq, d), gen, device)
+    k = _normal((T, Hq, d), gen, device)
+    q = _l2norm_bf16(q) if normalized_qk else q.to(torch.bfloat16)
+    k = _l2norm_bf16(k) if normalized_qk else k.to(torch.bfloat16)
     v = _normal((T, Hv, d), gen, device).to(torch.bfloat16)
     A_log, dt_bias = head_params(Hv, gen, device)
     a = _normal((T, Hv), gen, device).to(torch.bfloat16)

@@ -195,14 +195,17 @@ def decode_pool(q, k, v, A_log, a, dt_bias, b, scale, pool, in_slots, out_slots=
 
 
 # ---------------------------------------------------------------- prefill
-def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, qk_l2norm=False):
     """GDN prefill over packed variable-length sequences.  q, k [T,Hq,128];
     v [T,Hv,128]; state [N,Hv,V,K] or None; a, b [T,Hv]; cu_seqlens [N+1].
     Returns (o bf16 bits [T,Hv,128], new_state fp32 [N,Hv,V,K]).
 
     Follows definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md:108-142 token by
     token; sequences of length <= 0 keep a zero final state (def :113-114 skips
-    them and new_state starts at zero)."""
+    them and new_state starts at zero).  ``qk_l2norm`` first normalises q and k
+    per head in fp32 (``l2norm_heads``), the in-kernel option of the GPU path."""
+    if qk_l2norm:
+        q, k = l2norm_heads(q), l2norm_heads(k)
     q = np.asarray(q, np.float32)
     T, Hq, K = q.shape
     Hv = v.shape[1]
