@@ -784,12 +784,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       PHASE(12)
       if (DEBUG && dbg_cta && c == p.dbg_chunk + 2 && lane == 0) p.debug[DBG_EV + warp * 5 + 0] = float(clock64() - t_base);
-      wait_mma(BAR_PV, par);
-      PHASE(13)
-      if (DEBUG && dbg_cta && c == p.dbg_chunk + 2 && lane == 0) p.debug[DBG_EV + warp * 5 + 1] = float(clock64() - t_base);
-
       // ---- output: O[t][v] = scale (e^{gamma_t} (QS)^T[v][t] + (P Vn)^T[v][t]),
-      //      lane v, tokens t in [16 cq, 16 cq + 16).  Full chunks go to the
+      //      lane v, tokens t in [16 cq, 16 cq + 16).  The (QS)^T half is read
+      //      and scaled while the (P Vn)^T MMAs still run.  Full chunks go to the
       //      swizzled output tile (each warp store: 64 contiguous bytes of row
       //      t), stored by TMA from the issue thread; a partial chunk stores
       //      directly. ---------------------------------------------------
@@ -800,13 +797,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool odd = rowv & 1;
         const uint32_t ocol = sb + OFF_O + (rowv >> 6) * 8192 + 4 * ((rowv & 7) >> 1);
         const int och = (rowv & 63) >> 3;
-        float qs[16], pv[16];
+        float qs[16];
         tmem_ld16(tmem + lane_base + TM_KQS + 64 + 16 * cq, qs);
-        tmem_ld16(tmem + lane_base + TM_VN + 16 * cq, pv);
-        tmem_wait_ld();
-        reg_fence(qs);
-        reg_fence(pv);
-        const int64_t tstride = static_cast<int64_t>(p.Hv) * kHead;
         float eg[16];  // scale * 2^g_t of this warp's 16 tokens
         load_table16(gam + G_EG + 16 * cq, eg);
         if constexpr (L2) {  // Q S columns / |q_t|
@@ -815,12 +807,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 16; ++e) eg[e] *= rq[e];
         }
-        __nv_bfloat16* orow = p.out + (t0 * p.Hv + h) * kHead + rowv;
+        tmem_wait_ld();
+        reg_fence(qs);
         float o[16];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {  // (P Vn)^T already carries the scale (P tile)
-          const float2 r = __ffma2_rn(make_float2(eg[i], eg[i + 1]), make_float2(qs[i], qs[i + 1]),
-                                      mul2(pv[i], pv[i + 1], p.scale, p.scale));
+        for (int i = 0; i < 16; i += 2) {
+          const float2 r = mul2(eg[i], eg[i + 1], qs[i], qs[i + 1]);
+          o[i] = r.x;
+          o[i + 1] = r.y;
+        }
+        wait_mma(BAR_PV, par);
+        PHASE(13)
+        if (DEBUG && dbg_cta && c == p.dbg_chunk + 2 && lane == 0) p.debug[DBG_EV + warp * 5 + 1] = float(clock64() - t_base);
+        float pv[16];
+        tmem_ld16(tmem + lane_base + TM_VN + 16 * cq, pv);
+        tmem_wait_ld();
+        reg_fence(pv);
+        const int64_t tstride = static_cast<int64_t>(p.Hv) * kHead;
+        __nv_bfloat16* orow = p.out + (t0 * p.Hv + h) * kHead + rowv;
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float2 r = __ffma2_rn(make_float2(p.scale, p.scale), make_float2(pv[i], pv[i + 1]),
+                                      make_float2(o[i], o[i + 1]));
           o[i] = r.x;
           o[i + 1] = r.y;
         }
