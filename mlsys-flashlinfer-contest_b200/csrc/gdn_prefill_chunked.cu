@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* gates_buf = reinterpret_cast<float*>(smem + OFF_MISC);  // [2][kGateFloats]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_MISC + kMiscBarOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile uint32_t* abort_flag = tmem_slot + 1;  // a compute thread gave up on a wait
   float* At = reinterpret_cast<float*>(smem + OFF_AT);   // A column-major: At[k][i] = A[i][k]
   float* Tcm = reinterpret_cast<float*>(smem + OFF_TC);  // Tcm[j][i] = T[i][j]
   float* Mcm = reinterpret_cast<float*>(smem + OFF_MC);  // (A21 T11) column-major, pitch 36
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kNumBars; ++i)
       mbar_init(&bars[i], (i >= RDY_S && i <= RDY_V) ? kComputeWarps : i == RDY_T1 ? 4 : 1);
     fence_mbar_init();
+    *abort_flag = 0u;
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
@@ -396,11 +398,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // previous chunk's state update done: St is final and its TMEM operands
       // are free.  The barrier also publishes this chunk's gates (warp 1).
-      if (c > 0) wait_mma(BAR_ST, par ^ 1u);
+      if (c > 0) {  // the state update is the next step on the chain: poll it closely
+        bool done = false;
+#pragma unroll 1
+        for (int i = 0; i < 256 && !done; ++i) done = mbar_test(&bars[BAR_ST], par ^ 1u);
+        if (!done) wait_mma(BAR_ST, par ^ 1u);
+        tc_fence_after();
+      }
       PHASE(17)
       if (DEBUG && dbg_cta && c == p.dbg_chunk + 3 && lane == 0)
         p.debug[DBG_EV + warp * 5 + 3] = float(clock64() - t_base);
-      if (named_any(kComputeBar, kComputeThreads, failed)) { aborted = true; break; }
+      if (failed) *abort_flag = 1u;
+      named_sync(kComputeBar, kComputeThreads);
+      if (*abort_flag) { aborted = true; break; }
       if (DEBUG && dbg_cta && c == p.dbg_chunk + 3 && lane == 0)
         p.debug[DBG_EV + warp * 5 + 4] = float(clock64() - t_base);
       if (dbg_cta && c - 1 == p.dbg_chunk) dump_state();
@@ -551,6 +561,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cq == 2 && quarter >= 2) convert_ks(3);
         tmem_wait_st();
         tc_fence_before();  // read by the Vn MMAs after the next barrier
+        if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk (published by
+          compute_gates(c + 1);              // the next loop-top barrier)
+          if (c + 2 < nchunks) prefetch_gates(c + 2);
+        }
       } else {
         const int u = tid - 32 * kL0Warp;
         const int b = u >> 4, j = u & 15, b0 = 16 * b;
@@ -729,10 +743,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               Tcm[tid * kTcPitch + i] + ((tid < 32 && i >= 48) ? Tcm2[tid * 20 + i - 48] : 0.f);
       signal(RDY_T, true);  // T tiles and the P tile are read by the tensor pipe
       PHASE(8)
-      if (warp == 1 && c + 1 < nchunks) {  // gates of the next chunk overlap the Vn MMAs
-        compute_gates(c + 1);
-        if (c + 2 < nchunks) prefetch_gates(c + 2);
-      }
       wait_mma(BAR_M3, par);
       PHASE(11)
 
