@@ -574,6 +574,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-pool", action="store_true", help="skip the pooled-decode leg")
+    ap.add_argument("--pool-only", action="store_true",
+                    help="run only the pooled-decode leg and print its JSON (profiling runs)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--batch-per-rank", type=int, default=256,
                     help="sequences per rank (default 256 = BASELINE config 1; smaller only for profiling)")
@@ -606,6 +608,12 @@ def main():
                                  device_id=torch.device("cuda", local_rank))
         dist = tdist
     try:
+        if args.pool_only:
+            dev = torch.device("cuda", local_rank)
+            torch.cuda.set_device(dev)
+            if rank == 0:
+                print(json.dumps(run_pool_bench(args, dev)), flush=True)
+            return
         if args.prefill_only:
             dev = torch.device("cuda", local_rank)
             torch.cuda.set_device(dev)
