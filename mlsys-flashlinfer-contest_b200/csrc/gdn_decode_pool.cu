@@ -233,6 +233,110 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_pool_kernel(DecodePool
   }
 }
 
+// Single-token step on a bf16 pool: the loaded rows stay packed (two bf16 per
+// register) until their turn, so a thread holds 8 rows -- as many bytes in flight
+// as the fp32 form's 4 -- and each row is updated and written back right away.
+// 128 threads (4 warps x 4 octets x 8 rows = one head's 128 rows), 4 CTAs per SM.
+constexpr int kPackedThreads = 128, kPackedU = 8;
+
+template <bool L2NORM>
+__global__ void __launch_bounds__(kPackedThreads, 4) gdn_decode_pool_bf16_kernel(DecodePoolArgs p) {
+  constexpr int U = kPackedU;
+  const int64_t bh = blockIdx.x;  // b * Hv + h
+  const int64_t bidx = bh / p.Hv;
+  const int h = static_cast<int>(bh % p.Hv);
+  const int qh = h / static_cast<int>(p.Hv / p.Hq);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int oct = lane >> 3;
+  const int j = lane & 7;
+  const int row0 = warp * (4 * U) + oct;  // rows row0 + 4u
+  constexpr int64_t kTile = kHead * kHead;
+
+  const int32_t sin = p.in_slots[bidx];
+  const int32_t sout = p.out_slots ? p.out_slots[bidx] : sin;
+  const bool has_in = sin >= 0 && sin < p.pool_size;
+  const bool write_back = !p.no_state_update && sout >= 0 && sout < p.pool_size;
+
+  uint4 sp[U][2];  // this lane's 16 bf16 of each row (k = 64 i + 8 j + c)
+  if (has_in) {
+    const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(p.pool) +
+                                (static_cast<int64_t>(sin) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 8 * j;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) sp[u][i] = ld_stream_u4(base + u * 4 * kHead + 64 * i);
+  } else {
+#pragma unroll
+    for (int u = 0; u < U; ++u) sp[u][0] = sp[u][1] = make_uint4(0u, 0u, 0u, 0u);
+  }
+
+  const int64_t bt = bidx;  // one token: bt = b
+  const float g = expf(log_decay(p.A_log[h], __bfloat162float(static_cast<const __nv_bfloat16*>(p.a)[bt * p.Hv + h]),
+                                 p.dt_bias[h]));
+  const float beta = sigmoidf_acc(__bfloat162float(static_cast<const __nv_bfloat16*>(p.b)[bt * p.Hv + h]));
+  float kf[16], qf[16];
+  ld_vec16<true>(static_cast<const __nv_bfloat16*>(p.k) + (bt * p.Hq + qh) * kHead, j, kf);
+  ld_vec16<true>(static_cast<const __nv_bfloat16*>(p.q) + (bt * p.Hq + qh) * kHead, j, qf);
+  if constexpr (L2NORM) {
+    float sk = 0.0f, sq = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      sk = fmaf(kf[c], kf[c], sk);
+      sq = fmaf(qf[c], qf[c], sq);
+    }
+    const float rk = rsqrtf(octet_sum(sk) + 1e-6f), rq = rsqrtf(octet_sum(sq) + 1e-6f);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      kf[c] *= rk;
+      qf[c] *= rq;
+    }
+  }
+  const __nv_bfloat16* vrow = static_cast<const __nv_bfloat16*>(p.v) + (bt * p.Hv + h) * kHead;
+  __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (bt * p.Hv + h) * kHead;
+  __nv_bfloat16* wbase = static_cast<__nv_bfloat16*>(p.pool) +
+                         (static_cast<int64_t>(sout) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 8 * j;
+  __nv_bfloat16* ibase = p.intermediate ? static_cast<__nv_bfloat16*>(p.intermediate) + bh * kTile +
+                                              static_cast<int64_t>(row0) * kHead + 8 * j
+                                        : nullptr;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    float s[16];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t w[4] = {sp[u][i].x, sp[u][i].y, sp[u][i].z, sp[u][i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s[8 * i + 2 * e] = bf16_lo(w[e]);
+        s[8 * i + 2 * e + 1] = bf16_hi(w[e]);
+      }
+    }
+    const int row = row0 + 4 * u;
+    float dot = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      s[c] *= g;
+      dot = fmaf(kf[c], s[c], dot);
+    }
+    const float delta = beta * (__bfloat162float(vrow[row]) - octet_sum(dot));
+    float ov = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      s[c] = fmaf(kf[c], delta, s[c]);
+      ov = fmaf(qf[c], s[c], ov);
+    }
+    ov = octet_sum(ov);
+    if (j == 0) orow[row] = __float2bfloat16_rn(p.scale * ov);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 w = make_uint4(pack_bf16x2(s[8 * i + 0], s[8 * i + 1]), pack_bf16x2(s[8 * i + 2], s[8 * i + 3]),
+                                 pack_bf16x2(s[8 * i + 4], s[8 * i + 5]), pack_bf16x2(s[8 * i + 6], s[8 * i + 7]));
+      if (write_back) st_stream_u4(wbase + u * 4 * kHead + 64 * i, w);
+      if (ibase) st_stream_u4(ibase + u * 4 * kHead + 64 * i, w);
+    }
+  }
+}
+
 template <int U, bool BF16>
 cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
   const int64_t ctas = a.B * a.Hv * (kHead / (32 * U));
@@ -254,6 +358,15 @@ cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
 
 template <bool BF16>
 cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
+  if (BF16 && a.T == 1 && a.B * a.Hv >= 2 * 148) {  // the packed single-token form
+    const int64_t ctas = a.B * a.Hv;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+    if (a.qk_l2norm)
+      gdn_decode_pool_bf16_kernel<true><<<static_cast<unsigned>(ctas), kPackedThreads, 0, s>>>(a);
+    else
+      gdn_decode_pool_bf16_kernel<false><<<static_cast<unsigned>(ctas), kPackedThreads, 0, s>>>(a);
+    return cudaGetLastError();
+  }
   // enough CTAs to fill the 148 SMs several times before the tile grows
   const int64_t tiles = a.B * a.Hv;
   // (multi-token: at most 64 rows per thread block, whose registers also hold
