@@ -337,6 +337,184 @@ __global__ void __launch_bounds__(kPackedThreads, 4) gdn_decode_pool_bf16_kernel
   }
 }
 
+// Multi-token steps on a bf16 pool, row by row: the T tokens' q, k (normalised
+// here when asked), v and gates are staged in shared memory first, then each
+// thread takes its 8 packed rows one at a time through all T tokens (fp32 between
+// tokens, one bf16 rounding per store) -- the state stream keeps the bytes in flight
+// of the single-token form instead of holding every row in fp32 across tokens.
+// Shared memory per token: q, k, v as fp32 (3 x 512 B) + g, beta.
+constexpr int kMtpMaxT = 32;
+
+template <bool L2NORM>
+__global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_kernel(DecodePoolArgs p) {
+  constexpr int U = kPackedU;
+  extern __shared__ __align__(16) float tok[];  // [T][384]: q | k | v, then [T][2]: g, beta
+  const int T = static_cast<int>(p.T);
+  float* gb = tok + T * 3 * kHead;
+  const int64_t bh = blockIdx.x;  // b * Hv + h
+  const int64_t bidx = bh / p.Hv;
+  const int h = static_cast<int>(bh % p.Hv);
+  const int qh = h / static_cast<int>(p.Hv / p.Hq);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int oct = lane >> 3;
+  const int j = lane & 7;
+  const int row0 = warp * (4 * U) + oct;
+  constexpr int64_t kTile = kHead * kHead;
+
+  const int32_t sin = p.in_slots[bidx];
+  const int32_t sout = p.out_slots ? p.out_slots[bidx] : sin;
+  const bool has_in = sin >= 0 && sin < p.pool_size;
+  const bool write_back = !p.no_state_update && sout >= 0 && sout < p.pool_size;
+
+  uint4 sp[U][2];
+  if (has_in) {
+    const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(p.pool) +
+                                (static_cast<int64_t>(sin) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 8 * j;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) sp[u][i] = ld_stream_u4(base + u * 4 * kHead + 64 * i);
+  } else {
+#pragma unroll
+    for (int u = 0; u < U; ++u) sp[u][0] = sp[u][1] = make_uint4(0u, 0u, 0u, 0u);
+  }
+
+  // stage the tokens: warp w takes tokens w, w + 4, ...; lane l holds elements 4l..4l+3
+  for (int t = warp; t < T; t += kPackedThreads / 32) {
+    const int64_t bt = bidx * p.T + t;
+    float qv[4], kv[4];
+    ld_bf16x4(static_cast<const __nv_bfloat16*>(p.q) + (bt * p.Hq + qh) * kHead + 4 * lane, qv);
+    ld_bf16x4(static_cast<const __nv_bfloat16*>(p.k) + (bt * p.Hq + qh) * kHead + 4 * lane, kv);
+    if constexpr (L2NORM) {
+      float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        sq = fmaf(qv[c], qv[c], sq);
+        sk = fmaf(kv[c], kv[c], sk);
+      }
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, d);
+        sk += __shfl_xor_sync(0xffffffffu, sk, d);
+      }
+      const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        qv[c] *= rq;
+        kv[c] *= rk;
+      }
+    }
+    float vv[4];
+    ld_bf16x4(static_cast<const __nv_bfloat16*>(p.v) + (bt * p.Hv + h) * kHead + 4 * lane, vv);
+    float* dst = tok + t * 3 * kHead + 4 * lane;
+    *reinterpret_cast<float4*>(dst) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+    *reinterpret_cast<float4*>(dst + kHead) = make_float4(kv[0], kv[1], kv[2], kv[3]);
+    *reinterpret_cast<float4*>(dst + 2 * kHead) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    if (lane == 0) {
+      gb[2 * t] = expf(log_decay(p.A_log[h], __bfloat162float(static_cast<const __nv_bfloat16*>(p.a)[bt * p.Hv + h]),
+                                 p.dt_bias[h]));
+      gb[2 * t + 1] = sigmoidf_acc(__bfloat162float(static_cast<const __nv_bfloat16*>(p.b)[bt * p.Hv + h]));
+    }
+  }
+  __syncthreads();
+
+  __nv_bfloat16* wbase = static_cast<__nv_bfloat16*>(p.pool) +
+                         (static_cast<int64_t>(sout) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead + 8 * j;
+  // two rows at a time (independent chains), each token's dot products split in
+  // two partial sums
+  constexpr int R = 4;
+#pragma unroll
+  for (int u0 = 0; u0 < U; u0 += R) {
+    float s[R][16];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const uint32_t w[4] = {sp[u0 + r][i].x, sp[u0 + r][i].y, sp[u0 + r][i].z, sp[u0 + r][i].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s[r][8 * i + 2 * e] = bf16_lo(w[e]);
+          s[r][8 * i + 2 * e + 1] = bf16_hi(w[e]);
+        }
+      }
+#pragma unroll 1
+    for (int t = 0; t < T; ++t) {
+      const float* tq = tok + t * 3 * kHead;
+      float kf[16], qf[16];
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float4 k4 = *reinterpret_cast<const float4*>(tq + kHead + 64 * i + 8 * j + 4 * hh);
+          const float4 q4 = *reinterpret_cast<const float4*>(tq + 64 * i + 8 * j + 4 * hh);
+          kf[8 * i + 4 * hh + 0] = k4.x;
+          kf[8 * i + 4 * hh + 1] = k4.y;
+          kf[8 * i + 4 * hh + 2] = k4.z;
+          kf[8 * i + 4 * hh + 3] = k4.w;
+          qf[8 * i + 4 * hh + 0] = q4.x;
+          qf[8 * i + 4 * hh + 1] = q4.y;
+          qf[8 * i + 4 * hh + 2] = q4.z;
+          qf[8 * i + 4 * hh + 3] = q4.w;
+        }
+      const float g = gb[2 * t], beta = gb[2 * t + 1];
+      float dot[R][2];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        dot[r][0] = dot[r][1] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          s[r][c] *= g;
+          dot[r][c & 1] = fmaf(kf[c], s[r][c], dot[r][c & 1]);
+        }
+      }
+      float delta[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        delta[r] = beta * (tq[2 * kHead + row0 + 4 * (u0 + r)] - octet_sum(dot[r][0] + dot[r][1]));
+      float ov[R][2];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        ov[r][0] = ov[r][1] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          s[r][c] = fmaf(kf[c], delta[r], s[r][c]);
+          ov[r][c & 1] = fmaf(qf[c], s[r][c], ov[r][c & 1]);
+        }
+      }
+      const int64_t bt = bidx * p.T + t;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float o = octet_sum(ov[r][0] + ov[r][1]);
+        const int row = row0 + 4 * (u0 + r);
+        if (j == 0)
+          static_cast<__nv_bfloat16*>(p.out)[(bt * p.Hv + h) * kHead + row] = __float2bfloat16_rn(p.scale * o);
+        if (p.intermediate) {
+          __nv_bfloat16* ip = static_cast<__nv_bfloat16*>(p.intermediate) + (bt * p.Hv + h) * kTile +
+                              static_cast<int64_t>(row) * kHead + 8 * j;
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            st_stream_u4(ip + 64 * i, make_uint4(pack_bf16x2(s[r][8 * i + 0], s[r][8 * i + 1]),
+                                                 pack_bf16x2(s[r][8 * i + 2], s[r][8 * i + 3]),
+                                                 pack_bf16x2(s[r][8 * i + 4], s[r][8 * i + 5]),
+                                                 pack_bf16x2(s[r][8 * i + 6], s[r][8 * i + 7])));
+        }
+      }
+    }
+    if (write_back) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          st_stream_u4(wbase + (u0 + r) * 4 * kHead + 64 * i,
+                       make_uint4(pack_bf16x2(s[r][8 * i + 0], s[r][8 * i + 1]),
+                                  pack_bf16x2(s[r][8 * i + 2], s[r][8 * i + 3]),
+                                  pack_bf16x2(s[r][8 * i + 4], s[r][8 * i + 5]),
+                                  pack_bf16x2(s[r][8 * i + 6], s[r][8 * i + 7])));
+    }
+  }
+}
+
 template <int U, bool BF16>
 cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
   const int64_t ctas = a.B * a.Hv * (kHead / (32 * U));
@@ -358,6 +536,16 @@ cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
 
 template <bool BF16>
 cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
+  if (BF16 && a.T > 1 && a.T <= kMtpMaxT) {  // packed rows, tokens staged in shared memory
+    const int64_t ctas = a.B * a.Hv;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+    const size_t smem = static_cast<size_t>(a.T) * (3 * kHead + 2) * sizeof(float);
+    if (a.qk_l2norm)
+      gdn_decode_pool_bf16_mtp_kernel<true><<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
+    else
+      gdn_decode_pool_bf16_mtp_kernel<false><<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
+    return cudaGetLastError();
+  }
   if (BF16 && a.T == 1 && a.B * a.Hv >= 2 * 148) {  // the packed single-token form
     const int64_t ctas = a.B * a.Hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
