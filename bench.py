@@ -498,6 +498,33 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
         res["allgather_o"] = {"ms": round(float(ag.item()), 4), "bytes_received_per_rank": recv,
                               "GBps_per_rank": round(recv / (float(ag.item()) / 1e3) / 1e9, 1),
                               "value_with_gather": round(T / ((ms + float(ag.item())) / 1e3), 1)}
+        # the same gather fused into the kernel: every rank's output tiles go to every
+        # rank's full buffer over NVLink (peer-mapped), no collective
+        from gdn_b200.sharding import PeerOutputs, prefill_gathered
+        bufs = PeerOutputs(T, HV, dev)
+        ns_g = torch.empty_like(ns)
+        for _ in range(2):
+            prefill_gathered(inp, sh.v0, bufs, ns_g)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record(stream)
+        for _ in range(reps):
+            prefill_gathered(inp, sh.v0, bufs, ns_g)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        fg = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(fg, op=dist.ReduceOp.MAX)
+        dist.barrier()  # every rank's stores have landed in every buffer
+        same = torch.tensor([1 if torch.equal(bufs.output, full) else 0], device=dev)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        dist.barrier()
+        bufs.close()
+        res["allgather_fused"] = {
+            "ms_per_call_with_gather": round(float(fg.item()), 4),
+            "value_with_gather": round(T / (float(fg.item()) / 1e3), 1),
+            "matches_nccl_allgather": bool(same.item()),
+            "how": "C ABI gdn_prefill_chunked_peers: the kernel's output TMA stores also target "
+                   "every peer's full output buffer (CUDA IPC mapping); no collective"}
         del full
     return res
 

@@ -162,6 +162,28 @@ int gdn_prefill_ex(const void *q, const void *k, const void *v, const float *sta
                    int path, void *stream);
 
 /*
+ * Head-sharded chunked prefill with the output all-gather fused into the kernel.
+ * Replaces the pair "gdn_prefill_chunked on this rank's heads, then an NCCL
+ * all_gather of o" (the multi-GPU form of gdn_prefill; the reference has no
+ * multi-GPU path).  `output` is this rank's full [T, num_v_heads_out, 128] bf16
+ * buffer; the call's num_v_heads heads (q/k/v/a/b/state/new_state hold only those)
+ * are written at heads [head_offset, head_offset + num_v_heads) of it and of each
+ * of the num_peers (<= 7) buffers in peer_outputs: device pointers, valid in this
+ * process (peer-mapped, e.g. cudaIpcOpenMemHandle), of the other ranks' full output
+ * buffers.  The kernel's own output stores go to every buffer; no collective runs.
+ * The caller makes the writes visible (a barrier after every rank's call has
+ * completed) before reading its buffer.  Buffers need 16-byte alignment.
+ */
+int gdn_prefill_chunked_peers(const void *q, const void *k, const void *v, const float *state,
+                              const float *A_log, const void *a, const float *dt_bias,
+                              const void *b, const int64_t *cu_seqlens, float scale,
+                              void *output, float *new_state, int64_t total_seq_len,
+                              int64_t num_seqs, int64_t num_q_heads, int64_t num_k_heads,
+                              int64_t num_v_heads, int64_t head_size, int64_t num_v_heads_out,
+                              int64_t head_offset, void *const *peer_outputs, int num_peers,
+                              void *stream);
+
+/*
  * Chunk metadata (chunk size 64) for packed sequences.
  * Replaces prep_meta_v2 (gdn_prefill/solution/python/cuda_prep_meta_v2.cu:72-94),
  * without its N <= 256 limit.

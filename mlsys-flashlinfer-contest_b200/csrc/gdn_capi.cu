@@ -215,6 +215,35 @@ int gdn_prefill_ex(const void* q, const void* k, const void* v, const float* sta
                    : cuda_status(gdn::launch_prefill_chunked(p, st), "gdn_prefill_chunked launch");
 }
 
+int gdn_prefill_chunked_peers(const void* q, const void* k, const void* v, const float* state,
+                              const float* A_log, const void* a, const float* dt_bias, const void* b,
+                              const int64_t* cu_seqlens, float scale, void* output, float* new_state,
+                              int64_t T, int64_t N, int64_t Hq, int64_t Hk, int64_t Hv, int64_t D,
+                              int64_t Hv_out, int64_t head_offset, void* const* peer_outputs,
+                              int num_peers, void* stream) {
+  if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
+                            N, Hq, Hk, Hv, D))
+    return e;
+  if (T > 0x7fffffffLL - 64) return fail(GDN_ERR_VALUE, "total_seq_len too large");
+  if (num_peers < 0 || num_peers > gdn::kMaxPeers)
+    return fail(GDN_ERR_VALUE, "num_peers must be in [0, %d]", gdn::kMaxPeers);
+  if (num_peers > 0 && !peer_outputs) return fail(GDN_ERR_VALUE, "null pointer argument");
+  if (head_offset < 0 || Hv_out < Hv || head_offset + Hv > Hv_out || Hv_out > 0x7fffffffLL)
+    return fail(GDN_ERR_VALUE, "heads [head_offset, head_offset + num_v_heads) must lie in the output");
+  if (!aligned(output, 16)) return fail(GDN_ERR_VALUE, "output must be 16-byte aligned");
+  for (int r = 0; r < num_peers; ++r)
+    if (!peer_outputs[r] || !aligned(peer_outputs[r], 16))
+      return fail(GDN_ERR_VALUE, "peer output %d is null or not 16-byte aligned", r);
+  gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                     scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv};
+  p.out_heads = Hv_out;
+  p.out_head_off = head_offset;
+  p.n_peers = num_peers;
+  p.peer_out = peer_outputs;
+  return cuda_status(gdn::launch_prefill_chunked(p, static_cast<cudaStream_t>(stream)),
+                     "gdn_prefill_chunked_peers launch");
+}
+
 int gdn_prefill_chunked_debug(const void* q, const void* k, const void* v, const float* state,
                               const float* A_log, const void* a, const float* dt_bias,
                               const void* b, const int64_t* cu_seqlens, float scale, void* output,

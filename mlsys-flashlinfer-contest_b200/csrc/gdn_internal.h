@@ -67,7 +67,15 @@ struct PrefillArgs {
   float* new_state;        // [N,Hv,128,128] fp32
   int64_t T, N, Hq, Hv;
   bool qk_l2norm = false;  // L2-normalise q and k per head: x / sqrt(sum x^2 + 1e-6)
+  // output routing (chunked kernel): `out` holds out_heads heads (0 = Hv) and this
+  // call's heads land at [out_head_off, out_head_off + Hv); each of the n_peers
+  // peer-mapped buffers of the same shape gets the same rows (the all-gather of a
+  // head-sharded call, done by the kernel's own stores over NVLink)
+  int64_t out_heads = 0, out_head_off = 0;
+  int n_peers = 0;
+  void* const* peer_out = nullptr;
 };
+constexpr int kMaxPeers = 7;
 
 cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);
 

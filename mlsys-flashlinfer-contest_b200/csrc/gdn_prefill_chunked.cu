@@ -129,9 +129,17 @@ struct ChunkParams {
   float* debug;  // optional dump of one chunk's intermediates
   float scale;
   int tma_out;   // output rows of full chunks go through a TMA store (out is 16-byte aligned)
+  int Hv_out, head_off;  // heads of the output buffer(s), position of this call's heads
+  int n_peers;           // peer buffers that receive the same output rows
+  __nv_bfloat16* peer_out[kMaxPeers];
   int64_t T, N;
   int Hq, Hv;
   int dbg_seq, dbg_head, dbg_chunk;
+};
+
+// Tensor maps of the peer output buffers (n_peers used).
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];
 };
 
 constexpr int kClkSlots = 20;  // phase clock slots per compute warp (debug build)
@@ -174,7 +182,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                                const __grid_constant__ CUtensorMap tm_k,
                                const __grid_constant__ CUtensorMap tm_v,
-                               const __grid_constant__ CUtensorMap tm_o, const ChunkParams p) {
+                               const __grid_constant__ CUtensorMap tm_o,
+                               const __grid_constant__ PeerMaps pm, const ChunkParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Align by offsetting the __shared__ array itself (not through an integer
   // cast), so every derived pointer stays in the shared state space and its
@@ -833,8 +842,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(tmem + lane_base + TM_VN + 16 * cq, pv);
         tmem_wait_ld();
         reg_fence(pv);
-        const int64_t tstride = static_cast<int64_t>(p.Hv) * kHead;
-        __nv_bfloat16* orow = p.out + (t0 * p.Hv + h) * kHead + rowv;
+        const int64_t tstride = static_cast<int64_t>(p.Hv_out) * kHead;
+        const int64_t oelem = (t0 * p.Hv_out + h + p.head_off) * kHead + rowv;
+        __nv_bfloat16* orow = p.out + oelem;
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
           const float2 r = __ffma2_rn(make_float2(p.scale, p.scale), make_float2(pv[i], pv[i + 1]),
@@ -856,6 +866,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             if (16 * cq + i < L) orow[(16 * cq + i) * tstride] = __float2bfloat16_rn(o[i]);
+          for (int r = 0; r < p.n_peers; ++r)
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (16 * cq + i < L) p.peer_out[r][oelem + (16 * cq + i) * tstride] = __float2bfloat16_rn(o[i]);
         }
         if (dbg)
           for (int i = 0; i < 16; ++i) {
@@ -879,8 +893,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_sync(kComputeBar, kComputeThreads);
       if (tid == 0) {
         const int tl = static_cast<int>(bos + static_cast<int64_t>(nchunks - 1) * kChunk);
-        tma_store_3d(&tm_o, smem + OFF_O, 0, h, tl);
-        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, tl);
+        const int gh = h + p.head_off;
+        tma_store_3d(&tm_o, smem + OFF_O, 0, gh, tl);
+        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, gh, tl);
+        for (int r = 0; r < p.n_peers; ++r) {  // the same rows into every peer's buffer
+          tma_store_3d(&pm.m[r], smem + OFF_O, 0, gh, tl);
+          tma_store_3d(&pm.m[r], smem + OFF_O + 8192, 64, gh, tl);
+        }
         bulk_commit();
         bulk_wait_all();
       }
@@ -1010,8 +1029,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // partial) is complete and fenced by every compute thread before RDY_T
       if (c > 0 && p.tma_out) {
         const int tp = static_cast<int>(bos + static_cast<int64_t>(c - 1) * kChunk);
-        tma_store_3d(&tm_o, smem + OFF_O, 0, h, tp);
-        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, h, tp);
+        const int gh = h + p.head_off;
+        tma_store_3d(&tm_o, smem + OFF_O, 0, gh, tp);
+        tma_store_3d(&tm_o, smem + OFF_O + 8192, 64, gh, tp);
+        for (int r = 0; r < p.n_peers; ++r) {  // the same rows into every peer's buffer
+          tma_store_3d(&pm.m[r], smem + OFF_O, 0, gh, tp);
+          tma_store_3d(&pm.m[r], smem + OFF_O + 8192, 64, gh, tp);
+        }
         bulk_commit();
       }
       vn_mmas(0);
@@ -1133,14 +1157,21 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
                            static_cast<size_t>(a.N) * a.Hv * kHead * kHead * sizeof(float), s);
   }
   CUtensorMap mq, mk, mv, mo;
+  PeerMaps pm;
+  memset(&pm, 0, sizeof(pm));
   cudaError_t e;
+  const int64_t out_heads = a.out_heads > 0 ? a.out_heads : a.Hv;
   if ((e = make_head_map(&mq, a.q, a.Hq, a.T)) != cudaSuccess) return e;
   if ((e = make_head_map(&mk, a.k, a.Hq, a.T)) != cudaSuccess) return e;
   if ((e = make_head_map(&mv, a.v, a.Hv, a.T)) != cudaSuccess) return e;
   // full-chunk output rows go out by TMA store when the output allows a tensor map
-  const int tma_out = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) ? 1 : 0;
+  int tma_out = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) ? 1 : 0;
+  for (int r = 0; r < a.n_peers; ++r)
+    if (reinterpret_cast<uintptr_t>(a.peer_out[r]) % 16 != 0) tma_out = 0;
   memset(&mo, 0, sizeof(mo));
-  if (tma_out && (e = make_head_map(&mo, a.out, a.Hv, a.T)) != cudaSuccess) return e;
+  if (tma_out && (e = make_head_map(&mo, a.out, out_heads, a.T)) != cudaSuccess) return e;
+  for (int r = 0; tma_out && r < a.n_peers; ++r)
+    if ((e = make_head_map(&pm.m[r], a.peer_out[r], out_heads, a.T)) != cudaSuccess) return e;
   auto kernel = gdn_prefill_chunked_kernel<DEBUG, false>;
   if constexpr (!DEBUG) {
     if (a.qk_l2norm) kernel = gdn_prefill_chunked_kernel<false, true>;
@@ -1154,11 +1185,12 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   ChunkParams p{a.state, a.A_log, a.dt_bias,
                 static_cast<const __nv_bfloat16*>(a.a), static_cast<const __nv_bfloat16*>(a.b),
                 a.cu_seqlens, static_cast<__nv_bfloat16*>(a.out), a.new_state, debug, a.scale,
-                tma_out, a.T, a.N, static_cast<int>(a.Hq), static_cast<int>(a.Hv), dbg_seq, dbg_head,
-                dbg_chunk};
+                tma_out, static_cast<int>(out_heads), static_cast<int>(a.out_head_off), a.n_peers, {},
+                a.T, a.N, static_cast<int>(a.Hq), static_cast<int>(a.Hv), dbg_seq, dbg_head, dbg_chunk};
+  for (int r = 0; r < a.n_peers; ++r) p.peer_out[r] = static_cast<__nv_bfloat16*>(a.peer_out[r]);
   const int64_t ctas = a.N * a.Hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  kernel<<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, p);
+  kernel<<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, pm, p);
   return cudaGetLastError();
 }
 

@@ -30,6 +30,8 @@ SIGNATURES = {
     "gdn_prep_meta": (I, [P, I64, P, P, I64, P]),
     "gdn_chunk_upper_bound": (I64, [I64, I64]),
     "gdn_prefill_chunked": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P]),
+    "gdn_prefill_chunked_peers": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64,
+                                      I64, I64, I64, P, I, P]),
     "gdn_prefill_chunked_debug": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64,
                                       I64, P, I64, I64, I64, I64, P]),
     "gdn_prefill_chunked_debug_floats": (I64, []),

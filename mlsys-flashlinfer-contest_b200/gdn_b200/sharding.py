@@ -10,8 +10,11 @@ GPUs the work splits into independent units with no data-path collective:
 * prefill: heads are independent and the chunk scan stays per (sequence,
   head) -> shard v-heads in whole GVA groups (a q/k head and its Hv/Hq
   v-heads stay on one rank).  The only exchange is an optional all-gather of
-  the output ``o`` when a caller needs all heads on every rank
-  (``all_gather_heads``), one NCCL ``all_gather_into_tensor``.
+  the output ``o`` when a caller needs all heads on every rank: either one NCCL
+  ``all_gather_into_tensor`` after the kernel (``all_gather_heads``), or fused into
+  the kernel (``PeerOutputs`` + ``prefill_gathered``): every rank's chunked kernel
+  writes its output tiles into every rank's full output buffer over NVLink
+  (buffers peer-mapped through CUDA IPC), so no collective runs at all.
 """
 from __future__ import annotations
 
@@ -92,3 +95,94 @@ def all_gather_heads(o_local: torch.Tensor, group=None) -> torch.Tensor:
     buf = torch.empty((world * T, hl, D), dtype=o_local.dtype, device=o_local.device)
     dist.all_gather_into_tensor(buf, o_local.contiguous(), group=group)
     return buf.view(world, T, hl, D).permute(1, 0, 2, 3).reshape(T, world * hl, D)
+
+
+class _DevBuf:
+    """A raw device allocation seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3}
+
+
+class PeerOutputs:
+    """Full prefill output buffers [T, Hv, 128] bf16, one per rank, each mapped into
+    every other rank's address space (CUDA IPC), for ``prefill_gathered``.
+
+    Collective to create (an all_gather_object of the IPC handles); ``close()``
+    unmaps the peers' buffers and frees this rank's (it must run on every rank,
+    after the last kernel that writes into the buffers has completed everywhere).
+    The buffers are plain cudaMalloc allocations, outside torch's caching
+    allocator, so the IPC handles cover exactly them."""
+
+    def __init__(self, T: int, Hv: int, device, group=None):
+        import torch.distributed as dist
+        from cuda.bindings import runtime as rt
+        self._rt = rt
+        self.T, self.Hv = int(T), int(Hv)
+        self.device = torch.device(device)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        nbytes = max(self.T * self.Hv * 128 * 2, 16)
+        with torch.cuda.device(self.device):
+            err, ptr = rt.cudaMalloc(nbytes)
+            self._check(err, "cudaMalloc")
+            self._ptr = int(ptr)
+            err, h = rt.cudaIpcGetMemHandle(self._ptr)
+            self._check(err, "cudaIpcGetMemHandle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h.reserved), group=group)
+        self.peer_ptrs = []
+        with torch.cuda.device(self.device):
+            for r in range(self.world):
+                if r == self.rank:
+                    continue
+                hr = rt.cudaIpcMemHandle_t()
+                hr.reserved = handles[r]
+                err, pp = rt.cudaIpcOpenMemHandle(hr, rt.cudaIpcMemLazyEnablePeerAccess)
+                self._check(err, "cudaIpcOpenMemHandle")
+                self.peer_ptrs.append(int(pp))
+        raw = torch.as_tensor(_DevBuf(self._ptr, (self.T, self.Hv, 128), "<i2"), device=self.device)
+        self.output = raw.view(torch.bfloat16)  # this rank's full output buffer
+
+    def _check(self, err, what):
+        if int(err) != 0:
+            raise RuntimeError(f"{what} failed: {err}")
+
+    def close(self):
+        rt = self._rt
+        with torch.cuda.device(self.device):
+            for pp in self.peer_ptrs:
+                rt.cudaIpcCloseMemHandle(pp)
+            self.peer_ptrs = []
+            if self._ptr:
+                rt.cudaFree(self._ptr)
+                self._ptr = 0
+
+
+def prefill_gathered(inp_local, head_offset: int, bufs: PeerOutputs, new_state=None):
+    """Chunked prefill of this rank's heads (``inp_local`` as ``slice_prefill_heads``
+    builds it) whose output tiles go to heads [head_offset, head_offset + Hv_local)
+    of every rank's full output buffer (C ABI gdn_prefill_chunked_peers).  Returns
+    (this rank's full output buffer, this rank's new states).  The buffer holds all
+    heads only after every rank's call has completed: synchronise and barrier first."""
+    import ctypes
+    from . import _native as N
+    from ._checks import HEAD, resolve_scale
+    q, k, v = inp_local.q, inp_local.k, inp_local.v
+    T, Hq, _ = q.shape
+    Hv = v.shape[1]
+    Nseq = inp_local.cu_seqlens.shape[0] - 1
+    if new_state is None:
+        new_state = torch.empty((Nseq, Hv, HEAD, HEAD), dtype=torch.float32, device=q.device)
+    peers = (ctypes.c_void_p * max(len(bufs.peer_ptrs), 1))(*bufs.peer_ptrs)
+    with torch.cuda.device(q.device):
+        rc = N.lib().gdn_prefill_chunked_peers(
+            N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(inp_local.state), N.ptr(inp_local.A_log),
+            N.ptr(inp_local.a), N.ptr(inp_local.dt_bias), N.ptr(inp_local.b),
+            N.ptr(inp_local.cu_seqlens), resolve_scale(inp_local.scale), N.ptr(bufs.output),
+            N.ptr(new_state), T, Nseq, Hq, k.shape[1], Hv, HEAD, bufs.Hv, head_offset,
+            ctypes.cast(peers, ctypes.c_void_p), len(bufs.peer_ptrs), N.stream_handle(q.device))
+    N.check(rc, "gdn_prefill_chunked_peers")
+    return bufs.output, new_state
+
