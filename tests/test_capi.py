@@ -96,3 +96,44 @@ def test_check_maps_codes_to_exceptions():
         N.check(N.GDN_ERR_TYPE)
     with pytest.raises(RuntimeError):
         N.check(N.GDN_ERR_CUDA)
+
+
+def _peers_call(Hv_out=16, off=0, npeers=1, peers=(1 << 22,), out=1 << 20):
+    L = N.lib()
+    P = ctypes.c_void_p
+    arr = (ctypes.c_void_p * max(len(peers), 1))(*peers)
+    return L.gdn_prefill_chunked_peers(P(1 << 20), P(1 << 20), P(1 << 20), None, P(1 << 20),
+                                       P(1 << 20), P(1 << 20), P(1 << 20), P(1 << 20), 0.0, P(out),
+                                       P(1 << 21), 10, 1, 4, 4, 8, 128, Hv_out, off,
+                                       ctypes.cast(arr, ctypes.c_void_p), npeers, None)
+
+
+@pytest.mark.parametrize("over,msg", [
+    (dict(npeers=8, peers=(1 << 22,) * 8), "num_peers"),
+    (dict(off=9), "must lie in the output"),
+    (dict(Hv_out=4), "must lie in the output"),
+    (dict(peers=((1 << 22) + 2,)), "peer output 0"),
+    (dict(peers=(0,)), "peer output 0"),
+    (dict(out=(1 << 20) + 8), "16-byte aligned"),
+])
+def test_prefill_peers_validation_errors(over, msg):
+    """The fused-gather prefill entry rejects bad routing before touching the GPU."""
+    rc = _peers_call(**over)
+    assert rc == N.GDN_ERR_VALUE
+    assert msg in N.lib().gdn_last_error().decode()
+
+
+def test_decode_pool_validation_errors():
+    L = N.lib()
+    P = ctypes.c_void_p
+    base = [P(1 << 20)] * 7 + [0.0, P(1 << 21), 1, 4, P(1 << 22), None, None, 0, P(1 << 23),
+                               2, 1, 4, 4, 8, 128, None]
+    def call(**kw):
+        a = list(base)
+        for i, v in kw.items():
+            a[int(i[1:])] = v
+        return L.gdn_decode_pool(*a)
+    assert call(a9=7) == N.GDN_ERR_TYPE                      # state dtype
+    assert call(a17=0) == N.GDN_ERR_VALUE                    # seq_len 0
+    assert call(a14=4) == N.GDN_ERR_VALUE                    # unknown flag
+    assert call(a0=P((1 << 20) + 8)) == N.GDN_ERR_VALUE      # q alignment
