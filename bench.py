@@ -598,11 +598,15 @@ def run_replay(args):
         c_us = cpu_us(lambda: c_oracle.decode(*inp.args()))
         dinp = W.make_decode_inputs(B, hq, hv, seed=500 + B, device=dev)
         g_us = gpu_us(lambda: decode.run(*dinp.args()))
+        from gdn_b200.graphs import DecodeGraph
+        dg = DecodeGraph(dinp.q, dinp.k, dinp.v, dinp.state.clone(), dinp.A_log, dinp.a, dinp.dt_bias,
+                         dinp.b, dinp.scale)
+        gr_us = gpu_us(dg.step)
         r = None if c_us is None else c_us / g_us
         if r:
             ratios.append(r)
-        rows_d.append({"batch": B, "us": round(g_us, 2), "cpu_us": c_us and round(c_us, 1),
-                       "speedup_vs_cpu": r and round(r, 1)})
+        rows_d.append({"batch": B, "us": round(g_us, 2), "graph_replay_us": round(gr_us, 2),
+                       "cpu_us": c_us and round(c_us, 1), "speedup_vs_cpu": r and round(r, 1)})
     for i, lengths in enumerate(W.contest_prefill_cases()):
         inp = W.make_prefill_inputs(lengths, hq, hv, seed=700 + i)
         c_us = cpu_us(lambda: c_oracle.prefill(*inp.args()))
