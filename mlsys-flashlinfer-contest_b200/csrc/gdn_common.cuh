@@ -78,10 +78,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
-__device__ __forceinline__ uint16_t f32_to_bf16_bits(float x) {
-  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
-}
-
 // ------------------------------------------------------------------ memory
 // 128-bit streaming load (evict-first in L1 and L2): state tiles are read once.
 __device__ __forceinline__ float4 ld_stream_f4(const float* p) {

@@ -53,20 +53,6 @@ __device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-// Named barrier that also ORs a predicate over the participating threads.
-__device__ __forceinline__ bool named_any(uint32_t id, uint32_t n, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(n)
-      : "memory");
-  return r != 0;
-}
-
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -164,21 +150,12 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle.  lbo/sbo in bytes.
+// Shared-memory matrix descriptor, 128-byte swizzle, from a precomputed start
+// field (saddr >> 4, a 16-byte aligned address below 256 KiB); lbo/sbo in bytes.
 //   bits [0,14) start>>4, [16,30) LBO>>4, [32,46) SBO>>4, [46,48) version=1,
 //   [49,52) base offset=0 (tiles are 1024-byte aligned), [61,64) layout=2 (SW128).
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
-  d |= 1ull << 46;
-  d |= 2ull << 61;
-  return d;
-}
-
-// The same descriptor from a precomputed start field (saddr >> 4, a 16-byte
-// aligned address below 256 KiB): the high word and the LBO bits are constants,
-// so a k-step offset costs one 32-bit add.
+// The high word and the LBO bits are constants, so a k-step offset costs one
+// 32-bit add.
 __device__ __forceinline__ uint64_t sdesc_sw128_f(uint32_t start16, uint32_t lbo, uint32_t sbo) {
   const uint32_t lo = start16 | (((lbo >> 4) & 0x3FFFu) << 16);
   const uint32_t hi = ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
@@ -242,19 +219,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15]))
-      : "memory");
-}
-
 // Same shape, 32 consecutive columns.
 // 8 / 16 raw 32-bit columns of this thread's lane (32x32b shape)
 __device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* r) {
@@ -307,48 +271,8 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
-// 16 lanes x 256 bits, repeated 8 times along the columns (64 columns): with
-// g = lane/4 and c = lane%4, v[4j+0..1] = (lane base + g, columns 8j+2c, 8j+2c+1)
-// and v[4j+2..3] = (lane base + g + 8, same columns), j = 0..7.  Matches the
-// M=64 accumulator layout, whose 16 rows per warp quarter sit in lanes 0..15.
-__device__ __forceinline__ void tmem_ld16x256_x8(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-      "%28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Same shape repeated 4 times (32 columns): v[4j+0..3] for column group j = 0..3.
-__device__ __forceinline__ void tmem_ld16x256_x4(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-      "%11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ void sts32(uint32_t addr, uint32_t a) {
   asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(a) : "memory");
-}
-
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t a;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(a) : "r"(addr));
-  return a;
 }
 
 // ------------------------------------------------------------------ mma.sync
