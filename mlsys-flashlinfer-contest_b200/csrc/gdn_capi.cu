@@ -159,10 +159,17 @@ size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv)
   return 0;
 }
 
-// Chooses the token-recurrent kernel for tiny inputs, as the reference's
-// dispatch does (gdn_prefill/solution/python/gdn_prefill_mix.py:29:
-// N <= 2 and T <= 30 N), and the fused chunked kernel otherwise.
-static bool use_recurrent(int64_t T, int64_t N) { return N <= 2 && T <= 30 * N; }
+// Chooses the token-recurrent kernel for tiny inputs and the fused chunked
+// kernel otherwise.  The reference dispatches on the same two sizes
+// (gdn_prefill/solution/python/gdn_prefill_mix.py:29: N <= 2 and T <= 30 N);
+// the bounds here come from timing both kernels on a B200 over N = 1..32
+// sequences of 8..512 tokens (Hv = 8 and 32): the recurrent kernel walks one
+// token at a time (~0.6 us each) while the chunked kernel's floor is one chunk
+// (~15 us per call, launch included), so recurrent wins only for sequences of
+// at most ~16 tokens (8 once N Hv reaches 64) and few (sequence, head) pairs.
+static bool use_recurrent(int64_t T, int64_t N, int64_t Hv) {
+  return (T <= 16 * N && N * Hv <= 32) || (T <= 8 * N && N * Hv <= 64);
+}
 
 int gdn_prefill_chunked(const void* q, const void* k, const void* v, const float* state,
                         const float* A_log, const void* a, const float* dt_bias, const void* b,
@@ -186,7 +193,7 @@ int gdn_prefill(const void* q, const void* k, const void* v, const float* state,
                 void* stream) {
   (void)workspace;
   (void)workspace_bytes;
-  if (use_recurrent(T, N))
+  if (use_recurrent(T, N, Hv))
     return gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                                  new_state, T, N, Hq, Hk, Hv, D, stream);
   return gdn_prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
@@ -209,7 +216,7 @@ int gdn_prefill_ex(const void* q, const void* k, const void* v, const float* sta
                      scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv,
                      (flags & GDN_PREFILL_QK_L2NORM) != 0};
   const bool recurrent =
-      path == GDN_PREFILL_PATH_RECURRENT || (path == GDN_PREFILL_PATH_AUTO && use_recurrent(T, N));
+      path == GDN_PREFILL_PATH_RECURRENT || (path == GDN_PREFILL_PATH_AUTO && use_recurrent(T, N, Hv));
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   return recurrent ? cuda_status(gdn::launch_prefill_recurrent(p, st), "gdn_prefill_recurrent launch")
                    : cuda_status(gdn::launch_prefill_chunked(p, st), "gdn_prefill_chunked launch");

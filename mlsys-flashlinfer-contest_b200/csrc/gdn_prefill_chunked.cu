@@ -1133,7 +1133,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // [T, heads, 128] bf16, box = 64 tokens x 1 head x 64 dims, 128-byte swizzle.
-cudaError_t make_head_map(CUtensorMap* m, const void* base, int64_t heads, int64_t T) {
+cudaError_t encode_head_map(CUtensorMap* m, const void* base, int64_t heads, int64_t T) {
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHead), static_cast<cuuint64_t>(heads),
@@ -1146,6 +1146,32 @@ cudaError_t make_head_map(CUtensorMap* m, const void* base, int64_t heads, int64
                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Encoding a tensor map costs about a microsecond of host time and a call needs
+// four; a small per-thread cache of encoded maps, keyed by what the encoding
+// depends on (base address, heads, T), skips it when a caller reuses its
+// buffers (a serving loop, or the caching allocator handing back a block).
+cudaError_t make_head_map(CUtensorMap* m, const void* base, int64_t heads, int64_t T) {
+  struct Entry {
+    const void* base;
+    int64_t heads, T;
+    CUtensorMap map;
+  };
+  constexpr int kEntries = 16;
+  thread_local Entry cache[kEntries];
+  thread_local int used = 0, next = 0;
+  for (int i = 0; i < used; ++i)
+    if (cache[i].base == base && cache[i].heads == heads && cache[i].T == T) {
+      *m = cache[i].map;
+      return cudaSuccess;
+    }
+  const cudaError_t e = encode_head_map(m, base, heads, T);
+  if (e != cudaSuccess) return e;
+  cache[next] = Entry{base, heads, T, *m};
+  next = (next + 1) % kEntries;
+  if (used < kEntries) ++used;
+  return cudaSuccess;
 }
 
 template <bool DEBUG>
