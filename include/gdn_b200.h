@@ -114,6 +114,7 @@ int gdn_decode_pool(const void *q, const void *k, const void *v, const float *A_
  *   output    [T, Hv, 128] bf16            new_state [N, Hv, 128, 128] fp32
  *   workspace device buffer of at least gdn_prefill_workspace_bytes(T, N, Hq, Hv)
  *             bytes, 256-byte aligned (may be NULL when that size is 0)
+ * q, k, v, state and new_state need 16-byte alignment, cu_seqlens 8-byte.
  * A sequence of length 0 gets a zero final state (as in the definition).
  * cu_seqlens is read only on the device; values outside [0, T] are clamped.
  */

@@ -126,7 +126,8 @@ static int check_prefill(const void* q, const void* k, const void* v, const floa
   if (T < 0) return fail(GDN_ERR_VALUE, "total_seq_len must be non-negative");
   if (!cu || !A_log || !dt_bias || !new_state) return fail(GDN_ERR_VALUE, "null pointer argument");
   if (T > 0 && (!q || !k || !v || !a || !b || !out)) return fail(GDN_ERR_VALUE, "null pointer argument");
-  if (!aligned(q, 8) || !aligned(k, 8)) return fail(GDN_ERR_VALUE, "q and k must be 8-byte aligned");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
+    return fail(GDN_ERR_VALUE, "q, k and v must be 16-byte aligned");
   if (!aligned(new_state, 16) || (state && !aligned(state, 16)))
     return fail(GDN_ERR_VALUE, "state and new_state must be 16-byte aligned");
   if (!aligned(cu, 8)) return fail(GDN_ERR_VALUE, "cu_seqlens must be 8-byte aligned");
@@ -164,11 +165,15 @@ size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv)
 // (gdn_prefill/solution/python/gdn_prefill_mix.py:29: N <= 2 and T <= 30 N);
 // the bounds here come from timing both kernels on a B200 over N = 1..32
 // sequences of 8..512 tokens (Hv = 8 and 32): the recurrent kernel walks one
-// token at a time (~0.6 us each) while the chunked kernel's floor is one chunk
-// (~15 us per call, launch included), so recurrent wins only for sequences of
-// at most ~16 tokens (8 once N Hv reaches 64) and few (sequence, head) pairs.
+// token at a time (~0.33 us each) while the chunked kernel's floor is one chunk
+// (~14.5 us per call, launch included).  Recurrent wins for sequences of up to
+// ~32 tokens when there are at most 16 (sequence, head) pairs, up to 16 tokens
+// at up to 64 pairs, and up to 8 tokens at any count.  The last bound also caps
+// T, because only the mean length is known on the host: one long sequence among
+// many short ones walks all its tokens.
 static bool use_recurrent(int64_t T, int64_t N, int64_t Hv) {
-  return (T <= 16 * N && N * Hv <= 32) || (T <= 8 * N && N * Hv <= 64);
+  return (T <= 32 * N && N * Hv <= 16) || (T <= 16 * N && N * Hv <= 64) ||
+         (T <= 8 * N && T <= 256);
 }
 
 int gdn_prefill_chunked(const void* q, const void* k, const void* v, const float* state,
