@@ -113,7 +113,10 @@ int gdn_decode_pool(const void *q, const void *k, const void *v, const float *A_
  *                                          non-decreasing, cu_seqlens[N] == T
  *   output    [T, Hv, 128] bf16            new_state [N, Hv, 128, 128] fp32
  *   workspace device buffer of at least gdn_prefill_workspace_bytes(T, N, Hq, Hv)
- *             bytes, 256-byte aligned (may be NULL when that size is 0)
+ *             bytes, 256-byte aligned (may be NULL when that size is 0); it holds
+ *             the piece states of the segmented form (gdn_prefill_segmented),
+ *             which the call takes when the (sequence, head) pairs would leave
+ *             most SMs idle and the workspace is large enough
  * q, k, v, state and new_state need 16-byte alignment, cu_seqlens 8-byte.
  * A sequence of length 0 gets a zero final state (as in the definition).
  * cu_seqlens is read only on the device; values outside [0, T] are clamped.
@@ -125,7 +128,7 @@ int gdn_prefill(const void *q, const void *k, const void *v, const float *state,
                 int64_t num_k_heads, int64_t num_v_heads, int64_t head_size, void *workspace,
                 size_t workspace_bytes, void *stream);
 
-/* Workspace bytes gdn_prefill needs for these sizes (0 when none). */
+/* Workspace bytes gdn_prefill wants for these sizes (0 when none). */
 size_t gdn_prefill_workspace_bytes(int64_t total_seq_len, int64_t num_seqs, int64_t num_q_heads,
                                    int64_t num_v_heads);
 
@@ -182,7 +185,33 @@ int gdn_prefill_chunked_peers(const void *q, const void *k, const void *v, const
                               int64_t num_seqs, int64_t num_q_heads, int64_t num_k_heads,
                               int64_t num_v_heads, int64_t head_size, int64_t num_v_heads_out,
                               int64_t head_offset, void *const *peer_outputs, int num_peers,
-                              void *stream);
+                              int segments, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Sequence-parallel (segmented) prefill; no counterpart in the reference, whose
+ * chunked pipeline runs one state scan per (sequence, head).  Each sequence of
+ * at least 2 * segments chunks is cut at chunk boundaries into `segments` pieces;
+ * pass 1 runs piece 0 from the initial state and, for each middle piece g, its
+ * final state from zero (F_g) and its transition matrix (P_g: the final state
+ * from the identity with v = 0); S_{g+1} = S_g P_g + F_g gives the start states
+ * (fp32); pass 2 runs pieces 1.. from them.  3 + (segments - 2) launches on the
+ * stream; the critical path is ~2/segments of the sequence.  Same arguments as
+ * gdn_prefill plus flags (GDN_PREFILL_QK_L2NORM), segments (0 = the automatic
+ * choice, gdn_prefill_segments; 1 = one chain per pair; at most 64) and a
+ * 256-byte aligned workspace of gdn_prefill_segmented_workspace_bytes(N, Hv,
+ * segments) bytes.  gdn_prefill_chunked_peers takes the same three arguments.
+ */
+int gdn_prefill_segmented(const void *q, const void *k, const void *v, const float *state,
+                          const float *A_log, const void *a, const float *dt_bias, const void *b,
+                          const int64_t *cu_seqlens, float scale, void *output, float *new_state,
+                          int64_t total_seq_len, int64_t num_seqs, int64_t num_q_heads,
+                          int64_t num_k_heads, int64_t num_v_heads, int64_t head_size, int flags,
+                          int segments, void *workspace, size_t workspace_bytes, void *stream);
+size_t gdn_prefill_segmented_workspace_bytes(int64_t num_seqs, int64_t num_v_heads, int segments);
+/* The automatic segment count for these sizes (1: no cut).  The largest count
+ * <= 8 whose pass 1 fits in one wave of SMs, num_seqs * num_v_heads * (2 segments - 3)
+ * <= SMs, with pieces of >= 4 chunks on average; 1 below 3. */
+int gdn_prefill_segments(int64_t total_seq_len, int64_t num_seqs, int64_t num_v_heads);
 
 /*
  * Chunk metadata (chunk size 64) for packed sequences.

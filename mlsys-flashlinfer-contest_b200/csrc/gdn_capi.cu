@@ -151,15 +151,6 @@ int gdn_prefill_recurrent(const void* q, const void* k, const void* v, const flo
                      "gdn_prefill_recurrent launch");
 }
 
-size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv) {
-  // The fused chunked kernel keeps every intermediate on chip.
-  (void)T;
-  (void)N;
-  (void)Hq;
-  (void)Hv;
-  return 0;
-}
-
 // Chooses the token-recurrent kernel for tiny inputs and the fused chunked
 // kernel otherwise.  The reference dispatches on the same two sizes
 // (gdn_prefill/solution/python/gdn_prefill_mix.py:29: N <= 2 and T <= 30 N);
@@ -174,6 +165,44 @@ size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv)
 static bool use_recurrent(int64_t T, int64_t N, int64_t Hv) {
   return (T <= 32 * N && N * Hv <= 16) || (T <= 16 * N && N * Hv <= 64) ||
          (T <= 8 * N && T <= 256);
+}
+
+// Segment count of the sequence-parallel prefill (1: one chain per (sequence,
+// head)).  Each pass-1 job holds one SM for a piece of ~L/G chunks, so G is the
+// largest count (at most 8) whose pass 1 fits in one wave of SMs, N Hv (2G - 3)
+// <= SMs, with pieces of at least 4 chunks on average; below G = 3 there is no
+// gain (pass 1 and pass 2 would each take half of the sequence).
+static int sm_count() {
+  static int n = [] {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    return v;
+  }();
+  return n;
+}
+
+static int choose_segments(int64_t T, int64_t N, int64_t Hv) {
+  if (N <= 0 || Hv <= 0) return 1;
+  const int64_t pairs = N * Hv, mean_chunks = T / (gdn::kChunk * N);
+  int best = 1;
+  for (int G = 3; G <= 8; ++G)
+    if (pairs * (2 * G - 3) <= sm_count() && mean_chunks >= 4 * G) best = G;
+  return best;
+}
+
+int gdn_prefill_segments(int64_t T, int64_t N, int64_t Hv) {
+  return use_recurrent(T, N, Hv) ? 1 : choose_segments(T, N, Hv);
+}
+
+size_t gdn_prefill_segmented_workspace_bytes(int64_t N, int64_t Hv, int segments) {
+  return gdn::prefill_segments_bytes(N, Hv, segments);
+}
+
+size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv) {
+  (void)Hq;
+  return gdn::prefill_segments_bytes(N, Hv, gdn_prefill_segments(T, N, Hv));
 }
 
 int gdn_prefill_chunked(const void* q, const void* k, const void* v, const float* state,
@@ -196,13 +225,48 @@ int gdn_prefill(const void* q, const void* k, const void* v, const float* state,
                 float scale, void* output, float* new_state, int64_t T, int64_t N, int64_t Hq,
                 int64_t Hk, int64_t Hv, int64_t D, void* workspace, size_t workspace_bytes,
                 void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (use_recurrent(T, N, Hv))
     return gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                                  new_state, T, N, Hq, Hk, Hv, D, stream);
+  const int G = choose_segments(T, N, Hv);
+  if (G > 1 && workspace && workspace_bytes >= gdn::prefill_segments_bytes(N, Hv, G))
+    return gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                                 new_state, T, N, Hq, Hk, Hv, D, 0, G, workspace, workspace_bytes,
+                                 stream);
   return gdn_prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                              new_state, T, N, Hq, Hk, Hv, D, stream);
+}
+
+// Checks shared by the segmented entries; segments 0 = automatic.
+static int segmented_setup(int64_t T, int64_t N, int64_t Hv, int* segments, void* workspace,
+                           size_t workspace_bytes) {
+  if (*segments < 0 || *segments > 64) return fail(GDN_ERR_VALUE, "segments must be in [0, 64]");
+  if (*segments == 0) *segments = choose_segments(T, N, Hv);
+  const size_t need = gdn::prefill_segments_bytes(N, Hv, *segments);
+  if (need > 0 && (!workspace || workspace_bytes < need))
+    return fail(GDN_ERR_VALUE, "workspace needs %zu bytes", need);
+  if (!aligned(workspace, 256)) return fail(GDN_ERR_VALUE, "workspace must be 256-byte aligned");
+  return GDN_OK;
+}
+
+int gdn_prefill_segmented(const void* q, const void* k, const void* v, const float* state,
+                          const float* A_log, const void* a, const float* dt_bias, const void* b,
+                          const int64_t* cu_seqlens, float scale, void* output, float* new_state,
+                          int64_t T, int64_t N, int64_t Hq, int64_t Hk, int64_t Hv, int64_t D,
+                          int flags, int segments, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  if (flags & ~GDN_PREFILL_QK_L2NORM) return fail(GDN_ERR_VALUE, "unknown flags");
+  if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
+                            N, Hq, Hk, Hv, D))
+    return e;
+  if (T > 0x7fffffffLL - 64) return fail(GDN_ERR_VALUE, "total_seq_len too large");
+  if (int e = segmented_setup(T, N, Hv, &segments, workspace, workspace_bytes)) return e;
+  gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                     scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv,
+                     (flags & GDN_PREFILL_QK_L2NORM) != 0};
+  return cuda_status(gdn::launch_prefill_segmented(p, segments, workspace, workspace_bytes,
+                                                   static_cast<cudaStream_t>(stream)),
+                     "gdn_prefill_segmented launch");
 }
 
 int gdn_prefill_ex(const void* q, const void* k, const void* v, const float* state,
@@ -232,7 +296,8 @@ int gdn_prefill_chunked_peers(const void* q, const void* k, const void* v, const
                               const int64_t* cu_seqlens, float scale, void* output, float* new_state,
                               int64_t T, int64_t N, int64_t Hq, int64_t Hk, int64_t Hv, int64_t D,
                               int64_t Hv_out, int64_t head_offset, void* const* peer_outputs,
-                              int num_peers, void* stream) {
+                              int num_peers, int segments, void* workspace, size_t workspace_bytes,
+                              void* stream) {
   if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
                             N, Hq, Hk, Hv, D))
     return e;
@@ -246,13 +311,15 @@ int gdn_prefill_chunked_peers(const void* q, const void* k, const void* v, const
   for (int r = 0; r < num_peers; ++r)
     if (!peer_outputs[r] || !aligned(peer_outputs[r], 16))
       return fail(GDN_ERR_VALUE, "peer output %d is null or not 16-byte aligned", r);
+  if (int e = segmented_setup(T, N, Hv, &segments, workspace, workspace_bytes)) return e;
   gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
                      scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv};
   p.out_heads = Hv_out;
   p.out_head_off = head_offset;
   p.n_peers = num_peers;
   p.peer_out = peer_outputs;
-  return cuda_status(gdn::launch_prefill_chunked(p, static_cast<cudaStream_t>(stream)),
+  return cuda_status(gdn::launch_prefill_segmented(p, segments, workspace, workspace_bytes,
+                                                   static_cast<cudaStream_t>(stream)),
                      "gdn_prefill_chunked_peers launch");
 }
 

@@ -74,10 +74,38 @@ struct PrefillArgs {
   int64_t out_heads = 0, out_head_off = 0;
   int n_peers = 0;
   void* const* peer_out = nullptr;
+  // chunked kernel only: a job table in device memory (one job per group of Hv
+  // CTAs) replaces cu_seqlens / state / new_state when set
+  const struct SegJob* jobs = nullptr;
+  int64_t njobs = 0;
+};
+
+// One job of the segmented prefill: the tokens [bos, eos) of one sequence
+// segment for all Hv heads, from state_in ([Hv,128,128] fp32; nullptr = zero;
+// ignored with kJobIdentity) to state_out ([Hv,128,128]; nullptr = not stored).
+enum : uint32_t {
+  kJobIdentity = 1u,  // initial state = identity (the segment's transition matrix)
+  kJobNoV = 2u,       // v = 0
+  kJobNoOut = 4u,     // outputs not written
+};
+struct SegJob {
+  int64_t bos, eos;
+  const float* state_in;
+  float* state_out;
+  uint32_t flags, pad;
 };
 constexpr int kMaxPeers = 7;
 
 cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);
+// Segmented (sequence-parallel) prefill: every sequence long enough is cut into
+// `segments` pieces at chunk boundaries; pass 1 runs piece 0 from the initial
+// state and, for the middle pieces, their final state from zero (F) and their
+// transition matrix (P, the final state from the identity with v = 0); the
+// start states of pieces 2.. follow from S_{g+1} = S_g P_g + F_g in fp32; pass 2
+// runs pieces 1.. from their start states.  Workspace: prefill_segments_bytes.
+size_t prefill_segments_bytes(int64_t N, int64_t Hv, int segments);
+cudaError_t launch_prefill_segmented(const PrefillArgs& a, int segments, void* workspace,
+                                     size_t workspace_bytes, cudaStream_t s);
 
 // fused chunked (C=64) prefill on tcgen05; no workspace
 cudaError_t launch_prefill_chunked(const PrefillArgs& a, cudaStream_t s);

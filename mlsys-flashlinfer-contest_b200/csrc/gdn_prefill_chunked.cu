@@ -127,6 +127,7 @@ struct ChunkParams {
   __nv_bfloat16* out;
   float* new_state;
   float* debug;  // optional dump of one chunk's intermediates
+  const SegJob* jobs;  // segmented prefill: job table (nullptr: sequences from cu_seqlens)
   float scale;
   int tma_out;   // output rows of full chunks go through a TMA store (out is 16-byte aligned)
   int Hv_out, head_off;  // heads of the output buffer(s), position of this call's heads
@@ -211,14 +212,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h = static_cast<int>(blockIdx.x % p.Hv);
   const int64_t n = blockIdx.x / p.Hv;
   const int qh = h / (p.Hv / p.Hq);
-  const int64_t bos = min(max(p.cu_seqlens[n], int64_t(0)), p.T);
-  const int64_t eos = min(max(p.cu_seqlens[n + 1], bos), p.T);
+  constexpr int64_t kStateFloats = kHead * kHead;
+  int64_t bos, eos;
+  const float* state_in;  // this head's initial state (nullptr: zero)
+  float* ns_rows;         // this head's final state (nullptr: not stored)
+  uint32_t jflags = 0;
+  if (p.jobs) {  // one segment of a sequence (job values are written on the device)
+    const SegJob jb = p.jobs[n];
+    bos = min(max(jb.bos, int64_t(0)), p.T);
+    eos = min(max(jb.eos, bos), p.T);
+    state_in = jb.state_in ? jb.state_in + h * kStateFloats : nullptr;
+    ns_rows = jb.state_out ? jb.state_out + h * kStateFloats : nullptr;
+    jflags = jb.flags;
+  } else {
+    bos = min(max(p.cu_seqlens[n], int64_t(0)), p.T);
+    eos = min(max(p.cu_seqlens[n + 1], bos), p.T);
+    state_in = p.state ? p.state + (n * p.Hv + h) * kStateFloats : nullptr;
+    ns_rows = p.new_state + (n * p.Hv + h) * kStateFloats;
+  }
   const int64_t Ltot = eos - bos;
-  float* ns_rows = p.new_state + (n * p.Hv + h) * (kHead * kHead);
+  const bool init_identity = jflags & kJobIdentity, v_zero = jflags & kJobNoV;
+  const bool write_out = !(jflags & kJobNoOut);
 
   if (Ltot <= 0) {  // empty sequence: zero final state (definition skips it)
-    for (int i = tid; i < kHead * kHead / 4; i += kThreads)
-      reinterpret_cast<float4*>(ns_rows)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ns_rows)
+      for (int i = tid; i < kHead * kHead / 4; i += kThreads)
+        reinterpret_cast<float4*>(ns_rows)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     return;
   }
   const int nchunks = static_cast<int>((Ltot + kChunk - 1) / kChunk);
@@ -267,8 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- initial state -> TMEM (row rowv, columns [32 cq, 32 cq + 32)) -----
     {
-      const float* src = p.state ? p.state + (n * p.Hv + h) * (kHead * kHead) + rowv * kHead + 32 * cq
-                                 : nullptr;
+      const float* src = state_in && !init_identity ? state_in + rowv * kHead + 32 * cq : nullptr;
       float v[32];
 #pragma unroll
       for (int q4 = 0; q4 < 8; ++q4) {
@@ -277,6 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         v[4 * q4 + 1] = x.y;
         v[4 * q4 + 2] = x.z;
         v[4 * q4 + 3] = x.w;
+      }
+      if (init_identity) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = (rowv == 32 * cq + i) ? 1.f : 0.f;
       }
       tmem_st32(tq_st, v);
       tmem_wait_st();
@@ -392,6 +414,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = tid; i < 8192 / 16; i += kComputeThreads)  // Bl: zero off the diagonal
       sts128(sb + OFF_BL + 16 * i, 0u, 0u, 0u, 0u);
+    if (v_zero) {  // no V loads: both V stages hold zeros for the whole sequence
+      for (int i = tid; i < 2 * kVStage / 16; i += kComputeThreads)
+        sts128(sb + OFF_V + 16 * i, 0u, 0u, 0u, 0u);
+      fence_async_smem();
+    }
     if constexpr (L2) {  // chunk 0's factors, published by the first loop-top barrier
       wait_mma(BAR_M1, 0u);
       qk_norms(0);
@@ -810,7 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       //      t), stored by TMA from the issue thread; a partial chunk stores
       //      directly. ---------------------------------------------------
       {
-        const bool via_tma = p.tma_out && L == kChunk;
+        const bool via_tma = write_out && p.tma_out && L == kChunk;
         // lanes pair up (v even, v + 1): the even lane stores the bf16x2 words
         // of tokens 0-7 of this warp's 16, the odd lane those of tokens 8-15
         const bool odd = rowv & 1;
@@ -862,7 +889,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t w = odd ? pack_bf16x2(theirs, mine) : pack_bf16x2(mine, theirs);
             sts32(ocol + t * 128 + ((och ^ (t & 7)) << 4), w);
           }
-        } else {
+        } else if (write_out) {
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             if (16 * cq + i < L) orow[(16 * cq + i) * tstride] = __float2bfloat16_rn(o[i]);
@@ -887,7 +914,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 #undef PHASE
 
-    if (!aborted && p.tma_out && eos - (bos + static_cast<int64_t>(nchunks - 1) * kChunk) == kChunk) {
+    if (!aborted && write_out && p.tma_out &&
+        eos - (bos + static_cast<int64_t>(nchunks - 1) * kChunk) == kChunk) {
       // output tile of the last (full) chunk
       fence_async_smem();
       named_sync(kComputeBar, kComputeThreads);
@@ -908,7 +936,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- final state -> new_state (row rowv, this warp's 32 columns) --------
     if (!aborted) {
       wait_mma(BAR_ST, static_cast<uint32_t>((nchunks - 1) & 1));
-      if (!failed) {
+      if (!failed && ns_rows) {
         if (dbg_cta && nchunks - 1 == p.dbg_chunk) dump_state();
         float* dst = ns_rows + rowv * kHead + 32 * cq;
         float v[32];
@@ -949,14 +977,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = cc & 1;
       const int tok = static_cast<int>(bos + static_cast<int64_t>(cc) * kChunk);
       uint64_t* bar = &bars[BAR_TMA0 + s];
-      mbar_arrive_expect_tx(bar, kTmaBytes);
+      mbar_arrive_expect_tx(bar, v_zero ? kTmaBytes - kVStage : kTmaBytes);
       uint8_t* kq = smem + OFF_KQ + s * kKQStage;
       uint8_t* vs = smem + OFF_V + s * kVStage;
 #pragma unroll
       for (int kb = 0; kb < 2; ++kb) {
         tma_load_3d(kq + kb * 16384, &tm_k, bar, kb * 64, qh, tok);
         tma_load_3d(kq + kb * 16384 + 8192, &tm_q, bar, kb * 64, qh, tok);
-        tma_load_3d(vs + kb * 8192, &tm_v, bar, kb * 64, h, tok);
+        if (!v_zero) tma_load_3d(vs + kb * 8192, &tm_v, bar, kb * 64, h, tok);
       }
       tma_issued = cc + 1;
     };
@@ -1027,7 +1055,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       MPHASE(2)
       // the output tile of chunk c-1 (full: only a sequence's last chunk can be
       // partial) is complete and fenced by every compute thread before RDY_T
-      if (c > 0 && p.tma_out) {
+      if (c > 0 && p.tma_out && write_out) {
         const int tp = static_cast<int>(bos + static_cast<int64_t>(c - 1) * kChunk);
         const int gh = h + p.head_off;
         tma_store_3d(&tm_o, smem + OFF_O, 0, gh, tp);
@@ -1177,8 +1205,8 @@ cudaError_t make_head_map(CUtensorMap* m, const void* base, int64_t heads, int64
 template <bool DEBUG>
 cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg_head,
                         int dbg_chunk, cudaStream_t s) {
-  if (a.N == 0) return cudaSuccess;
-  if (a.T == 0) {  // every sequence is empty: zero final states
+  if ((a.jobs ? a.njobs : a.N) == 0) return cudaSuccess;
+  if (a.T == 0 && !a.jobs) {  // every sequence is empty: zero final states
     return cudaMemsetAsync(a.new_state, 0,
                            static_cast<size_t>(a.N) * a.Hv * kHead * kHead * sizeof(float), s);
   }
@@ -1210,11 +1238,11 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   }
   ChunkParams p{a.state, a.A_log, a.dt_bias,
                 static_cast<const __nv_bfloat16*>(a.a), static_cast<const __nv_bfloat16*>(a.b),
-                a.cu_seqlens, static_cast<__nv_bfloat16*>(a.out), a.new_state, debug, a.scale,
+                a.cu_seqlens, static_cast<__nv_bfloat16*>(a.out), a.new_state, debug, a.jobs, a.scale,
                 tma_out, static_cast<int>(out_heads), static_cast<int>(a.out_head_off), a.n_peers, {},
                 a.T, a.N, static_cast<int>(a.Hq), static_cast<int>(a.Hv), dbg_seq, dbg_head, dbg_chunk};
   for (int r = 0; r < a.n_peers; ++r) p.peer_out[r] = static_cast<__nv_bfloat16*>(a.peer_out[r]);
-  const int64_t ctas = a.N * a.Hv;
+  const int64_t ctas = (a.jobs ? a.njobs : a.N) * a.Hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
   kernel<<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, pm, p);
   return cudaGetLastError();

@@ -1,0 +1,186 @@
+// Segmented (sequence-parallel) prefill on top of the fused chunked kernel.
+//
+// The chunked kernel walks a (sequence, v-head) pair's chunks in order on one
+// SM, so a call with few pairs leaves most of the 148 SMs idle (one long
+// sequence of a few heads, or a head-sharded multi-GPU call).  The state update
+// is affine in the state: over tokens a..b,
+//     S_b = S_{a-1} P + F,   P = A_a ... A_b,  A_t = g_t (I - beta_t k_t k_t^T),
+// F the final state of the same tokens from a zero state, and P the final state
+// from the identity with v = 0 (rows of the "state" are then k rows).  So a
+// sequence cut into G pieces at chunk boundaries runs as
+//   pass 1 (one launch): piece 0 from the initial state (outputs written, its
+//          final state = the start state of piece 1) and, for pieces 1..G-2,
+//          F_g and P_g (outputs not written);
+//   combine (G-2 launches): S_{g+1} = S_g P_g + F_g, fp32 on CUDA cores;
+//   pass 2 (one launch): pieces 1..G-1 from their start states (outputs, and the
+//          final state of the last piece).
+// The chain is about 2/G of the sequence's chunks long instead of all of them,
+// for (3G-4)/G times the chunk work: worth it when the pairs fill few SMs.  The
+// jobs are built on the device from cu_seqlens (a one-CTA kernel), so the host
+// never reads the lengths.  The reference has no counterpart: its chunked
+// pipeline (chunk_v12.py:36-116) runs one state scan per (sequence, head).
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+
+namespace gdn {
+namespace {
+
+constexpr size_t kStateBytes1 = static_cast<size_t>(kHead) * kHead * sizeof(float);
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct SegLayout {
+  SegJob* jobs1;    // [N][2G-3]
+  SegJob* jobs2;    // [N][G-1]
+  int32_t* split;   // [N]: sequence cut into G pieces
+  float* sin;       // [N][G-1][Hv][128][128]: start state of piece g (g = 1..G-1)
+  float* fst;       // [N][G-2][Hv][128][128]: F_g (g = 1..G-2)
+  float* pst;       // [N][G-2][Hv][128][128]: P_g
+};
+
+SegLayout carve(void* ws, int64_t N, int64_t Hv, int G, size_t* bytes) {
+  SegLayout l{};
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += align256(n);
+    return p;
+  };
+  const size_t st = static_cast<size_t>(Hv) * kStateBytes1;
+  const int64_t mid = G > 2 ? G - 2 : 0;
+  l.jobs1 = reinterpret_cast<SegJob*>(take(static_cast<size_t>(N) * (2 * G - 3) * sizeof(SegJob)));
+  l.jobs2 = reinterpret_cast<SegJob*>(take(static_cast<size_t>(N) * (G - 1) * sizeof(SegJob)));
+  l.split = reinterpret_cast<int32_t*>(take(static_cast<size_t>(N) * sizeof(int32_t)));
+  l.sin = reinterpret_cast<float*>(take(static_cast<size_t>(N) * (G - 1) * st));
+  l.fst = reinterpret_cast<float*>(take(static_cast<size_t>(N) * mid * st));
+  l.pst = reinterpret_cast<float*>(take(static_cast<size_t>(N) * mid * st));
+  *bytes = off;
+  return l;
+}
+
+// One thread per sequence: cut it into G pieces of equal chunk counts (when it
+// has at least two chunks per piece) and write its jobs of both passes.
+__global__ void gdn_segment_jobs_kernel(const int64_t* cu_seqlens, int64_t N, int64_t T, int64_t Hv,
+                                        int G, const float* state, float* new_state, SegLayout l) {
+  const int64_t st = Hv * kHead * kHead;  // floats of one sequence's (or piece's) states
+  const int64_t mid = G > 2 ? G - 2 : 0;
+  for (int64_t n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+    const int64_t bos = min(max(cu_seqlens[n], int64_t(0)), T);
+    const int64_t eos = min(max(cu_seqlens[n + 1], bos), T);
+    const int64_t nch = (eos - bos + kChunk - 1) / kChunk;
+    SegJob* j1 = l.jobs1 + n * (2 * G - 3);
+    SegJob* j2 = l.jobs2 + n * (G - 1);
+    const float* s0 = state ? state + n * st : nullptr;
+    float* s_out = new_state + n * st;
+    const SegJob none{0, 0, nullptr, nullptr, 0u, 0u};
+    const bool split = nch >= 2 * G;
+    l.split[n] = split ? 1 : 0;
+    if (!split) {
+      j1[0] = SegJob{bos, eos, s0, s_out, 0u, 0u};
+      for (int j = 1; j < 2 * G - 3; ++j) j1[j] = none;
+      for (int j = 0; j < G - 1; ++j) j2[j] = none;
+      continue;
+    }
+    auto piece = [&](int g, int64_t* b, int64_t* e) {
+      *b = bos + (g * nch / G) * kChunk;
+      *e = min(bos + ((g + 1) * nch / G) * kChunk, eos);
+    };
+    auto sin = [&](int g) { return l.sin + ((n * (G - 1) + (g - 1)) * st); };
+    int64_t b, e;
+    piece(0, &b, &e);
+    j1[0] = SegJob{b, e, s0, sin(1), 0u, 0u};
+    for (int g = 1; g <= G - 2; ++g) {
+      piece(g, &b, &e);
+      float* f = l.fst + (n * mid + (g - 1)) * st;
+      float* pm = l.pst + (n * mid + (g - 1)) * st;
+      j1[2 * g - 1] = SegJob{b, e, nullptr, f, kJobNoOut, 0u};
+      j1[2 * g] = SegJob{b, e, nullptr, pm, kJobIdentity | kJobNoV | kJobNoOut, 0u};
+    }
+    for (int g = 1; g <= G - 1; ++g) {
+      piece(g, &b, &e);
+      j2[g - 1] = SegJob{b, e, sin(g), g == G - 1 ? s_out : nullptr, 0u, 0u};
+    }
+  }
+}
+
+// S_{g+1} = S_g P_g + F_g for every cut sequence and head: a CTA computes 16
+// rows (of 128) of one head, k in tiles of 32 rows of P staged in shared memory.
+constexpr int kCombRows = 16;
+constexpr int kCombKTile = 32;
+__global__ void __launch_bounds__(256) gdn_segment_combine_kernel(int64_t N, int64_t Hv, int G, int g,
+                                                                  SegLayout l) {
+  const int64_t cta = blockIdx.x;
+  const int rb = static_cast<int>(cta % (kHead / kCombRows));
+  const int64_t nh = cta / (kHead / kCombRows);
+  const int64_t n = nh / Hv, h = nh % Hv;
+  if (n >= N || !l.split[n]) return;
+  const int64_t hs = h * kHead * kHead;
+  const int64_t st = Hv * kHead * kHead;
+  const int64_t mid = G - 2;
+  const float* S = l.sin + (n * (G - 1) + (g - 1)) * st + hs + rb * kCombRows * kHead;
+  float* out = l.sin + (n * (G - 1) + g) * st + hs + rb * kCombRows * kHead;
+  const float* F = l.fst + (n * mid + (g - 1)) * st + hs + rb * kCombRows * kHead;
+  const float* P = l.pst + (n * mid + (g - 1)) * st + hs;
+  __shared__ __align__(16) float s_s[kCombRows][kHead];
+  __shared__ __align__(16) float p_s[kCombKTile][kHead];
+  const int t = threadIdx.x, c = t & (kHead - 1), r0 = (t >> 7) * 8;
+  for (int i = t; i < kCombRows * kHead / 4; i += 256)
+    reinterpret_cast<float4*>(&s_s[0][0])[i] = reinterpret_cast<const float4*>(S)[i];
+  float acc[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) acc[r] = F[(r0 + r) * kHead + c];
+  for (int k0 = 0; k0 < kHead; k0 += kCombKTile) {
+    __syncthreads();  // s_s loaded / the previous tile consumed
+    for (int i = t; i < kCombKTile * kHead / 4; i += 256)
+      reinterpret_cast<float4*>(&p_s[0][0])[i] = reinterpret_cast<const float4*>(P + k0 * kHead)[i];
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kCombKTile; ++k) {
+      const float pk = p_s[k][c];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) acc[r] = fmaf(s_s[r0 + r][k0 + k], pk, acc[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r) out[(r0 + r) * kHead + c] = acc[r];
+}
+
+}  // namespace
+
+size_t prefill_segments_bytes(int64_t N, int64_t Hv, int segments) {
+  if (segments < 2 || N <= 0) return 0;
+  size_t bytes = 0;
+  carve(nullptr, N, Hv, segments, &bytes);
+  return bytes;
+}
+
+cudaError_t launch_prefill_segmented(const PrefillArgs& a, int G, void* ws, size_t ws_bytes,
+                                     cudaStream_t s) {
+  if (G < 2 || a.N == 0 || a.T == 0) return launch_prefill_chunked(a, s);
+  size_t need = 0;
+  const SegLayout l = carve(ws, a.N, a.Hv, G, &need);
+  if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return cudaErrorInvalidValue;
+  const int64_t jt = 256;
+  const int64_t jb = (a.N + jt - 1) / jt;
+  gdn_segment_jobs_kernel<<<static_cast<unsigned>(jb > 1024 ? 1024 : jb), jt, 0, s>>>(
+      a.cu_seqlens, a.N, a.T, a.Hv, G, a.state, a.new_state, l);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  PrefillArgs p1 = a;
+  p1.jobs = l.jobs1;
+  p1.njobs = a.N * (2 * G - 3);
+  if ((e = launch_prefill_chunked(p1, s)) != cudaSuccess) return e;
+  const int64_t cctas = a.N * a.Hv * (kHead / kCombRows);
+  if (cctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+  for (int g = 1; g <= G - 2; ++g) {
+    gdn_segment_combine_kernel<<<static_cast<unsigned>(cctas), 256, 0, s>>>(a.N, a.Hv, G, g, l);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  PrefillArgs p2 = a;
+  p2.jobs = l.jobs2;
+  p2.njobs = a.N * (G - 1);
+  return launch_prefill_chunked(p2, s);
+}
+
+}  // namespace gdn

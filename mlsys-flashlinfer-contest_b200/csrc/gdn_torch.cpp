@@ -128,8 +128,10 @@ std::tuple<at::Tensor, at::Tensor> decode(const at::Tensor& q, const at::Tensor&
 
 // prefill: q, k [T,Hq,128] bf16; v [T,Hv,128] bf16; state [N,Hv,128,128] fp32 or
 // None; a, b [T,Hv] bf16; cu_seqlens [N+1] int64 -> (output, new_state).
-// path: 0 = the default dispatch (gdn_prefill), 1 = token-recurrent kernel,
-// 2 = chunked kernel; qk_l2norm: in-kernel q/k L2 normalisation.
+// path: 0 = the default dispatch (gdn_prefill: recurrent, segmented or chunked),
+// 1 = token-recurrent kernel, 2 = chunked kernel, 3 = segmented with `segments`
+// pieces (0 = automatic); qk_l2norm: in-kernel q/k L2 normalisation.  The
+// segmented form's workspace comes from the caching allocator.
 std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor& k,
                                            const at::Tensor& v,
                                            const c10::optional<at::Tensor>& state,
@@ -138,7 +140,7 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
                                            const at::Tensor& cu_seqlens, double scale,
                                            c10::optional<at::Tensor> output,
                                            c10::optional<at::Tensor> new_state, int64_t path,
-                                           bool qk_l2norm) {
+                                           bool qk_l2norm, int64_t segments) {
   const std::pair<const at::Tensor*, const char*> ins[] = {
       {&q, "q"}, {&k, "k"},           {&v, "v"}, {&A_log, "A_log"}, {&a, "a"}, {&dt_bias, "dt_bias"},
       {&b, "b"}, {&cu_seqlens, "cu_seqlens"}};
@@ -154,7 +156,9 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
   const int64_t T = q.size(0), Hq = q.size(1), Nseq = cu_seqlens.size(0) - 1;
   const int64_t Hk = k.size(1), Hv = v.size(1);
   TORCH_CHECK_VALUE(Nseq > 0, "must have at least one sequence");
-  TORCH_CHECK_VALUE(path >= 0 && path <= 2, "path must be 0 (auto), 1 (recurrent) or 2 (chunked)");
+  TORCH_CHECK_VALUE(path >= 0 && path <= 3,
+                    "path must be 0 (auto), 1 (recurrent), 2 (chunked) or 3 (segmented)");
+  TORCH_CHECK_VALUE(segments >= 0 && segments <= 64, "segments must be in [0, 64]");
   TORCH_CHECK_VALUE(q.size(2) == kHead && k.size(2) == kHead && v.size(2) == kHead,
                     "head size must be 128");
   TORCH_CHECK_VALUE(k.size(0) == T && v.size(0) == T, "k/v shape mismatch");
@@ -202,11 +206,27 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
   }
   const c10::cuda::CUDAGuard guard(q.device());
   const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  int G = 1;  // pieces of the segmented form (1: not taken)
+  if (path == 3) G = segments > 0 ? static_cast<int>(segments) : gdn_prefill_segments(T, Nseq, Hv);
+  if (path == 0) G = gdn_prefill_segments(T, Nseq, Hv);
+  const int flags = qk_l2norm ? GDN_PREFILL_QK_L2NORM : 0;
+  if (G > 1) {
+    const size_t ws_bytes = gdn_prefill_segmented_workspace_bytes(Nseq, Hv, G);
+    at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(at::kByte));
+    check_rc(gdn_prefill_segmented(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
+                                   A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
+                                   b.data_ptr(), cu_seqlens.data_ptr<int64_t>(),
+                                   static_cast<float>(scale), output->data_ptr(),
+                                   new_state->data_ptr<float>(), T, Nseq, Hq, Hk, Hv, kHead, flags,
+                                   G, ws.data_ptr(), ws_bytes, stream),
+             "gdn_prefill_segmented");
+    return {*output, *new_state};
+  }
   check_rc(gdn_prefill_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
                           A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
                           b.data_ptr(), cu_seqlens.data_ptr<int64_t>(), static_cast<float>(scale),
                           output->data_ptr(), new_state->data_ptr<float>(), T, Nseq, Hq, Hk, Hv,
-                          kHead, qk_l2norm ? GDN_PREFILL_QK_L2NORM : 0, static_cast<int>(path),
+                          kHead, flags, path == 3 ? GDN_PREFILL_PATH_CHUNKED : static_cast<int>(path),
                           stream),
            "gdn_prefill_ex");
   return {*output, *new_state};
@@ -308,11 +328,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode", &decode, "GDN decode (C ABI gdn_decode)", py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("state"), py::arg("A_log"), py::arg("a"), py::arg("dt_bias"), py::arg("b"),
         py::arg("scale"), py::arg("output") = py::none(), py::arg("new_state") = py::none());
-  m.def("prefill", &prefill, "GDN prefill (C ABI gdn_prefill / gdn_prefill_recurrent)",
-        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("state"), py::arg("A_log"), py::arg("a"),
-        py::arg("dt_bias"), py::arg("b"), py::arg("cu_seqlens"), py::arg("scale"),
-        py::arg("output") = py::none(), py::arg("new_state") = py::none(), py::arg("path") = 0,
-        py::arg("qk_l2norm") = false);
+  m.def("prefill", &prefill,
+        "GDN prefill (C ABI gdn_prefill_ex / gdn_prefill_segmented)", py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("state"), py::arg("A_log"), py::arg("a"), py::arg("dt_bias"),
+        py::arg("b"), py::arg("cu_seqlens"), py::arg("scale"), py::arg("output") = py::none(),
+        py::arg("new_state") = py::none(), py::arg("path") = 0, py::arg("qk_l2norm") = false,
+        py::arg("segments") = 0);
   m.def("decode_pool", &decode_pool, "pooled multi-token GDN decode (C ABI gdn_decode_pool)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("A_log"), py::arg("a"), py::arg("dt_bias"),
         py::arg("b"), py::arg("scale"), py::arg("state_pool"), py::arg("in_slots"),

@@ -31,7 +31,11 @@ SIGNATURES = {
     "gdn_chunk_upper_bound": (I64, [I64, I64]),
     "gdn_prefill_chunked": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64, P]),
     "gdn_prefill_chunked_peers": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64,
-                                      I64, I64, I64, P, I, P]),
+                                      I64, I64, I64, P, I, I, P, SZ, P]),
+    "gdn_prefill_segmented": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64,
+                                  I, I, P, SZ, P]),
+    "gdn_prefill_segmented_workspace_bytes": (SZ, [I64, I64, I]),
+    "gdn_prefill_segments": (I, [I64, I64, I64]),
     "gdn_prefill_chunked_debug": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64,
                                       I64, P, I64, I64, I64, I64, P]),
     "gdn_prefill_chunked_debug_floats": (I64, []),

@@ -90,7 +90,7 @@ def launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_
     ext = N.torch_ext()
     if ext is not None and workspace is None:
         return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, resolve_scale(scale),
-                           output, new_state, path, use_qk_l2norm)
+                           output, new_state, path, use_qk_l2norm, 0)
     T, Nseq, Hq, Hk, Hv = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output,
                                     new_state)
     L = N.lib()
@@ -130,7 +130,7 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, use_qk_l2norm: 
     ext = N.torch_ext()
     if ext is not None:
         return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, _widen(cu_seqlens),
-                           resolve_scale(scale), None, None, 0, use_qk_l2norm)
+                           resolve_scale(scale), None, None, 0, use_qk_l2norm, 0)
     Nseq = cu_seqlens.shape[0] - 1
     Hv = v.shape[1]
     output = torch.empty_like(v)
@@ -145,7 +145,7 @@ def run_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
     ext = N.torch_ext()
     if ext is not None:
         return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, _widen(cu_seqlens),
-                           resolve_scale(scale), None, None, 1, use_qk_l2norm)
+                           resolve_scale(scale), None, None, 1, use_qk_l2norm, 0)
     Nseq = cu_seqlens.shape[0] - 1
     output = torch.empty_like(v)
     new_state = torch.empty((max(Nseq, 0), v.shape[1], HEAD, HEAD), dtype=torch.float32,
@@ -164,3 +164,39 @@ def run_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
                             device=v.device)
     return launch(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
                   chunked=True, use_qk_l2norm=use_qk_l2norm)
+
+
+def segments_for(T: int, Nseq: int, Hv: int) -> int:
+    """The automatic piece count of the segmented prefill (1: one chain per pair)."""
+    return int(N.lib().gdn_prefill_segments(T, Nseq, Hv))
+
+
+def run_segmented(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, segments: int = 0,
+                  use_qk_l2norm: bool = False, output=None, new_state=None):
+    """Sequence-parallel prefill (C ABI gdn_prefill_segmented): sequences of at least
+    2 * segments chunks are cut into ``segments`` pieces whose start states follow
+    from each piece's transition matrix; ``segments`` 0 = the automatic count.
+    Returns (output, new_state)."""
+    cu_seqlens = _widen(cu_seqlens)
+    ext = N.torch_ext()
+    if ext is not None:
+        return ext.prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, resolve_scale(scale),
+                           output, new_state, 3, use_qk_l2norm, segments)
+    T, Nseq, Hq, Hk, Hv = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output,
+                                    new_state)
+    if output is None:
+        output = torch.empty_like(v)
+    if new_state is None:
+        new_state = torch.empty((Nseq, Hv, HEAD, HEAD), dtype=torch.float32, device=v.device)
+    L = N.lib()
+    G = segments if segments > 0 else segments_for(T, Nseq, Hv)
+    ws_bytes = int(L.gdn_prefill_segmented_workspace_bytes(Nseq, Hv, G))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+    with torch.cuda.device(q.device):
+        rc = L.gdn_prefill_segmented(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(state), N.ptr(A_log),
+                                     N.ptr(a), N.ptr(dt_bias), N.ptr(b), N.ptr(cu_seqlens),
+                                     resolve_scale(scale), N.ptr(output), N.ptr(new_state), T,
+                                     Nseq, Hq, Hk, Hv, HEAD, 1 if use_qk_l2norm else 0, G,
+                                     N.ptr(ws), ws_bytes, N.stream_handle(q.device))
+    N.check(rc, "gdn_prefill_segmented")
+    return output, new_state

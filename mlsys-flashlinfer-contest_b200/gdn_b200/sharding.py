@@ -160,12 +160,15 @@ class PeerOutputs:
                 self._ptr = 0
 
 
-def prefill_gathered(inp_local, head_offset: int, bufs: PeerOutputs, new_state=None):
+def prefill_gathered(inp_local, head_offset: int, bufs: PeerOutputs, new_state=None,
+                     segments: int = 0, workspace=None):
     """Chunked prefill of this rank's heads (``inp_local`` as ``slice_prefill_heads``
     builds it) whose output tiles go to heads [head_offset, head_offset + Hv_local)
     of every rank's full output buffer (C ABI gdn_prefill_chunked_peers).  Returns
     (this rank's full output buffer, this rank's new states).  The buffer holds all
-    heads only after every rank's call has completed: synchronise and barrier first."""
+    heads only after every rank's call has completed: synchronise and barrier first.
+    ``segments``: 0 = the automatic sequence-parallel cut (a head shard has few
+    (sequence, head) pairs), 1 = none; the workspace is allocated when not given."""
     import ctypes
     from . import _native as N
     from ._checks import HEAD, resolve_scale
@@ -176,13 +179,20 @@ def prefill_gathered(inp_local, head_offset: int, bufs: PeerOutputs, new_state=N
     if new_state is None:
         new_state = torch.empty((Nseq, Hv, HEAD, HEAD), dtype=torch.float32, device=q.device)
     peers = (ctypes.c_void_p * max(len(bufs.peer_ptrs), 1))(*bufs.peer_ptrs)
+    L = N.lib()
+    if segments == 0:
+        segments = L.gdn_prefill_segments(T, Nseq, Hv)
+    ws_bytes = L.gdn_prefill_segmented_workspace_bytes(Nseq, Hv, segments)
+    if workspace is None and ws_bytes > 0:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
-        rc = N.lib().gdn_prefill_chunked_peers(
+        rc = L.gdn_prefill_chunked_peers(
             N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(inp_local.state), N.ptr(inp_local.A_log),
             N.ptr(inp_local.a), N.ptr(inp_local.dt_bias), N.ptr(inp_local.b),
             N.ptr(inp_local.cu_seqlens), resolve_scale(inp_local.scale), N.ptr(bufs.output),
             N.ptr(new_state), T, Nseq, Hq, k.shape[1], Hv, HEAD, bufs.Hv, head_offset,
-            ctypes.cast(peers, ctypes.c_void_p), len(bufs.peer_ptrs), N.stream_handle(q.device))
+            ctypes.cast(peers, ctypes.c_void_p), len(bufs.peer_ptrs), segments, N.ptr(workspace),
+            ws_bytes, N.stream_handle(q.device))
     N.check(rc, "gdn_prefill_chunked_peers")
     return bufs.output, new_state
 

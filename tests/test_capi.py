@@ -105,7 +105,7 @@ def _peers_call(Hv_out=16, off=0, npeers=1, peers=(1 << 22,), out=1 << 20):
     return L.gdn_prefill_chunked_peers(P(1 << 20), P(1 << 20), P(1 << 20), None, P(1 << 20),
                                        P(1 << 20), P(1 << 20), P(1 << 20), P(1 << 20), 0.0, P(out),
                                        P(1 << 21), 10, 1, 4, 4, 8, 128, Hv_out, off,
-                                       ctypes.cast(arr, ctypes.c_void_p), npeers, None)
+                                       ctypes.cast(arr, ctypes.c_void_p), npeers, 1, None, 0, None)
 
 
 @pytest.mark.parametrize("over,msg", [
@@ -137,3 +137,40 @@ def test_decode_pool_validation_errors():
     assert call(a17=0) == N.GDN_ERR_VALUE                    # seq_len 0
     assert call(a14=4) == N.GDN_ERR_VALUE                    # unknown flag
     assert call(a0=P((1 << 20) + 8)) == N.GDN_ERR_VALUE      # q alignment
+
+
+def test_prefill_segment_choice():
+    """Automatic piece count of the segmented prefill (148 SMs without a GPU):
+    a head shard of config 3 is cut, the full 32-head call is not."""
+    L = N.lib()
+    assert L.gdn_prefill_segments(65536, 4, 32) == 1     # 128 pairs fill the SMs
+    assert L.gdn_prefill_segments(65536, 4, 16) == 1     # 64 pairs: 3 pieces would need 192 SMs
+    assert L.gdn_prefill_segments(65536, 4, 8) == 3
+    assert L.gdn_prefill_segments(65536, 4, 4) == 6
+    assert L.gdn_prefill_segments(8192, 1, 8) == 8
+    assert L.gdn_prefill_segments(700, 1, 8) == 1        # pieces would be shorter than 4 chunks
+    assert L.gdn_prefill_segments(16, 1, 8) == 1         # the recurrent kernel's size
+    assert L.gdn_prefill_workspace_bytes(65536, 4, 16, 32) == 0
+    ws = L.gdn_prefill_workspace_bytes(65536, 4, 4, 4)
+    assert ws == L.gdn_prefill_segmented_workspace_bytes(4, 4, 6)
+    # start states of pieces 1-5 and F, P of pieces 1-4, 64 KiB per head
+    assert ws >= 4 * 4 * 65536 * (5 + 2 * 4)
+    assert L.gdn_prefill_segmented_workspace_bytes(4, 4, 1) == 0
+
+
+def test_prefill_segmented_validation_errors():
+    L = N.lib()
+    P = ctypes.c_void_p
+    def call(segments, ws, ws_bytes, flags=0):
+        return L.gdn_prefill_segmented(P(1 << 20), P(1 << 20), P(1 << 20), None, P(1 << 20),
+                                       P(1 << 20), P(1 << 20), P(1 << 20), P(1 << 20), 0.0,
+                                       P(1 << 20), P(1 << 21), 8192, 1, 4, 4, 8, 128, flags,
+                                       segments, ws, ws_bytes, None)
+    assert call(65, None, 0) == N.GDN_ERR_VALUE
+    assert "segments" in L.gdn_last_error().decode()
+    assert call(3, None, 0) == N.GDN_ERR_VALUE
+    assert "workspace" in L.gdn_last_error().decode()
+    assert call(3, P((1 << 24) + 16), 1 << 30) == N.GDN_ERR_VALUE
+    assert "256-byte" in L.gdn_last_error().decode()
+    assert call(3, P(1 << 24), 1 << 30, flags=8) == N.GDN_ERR_VALUE
+    assert "flags" in L.gdn_last_error().decode()
