@@ -208,6 +208,32 @@ int gdn_prefill_segmented(const void *q, const void *k, const void *v, const flo
                           int64_t num_k_heads, int64_t num_v_heads, int64_t head_size, int flags,
                           int segments, void *workspace, size_t workspace_bytes, void *stream);
 size_t gdn_prefill_segmented_workspace_bytes(int64_t num_seqs, int64_t num_v_heads, int segments);
+/*
+ * gdn_prefill_segmented without a workspace argument, for callers that cannot
+ * allocate device memory per call: a host whose device memory belongs to its
+ * own allocator (an inference server's arena, a plugin that is handed its
+ * buffers and may not call cudaMalloc), or one that cannot afford the device
+ * synchronisation cudaMalloc / cudaFree imply.  No counterpart in the reference
+ * (its prefill entries take no workspace and allocate through torch).  The
+ * scratch is a device array inside this library, GDN_NOALLOC_SCRATCH_BYTES
+ * (16 MiB) on every GPU that loads it, kept until the process exits; a call
+ * whose pieces need more (gdn_prefill_segmented_workspace_bytes) fails with
+ * GDN_ERR_VALUE.  The first call on a device looks up the array's address on
+ * that device (cudaGetSymbolAddress): make that first call before any stream
+ * capture.  Every call shares the array, so calls that overlap on the GPU (on
+ * two streams, or from two host threads) race; calls in one stream do not.
+ * Nothing in it needs to start at zero (each call writes what it reads).  The
+ * call allocates nothing: no cudaMalloc, cudaFree or allocating library routine.
+ */
+#define GDN_NOALLOC_SCRATCH_BYTES (16u << 20)
+int gdn_prefill_segmented_noalloc(const void *q, const void *k, const void *v, const float *state,
+                                  const float *A_log, const void *a, const float *dt_bias,
+                                  const void *b, const int64_t *cu_seqlens, float scale,
+                                  void *output, float *new_state, int64_t total_seq_len,
+                                  int64_t num_seqs, int64_t num_q_heads, int64_t num_k_heads,
+                                  int64_t num_v_heads, int64_t head_size, int flags, int segments,
+                                  void *stream);
+
 /* The automatic segment count for these sizes (1: no cut).  The largest count
  * <= 8 whose pass 1 fits in one wave of SMs, num_seqs * num_v_heads * (2 segments - 3)
  * <= SMs, with pieces of >= 4 chunks on average; 1 below 3. */

@@ -291,6 +291,38 @@ int gdn_prefill_ex(const void* q, const void* k, const void* v, const float* sta
                    : cuda_status(gdn::launch_prefill_chunked(p, st), "gdn_prefill_chunked launch");
 }
 
+// No-allocation form of gdn_prefill_segmented: the scratch is the library's own
+// device array (gdn::kNoAllocScratchBytes per GPU), whose address on the current
+// device is looked up on the first call on that device.
+int gdn_prefill_segmented_noalloc(const void* q, const void* k, const void* v, const float* state,
+                                  const float* A_log, const void* a, const float* dt_bias,
+                                  const void* b, const int64_t* cu_seqlens, float scale,
+                                  void* output, float* new_state, int64_t T, int64_t N, int64_t Hq,
+                                  int64_t Hk, int64_t Hv, int64_t D, int flags, int segments,
+                                  void* stream) {
+  static_assert(GDN_NOALLOC_SCRATCH_BYTES == gdn::kNoAllocScratchBytes, "scratch size");
+  if (flags & ~GDN_PREFILL_QK_L2NORM) return fail(GDN_ERR_VALUE, "unknown flags");
+  if (int e = check_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, output, new_state, T,
+                            N, Hq, Hk, Hv, D))
+    return e;
+  if (T > 0x7fffffffLL - 64) return fail(GDN_ERR_VALUE, "total_seq_len too large");
+  if (segments < 0 || segments > 64) return fail(GDN_ERR_VALUE, "segments must be in [0, 64]");
+  if (segments == 0) segments = choose_segments(T, N, Hv);
+  const size_t need = gdn::prefill_segments_bytes(N, Hv, segments);
+  if (need > gdn::kNoAllocScratchBytes)
+    return fail(GDN_ERR_VALUE,
+                "%lld sequences x %lld heads in %d pieces need %zu bytes of scratch; the "
+                "no-allocation entry holds %zu (use gdn_prefill_segmented with a workspace)",
+                static_cast<long long>(N), static_cast<long long>(Hv), segments, need,
+                gdn::kNoAllocScratchBytes);
+  gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
+                     scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv,
+                     (flags & GDN_PREFILL_QK_L2NORM) != 0};
+  return cuda_status(gdn::launch_prefill_segmented_noalloc(p, segments,
+                                                           static_cast<cudaStream_t>(stream)),
+                     "gdn_prefill_segmented_noalloc launch");
+}
+
 int gdn_prefill_chunked_peers(const void* q, const void* k, const void* v, const float* state,
                               const float* A_log, const void* a, const float* dt_bias, const void* b,
                               const int64_t* cu_seqlens, float scale, void* output, float* new_state,

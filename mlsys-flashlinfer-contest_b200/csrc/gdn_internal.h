@@ -106,6 +106,10 @@ cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);
 size_t prefill_segments_bytes(int64_t N, int64_t Hv, int segments);
 cudaError_t launch_prefill_segmented(const PrefillArgs& a, int segments, void* workspace,
                                      size_t workspace_bytes, cudaStream_t s);
+// The same with the workspace in a file-scope device array of kNoAllocScratchBytes
+// (the no-allocation entry); the caller checks prefill_segments_bytes against it.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+cudaError_t launch_prefill_segmented_noalloc(const PrefillArgs& a, int segments, cudaStream_t s);
 
 // fused chunked (C=64) prefill on tcgen05; no workspace
 cudaError_t launch_prefill_chunked(const PrefillArgs& a, cudaStream_t s);

@@ -19,10 +19,23 @@
 // jobs are built on the device from cu_seqlens (a one-CTA kernel), so the host
 // never reads the lengths.  The reference has no counterpart: its chunked
 // pipeline (chunk_v12.py:36-116) runs one state scan per (sequence, head).
+#include <mutex>
+
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 
 namespace gdn {
+
+// Scratch of the no-allocation entry (gdn_prefill_segmented_noalloc): the job
+// tables and piece states of one segmented call, in a file-scope device array
+// that every GPU loading this library holds until the process exits.  Host code
+// must not pass the array's name to a kernel (on the host it is a stand-in, not
+// a device address): its address on each device comes from cudaGetSymbolAddress.
+// Every call writes each byte it reads before reading it, so nothing in it has to
+// start at zero; calls that overlap on the GPU (two streams, two threads) share
+// it and race.
+static __device__ __align__(256) unsigned char g_segment_scratch[kNoAllocScratchBytes];
+
 namespace {
 
 constexpr size_t kStateBytes1 = static_cast<size_t>(kHead) * kHead * sizeof(float);
@@ -181,6 +194,29 @@ cudaError_t launch_prefill_segmented(const PrefillArgs& a, int G, void* ws, size
   p2.jobs = l.jobs2;
   p2.njobs = a.N * (G - 1);
   return launch_prefill_chunked(p2, s);
+}
+
+// Device address of g_segment_scratch on the current device, looked up on the
+// first call on that device (then cached).
+cudaError_t launch_prefill_segmented_noalloc(const PrefillArgs& a, int segments, cudaStream_t s) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+      void* p = nullptr;
+      if ((e = cudaGetSymbolAddress(&p, g_segment_scratch)) != cudaSuccess) return e;
+      addr[dev] = p;
+    }
+    ptr = addr[dev];
+  }
+  return launch_prefill_segmented(a, segments, ptr, kNoAllocScratchBytes, s);
 }
 
 }  // namespace gdn

@@ -35,6 +35,8 @@ SIGNATURES = {
     "gdn_prefill_segmented": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64, I64,
                                   I, I, P, SZ, P]),
     "gdn_prefill_segmented_workspace_bytes": (SZ, [I64, I64, I]),
+    "gdn_prefill_segmented_noalloc": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64,
+                                          I64, I, I, P]),
     "gdn_prefill_segments": (I, [I64, I64, I64]),
     "gdn_prefill_chunked_debug": (I, [P, P, P, P, P, P, P, P, P, F, P, P, I64, I64, I64, I64, I64,
                                       I64, P, I64, I64, I64, I64, P]),
