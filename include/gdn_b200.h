@@ -194,8 +194,8 @@ int gdn_prefill_chunked_peers(const void *q, const void *k, const void *v, const
  * pass 1 runs piece 0 from the initial state and, for each middle piece g, its
  * final state from zero (F_g) and its transition matrix (P_g: the final state
  * from the identity with v = 0); S_{g+1} = S_g P_g + F_g gives the start states
- * (fp32); pass 2 runs pieces 1.. from them.  3 + (segments - 2) launches on the
- * stream; the critical path is ~2/segments of the sequence.  Same arguments as
+ * (fp32); pass 2 runs pieces 1.. from them.  Four launches on the stream (three
+ * for 2 pieces); the critical path is ~2/segments of the sequence.  Same arguments as
  * gdn_prefill plus flags (GDN_PREFILL_QK_L2NORM), segments (0 = the automatic
  * choice, gdn_prefill_segments; 1 = one chain per pair; at most 64) and a
  * 256-byte aligned workspace of gdn_prefill_segmented_workspace_bytes(N, Hv,

@@ -11,7 +11,8 @@
 //   pass 1 (one launch): piece 0 from the initial state (outputs written, its
 //          final state = the start state of piece 1) and, for pieces 1..G-2,
 //          F_g and P_g (outputs not written);
-//   combine (G-2 launches): S_{g+1} = S_g P_g + F_g, fp32 on CUDA cores;
+//   combine (one launch): S_{g+1} = S_g P_g + F_g for g = 1..G-2, fp32 on CUDA
+//          cores;
 //   pass 2 (one launch): pieces 1..G-1 from their start states (outputs, and the
 //          final state of the last piece).
 // The chain is about 2/G of the sequence's chunks long instead of all of them,
@@ -117,46 +118,56 @@ __global__ void gdn_segment_jobs_kernel(const int64_t* cu_seqlens, int64_t N, in
   }
 }
 
-// S_{g+1} = S_g P_g + F_g for every cut sequence and head: a CTA computes 16
-// rows (of 128) of one head, k in tiles of 32 rows of P staged in shared memory.
+// S_{g+1} = S_g P_g + F_g for every cut sequence and head, g = 1..G-2.  Rows r of
+// S_{g+1} depend only on rows r of S_g, so a CTA owns 16 rows of one head and
+// walks g in order with its rows in shared memory (no CTA waits on another);
+// P_g is staged 32 rows at a time.
 constexpr int kCombRows = 16;
 constexpr int kCombKTile = 32;
-__global__ void __launch_bounds__(256) gdn_segment_combine_kernel(int64_t N, int64_t Hv, int G, int g,
+__global__ void __launch_bounds__(256) gdn_segment_combine_kernel(int64_t N, int64_t Hv, int G,
                                                                   SegLayout l) {
   const int64_t cta = blockIdx.x;
   const int rb = static_cast<int>(cta % (kHead / kCombRows));
   const int64_t nh = cta / (kHead / kCombRows);
   const int64_t n = nh / Hv, h = nh % Hv;
   if (n >= N || !l.split[n]) return;
-  const int64_t hs = h * kHead * kHead;
+  const int64_t hs = h * kHead * kHead + rb * kCombRows * kHead;
   const int64_t st = Hv * kHead * kHead;
   const int64_t mid = G - 2;
-  const float* S = l.sin + (n * (G - 1) + (g - 1)) * st + hs + rb * kCombRows * kHead;
-  float* out = l.sin + (n * (G - 1) + g) * st + hs + rb * kCombRows * kHead;
-  const float* F = l.fst + (n * mid + (g - 1)) * st + hs + rb * kCombRows * kHead;
-  const float* P = l.pst + (n * mid + (g - 1)) * st + hs;
   __shared__ __align__(16) float s_s[kCombRows][kHead];
   __shared__ __align__(16) float p_s[kCombKTile][kHead];
   const int t = threadIdx.x, c = t & (kHead - 1), r0 = (t >> 7) * 8;
-  for (int i = t; i < kCombRows * kHead / 4; i += 256)
-    reinterpret_cast<float4*>(&s_s[0][0])[i] = reinterpret_cast<const float4*>(S)[i];
-  float acc[8];
+  {
+    const float* S1 = l.sin + (n * (G - 1)) * st + hs;  // piece 1's start state (from pass 1)
+    for (int i = t; i < kCombRows * kHead / 4; i += 256)
+      reinterpret_cast<float4*>(&s_s[0][0])[i] = reinterpret_cast<const float4*>(S1)[i];
+  }
+  for (int g = 1; g <= G - 2; ++g) {
+    const float* F = l.fst + (n * mid + (g - 1)) * st + hs;
+    const float* P = l.pst + (n * mid + (g - 1)) * st + (hs - rb * kCombRows * kHead);
+    float acc[8];
 #pragma unroll
-  for (int r = 0; r < 8; ++r) acc[r] = F[(r0 + r) * kHead + c];
-  for (int k0 = 0; k0 < kHead; k0 += kCombKTile) {
-    __syncthreads();  // s_s loaded / the previous tile consumed
-    for (int i = t; i < kCombKTile * kHead / 4; i += 256)
-      reinterpret_cast<float4*>(&p_s[0][0])[i] = reinterpret_cast<const float4*>(P + k0 * kHead)[i];
-    __syncthreads();
+    for (int r = 0; r < 8; ++r) acc[r] = F[(r0 + r) * kHead + c];
+    for (int k0 = 0; k0 < kHead; k0 += kCombKTile) {
+      __syncthreads();  // s_s written / the previous P tile consumed
+      for (int i = t; i < kCombKTile * kHead / 4; i += 256)
+        reinterpret_cast<float4*>(&p_s[0][0])[i] = reinterpret_cast<const float4*>(P + k0 * kHead)[i];
+      __syncthreads();
 #pragma unroll 8
-    for (int k = 0; k < kCombKTile; ++k) {
-      const float pk = p_s[k][c];
+      for (int k = 0; k < kCombKTile; ++k) {
+        const float pk = p_s[k][c];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) acc[r] = fmaf(s_s[r0 + r][k0 + k], pk, acc[r]);
+        for (int r = 0; r < 8; ++r) acc[r] = fmaf(s_s[r0 + r][k0 + k], pk, acc[r]);
+      }
+    }
+    __syncthreads();  // every thread is done reading s_s
+    float* out = l.sin + (n * (G - 1) + g) * st + hs;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      out[(r0 + r) * kHead + c] = acc[r];
+      s_s[r0 + r][c] = acc[r];
     }
   }
-#pragma unroll
-  for (int r = 0; r < 8; ++r) out[(r0 + r) * kHead + c] = acc[r];
 }
 
 }  // namespace
@@ -184,10 +195,10 @@ cudaError_t launch_prefill_segmented(const PrefillArgs& a, int G, void* ws, size
   p1.jobs = l.jobs1;
   p1.njobs = a.N * (2 * G - 3);
   if ((e = launch_prefill_chunked(p1, s)) != cudaSuccess) return e;
-  const int64_t cctas = a.N * a.Hv * (kHead / kCombRows);
-  if (cctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  for (int g = 1; g <= G - 2; ++g) {
-    gdn_segment_combine_kernel<<<static_cast<unsigned>(cctas), 256, 0, s>>>(a.N, a.Hv, G, g, l);
+  if (G > 2) {
+    const int64_t cctas = a.N * a.Hv * (kHead / kCombRows);
+    if (cctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+    gdn_segment_combine_kernel<<<static_cast<unsigned>(cctas), 256, 0, s>>>(a.N, a.Hv, G, l);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   PrefillArgs p2 = a;
