@@ -119,53 +119,95 @@ __global__ void gdn_segment_jobs_kernel(const int64_t* cu_seqlens, int64_t N, in
 }
 
 // S_{g+1} = S_g P_g + F_g for every cut sequence and head, g = 1..G-2.  Rows r of
-// S_{g+1} depend only on rows r of S_g, so a CTA owns 16 rows of one head and
+// S_{g+1} depend only on rows r of S_g, so a CTA owns 8 rows of one head and
 // walks g in order with its rows in shared memory (no CTA waits on another);
-// P_g is staged 32 rows at a time.
-constexpr int kCombRows = 16;
+// small CTAs (4 warps, 20 KB of shared memory) let several share an SM.  A
+// thread computes a 2 x 4 tile (rows 2w, 2w+1 of warp w; columns 4 lane .. +3):
+// per k one float4 of P and two broadcast values of S for 8 FMAs.  P goes
+// through shared memory 32 rows (16 KB) at a time, the next tile's loads in
+// flight in registers while the current tile is used.
+constexpr int kCombRows = 8;
+constexpr int kCombThreads = 32 * kCombRows / 2;
 constexpr int kCombKTile = 32;
-__global__ void __launch_bounds__(256) gdn_segment_combine_kernel(int64_t N, int64_t Hv, int G,
+constexpr int kCombTiles = kHead / kCombKTile;  // per g
+__global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64_t N, int64_t Hv, int G,
                                                                   SegLayout l) {
   const int64_t cta = blockIdx.x;
   const int rb = static_cast<int>(cta % (kHead / kCombRows));
   const int64_t nh = cta / (kHead / kCombRows);
   const int64_t n = nh / Hv, h = nh % Hv;
   if (n >= N || !l.split[n]) return;
-  const int64_t hs = h * kHead * kHead + rb * kCombRows * kHead;
+  const int64_t hrow = h * kHead * kHead + rb * kCombRows * kHead;  // this CTA's rows of a state
+  const int64_t hmat = h * kHead * kHead;
   const int64_t st = Hv * kHead * kHead;
   const int64_t mid = G - 2;
   __shared__ __align__(16) float s_s[kCombRows][kHead];
   __shared__ __align__(16) float p_s[kCombKTile][kHead];
-  const int t = threadIdx.x, c = t & (kHead - 1), r0 = (t >> 7) * 8;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int r0 = 2 * w, c0 = 4 * lane;
   {
-    const float* S1 = l.sin + (n * (G - 1)) * st + hs;  // piece 1's start state (from pass 1)
-    for (int i = t; i < kCombRows * kHead / 4; i += 256)
+    const float* S1 = l.sin + (n * (G - 1)) * st + hrow;  // piece 1's start state (from pass 1)
+    for (int i = t; i < kCombRows * kHead / 4; i += kCombThreads)
       reinterpret_cast<float4*>(&s_s[0][0])[i] = reinterpret_cast<const float4*>(S1)[i];
   }
-  for (int g = 1; g <= G - 2; ++g) {
-    const float* F = l.fst + (n * mid + (g - 1)) * st + hs;
-    const float* P = l.pst + (n * mid + (g - 1)) * st + (hs - rb * kCombRows * kHead);
-    float acc[8];
+  // tile i of the whole walk: g = 1 + i / kCombTiles, rows 32 (i % kCombTiles) .. of P_g
+  const int ntiles = (G - 2) * kCombTiles;
+  auto tile_src = [&](int i) {
+    const int g = 1 + i / kCombTiles;
+    return reinterpret_cast<const float4*>(l.pst + (n * mid + (g - 1)) * st + hmat +
+                                           (i % kCombTiles) * kCombKTile * kHead);
+  };
+  constexpr int kPer = kCombKTile * kHead / 4 / kCombThreads;  // float4 per thread and tile
+  float4 nxt[kPer];  // this thread's share of the next tile
+  {
+    const float4* src = tile_src(0);
 #pragma unroll
-    for (int r = 0; r < 8; ++r) acc[r] = F[(r0 + r) * kHead + c];
-    for (int k0 = 0; k0 < kHead; k0 += kCombKTile) {
-      __syncthreads();  // s_s written / the previous P tile consumed
-      for (int i = t; i < kCombKTile * kHead / 4; i += 256)
-        reinterpret_cast<float4*>(&p_s[0][0])[i] = reinterpret_cast<const float4*>(P + k0 * kHead)[i];
-      __syncthreads();
-#pragma unroll 8
-      for (int k = 0; k < kCombKTile; ++k) {
-        const float pk = p_s[k][c];
+    for (int j = 0; j < kPer; ++j) nxt[j] = src[t + kCombThreads * j];
+  }
+  float acc[2][4];
+  for (int i = 0; i < ntiles; ++i) {
+    const int g = 1 + i / kCombTiles, k0 = (i % kCombTiles) * kCombKTile;
+    if (k0 == 0) {  // a new g: start from F_g
+      const float* F = l.fst + (n * mid + (g - 1)) * st + hrow;
 #pragma unroll
-        for (int r = 0; r < 8; ++r) acc[r] = fmaf(s_s[r0 + r][k0 + k], pk, acc[r]);
+      for (int r = 0; r < 2; ++r) {
+        const float4 f = *reinterpret_cast<const float4*>(F + (r0 + r) * kHead + c0);
+        acc[r][0] = f.x;
+        acc[r][1] = f.y;
+        acc[r][2] = f.z;
+        acc[r][3] = f.w;
       }
     }
-    __syncthreads();  // every thread is done reading s_s
-    float* out = l.sin + (n * (G - 1) + g) * st + hs;
+    __syncthreads();  // the previous tile is consumed (and s_s written)
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      out[(r0 + r) * kHead + c] = acc[r];
-      s_s[r0 + r][c] = acc[r];
+    for (int j = 0; j < kPer; ++j) reinterpret_cast<float4*>(&p_s[0][0])[t + kCombThreads * j] = nxt[j];
+    __syncthreads();
+    if (i + 1 < ntiles) {
+      const float4* src = tile_src(i + 1);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) nxt[j] = src[t + kCombThreads * j];
+    }
+#pragma unroll 8
+    for (int k = 0; k < kCombKTile; ++k) {
+      const float4 pk = *reinterpret_cast<const float4*>(&p_s[k][c0]);
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float sv = s_s[r0 + r][k0 + k];
+        acc[r][0] = fmaf(sv, pk.x, acc[r][0]);
+        acc[r][1] = fmaf(sv, pk.y, acc[r][1]);
+        acc[r][2] = fmaf(sv, pk.z, acc[r][2]);
+        acc[r][3] = fmaf(sv, pk.w, acc[r][3]);
+      }
+    }
+    if (k0 + kCombKTile == kHead) {  // S_{g+1} done: to the workspace and to s_s
+      __syncthreads();  // every thread is done reading s_s for this g
+      float* out = l.sin + (n * (G - 1) + g) * st + hrow;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float4 v = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        *reinterpret_cast<float4*>(out + (r0 + r) * kHead + c0) = v;
+        *reinterpret_cast<float4*>(&s_s[r0 + r][c0]) = v;
+      }
     }
   }
 }
@@ -198,7 +240,7 @@ cudaError_t launch_prefill_segmented(const PrefillArgs& a, int G, void* ws, size
   if (G > 2) {
     const int64_t cctas = a.N * a.Hv * (kHead / kCombRows);
     if (cctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-    gdn_segment_combine_kernel<<<static_cast<unsigned>(cctas), 256, 0, s>>>(a.N, a.Hv, G, l);
+    gdn_segment_combine_kernel<<<static_cast<unsigned>(cctas), kCombThreads, 0, s>>>(a.N, a.Hv, G, l);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   PrefillArgs p2 = a;
