@@ -151,7 +151,8 @@ int gdn_prefill_recurrent(const void *q, const void *k, const void *v, const flo
 #define GDN_PREFILL_PATH_CHUNKED 2
 
 /*
- * gdn_prefill with options (no workspace: none of the kernels needs one).  The
+ * gdn_prefill with options, without a workspace (so never the segmented form:
+ * gdn_prefill_segmented takes one).  The
  * reference's prefill entry has no flags; GDN_PREFILL_QK_L2NORM is the in-kernel
  * q/k normalisation that FlashInfer's chunk_gated_delta_rule exposes as
  * use_qk_l2norm_in_kernel (rejected by the reference's baseline wrapper,

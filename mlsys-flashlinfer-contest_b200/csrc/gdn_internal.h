@@ -111,7 +111,8 @@ cudaError_t launch_prefill_segmented(const PrefillArgs& a, int segments, void* w
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 cudaError_t launch_prefill_segmented_noalloc(const PrefillArgs& a, int segments, cudaStream_t s);
 
-// fused chunked (C=64) prefill on tcgen05; no workspace
+// fused chunked (C=64) prefill on tcgen05 (a job table in PrefillArgs: the
+// segmented form's passes)
 cudaError_t launch_prefill_chunked(const PrefillArgs& a, cudaStream_t s);
 // same kernel, dumping one chunk's intermediates (gamma, beta, A, P, T, U, W,
 // Vn, QS, PV, St) of (dbg_seq, dbg_head, dbg_chunk) into `debug`
