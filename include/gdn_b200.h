@@ -197,10 +197,13 @@ int gdn_prefill_chunked_peers(const void *q, const void *k, const void *v, const
  * from the identity with v = 0); S_{g+1} = S_g P_g + F_g gives the start states
  * (fp32); pass 2 runs pieces 1.. from them.  Four launches on the stream (three
  * for 2 pieces); the critical path is ~2/segments of the sequence.  Same arguments as
- * gdn_prefill plus flags (GDN_PREFILL_QK_L2NORM), segments (0 = the automatic
- * choice, gdn_prefill_segments; 1 = one chain per pair; at most 64) and a
- * 256-byte aligned workspace of gdn_prefill_segmented_workspace_bytes(N, Hv,
- * segments) bytes.  gdn_prefill_chunked_peers takes the same three arguments.
+ * gdn_prefill plus flags (GDN_PREFILL_QK_L2NORM), segments (0 = automatic: each
+ * sequence's count chosen on the device under gdn_prefill_segments' bound; 1 =
+ * one chain per pair; 2..64 = that count for every sequence of at least 2 x that
+ * many chunks) and a 256-byte aligned workspace of
+ * gdn_prefill_segmented_workspace_bytes(N, Hv, segments) bytes (with segments 0,
+ * sized for any bound: about 1.5 x SMs x 64 KiB of piece states plus the job
+ * tables).  gdn_prefill_chunked_peers takes the same three arguments.
  */
 int gdn_prefill_segmented(const void *q, const void *k, const void *v, const float *state,
                           const float *A_log, const void *a, const float *dt_bias, const void *b,
@@ -235,9 +238,15 @@ int gdn_prefill_segmented_noalloc(const void *q, const void *k, const void *v, c
                                   int64_t num_v_heads, int64_t head_size, int flags, int segments,
                                   void *stream);
 
-/* The automatic segment count for these sizes (1: no cut).  The largest count
- * <= 8 whose pass 1 fits in one wave of SMs, num_seqs * num_v_heads * (2 segments - 3)
- * <= SMs, with pieces of >= 4 chunks on average; 1 below 3. */
+/* Upper bound of the automatic piece count for these sizes (1: the call is not
+ * cut).  With segments 0 the call's first kernel picks each sequence's count
+ * under it from the lengths on the device: the shortest longest-chain (pass 1 +
+ * pass 2 pieces, ~2 ceil(chunks / pieces); whole sequences their length) whose
+ * pass 1 fits one wave of SMs, with pieces of at least 2 chunks and counts of 1
+ * or at least 3, and no cut at all unless it shortens the longest chain by a
+ * fifth.  The bound is 1 when the (sequence, head) pairs are more than a third
+ * of the SMs, else the largest G <= 8 with num_seqs * num_v_heads * (2G - 3) <=
+ * 4 x SMs and total_seq_len >= 6 G chunks. */
 int gdn_prefill_segments(int64_t total_seq_len, int64_t num_seqs, int64_t num_v_heads);
 
 /*

@@ -167,11 +167,13 @@ static bool use_recurrent(int64_t T, int64_t N, int64_t Hv) {
          (T <= 8 * N && T <= 256);
 }
 
-// Segment count of the sequence-parallel prefill (1: one chain per (sequence,
-// head)).  Each pass-1 job holds one SM for a piece of ~L/G chunks, so G is the
-// largest count (at most 8) whose pass 1 fits in one wave of SMs, N Hv (2G - 3)
-// <= SMs, with pieces of at least 4 chunks on average; below G = 3 there is no
-// gain (pass 1 and pass 2 would each take half of the sequence).
+// Upper bound on the piece count of the sequence-parallel prefill (1: one chain
+// per (sequence, head)).  The job builder picks each sequence's count under it
+// from the lengths on the device (the shortest longest-chain whose pass 1 fits
+// one wave of SMs), so the host only rules out calls that cannot gain: more
+// (sequence, head) pairs than a third of the SMs (then not even equal sequences
+// could all be cut in 3 within one wave), or too few chunks in all; the bound is
+// the largest G <= 8 with N Hv (2G - 3) <= 4 SMs and T >= 6 G chunks.
 static int sm_count() {
   static int n = [] {
     int dev = 0, v = 0;
@@ -184,11 +186,11 @@ static int sm_count() {
 }
 
 static int choose_segments(int64_t T, int64_t N, int64_t Hv) {
-  if (N <= 0 || Hv <= 0) return 1;
-  const int64_t pairs = N * Hv, mean_chunks = T / (gdn::kChunk * N);
+  if (N <= 0 || Hv <= 0 || 3 * N * Hv > sm_count()) return 1;
+  const int64_t chunks = T / gdn::kChunk;
   int best = 1;
   for (int G = 3; G <= 8; ++G)
-    if (pairs * (2 * G - 3) <= sm_count() && mean_chunks >= 4 * G) best = G;
+    if (N * Hv * (2 * G - 3) <= 4 * sm_count() && chunks >= 6 * G) best = G;
   return best;
 }
 
@@ -196,13 +198,16 @@ int gdn_prefill_segments(int64_t T, int64_t N, int64_t Hv) {
   return use_recurrent(T, N, Hv) ? 1 : choose_segments(T, N, Hv);
 }
 
+// segments 0: the automatic form (sized for the largest bound, 8)
 size_t gdn_prefill_segmented_workspace_bytes(int64_t N, int64_t Hv, int segments) {
-  return gdn::prefill_segments_bytes(N, Hv, segments);
+  if (segments == 0) return gdn::prefill_segments_bytes(N, Hv, 8, true, sm_count());
+  return gdn::prefill_segments_bytes(N, Hv, segments, false, sm_count());
 }
 
 size_t gdn_prefill_workspace_bytes(int64_t T, int64_t N, int64_t Hq, int64_t Hv) {
   (void)Hq;
-  return gdn::prefill_segments_bytes(N, Hv, gdn_prefill_segments(T, N, Hv));
+  const int G = gdn_prefill_segments(T, N, Hv);
+  return G > 1 ? gdn::prefill_segments_bytes(N, Hv, G, true, sm_count()) : 0;
 }
 
 int gdn_prefill_chunked(const void* q, const void* k, const void* v, const float* state,
@@ -229,20 +234,22 @@ int gdn_prefill(const void* q, const void* k, const void* v, const float* state,
     return gdn_prefill_recurrent(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                                  new_state, T, N, Hq, Hk, Hv, D, stream);
   const int G = choose_segments(T, N, Hv);
-  if (G > 1 && workspace && workspace_bytes >= gdn::prefill_segments_bytes(N, Hv, G))
+  if (G > 1 && workspace && workspace_bytes >= gdn::prefill_segments_bytes(N, Hv, G, true, sm_count()))
     return gdn_prefill_segmented(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
-                                 new_state, T, N, Hq, Hk, Hv, D, 0, G, workspace, workspace_bytes,
+                                 new_state, T, N, Hq, Hk, Hv, D, 0, 0, workspace, workspace_bytes,
                                  stream);
   return gdn_prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                              new_state, T, N, Hq, Hk, Hv, D, stream);
 }
 
-// Checks shared by the segmented entries; segments 0 = automatic.
-static int segmented_setup(int64_t T, int64_t N, int64_t Hv, int* segments, void* workspace,
-                           size_t workspace_bytes) {
+// Checks shared by the segmented entries; segments 0 = automatic (an upper bound
+// for the device's per-sequence choice).
+static int segmented_setup(int64_t T, int64_t N, int64_t Hv, int* segments, bool* adaptive,
+                           void* workspace, size_t workspace_bytes) {
   if (*segments < 0 || *segments > 64) return fail(GDN_ERR_VALUE, "segments must be in [0, 64]");
-  if (*segments == 0) *segments = choose_segments(T, N, Hv);
-  const size_t need = gdn::prefill_segments_bytes(N, Hv, *segments);
+  *adaptive = *segments == 0;
+  if (*adaptive) *segments = choose_segments(T, N, Hv);
+  const size_t need = gdn::prefill_segments_bytes(N, Hv, *segments, *adaptive, sm_count());
   if (need > 0 && (!workspace || workspace_bytes < need))
     return fail(GDN_ERR_VALUE, "workspace needs %zu bytes", need);
   if (!aligned(workspace, 256)) return fail(GDN_ERR_VALUE, "workspace must be 256-byte aligned");
@@ -260,12 +267,13 @@ int gdn_prefill_segmented(const void* q, const void* k, const void* v, const flo
                             N, Hq, Hk, Hv, D))
     return e;
   if (T > 0x7fffffffLL - 64) return fail(GDN_ERR_VALUE, "total_seq_len too large");
-  if (int e = segmented_setup(T, N, Hv, &segments, workspace, workspace_bytes)) return e;
+  bool adaptive = false;
+  if (int e = segmented_setup(T, N, Hv, &segments, &adaptive, workspace, workspace_bytes)) return e;
   gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
                      scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv,
                      (flags & GDN_PREFILL_QK_L2NORM) != 0};
-  return cuda_status(gdn::launch_prefill_segmented(p, segments, workspace, workspace_bytes,
-                                                   static_cast<cudaStream_t>(stream)),
+  return cuda_status(gdn::launch_prefill_segmented(p, segments, adaptive, sm_count(), workspace,
+                                                   workspace_bytes, static_cast<cudaStream_t>(stream)),
                      "gdn_prefill_segmented launch");
 }
 
@@ -307,8 +315,9 @@ int gdn_prefill_segmented_noalloc(const void* q, const void* k, const void* v, c
     return e;
   if (T > 0x7fffffffLL - 64) return fail(GDN_ERR_VALUE, "total_seq_len too large");
   if (segments < 0 || segments > 64) return fail(GDN_ERR_VALUE, "segments must be in [0, 64]");
-  if (segments == 0) segments = choose_segments(T, N, Hv);
-  const size_t need = gdn::prefill_segments_bytes(N, Hv, segments);
+  const bool adaptive = segments == 0;
+  if (adaptive) segments = choose_segments(T, N, Hv);
+  const size_t need = gdn::prefill_segments_bytes(N, Hv, segments, adaptive, sm_count());
   if (need > gdn::kNoAllocScratchBytes)
     return fail(GDN_ERR_VALUE,
                 "%lld sequences x %lld heads in %d pieces need %zu bytes of scratch; the "
@@ -318,7 +327,7 @@ int gdn_prefill_segmented_noalloc(const void* q, const void* k, const void* v, c
   gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
                      scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv,
                      (flags & GDN_PREFILL_QK_L2NORM) != 0};
-  return cuda_status(gdn::launch_prefill_segmented_noalloc(p, segments,
+  return cuda_status(gdn::launch_prefill_segmented_noalloc(p, segments, adaptive, sm_count(),
                                                            static_cast<cudaStream_t>(stream)),
                      "gdn_prefill_segmented_noalloc launch");
 }
@@ -343,15 +352,16 @@ int gdn_prefill_chunked_peers(const void* q, const void* k, const void* v, const
   for (int r = 0; r < num_peers; ++r)
     if (!peer_outputs[r] || !aligned(peer_outputs[r], 16))
       return fail(GDN_ERR_VALUE, "peer output %d is null or not 16-byte aligned", r);
-  if (int e = segmented_setup(T, N, Hv, &segments, workspace, workspace_bytes)) return e;
+  bool adaptive = false;
+  if (int e = segmented_setup(T, N, Hv, &segments, &adaptive, workspace, workspace_bytes)) return e;
   gdn::PrefillArgs p{q, k, v, state, A_log, a, dt_bias, b, cu_seqlens,
                      scale == 0.0f ? 0.08838834764831845f : scale, output, new_state, T, N, Hq, Hv};
   p.out_heads = Hv_out;
   p.out_head_off = head_offset;
   p.n_peers = num_peers;
   p.peer_out = peer_outputs;
-  return cuda_status(gdn::launch_prefill_segmented(p, segments, workspace, workspace_bytes,
-                                                   static_cast<cudaStream_t>(stream)),
+  return cuda_status(gdn::launch_prefill_segmented(p, segments, adaptive, sm_count(), workspace,
+                                                   workspace_bytes, static_cast<cudaStream_t>(stream)),
                      "gdn_prefill_chunked_peers launch");
 }
 

@@ -97,19 +97,22 @@ struct SegJob {
 constexpr int kMaxPeers = 7;
 
 cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);
-// Segmented (sequence-parallel) prefill: every sequence long enough is cut into
-// `segments` pieces at chunk boundaries; pass 1 runs piece 0 from the initial
-// state and, for the middle pieces, their final state from zero (F) and their
-// transition matrix (P, the final state from the identity with v = 0); the
-// start states of pieces 2.. follow from S_{g+1} = S_g P_g + F_g in fp32; pass 2
-// runs pieces 1.. from their start states.  Workspace: prefill_segments_bytes.
-size_t prefill_segments_bytes(int64_t N, int64_t Hv, int segments);
-cudaError_t launch_prefill_segmented(const PrefillArgs& a, int segments, void* workspace,
-                                     size_t workspace_bytes, cudaStream_t s);
+// Segmented (sequence-parallel) prefill: sequences are cut into pieces at chunk
+// boundaries; pass 1 runs piece 0 from the initial state and, for the middle
+// pieces, their final state from zero (F) and their transition matrix (P, the
+// final state from the identity with v = 0); the start states of pieces 2..
+// follow from S_{g+1} = S_g P_g + F_g in fp32; pass 2 runs pieces 1.. from
+// their start states.  adaptive: `segments` is an upper bound and the device
+// picks each sequence's count (pass 1 within `sms` CTAs); else every sequence of
+// at least 2 segments chunks is cut into `segments`.
+size_t prefill_segments_bytes(int64_t N, int64_t Hv, int segments, bool adaptive, int sms);
+cudaError_t launch_prefill_segmented(const PrefillArgs& a, int segments, bool adaptive, int sms,
+                                     void* workspace, size_t workspace_bytes, cudaStream_t s);
 // The same with the workspace in a file-scope device array of kNoAllocScratchBytes
 // (the no-allocation entry); the caller checks prefill_segments_bytes against it.
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
-cudaError_t launch_prefill_segmented_noalloc(const PrefillArgs& a, int segments, cudaStream_t s);
+cudaError_t launch_prefill_segmented_noalloc(const PrefillArgs& a, int segments, bool adaptive,
+                                             int sms, cudaStream_t s);
 
 // fused chunked (C=64) prefill on tcgen05 (a job table in PrefillArgs: the
 // segmented form's passes)

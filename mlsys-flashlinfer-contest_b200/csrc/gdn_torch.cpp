@@ -206,19 +206,21 @@ std::tuple<at::Tensor, at::Tensor> prefill(const at::Tensor& q, const at::Tensor
   }
   const c10::cuda::CUDAGuard guard(q.device());
   const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
-  int G = 1;  // pieces of the segmented form (1: not taken)
-  if (path == 3) G = segments > 0 ? static_cast<int>(segments) : gdn_prefill_segments(T, Nseq, Hv);
-  if (path == 0) G = gdn_prefill_segments(T, Nseq, Hv);
+  // the segmented form: automatic (segments 0: the device picks each sequence's
+  // pieces under gdn_prefill_segments' bound) or a forced count
+  const bool cut = (path == 0 && gdn_prefill_segments(T, Nseq, Hv) > 1) || path == 3;
   const int flags = qk_l2norm ? GDN_PREFILL_QK_L2NORM : 0;
-  if (G > 1) {
-    const size_t ws_bytes = gdn_prefill_segmented_workspace_bytes(Nseq, Hv, G);
+  if (cut) {
+    const int G = path == 3 ? static_cast<int>(segments) : 0;
+    const size_t ws_bytes = G > 0 ? gdn_prefill_segmented_workspace_bytes(Nseq, Hv, G)
+                                  : gdn_prefill_workspace_bytes(T, Nseq, Hq, Hv);
     at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(at::kByte));
     check_rc(gdn_prefill_segmented(q.data_ptr(), k.data_ptr(), v.data_ptr(), state_ptr(state),
                                    A_log.data_ptr<float>(), a.data_ptr(), dt_bias.data_ptr<float>(),
                                    b.data_ptr(), cu_seqlens.data_ptr<int64_t>(),
                                    static_cast<float>(scale), output->data_ptr(),
                                    new_state->data_ptr<float>(), T, Nseq, Hq, Hk, Hv, kHead, flags,
-                                   G, ws.data_ptr(), ws_bytes, stream),
+                                   G, ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, stream),
              "gdn_prefill_segmented");
     return {*output, *new_state};
   }

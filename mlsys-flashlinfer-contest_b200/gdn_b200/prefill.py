@@ -167,7 +167,8 @@ def run_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
 
 
 def segments_for(T: int, Nseq: int, Hv: int) -> int:
-    """The automatic piece count of the segmented prefill (1: one chain per pair)."""
+    """Upper bound of the automatic piece count of the segmented prefill (1: the call
+    is not cut); the device picks each sequence's count under it."""
     return int(N.lib().gdn_prefill_segments(T, Nseq, Hv))
 
 
@@ -175,8 +176,8 @@ def run_segmented(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, segme
                   use_qk_l2norm: bool = False, output=None, new_state=None):
     """Sequence-parallel prefill (C ABI gdn_prefill_segmented): sequences of at least
     2 * segments chunks are cut into ``segments`` pieces whose start states follow
-    from each piece's transition matrix; ``segments`` 0 = the automatic count.
-    Returns (output, new_state)."""
+    from each piece's transition matrix; ``segments`` 0 = automatic (each sequence's
+    count chosen on the device from its length).  Returns (output, new_state)."""
     cu_seqlens = _widen(cu_seqlens)
     ext = N.torch_ext()
     if ext is not None:
@@ -189,7 +190,7 @@ def run_segmented(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, segme
     if new_state is None:
         new_state = torch.empty((Nseq, Hv, HEAD, HEAD), dtype=torch.float32, device=v.device)
     L = N.lib()
-    G = segments if segments > 0 else segments_for(T, Nseq, Hv)
+    G = segments
     ws_bytes = int(L.gdn_prefill_segmented_workspace_bytes(Nseq, Hv, G))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
     with torch.cuda.device(q.device):

@@ -180,8 +180,6 @@ def prefill_gathered(inp_local, head_offset: int, bufs: PeerOutputs, new_state=N
         new_state = torch.empty((Nseq, Hv, HEAD, HEAD), dtype=torch.float32, device=q.device)
     peers = (ctypes.c_void_p * max(len(bufs.peer_ptrs), 1))(*bufs.peer_ptrs)
     L = N.lib()
-    if segments == 0:
-        segments = L.gdn_prefill_segments(T, Nseq, Hv)
     ws_bytes = L.gdn_prefill_segmented_workspace_bytes(Nseq, Hv, segments)
     if workspace is None and ws_bytes > 0:
         workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)

@@ -59,14 +59,14 @@ def test_segmented_state_none_and_l2norm():
     PT.assert_state_close(ns, s_ref, PT.STATE_REL)
 
 
-def test_segmented_close_to_chunked_long():
-    # 4 x 4096 tokens, 4 heads (a head shard of a multi-GPU call): the automatic
-    # count cuts every sequence; against the one-chain kernel on the same inputs
-    inp = PT.to_device(W.make_prefill_inputs([4096] * 4, 4, 4, seed=8))
-    G = prefill.segments_for(16384, 4, 4)
-    assert G >= 3
+@pytest.mark.parametrize("lengths", [[4096] * 4, [4096, 2048, 1024, 512], [8192, 64, 64, 300]])
+def test_segmented_close_to_chunked_long(lengths):
+    # a head shard of a multi-GPU call, and ragged batches: the automatic form
+    # picks each sequence's pieces on the device; against the one-chain kernel
+    inp = PT.to_device(W.make_prefill_inputs(lengths, 4, 4, seed=8 + len(lengths)))
+    assert prefill.segments_for(sum(lengths), len(lengths), 4) >= 3
     o1, s1 = prefill.run_chunked(*inp.args())
-    o2, s2 = prefill.run_segmented(*inp.args(), segments=G)
+    o2, s2 = prefill.run_segmented(*inp.args(), segments=0)
     PT.assert_o_close(o2, o1)
     PT.assert_state_close(s2, s1.cpu().numpy(), PT.STATE_REL)
 

@@ -50,15 +50,15 @@ def _both(d, segments):
 @pytest.mark.gpu
 def test_noalloc_matches_workspace_entry_twice():
     L = N.lib()
-    # call 1: one long and one short sequence, 8 heads (the automatic cut, 8 pieces)
+    # call 1: one long and one short sequence, 8 heads, the automatic cut (segments
+    # 0: the device picks each sequence's pieces)
     d1 = PT.to_device(W.make_prefill_inputs([8192, 700], 4, 8, seed=70))
-    g1 = L.gdn_prefill_segments(8892, 2, 8)
-    assert g1 > 1
-    (o1, s1), (r1, t1) = _both(d1, g1)
+    assert L.gdn_prefill_segments(8892, 2, 8) > 1
+    (o1, s1), (r1, t1) = _both(d1, 0)
     PT.assert_o_close(o1, r1)
     PT.assert_state_close(s1, t1.cpu().numpy(), PT.STATE_REL)
-    # call 2: another shape and piece count through the same scratch (a head shard
-    # of 4 x 4096 tokens, 4 heads, slow decay so the piece start states matter)
+    # call 2: another shape and a forced piece count through the same scratch (a
+    # head shard of 4 x 4096 tokens, 4 heads, slow decay so the start states matter)
     w2 = W.make_prefill_inputs([4096] * 4, 2, 4, seed=71)
     w2.dt_bias[:] = -6.0
     d2 = PT.to_device(w2)
