@@ -176,9 +176,10 @@ __device__ __forceinline__ void load_table16(const float* src, float* v) {
   }
 }
 
-// L2: q/k L2 norm folded in as per-token factors (a separate instantiation so the
-// plain kernel carries none of it).
-template <bool DEBUG, bool L2>
+// L2: q/k L2 norm folded in as per-token factors; JOBS: the segmented prefill's
+// job table (identity start, v = 0, no outputs, optional final state).  Both are
+// separate instantiations so the plain kernel carries none of it.
+template <bool DEBUG, bool L2, bool JOBS>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                                const __grid_constant__ CUtensorMap tm_k,
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float* state_in;  // this head's initial state (nullptr: zero)
   float* ns_rows;         // this head's final state (nullptr: not stored)
   uint32_t jflags = 0;
-  if (p.jobs) {  // one segment of a sequence (job values are written on the device)
+  if constexpr (JOBS) {  // one segment of a sequence (job values are written on the device)
     const SegJob jb = p.jobs[n];
     bos = min(max(jb.bos, int64_t(0)), p.T);
     eos = min(max(jb.eos, bos), p.T);
@@ -231,8 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     ns_rows = p.new_state + (n * p.Hv + h) * kStateFloats;
   }
   const int64_t Ltot = eos - bos;
-  const bool init_identity = jflags & kJobIdentity, v_zero = jflags & kJobNoV;
-  const bool write_out = !(jflags & kJobNoOut);
+  const bool init_identity = JOBS && (jflags & kJobIdentity);
+  const bool v_zero = JOBS && (jflags & kJobNoV);
+  const bool write_out = !JOBS || !(jflags & kJobNoOut);
 
   if (Ltot <= 0) {  // empty sequence: zero final state (definition skips it)
     if (ns_rows)
@@ -1226,15 +1228,21 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   if (tma_out && (e = make_head_map(&mo, a.out, out_heads, a.T)) != cudaSuccess) return e;
   for (int r = 0; tma_out && r < a.n_peers; ++r)
     if ((e = make_head_map(&pm.m[r], a.peer_out[r], out_heads, a.T)) != cudaSuccess) return e;
-  auto kernel = gdn_prefill_chunked_kernel<DEBUG, false>;
+  auto kernel = gdn_prefill_chunked_kernel<DEBUG, false, false>;
+  const int variant = (a.qk_l2norm ? 1 : 0) + (a.jobs ? 2 : 0);
   if constexpr (!DEBUG) {
-    if (a.qk_l2norm) kernel = gdn_prefill_chunked_kernel<false, true>;
+    constexpr decltype(kernel) kernels[4] = {
+        gdn_prefill_chunked_kernel<false, false, false>, gdn_prefill_chunked_kernel<false, true, false>,
+        gdn_prefill_chunked_kernel<false, false, true>, gdn_prefill_chunked_kernel<false, true, true>};
+    kernel = kernels[variant];
+  } else if (a.jobs || a.qk_l2norm) {
+    return cudaErrorInvalidValue;  // the debug build covers the plain kernel only
   }
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[a.qk_l2norm ? 1 : 0]) {
+  static bool attr_set[4] = {false, false, false, false};
+  if (!attr_set[variant]) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_set[a.qk_l2norm ? 1 : 0] = true;
+    attr_set[variant] = true;
   }
   ChunkParams p{a.state, a.A_log, a.dt_bias,
                 static_cast<const __nv_bfloat16*>(a.a), static_cast<const __nv_bfloat16*>(a.b),
