@@ -464,12 +464,17 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
     t_hbm = bytes_call / (hbm_peak * 1e9)
     t_tc = flops_call / (tc_burst * 1e12)
     bound = "hbm" if t_hbm >= t_tc else "tensor"
+    # a head shard with few (sequence, head) pairs takes the segmented form
+    seg_bound = prefill.segments_for(T, Nseq, hv)
+    path = ("gdn_b200.prefill.launch: segmented prefill (job builder, pass 1, combine, pass 2; "
+            f"pieces picked on the device under a bound of {seg_bound})" if seg_bound > 1
+            else "gdn_b200.prefill.launch (fused chunked kernel)")
     res = {"metric": "gdn_prefill_tokens_per_s", "value": round(T / (ms / 1e3), 1),
            "unit": "tokens/s", "ms_per_call": round(ms, 4), "steps": reps,
            "workload": f"BASELINE config 3: {args.prefill_seqs} x {args.prefill_len} tokens, "
                        f"Hq={HQ}, Hv={HV} ({hv} v-heads on each of {world} ranks), random fp32 "
-                       f"initial states", "path": "gdn_b200.prefill.launch (fused chunked kernel)",
-           "gpu_launches_per_call": 1,
+                       f"initial states", "path": path,
+           "gpu_launches_per_call": 4 if seg_bound > 1 else 1,
            "roofline": {"bound": bound, "algorithmic_bytes_per_call": bytes_call,
                         "algorithmic_flops_per_call": flops_call,
                         "achieved_GBps": round(bytes_call / (ms / 1e3) / 1e9, 1),
@@ -478,7 +483,7 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
                         "roofline_ms": round(max(t_hbm, t_tc) * 1e3, 4),
                         "frac": round(max(t_hbm, t_tc) * 1e3 / ms, 4), "peak_source": peak_src}}
     full = profiled_traffic("gdn_prefill_chunked_config3.md")  # ncu, 1-GPU config-3 launch
-    if full is not None and args.prefill_seqs == 4 and args.prefill_len == 16384:
+    if full is not None and args.prefill_seqs == 4 and args.prefill_len == 16384 and seg_bound == 1:
         res["roofline"]["traffic"] = int(full * hv / HV)  # this rank's heads
     if dist and world > 1:
         from gdn_b200.sharding import all_gather_heads
