@@ -458,15 +458,22 @@ __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_ke
           qf[8 * i + 4 * hh + 3] = q4.w;
         }
       const float g = gb[2 * t], beta = gb[2 * t + 1];
+      // element pairs (c, c + 1) on the packed FMUL2 / FFMA2 path: each lane
+      // rounds like the scalar operation, and the pair's two lanes are the two
+      // partial sums of every dot product
       float dot[R][2];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        dot[r][0] = dot[r][1] = 0.0f;
+        float2 d2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          s[r][c] *= g;
-          dot[r][c & 1] = fmaf(kf[c], s[r][c], dot[r][c & 1]);
+        for (int c = 0; c < 16; c += 2) {
+          const float2 sv = __fmul2_rn(make_float2(s[r][c], s[r][c + 1]), make_float2(g, g));
+          s[r][c] = sv.x;
+          s[r][c + 1] = sv.y;
+          d2 = __ffma2_rn(make_float2(kf[c], kf[c + 1]), sv, d2);
         }
+        dot[r][0] = d2.x;
+        dot[r][1] = d2.y;
       }
       float delta[R];
 #pragma unroll
@@ -475,12 +482,17 @@ __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_ke
       float ov[R][2];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        ov[r][0] = ov[r][1] = 0.0f;
+        float2 o2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          s[r][c] = fmaf(kf[c], delta[r], s[r][c]);
-          ov[r][c & 1] = fmaf(qf[c], s[r][c], ov[r][c & 1]);
+        for (int c = 0; c < 16; c += 2) {
+          const float2 sv = __ffma2_rn(make_float2(kf[c], kf[c + 1]), make_float2(delta[r], delta[r]),
+                                       make_float2(s[r][c], s[r][c + 1]));
+          s[r][c] = sv.x;
+          s[r][c + 1] = sv.y;
+          o2 = __ffma2_rn(make_float2(qf[c], qf[c + 1]), sv, o2);
         }
+        ov[r][0] = o2.x;
+        ov[r][1] = o2.y;
       }
       const int64_t bt = bidx * p.T + t;
 #pragma unroll
