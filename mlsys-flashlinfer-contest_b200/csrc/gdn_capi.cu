@@ -156,7 +156,7 @@ int gdn_prefill_recurrent(const void* q, const void* k, const void* v, const flo
 // (gdn_prefill/solution/python/gdn_prefill_mix.py:29: N <= 2 and T <= 30 N);
 // the bounds here come from timing both kernels on a B200 over N = 1..32
 // sequences of 8..512 tokens (Hv = 8 and 32): the recurrent kernel walks one
-// token at a time (~0.33 us each) while the chunked kernel's floor is one chunk
+// token at a time (~0.3 us each) while the chunked kernel's floor is one chunk
 // (~14.5 us per call, launch included).  Recurrent wins for sequences of up to
 // ~32 tokens when there are at most 16 (sequence, head) pairs, up to 16 tokens
 // at up to 64 pairs, and up to 8 tokens at any count.  The last bound also caps

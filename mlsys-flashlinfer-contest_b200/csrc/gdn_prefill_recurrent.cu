@@ -149,21 +149,28 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_recurrent_kernel(Prefill
           qf[c] *= rq;
         }
       }
-      float dot = 0.0f;
+      // element pairs on the packed FMUL2 / FFMA2 path (each lane rounds like the
+      // scalar operation): two partial sums per dot product, half the chain
+      float2 d2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        S[c] *= g;
-        dot = fmaf(kf[c], S[c], dot);
+      for (int c = 0; c < 16; c += 2) {
+        const float2 sv = __fmul2_rn(make_float2(S[c], S[c + 1]), make_float2(g, g));
+        S[c] = sv.x;
+        S[c + 1] = sv.y;
+        d2 = __ffma2_rn(make_float2(kf[c], kf[c + 1]), sv, d2);
       }
-      dot = octet_sum(dot);
+      const float dot = octet_sum(d2.x + d2.y);
       const float delta = beta * (vv - dot);
-      float ov = 0.0f;
+      float2 o2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        S[c] = fmaf(kf[c], delta, S[c]);
-        ov = fmaf(qf[c], S[c], ov);
+      for (int c = 0; c < 16; c += 2) {
+        const float2 sv = __ffma2_rn(make_float2(kf[c], kf[c + 1]), make_float2(delta, delta),
+                                     make_float2(S[c], S[c + 1]));
+        S[c] = sv.x;
+        S[c + 1] = sv.y;
+        o2 = __ffma2_rn(make_float2(qf[c], qf[c + 1]), sv, o2);
       }
-      ov = octet_sum(ov);
+      const float ov = octet_sum(o2.x + o2.y);
       if (j == 0) out[((tb + u) * p.Hv + h) * kHead + row] = __float2bfloat16_rn(p.scale * ov);
     }
     if (more) finish_stage(buf ^ 1);
