@@ -105,8 +105,9 @@ int gdn_decode_pool(const void* q, const void* k, const void* v, const float* A_
   if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !output || !in_slots)
     return fail(GDN_ERR_VALUE, "null pointer argument");
   if (pool_size > 0 && !pool) return fail(GDN_ERR_VALUE, "null pointer argument");
-  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(pool, 16) || !aligned(intermediate, 16))
-    return fail(GDN_ERR_VALUE, "q, k, state_pool and intermediate must be 16-byte aligned");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(pool, 16) ||
+      !aligned(intermediate, 16))
+    return fail(GDN_ERR_VALUE, "q, k, v, state_pool and intermediate must be 16-byte aligned");
   if (!aligned(in_slots, 4) || !aligned(out_slots, 4))
     return fail(GDN_ERR_VALUE, "slot arrays must be 4-byte aligned");
   gdn::DecodePoolArgs p{q, k, v, A_log, a, dt_bias, b, scale == 0.0f ? 0.08838834764831845f : scale,
