@@ -342,10 +342,12 @@ __global__ void __launch_bounds__(kPackedThreads, 4) gdn_decode_pool_bf16_kernel
 // thread takes its 8 packed rows one at a time through all T tokens (fp32 between
 // tokens, one bf16 rounding per store) -- the state stream keeps the bytes in flight
 // of the single-token form instead of holding every row in fp32 across tokens.
-// Shared memory per token: q, k, v as fp32 (3 x 512 B) + g, beta.
+// Shared memory per token: q, k, v as fp32 (3 x 512 B) + g, beta.  INTER: the
+// per-token state cache is written (a separate instantiation: a runtime test per
+// row and token costs the token loop ~11 %).
 constexpr int kMtpMaxT = 32;
 
-template <bool L2NORM>
+template <bool L2NORM, bool INTER>
 __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_kernel(DecodePoolArgs p) {
   constexpr int U = kPackedU;
   extern __shared__ __align__(16) float tok[];  // [T][384]: q | k | v, then [T][2]: g, beta
@@ -495,13 +497,13 @@ __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_ke
         ov[r][1] = o2.y;
       }
       const int64_t bt = bidx * p.T + t;
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (bt * p.Hv + h) * kHead + row0 + 4 * u0;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const float o = octet_sum(ov[r][0] + ov[r][1]);
         const int row = row0 + 4 * (u0 + r);
-        if (j == 0)
-          static_cast<__nv_bfloat16*>(p.out)[(bt * p.Hv + h) * kHead + row] = __float2bfloat16_rn(p.scale * o);
-        if (p.intermediate) {
+        if (j == 0) orow[4 * r] = __float2bfloat16_rn(p.scale * o);
+        if (INTER) {
           __nv_bfloat16* ip = static_cast<__nv_bfloat16*>(p.intermediate) + (bt * p.Hv + h) * kTile +
                               static_cast<int64_t>(row) * kHead + 8 * j;
 #pragma unroll
@@ -552,10 +554,11 @@ cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
     const int64_t ctas = a.B * a.Hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
     const size_t smem = static_cast<size_t>(a.T) * (3 * kHead + 2) * sizeof(float);
-    if (a.qk_l2norm)
-      gdn_decode_pool_bf16_mtp_kernel<true><<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
-    else
-      gdn_decode_pool_bf16_mtp_kernel<false><<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
+    auto kernel = a.intermediate ? (a.qk_l2norm ? gdn_decode_pool_bf16_mtp_kernel<true, true>
+                                                : gdn_decode_pool_bf16_mtp_kernel<false, true>)
+                                 : (a.qk_l2norm ? gdn_decode_pool_bf16_mtp_kernel<true, false>
+                                                : gdn_decode_pool_bf16_mtp_kernel<false, false>);
+    kernel<<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
     return cudaGetLastError();
   }
   if (BF16 && a.T == 1 && a.B * a.Hv >= 2 * 148) {  // the packed single-token form
