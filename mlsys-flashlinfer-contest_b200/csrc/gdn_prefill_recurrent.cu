@@ -32,6 +32,8 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// L2: q/k L2 norm (a separate instantiation, so the plain token loop carries no test).
+template <bool L2>
 __global__ void __launch_bounds__(kThreads) gdn_prefill_recurrent_kernel(PrefillArgs p) {
   const int64_t cta = blockIdx.x;
   const int64_t nh = cta / kTilesPerHead;  // n * Hv + h
@@ -135,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_recurrent_kernel(Prefill
       }
       const float g = gb_s[buf][u][0], beta = gb_s[buf][u][1];
       const float vv = __bfloat162float(v_s[buf][u][r_in]);
-      if (p.qk_l2norm) {  // x / sqrt(sum x^2 + 1e-6), the sum over the octet
+      if constexpr (L2) {  // x / sqrt(sum x^2 + 1e-6), the sum over the octet
         float sk = 0.0f, sq = 0.0f;
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
@@ -188,7 +190,10 @@ cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s) {
   if (a.N == 0) return cudaSuccess;
   const int64_t ctas = a.N * a.Hv * kTilesPerHead;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  gdn_prefill_recurrent_kernel<<<static_cast<unsigned>(ctas), kThreads, 0, s>>>(a);
+  if (a.qk_l2norm)
+    gdn_prefill_recurrent_kernel<true><<<static_cast<unsigned>(ctas), kThreads, 0, s>>>(a);
+  else
+    gdn_prefill_recurrent_kernel<false><<<static_cast<unsigned>(ctas), kThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
