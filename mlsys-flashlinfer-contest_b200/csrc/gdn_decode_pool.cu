@@ -124,7 +124,9 @@ __device__ __forceinline__ void store_row16(void* base, int64_t elem, int j, con
 
 // MTP: T > 1 (the next token's inputs are prefetched); two CTAs per SM keep the
 // slot lookup, a dependent load in front of every state stream, overlapped.
-template <int U, bool BF16, bool L2NORM, bool MTP>
+// INTER: the per-token state cache may be written (multi-token instantiations
+// without it carry no test per row and token: 5 % at T = 4).
+template <int U, bool BF16, bool L2NORM, bool MTP, bool INTER = true>
 __global__ void __launch_bounds__(kThreads, 2) gdn_decode_pool_kernel(DecodePoolArgs p) {
   constexpr int kRows = 32 * U;
   constexpr int kTilesPerHead = kHead / kRows;
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_pool_kernel(DecodePool
       }
       ov = octet_sum(ov);
       if (j == 0) orow[row] = __float2bfloat16_rn(p.scale * ov);
-      if (p.intermediate)
+      if (INTER && p.intermediate)
         store_row16<BF16>(p.intermediate, (bt * p.Hv + h) * kTile + static_cast<int64_t>(row) * kHead, j, s[u]);
     }
     if (MTP && t + 1 < p.T) cur = nxt;
@@ -535,10 +537,14 @@ cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
   const unsigned grid = static_cast<unsigned>(ctas);
   if (a.T > 1) {
-    if (a.qk_l2norm)
+    if (a.qk_l2norm && a.intermediate)
       gdn_decode_pool_kernel<U, BF16, true, true><<<grid, kThreads, 0, s>>>(a);
-    else
+    else if (a.qk_l2norm)
+      gdn_decode_pool_kernel<U, BF16, true, true, false><<<grid, kThreads, 0, s>>>(a);
+    else if (a.intermediate)
       gdn_decode_pool_kernel<U, BF16, false, true><<<grid, kThreads, 0, s>>>(a);
+    else
+      gdn_decode_pool_kernel<U, BF16, false, true, false><<<grid, kThreads, 0, s>>>(a);
   } else {
     if (a.qk_l2norm)
       gdn_decode_pool_kernel<U, BF16, true, false><<<grid, kThreads, 0, s>>>(a);
