@@ -349,6 +349,23 @@ __global__ void __launch_bounds__(kPackedThreads, 4) gdn_decode_pool_bf16_kernel
 // row and token costs the token loop ~11 %).
 constexpr int kMtpMaxT = 32;
 
+// Octet sums of four rows at once (lane j of the octet holds x[r], its share of
+// row r's sum): a transposed butterfly -- at step 1 lanes j, j^1 swap two rows,
+// at step 2 lanes j, j^2 one row, then a full exchange with j^4 -- leaves the sum
+// of row 2 (j & 1) + ((j >> 1) & 1) in lanes j and j^4: 4 shuffles and 4 adds for
+// the four rows instead of 12 and 12.
+__device__ __forceinline__ float octet_sum4(const float (&x)[4], int j) {
+  const bool b0 = j & 1, b1 = j & 2;
+  const float s0 = b0 ? x[0] : x[2], s1 = b0 ? x[1] : x[3];
+  const float k0 = b0 ? x[2] : x[0], k1 = b0 ? x[3] : x[1];
+  const float y0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 1);
+  const float y1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 1);
+  const float z = (b1 ? y1 : y0) + __shfl_xor_sync(0xffffffffu, b1 ? y0 : y1, 2);
+  return z + __shfl_xor_sync(0xffffffffu, z, 4);
+}
+// The octet lane that holds row r's sum after octet_sum4 (also lane + 4).
+__device__ __forceinline__ int octet_sum4_lane(int r) { return (r >> 1) | ((r & 1) << 1); }
+
 template <bool L2NORM, bool INTER>
 __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_kernel(DecodePoolArgs p) {
   constexpr int U = kPackedU;
@@ -480,9 +497,18 @@ __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_ke
         dot[r][1] = d2.y;
       }
       float delta[R];
+      {
+        static_assert(R == 4, "octet_sum4 reduces four rows");
+        float part[4];
 #pragma unroll
-      for (int r = 0; r < R; ++r)
-        delta[r] = beta * (tq[2 * kHead + row0 + 4 * (u0 + r)] - octet_sum(dot[r][0] + dot[r][1]));
+        for (int r = 0; r < R; ++r) part[r] = dot[r][0] + dot[r][1];
+        const float red = octet_sum4(part, j);
+        const int obase = lane & ~7;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          delta[r] = beta * (tq[2 * kHead + row0 + 4 * (u0 + r)] -
+                             __shfl_sync(0xffffffffu, red, obase + octet_sum4_lane(r)));
+      }
       float ov[R][2];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
@@ -500,11 +526,16 @@ __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_ke
       }
       const int64_t bt = bidx * p.T + t;
       __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (bt * p.Hv + h) * kHead + row0 + 4 * u0;
+      {
+        float part[4];
+#pragma unroll
+        for (int r = 0; r < R; ++r) part[r] = ov[r][0] + ov[r][1];
+        const float o = octet_sum4(part, j);  // row 2 (j & 1) + ((j >> 1) & 1)
+        if (j < 4) orow[4 * (2 * (j & 1) + ((j >> 1) & 1))] = __float2bfloat16_rn(p.scale * o);
+      }
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const float o = octet_sum(ov[r][0] + ov[r][1]);
         const int row = row0 + 4 * (u0 + r);
-        if (j == 0) orow[4 * r] = __float2bfloat16_rn(p.scale * o);
         if (INTER) {
           __nv_bfloat16* ip = static_cast<__nv_bfloat16*>(p.intermediate) + (bt * p.Hv + h) * kTile +
                               static_cast<int64_t>(row) * kHead + 8 * j;
