@@ -11,6 +11,10 @@ nvcc cross-compiles, so no GPU is needed to build.
 csrc/gdn_torch.cpp, the torch-tensor binding of that C ABI, compiles with g++
 against the installed torch headers into gdn_b200/_gdn_torch.so (linked to
 libgdn_b200.so through an $ORIGIN rpath).
+
+csrc/gdn_tvm_ffi.cc, the TVM-FFI module (the binding the reference's Solutions
+load with tvm_ffi.load_module), compiles with g++ against the installed tvm_ffi
+headers into gdn_b200/gdn_tvm_ffi.so, linked to libgdn_b200.so and libtvm_ffi.so.
 """
 from __future__ import annotations
 
@@ -27,6 +31,7 @@ CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB = HERE / "gdn_b200" / "libgdn_b200.so"
 TORCH_EXT = HERE / "gdn_b200" / "_gdn_torch.so"
+TVM_FFI_MOD = HERE / "gdn_b200" / "gdn_tvm_ffi.so"
 REPO = HERE.parent
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -75,6 +80,7 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False, extra=()) -
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
     build_torch_ext(force=force, verbose=verbose)
+    build_tvm_ffi(force=force, verbose=verbose)
     return LIB
 
 
@@ -105,6 +111,33 @@ def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
         raise RuntimeError(f"torch binding build failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, TORCH_EXT)
     return TORCH_EXT
+
+
+def build_tvm_ffi(force: bool = False, verbose: bool = False) -> Path:
+    """g++ build of the TVM-FFI module (host code only: every export forwards to
+    the C ABI of libgdn_b200.so)."""
+    src = CSRC / "gdn_tvm_ffi.cc"
+    deps = [src, REPO / "include" / "gdn_b200.h", LIB]
+    if not force and TVM_FFI_MOD.exists() and TVM_FFI_MOD.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return TVM_FFI_MOD
+    import tvm_ffi.libinfo as tl
+    ffi_lib = Path(tl.find_libtvm_ffi()).resolve()
+    cuda = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+    incs = [tl.find_include_path(), tl.find_dlpack_include_path(), str(cuda / "include"),
+            str(REPO / "include")]
+    tmp = TVM_FFI_MOD.with_suffix(".so.tmp")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared",
+           *[f"-I{p}" for p in incs], str(src), "-o", str(tmp),
+           f"-L{ffi_lib.parent}", "-ltvm_ffi", f"-L{cuda / 'lib64'}", "-lcudart",
+           f"-L{LIB.parent}", "-lgdn_b200", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{ffi_lib.parent}",
+           f"-Wl,-rpath,{cuda / 'lib64'}"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"TVM-FFI module build failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, TVM_FFI_MOD)
+    return TVM_FFI_MOD
 
 
 if __name__ == "__main__":

@@ -175,16 +175,7 @@ static bool use_recurrent(int64_t T, int64_t N, int64_t Hv) {
 // (sequence, head) pairs than a third of the SMs (then not even equal sequences
 // could all be cut in 3 within one wave), or too few chunks in all; the bound is
 // the largest G <= 8 with N Hv (2G - 3) <= 4 SMs and T >= 6 G chunks.
-static int sm_count() {
-  static int n = [] {
-    int dev = 0, v = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
-      v = 148;
-    return v;
-  }();
-  return n;
-}
+static int sm_count() { return gdn::device_sm_count(); }
 
 static int choose_segments(int64_t T, int64_t N, int64_t Hv) {
   if (N <= 0 || Hv <= 0 || 3 * N * Hv > sm_count()) return 1;

@@ -151,9 +151,9 @@ cudaError_t launch_decode(const DecodeArgs& a, int rows_per_cta, cudaStream_t s)
   if (a.B == 0) return cudaSuccess;
   if (rows_per_cta == 0) rows_per_cta = rows_override();
   if (rows_per_cta == 0) {
-    // Enough CTAs to fill 148 SMs several times over before growing the tile.
-    const int64_t tiles = a.B * a.Hv;
-    rows_per_cta = tiles >= 4 * 148 ? 128 : (tiles >= 2 * 148 ? 64 : 32);
+    // Enough CTAs to fill the SMs several times over before growing the tile.
+    const int64_t tiles = a.B * a.Hv, sms = device_sm_count();
+    rows_per_cta = tiles >= 4 * sms ? 128 : (tiles >= 2 * sms ? 64 : 32);
   }
   switch (rows_per_cta) {
     case 32: return launch_u<1>(a, s);

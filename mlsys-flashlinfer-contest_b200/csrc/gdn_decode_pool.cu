@@ -595,10 +595,14 @@ cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
                                                 : gdn_decode_pool_bf16_mtp_kernel<false, true>)
                                  : (a.qk_l2norm ? gdn_decode_pool_bf16_mtp_kernel<true, false>
                                                 : gdn_decode_pool_bf16_mtp_kernel<false, false>);
+    // T > 11 stages more than the 48 KiB default (T = 32: 49,408 B)
+    const cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kernel), static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
     kernel<<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
     return cudaGetLastError();
   }
-  if (BF16 && a.T == 1 && a.B * a.Hv >= 2 * 148) {  // the packed single-token form
+  const int64_t sms = device_sm_count();
+  if (BF16 && a.T == 1 && a.B * a.Hv >= 2 * sms) {  // the packed single-token form
     const int64_t ctas = a.B * a.Hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
     if (a.qk_l2norm)
@@ -607,12 +611,12 @@ cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
       gdn_decode_pool_bf16_kernel<false><<<static_cast<unsigned>(ctas), kPackedThreads, 0, s>>>(a);
     return cudaGetLastError();
   }
-  // enough CTAs to fill the 148 SMs several times before the tile grows
+  // enough CTAs to fill the SMs several times before the tile grows
   const int64_t tiles = a.B * a.Hv;
   // (multi-token: at most 64 rows per thread block, whose registers also hold
   // the next token's inputs)
-  if (tiles >= 4 * 148 && a.T == 1) return launch_u<4, BF16>(a, s);
-  if (tiles >= 2 * 148) return launch_u<2, BF16>(a, s);
+  if (tiles >= 4 * sms && a.T == 1) return launch_u<4, BF16>(a, s);
+  if (tiles >= 2 * sms) return launch_u<2, BF16>(a, s);
   return launch_u<1, BF16>(a, s);
 }
 

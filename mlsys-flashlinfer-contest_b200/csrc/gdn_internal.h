@@ -14,6 +14,12 @@ constexpr int kHead = 128;   // head_size (K = V = 128, fixed by the definitions
 constexpr int kChunk = 64;   // chunk length of the chunked prefill
 #endif
 
+// SM count of the current device (cached per device).
+int device_sm_count();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for `func` on the current
+// device, once per (device, function); a no-op up to the 48 KiB default.
+cudaError_t set_max_dynamic_smem(const void* func, int bytes);
+
 struct DecodeArgs {
   const void* q;        // [B,1,Hq,128] bf16
   const void* k;        // [B,1,Hk,128] bf16 (Hk == Hq)

@@ -1238,12 +1238,9 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   } else if (a.jobs || a.qk_l2norm) {
     return cudaErrorInvalidValue;  // the debug build covers the plain kernel only
   }
-  static bool attr_set[4] = {false, false, false, false};
-  if (!attr_set[variant]) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[variant] = true;
-  }
+  // the opt-in is per device: a process may drive several GPUs
+  if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(kernel), kSmemBytes)) != cudaSuccess)
+    return e;
   ChunkParams p{a.state, a.A_log, a.dt_bias,
                 static_cast<const __nv_bfloat16*>(a.a), static_cast<const __nv_bfloat16*>(a.b),
                 a.cu_seqlens, static_cast<__nv_bfloat16*>(a.out), a.new_state, debug, a.jobs, a.scale,

@@ -1,7 +1,7 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a container where the reference workspace is mounted (its path is the
-first argument, default ``/root/reference``):
+Run in a container where the reference workspace is mounted; its root
+directory is the one required argument:
 
     python tests/golden/make_golden.py [REFERENCE_ROOT]
 
@@ -96,7 +96,9 @@ def state_subset(new_state: np.ndarray, seed: int):
 
 
 def main():
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT")
+    ref_root = Path(sys.argv[1])
     dec_md = ref_root / "definitions/gdn/gdn_decode_qk4_v8_d128_k_last.md"
     pre_md = ref_root / "definitions/gdn/gdn_prefill_qk4_v8_d128_k_last.md"
     torch.set_num_threads(os.cpu_count() or 1)

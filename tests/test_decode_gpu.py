@@ -79,17 +79,20 @@ def test_decode_deterministic():
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
 
 
-def test_decode_large_batch_properties():
-    # BASELINE config 1 size (B=256): oracle on a slice of sequences, plus the
-    # size-independent property that each sequence only depends on its own row.
-    inp = W.make_decode_inputs(256, 16, 32, seed=11, device="cuda")
+def test_decode_large_batch_all_sequences():
+    """BASELINE config 1 (B=256, Hq=16, Hv=32): every one of the 256 x 32
+    (sequence, v-head) updates against the C oracle (the reference decode
+    recurrence on all host threads)."""
+    from oracle import c_oracle as C
+    cpu = W.make_decode_inputs(256, 16, 32, seed=11)
+    o_ref, s_ref = C.decode(*cpu.args())
+    inp = PT.to_device(cpu)
     o, ns = decode.run(*inp.args())
-    idx = [0, 1, 127, 200, 255]
-    sl = W.DecodeInputs(*(x[idx].cpu() if isinstance(x, torch.Tensor) and x.dim() > 1 else
-                          (x.cpu() if isinstance(x, torch.Tensor) else x) for x in inp.args()))
-    o_ref, s_ref = O.decode(*PT.np_args(sl))
-    PT.assert_o_close(o[idx], o_ref)
-    PT.assert_state_close(ns[idx], s_ref, PT.STATE_RTOL_FP32)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    ns = ns.cpu()
+    for b0 in range(0, 256, 32):  # 32 sequences at a time keeps the float64 copies small
+        PT.assert_state_close(ns[b0:b0 + 32], s_ref[b0:b0 + 32].numpy(), PT.STATE_RTOL_FP32)
 
 
 def test_decode_dtype_and_shape_errors():

@@ -65,6 +65,21 @@ def test_pool_matches_oracle(T, bf16, l2, geom):
     _state_close(inter, inter_ref, bf16)
 
 
+@pytest.mark.parametrize("T", [12, 32])
+def test_pool_bf16_many_tokens(T):
+    """bf16 multi-token steps stage T tokens in shared memory: above T = 11 that is
+    more than the 48 KiB default (T = 32, the largest staged count: 49,408 B)."""
+    B, Hq, Hv, P = 3, 4, 8, 4
+    inp = W.make_decode_pool_inputs(B, T, Hq, Hv, P, seed=300 + T, device="cuda", state_bf16=True)
+    o_ref, pool_ref, _ = _oracle(inp, state_bf16=True)
+    pool = inp.pool.clone()
+    o = decode.run_pool(inp.q, inp.k, inp.v, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                        pool, inp.in_slots, inp.out_slots)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    _state_close(pool, pool_ref, True)
+
+
 def test_pool_no_state_update_leaves_pool():
     inp = W.make_decode_pool_inputs(4, 2, 4, 8, 6, seed=9, device="cuda", state_bf16=True)
     o_ref, _, _ = _oracle(inp, state_bf16=True, no_state_update=True)

@@ -140,11 +140,24 @@ def test_chunked_config2_varlen():
     PT.assert_state_close(ns, s_ref.numpy(), PT.STATE_REL)
 
 
-def test_chunked_matches_recurrent_at_config3_size():
-    # BASELINE config 3 (4 x 16384, Hq=16, Hv=32): the chunked kernel against
-    # our token-recurrent kernel (itself pinned to the oracle) on the full size
-    inp = W.make_prefill_inputs([16384] * 4, 16, 32, seed=3, device="cuda")
+def test_chunked_config3_full_size_against_c_oracle():
+    """BASELINE config 3 (4 x 16384 tokens, Hq=16, Hv=32, random fp32 initial
+    states) through the chunked kernel; sequence 0 (all 32 v-heads, 16384 tokens)
+    against the C oracle (the reference recurrence, definitions/gdn/
+    gdn_prefill_qk4_v8_d128_k_last.md:62-142, on all host threads), and all four
+    sequences against the token-recurrent kernel (fp32 throughout)."""
+    cpu = W.make_prefill_inputs([16384] * 4, 16, 32, seed=3)
+    L0 = 16384
+    seq0 = W.PrefillInputs(cpu.q[:L0], cpu.k[:L0], cpu.v[:L0], cpu.state[:1], cpu.A_log,
+                           cpu.a[:L0], cpu.dt_bias, cpu.b[:L0],
+                           torch.tensor([0, L0], dtype=torch.int64), cpu.scale)
+    o_ref, s_ref = C.prefill(*seq0.args())
+    inp = PT.to_device(W.make_prefill_inputs([16384] * 4, 16, 32, seed=3))
     o1, s1 = chunked(*inp.args())
+    torch.cuda.synchronize()
+    PT.assert_o_close(o1[:L0], o_ref)
+    err = PT.assert_state_close(s1[:1], s_ref.numpy(), PT.STATE_REL)
+    print(f"config 3 sequence 0 (16384 tokens x 32 heads): state rel err {err:.3e} (bound 1e-3)")
     o2, s2 = prefill.run_recurrent(*inp.args())
     torch.cuda.synchronize()
     PT.assert_o_close(o1, o2)
