@@ -278,6 +278,10 @@ def run_ours(args, rank, world, local_rank, dist):
         cpu = time_cpu_decode(args.cpu_budget)
         cpu.pop("s_per_step", None)
 
+    library = None
+    if world == 1 and not args.no_library:
+        library = run_library_baseline(args, dev)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
@@ -299,6 +303,7 @@ def run_ours(args, rank, world, local_rank, dist):
             "cpu_baseline": cpu,
             "prefill": prefill,
             "decode_pool": pool,
+            "library_baseline": library,
         }
         print(json.dumps(line), flush=True)
 
@@ -326,7 +331,8 @@ def run_e2e(args, inp, dev, stream, dist, world):
     states = [inp.state.clone(), torch.empty_like(inp.state)]
     h2d = sum(t[0].numel() * t[0].element_size() for t in host.values())
     d2h = o_host[0].numel() * o_host[0].element_size()
-    steps = max(args.steps // 4, 10)
+    steps = max(args.steps // 20, 40)  # per window; 5 windows: >= 200 steps
+    windows = 5
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]     # inputs of buffer i landed
     ev_used = [torch.cuda.Event() for _ in range(2)]   # kernel done with buffer i
@@ -355,24 +361,35 @@ def run_e2e(args, inp, dev, stream, dist, world):
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    s_in.wait_stream(stream)
-    s_out.wait_stream(stream)
-    for i in range(steps):
-        issue(i)
-    stream.wait_event(ev_out[(steps - 1) % 2])
-    stream.wait_event(ev_out[steps % 2])
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    # five windows of `steps` pipelined steps each: the value is their total; the
+    # windows' spread shows the run-to-run noise of the host copies
+    windows_ms = []
+    for w in range(windows):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        for i in range(steps):
+            issue(i)
+        stream.wait_event(ev_out[(steps - 1) % 2])
+        stream.wait_event(ev_out[steps % 2])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        windows_ms.append(e0.elapsed_time(e1))
+    t = torch.tensor(windows_ms, dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    value = B_PER_RANK * HV * UNIT_BYTES * world * steps / (ms / 1e3) / 1e9
+    windows_ms = [float(x) for x in t.tolist()]
+    ms = sum(windows_ms)
+    total_steps = steps * windows
+    value = B_PER_RANK * HV * UNIT_BYTES * world * total_steps / (ms / 1e3) / 1e9
+    per_step_us = sorted(w / steps * 1e3 for w in windows_ms)
+    med = statistics.median(per_step_us)
     return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "steps": steps, "us_per_step": round(ms / steps * 1e3, 2),
+            "d2h_bytes_per_step": d2h, "steps": total_steps, "us_per_step": round(ms / total_steps * 1e3, 2),
+            "us_per_step_median_window": round(med, 2),
+            "us_per_step_windows": [round(x, 2) for x in per_step_us],
+            "spread_pct": round((per_step_us[-1] - per_step_us[0]) / med * 100, 2),
             "api": "gdn_b200.decode.launch (destination passing)",
             "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's kernel (two buffer sets, "
                           "copy streams); every copy is inside the timed region",
@@ -419,73 +436,174 @@ def run_pool_bench(args, dev):
             "results": res}
 
 
-def run_prefill_bench(args, rank, world, local_rank, dev, dist):
-    """Prefill tokens/s on BASELINE config 3's shape (4 x 16384 tokens): each
-    rank owns Hv/N v-heads (whole GVA groups) of every sequence; the output
-    all-gather over NCCL is timed separately (only callers that need every
-    head on every rank pay it)."""
-    from gdn_b200 import prefill, sharding as S, workloads as W
-    if HQ % world:
-        return None
-    sh = S.head_shard(HQ, HV, world, rank)
-    hq, hv = sh.num_q_heads, sh.num_v_heads
-    lengths = [args.prefill_len] * args.prefill_seqs
-    inp = W.make_prefill_inputs(lengths, hq, hv, seed=77 + rank, device=dev)
-    T, Nseq = sum(lengths), len(lengths)
-    out = torch.empty_like(inp.v)
-    ns = torch.empty_like(inp.state)
+def prefill_unit_costs(T, Nseq, hq, hv):
+    """Algorithmic bytes and FLOPs of one prefill call (q, k, v, o, a, b per token,
+    the state read and written once per (sequence, v-head); 163,840 FLOP per token
+    and v-head)."""
+    tok_bytes = 2 * hq * D * 2 + 2 * hv * D * 2 + 2 * hv * 2
+    return T * tok_bytes + Nseq * hv * 2 * D * D * 4, T * hv * 163840
 
-    def once():
-        prefill.launch(*inp.args(), out, ns)
 
+def prefill_roofline(T, Nseq, hq, hv, ms):
+    bytes_call, flops_call = prefill_unit_costs(T, Nseq, hq, hv)
+    hbm_peak, tc_burst, _, peak_src = measured_peaks()
+    t_hbm = bytes_call / (hbm_peak * 1e9)
+    t_tc = flops_call / (tc_burst * 1e12)
+    return {"bound": "hbm" if t_hbm >= t_tc else "tensor", "algorithmic_bytes_per_call": bytes_call,
+            "algorithmic_flops_per_call": flops_call,
+            "achieved_GBps": round(bytes_call / (ms / 1e3) / 1e9, 1),
+            "achieved_TFLOPs": round(flops_call / (ms / 1e3) / 1e12, 2),
+            "hbm_peak_GBps": hbm_peak, "tc_peak_TFLOPs": tc_burst,
+            "roofline_ms": round(max(t_hbm, t_tc) * 1e3, 4),
+            "frac": round(max(t_hbm, t_tc) * 1e3 / ms, 4),
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs copy / bf16_tflops burst)"
+            if peak_src == "measured" else peak_src}
+
+
+def time_calls(fn, reps, dev, dist):
+    """Mean device time per call (ms), CUDA events on the current stream around
+    each call after two warm-up calls, max over ranks."""
     for _ in range(2):
-        once()
+        fn()
     torch.cuda.synchronize()
-    reps = args.prefill_steps
     stream = torch.cuda.current_stream(dev)
     if dist:
         dist.barrier()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
     evs[0].record(stream)
     for i in range(reps):
-        once()
+        fn()
         evs[i + 1].record(stream)
     torch.cuda.synchronize()
     per = [evs[i].elapsed_time(evs[i + 1]) for i in range(reps)]
     t = torch.tensor([statistics.mean(per)], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    # algorithmic traffic and work of one call on this rank
-    tok_bytes = 2 * hq * D * 2 + 2 * hv * D * 2 + 2 * hv * 2     # q,k + v,o + a,b
-    bytes_call = T * tok_bytes + Nseq * hv * 2 * D * D * 4        # + state in and out
-    flops_call = T * hv * 163840                                 # 5.24 MFLOP/token at Hv=32
-    hbm_peak, tc_burst, _, peak_src = measured_peaks()
-    t_hbm = bytes_call / (hbm_peak * 1e9)
-    t_tc = flops_call / (tc_burst * 1e12)
-    bound = "hbm" if t_hbm >= t_tc else "tensor"
-    # a head shard with few (sequence, head) pairs takes the segmented form
-    seg_bound = prefill.segments_for(T, Nseq, hv)
-    path = ("gdn_b200.prefill.launch: segmented prefill (job builder, pass 1, combine, pass 2; "
-            f"pieces picked on the device under a bound of {seg_bound})" if seg_bound > 1
-            else "gdn_b200.prefill.launch (fused chunked kernel)")
-    res = {"metric": "gdn_prefill_tokens_per_s", "value": round(T / (ms / 1e3), 1),
-           "unit": "tokens/s", "ms_per_call": round(ms, 4), "steps": reps,
-           "workload": f"BASELINE config 3: {args.prefill_seqs} x {args.prefill_len} tokens, "
-                       f"Hq={HQ}, Hv={HV} ({hv} v-heads on each of {world} ranks), random fp32 "
-                       f"initial states", "path": path,
-           "gpu_launches_per_call": 4 if seg_bound > 1 else 1,
-           "roofline": {"bound": bound, "algorithmic_bytes_per_call": bytes_call,
-                        "algorithmic_flops_per_call": flops_call,
-                        "achieved_GBps": round(bytes_call / (ms / 1e3) / 1e9, 1),
-                        "achieved_TFLOPs": round(flops_call / (ms / 1e3) / 1e12, 2),
-                        "hbm_peak_GBps": hbm_peak, "tc_peak_TFLOPs": tc_burst,
-                        "roofline_ms": round(max(t_hbm, t_tc) * 1e3, 4),
-                        "frac": round(max(t_hbm, t_tc) * 1e3 / ms, 4), "peak_source": peak_src}}
-    full = profiled_traffic("gdn_prefill_chunked_config3.md")  # ncu, 1-GPU config-3 launch
-    if full is not None and args.prefill_seqs == 4 and args.prefill_len == 16384 and seg_bound == 1:
-        res["roofline"]["traffic"] = int(full * hv / HV)  # this rank's heads
+    return float(t.item()), per
+
+
+def prefill_e2e(cpu_inp, dev, reps, dist):
+    """End to end through the public destination-passing API (prefill.launch): each
+    call copies q, k, v, a, b, cu_seqlens and the initial states from pinned host
+    memory, runs, and copies o and the final states back to pinned host memory,
+    all inside the timed region (one stream, calls back to back)."""
+    from gdn_b200 import prefill
+    names = ("q", "k", "v", "state", "a", "b", "cu_seqlens")
+    host = {n: getattr(cpu_inp, n).pin_memory() for n in names if getattr(cpu_inp, n) is not None}
+    devb = {n: torch.empty_like(t, device=dev) for n, t in host.items()}
+    A_log, dt_bias = cpu_inp.A_log.to(dev), cpu_inp.dt_bias.to(dev)
+    Nseq = cpu_inp.cu_seqlens.numel() - 1
+    hv = cpu_inp.v.shape[1]
+    o_dev = torch.empty_like(devb["v"])
+    ns_dev = torch.empty((Nseq, hv, D, D), dtype=torch.float32, device=dev)
+    o_host = torch.empty(o_dev.shape, dtype=o_dev.dtype, pin_memory=True)
+    ns_host = torch.empty(ns_dev.shape, dtype=ns_dev.dtype, pin_memory=True)
+    ws_bytes = prefill.workspace_bytes(cpu_inp.q.shape[0], Nseq, cpu_inp.q.shape[1], hv)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+
+    def call():
+        for n, t in host.items():
+            devb[n].copy_(t, non_blocking=True)
+        prefill.launch(devb["q"], devb["k"], devb["v"], devb.get("state"), A_log, devb["a"], dt_bias,
+                       devb["b"], devb["cu_seqlens"], cpu_inp.scale, o_dev, ns_dev,
+                       workspace=ws if ws_bytes else None)
+        o_host.copy_(o_dev, non_blocking=True)
+        ns_host.copy_(ns_dev, non_blocking=True)
+
+    ms, _ = time_calls(call, reps, dev, dist)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = o_host.numel() * o_host.element_size() + ns_host.numel() * ns_host.element_size()
+    T = cpu_inp.q.shape[0]
+    return {"value": round(T / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_call": round(ms, 4), "calls": reps,
+            "api": "gdn_b200.prefill.launch (destination passing)",
+            "copies": "H2D of every input and D2H of o and the final states inside the timed "
+                      "region, serialised with the call on one stream"}
+
+
+def cpu_prefill(lengths, hq, hv, seed, zero_every_other):
+    """The C restatement of the reference prefill recurrence on all host threads,
+    on the same workload (whole: every sequence and head)."""
+    from oracle import c_oracle
+    from gdn_b200 import workloads as W
+    inp = W.make_prefill_inputs(lengths, hq, hv, seed=seed, zero_state_every_other=zero_every_other)
+    nthreads = c_oracle.max_threads()
+    t0 = time.perf_counter()
+    c_oracle.prefill(*inp.args(), nthreads=nthreads)
+    el = time.perf_counter() - t0
+    n, model = cpu_count_info()
+    T = sum(lengths)
+    return {"value": round(T / el, 1), "unit": "tokens/s", "cores": nthreads, "kind": "port",
+            "sample": f"the whole workload ({len(lengths)} sequences, {T} tokens, Hv={hv}) once through "
+                      f"oracle/gdn_oracle.c, {el:.2f} s, {nthreads} threads on {n} cpus ({model})"}
+
+
+def run_prefill_bench(args, rank, world, local_rank, dev, dist):
+    """Prefill tokens/s on BASELINE config 3 (4 x 16384 tokens) and config 2 (16
+    varlen sequences, ~U[64, 1024] tokens, half zero states): each rank owns Hv/N
+    v-heads (whole GVA groups) of every sequence.  Per config: the device time of
+    prefill.launch with inputs resident in HBM and its roofline, the same call end
+    to end with host buffers (e2e), and the C restatement of the reference on the
+    host cores (rank 0, N = 1).  At N > 1 the output all-gather (NCCL, and fused
+    into the kernel's stores) is timed separately on config 3."""
+    from gdn_b200 import prefill, sharding as S, workloads as W
+    if HQ % world:
+        return None
+    sh = S.head_shard(HQ, HV, world, rank)
+    hq, hv = sh.num_q_heads, sh.num_v_heads
+    cfgs = [("config3", [args.prefill_len] * args.prefill_seqs, 77, False,
+             f"BASELINE config 3: {args.prefill_seqs} x {args.prefill_len} tokens, Hq={HQ}, Hv={HV} "
+             f"({hv} v-heads on each of {world} ranks), random fp32 initial states"),
+            ("config2", W.config_lengths("prefill_varlen"), 2, True,
+             f"BASELINE config 2: 16 sequences, lengths ~U[64,1024] (seeded), Hq={HQ}, Hv={HV} "
+             f"({hv} v-heads on each of {world} ranks), zero initial state for every other sequence")]
+    res = {}
+    for name, lengths, seed, zero_eo, desc in cfgs:
+        T, Nseq = sum(lengths), len(lengths)
+        cpu_inp = W.make_prefill_inputs(lengths, hq, hv, seed=seed + rank, zero_state_every_other=zero_eo)
+        inp = W.make_prefill_inputs(lengths, hq, hv, seed=seed + rank, device=dev,
+                                    zero_state_every_other=zero_eo)
+        out = torch.empty_like(inp.v)
+        ns = torch.empty_like(inp.state)
+        ws_bytes = prefill.workspace_bytes(T, Nseq, hq, hv)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+        reps = args.prefill_steps if name == "config3" else max(args.prefill_steps * 5, 20)
+        ms, _ = time_calls(lambda: prefill.launch(*inp.args(), out, ns, workspace=ws if ws_bytes else None),
+                           reps, dev, dist)
+        seg_bound = prefill.segments_for(T, Nseq, hv)
+        path = ("gdn_b200.prefill.launch: segmented prefill (job builder, pass 1, combine, pass 2; "
+                f"pieces picked on the device under a bound of {seg_bound})" if seg_bound > 1
+                else "gdn_b200.prefill.launch (fused chunked kernel)")
+        # every rank walks all T tokens for its heads: the job's rate is T / (max-over-ranks time)
+        r = {"metric": "gdn_prefill_tokens_per_s", "value": round(T / (ms / 1e3), 1),
+             "unit": "tokens/s", "ms_per_call": round(ms, 4), "steps": reps, "workload": desc,
+             "total_tokens": T, "num_seqs": Nseq, "path": path,
+             "gpu_launches_per_call": 4 if seg_bound > 1 else 1,
+             "roofline": prefill_roofline(T, Nseq, hq, hv, ms)}
+        if name == "config3":
+            full = profiled_traffic("gdn_prefill_chunked_config3.md")  # ncu, 1-GPU config-3 launch
+            if full is not None and args.prefill_seqs == 4 and args.prefill_len == 16384 and seg_bound == 1:
+                r["roofline"]["traffic"] = int(full * hv / HV)  # this rank's heads
+        if not args.no_e2e:
+            r["e2e"] = prefill_e2e(cpu_inp, dev, 3 if name == "config3" else 10, dist)
+        if rank == 0 and world == 1 and not args.no_cpu:
+            r["cpu_baseline"] = cpu_prefill(lengths, hq, hv, seed, zero_eo)
+        res[name] = r
+        del inp, out, ns, ws, cpu_inp
+    # the headline prefill object stays config 3; config 2 rides beside it
+    top = res["config3"]
+    top["config2"] = res["config2"]
     if dist and world > 1:
+        lengths = [args.prefill_len] * args.prefill_seqs
+        T = sum(lengths)
+        inp = W.make_prefill_inputs(lengths, hq, hv, seed=77 + rank, device=dev)
+        out = torch.empty_like(inp.v)
+        ns = torch.empty_like(inp.state)
+        prefill.launch(*inp.args(), out, ns)
+        torch.cuda.synchronize()
+        ms = top["ms_per_call"]
+        reps = args.prefill_steps
+        stream = torch.cuda.current_stream(dev)
         from gdn_b200.sharding import all_gather_heads
         for _ in range(2):
             all_gather_heads(out)
@@ -500,7 +618,7 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
         ag = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
         dist.all_reduce(ag, op=dist.ReduceOp.MAX)
         recv = (world - 1) * out.numel() * out.element_size()
-        res["allgather_o"] = {"ms": round(float(ag.item()), 4), "bytes_received_per_rank": recv,
+        top["allgather_o"] = {"ms": round(float(ag.item()), 4), "bytes_received_per_rank": recv,
                               "GBps_per_rank": round(recv / (float(ag.item()) / 1e3) / 1e9, 1),
                               "value_with_gather": round(T / ((ms + float(ag.item())) / 1e3), 1)}
         # the same gather fused into the kernel: every rank's output tiles go to every
@@ -524,14 +642,152 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
         dist.all_reduce(same, op=dist.ReduceOp.MIN)
         dist.barrier()
         bufs.close()
-        res["allgather_fused"] = {
+        top["allgather_fused"] = {
             "ms_per_call_with_gather": round(float(fg.item()), 4),
             "value_with_gather": round(T / (float(fg.item()) / 1e3), 1),
+            "bytes_received_per_rank": recv,
+            "nvlink_GBps_per_rank": round(recv / (float(fg.item()) / 1e3) / 1e9, 1),
             "matches_nccl_allgather": bool(same.item()),
             "how": "C ABI gdn_prefill_chunked_peers: the kernel's output TMA stores also target "
                    "every peer's full output buffer (CUDA IPC mapping); no collective"}
         del full
-    return res
+    return top
+
+
+# ---------------------------------------------------------------- library baselines
+def run_library_baseline(args, dev):
+    """FlashInfer's Blackwell GDN kernels, the bars the reference measures itself
+    against (reference_solutions/baseline/gdn/gdn_prefill_qk4_v8_d128_k_last/
+    flashinfer_wrapper_123ca6.md:30-59 and .../gdn_decode_qk4_v8_d128_k_last/
+    flashinfer_wrapper_9b7f1e.md:24-55), called as libraries on the same box and
+    the same inputs as our kernels.  Prefill: chunk_gated_delta_rule_sm100, the
+    CuTe-DSL SM100 kernel that flashinfer.chunk_gated_delta_rule dispatches to on
+    sm_100a (called directly: the dispatcher picks it only under a CUDA 13 torch);
+    its gates are formed in torch first, as the wrapper does.  Decode:
+    gated_delta_rule_decode_pretranspose on the fp32 k-last state, in place.
+    Each line gives the library's time, ours on the same inputs, ours' speed-up
+    (library time / our time) and the largest difference between the outputs."""
+    import torch.nn.functional as F
+    from gdn_b200 import decode, prefill, workloads as W
+    out = {}
+    try:
+        import flashinfer
+        out["flashinfer_version"] = flashinfer.__version__
+    except Exception as e:  # pragma: no cover - depends on the box
+        return {"unavailable": f"flashinfer import failed: {e!r}"[:400]}
+
+    def dev_time(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    try:
+        from flashinfer.gdn_kernels import chunk_gated_delta_rule_sm100 as fi_prefill
+        if fi_prefill is None:
+            raise ImportError("flashinfer.gdn_kernels.chunk_gated_delta_rule_sm100 is None")
+    except Exception as e:  # pragma: no cover
+        fi_prefill = None
+        out["prefill_unavailable"] = f"{e!r}"[:400]
+    cases = [("config3", [16384] * 4, HQ, HV, 77, False),
+             ("config2", W.config_lengths("prefill_varlen"), HQ, HV, 2, True),
+             ("contest_8192x1_qk4_v8", [8192], 4, 8, 5, False),
+             ("contest_even_8192x4_qk4_v8", W.even_lengths(8192, 4), 4, 8, 6, False)]
+    for name, lengths, hq, hv, seed, zeo in cases if fi_prefill is not None else []:
+        try:
+            inp = W.make_prefill_inputs(lengths, hq, hv, seed=seed, device=dev, zero_state_every_other=zeo)
+            T, Nseq = sum(lengths), len(lengths)
+            reps = 10 if T > 20000 else 30
+            o_ours = torch.empty_like(inp.v)
+            ns_ours = torch.empty_like(inp.state)
+            ws_bytes = prefill.workspace_bytes(T, Nseq, hq, hv)
+            ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+            ours_ms = dev_time(lambda: prefill.launch(*inp.args(), o_ours, ns_ours,
+                                                      workspace=ws if ws_bytes else None), reps)
+            cu32 = inp.cu_seqlens.to(torch.int32)
+            o_fi = torch.empty_like(inp.v)
+            ns_fi = torch.empty_like(inp.state)
+
+            def gates():
+                g = -torch.exp(inp.A_log.float()) * F.softplus(inp.a.float() + inp.dt_bias.float())
+                return g.contiguous(), torch.sigmoid(inp.b.float()).contiguous()
+
+            g, beta = gates()
+            kern = lambda: fi_prefill(inp.q, inp.k, inp.v, g, beta, o_fi, cu32, inp.state, ns_fi,
+                                      float(inp.scale))
+
+            def wrapper():
+                gg, bb = gates()
+                fi_prefill(inp.q, inp.k, inp.v, gg, bb, o_fi, cu32, inp.state, ns_fi, float(inp.scale))
+
+            t0 = time.perf_counter()
+            kern()  # first call compiles the CuTe-DSL kernel
+            torch.cuda.synchronize()
+            compile_s = time.perf_counter() - t0
+            lib_ms = dev_time(kern, reps)
+            lib_wrap_ms = dev_time(wrapper, reps)
+            kern()
+            prefill.launch(*inp.args(), o_ours, ns_ours, workspace=ws if ws_bytes else None)
+            torch.cuda.synchronize()
+            d_o = (o_ours.float() - o_fi.float()).abs().max().item()
+            ref = ns_ours.reshape(-1, D * D)
+            d_s = ((ns_fi.reshape(-1, D * D) - ref).norm(dim=1) / ref.norm(dim=1).clamp_min(1e-30)).max().item()
+            out[f"prefill_{name}"] = {
+                "workload": f"{Nseq} sequences, {T} tokens, Hq={hq}, Hv={hv}",
+                "library_kernel_ms": round(lib_ms, 4), "library_with_gates_ms": round(lib_wrap_ms, 4),
+                "ours_ms": round(ours_ms, 4),
+                "library_tokens_per_s": round(T / (lib_wrap_ms / 1e3), 1),
+                "ours_tokens_per_s": round(T / (ours_ms / 1e3), 1),
+                "speedup_ours_vs_library": round(lib_wrap_ms / ours_ms, 3),
+                "speedup_ours_vs_library_kernel_only": round(lib_ms / ours_ms, 3),
+                "max_abs_diff_o": d_o, "max_state_rel_diff": d_s,
+                "library_first_call_s": round(compile_s, 1)}
+            del inp, o_ours, ns_ours, o_fi, ns_fi, ws
+        except Exception as e:  # pragma: no cover
+            out[f"prefill_{name}"] = {"unavailable": f"{e!r}"[:400]}
+    try:
+        from flashinfer.gdn_decode import gated_delta_rule_decode_pretranspose as fi_decode
+        inp = W.make_decode_inputs(B_PER_RANK, HQ, HV, seed=1000, device=dev)
+        st_fi = inp.state.clone()
+        st_ours = inp.state.clone()
+        o_fi = torch.empty_like(inp.v)
+        o_ours = torch.empty_like(inp.v)
+        kern = lambda: fi_decode(inp.q, inp.k, inp.v, st_fi, inp.A_log, inp.a, inp.dt_bias, inp.b,
+                                 scale=float(inp.scale), output=o_fi, use_qk_l2norm=False)
+        ours = lambda: decode.launch(inp.q, inp.k, inp.v, st_ours, inp.A_log, inp.a, inp.dt_bias, inp.b,
+                                     inp.scale, o_ours, st_ours)
+        t0 = time.perf_counter()
+        kern()
+        torch.cuda.synchronize()
+        compile_s = time.perf_counter() - t0
+        lib_ms = dev_time(kern, 100)
+        ours_ms = dev_time(ours, 100)
+        # one step each from the same state: outputs and states compared
+        st_fi.copy_(inp.state)
+        st_ours.copy_(inp.state)
+        kern()
+        ours()
+        torch.cuda.synchronize()
+        ref = st_ours.reshape(-1, D * D)
+        d_s = ((st_fi.reshape(-1, D * D) - ref).norm(dim=1) / ref.norm(dim=1).clamp_min(1e-30)).max().item()
+        out["decode_config1"] = {
+            "workload": f"B={B_PER_RANK}, Hq={HQ}, Hv={HV}, fp32 state updated in place",
+            "library_us_per_step": round(lib_ms * 1e3, 2), "ours_us_per_step": round(ours_ms * 1e3, 2),
+            "library_GBps": round(B_PER_RANK * HV * UNIT_BYTES / (lib_ms / 1e3) / 1e9, 1),
+            "ours_GBps": round(B_PER_RANK * HV * UNIT_BYTES / (ours_ms / 1e3) / 1e9, 1),
+            "speedup_ours_vs_library": round(lib_ms / ours_ms, 3),
+            "max_abs_diff_o": (o_ours.float() - o_fi.float()).abs().max().item(),
+            "max_state_rel_diff": d_s, "library_first_call_s": round(compile_s, 1)}
+        del inp, st_fi, st_ours
+    except Exception as e:  # pragma: no cover
+        out["decode_config1"] = {"unavailable": f"{e!r}"[:400]}
+    return out
 
 
 # ---------------------------------------------------------------- reference arm
@@ -560,12 +816,17 @@ def run_reference(args, rank, world):
 
 
 def run_replay(args):
-    """Contest-shape replay (qk4_v8 geometry: Hq = Hk = 4, Hv = 8): latency of the
-    public ``run`` entry points over seeded synthetic shapes spanning the contest
-    workloads' axes, next to the C restatement of the reference on the host cores.
-    Back-to-back calls with inputs resident on the device, as a Solution harness
-    calls them; per case: median of 5 batches of 20 calls (CUDA events)."""
+    """Contest-record replay (qk4_v8 geometry: Hq = Hk = 4, Hv = 8): latency of the
+    public ``run`` entry points on every workload record of the reference's
+    workloads/gdn/*.md, with seeded synthetic tensors of each record's shape: the
+    54 decode records (batch_size) and the 100 prefill records (total_seq_len,
+    num_seqs) under both cu_seqlens rewrites of the reference's scripts ("even",
+    "uneven").  Back-to-back calls with inputs resident on the device, as a
+    Solution harness calls them; per record: median of 5 batches of 20 calls (CUDA
+    events), next to the C restatement of the reference on the host cores (within
+    a time budget)."""
     from gdn_b200 import decode, prefill, workloads as W
+    from gdn_b200.graphs import DecodeGraph
     from oracle import c_oracle
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -598,38 +859,44 @@ def run_replay(args):
         return dt * 1e6
 
     rows_d, rows_p, ratios = [], [], []
-    for B in W.CONTEST_DECODE_BATCHES:
-        inp = W.make_decode_inputs(B, hq, hv, seed=500 + B)
-        c_us = cpu_us(lambda: c_oracle.decode(*inp.args()))
-        dinp = W.make_decode_inputs(B, hq, hv, seed=500 + B, device=dev)
-        g_us = gpu_us(lambda: decode.run(*dinp.args()))
-        from gdn_b200.graphs import DecodeGraph
-        dg = DecodeGraph(dinp.q, dinp.k, dinp.v, dinp.state.clone(), dinp.A_log, dinp.a, dinp.dt_bias,
-                         dinp.b, dinp.scale)
-        gr_us = gpu_us(dg.step)
+    by_batch = {}
+    for i, B in enumerate(W.contest_decode_records()):
+        if B not in by_batch:  # records share batch sizes: time each size once
+            inp = W.make_decode_inputs(B, hq, hv, seed=500 + B)
+            c_us = cpu_us(lambda: c_oracle.decode(*inp.args()))
+            dinp = W.make_decode_inputs(B, hq, hv, seed=500 + B, device=dev)
+            g_us = gpu_us(lambda: decode.run(*dinp.args()))
+            dg = DecodeGraph(dinp.q, dinp.k, dinp.v, dinp.state.clone(), dinp.A_log, dinp.a,
+                             dinp.dt_bias, dinp.b, dinp.scale)
+            by_batch[B] = (g_us, gpu_us(dg.step), c_us)
+        g_us, gr_us, c_us = by_batch[B]
         r = None if c_us is None else c_us / g_us
         if r:
             ratios.append(r)
-        rows_d.append({"batch": B, "us": round(g_us, 2), "graph_replay_us": round(gr_us, 2),
+        rows_d.append({"record": i, "batch": B, "us": round(g_us, 2), "graph_replay_us": round(gr_us, 2),
                        "cpu_us": c_us and round(c_us, 1), "speedup_vs_cpu": r and round(r, 1)})
-    for i, lengths in enumerate(W.contest_prefill_cases()):
-        inp = W.make_prefill_inputs(lengths, hq, hv, seed=700 + i)
+    for j, (rec, split, lengths) in enumerate(W.contest_prefill_records()):
+        inp = W.make_prefill_inputs(lengths, hq, hv, seed=700 + j)
         c_us = cpu_us(lambda: c_oracle.prefill(*inp.args()))
-        dinp = W.make_prefill_inputs(lengths, hq, hv, seed=700 + i, device=dev)
+        dinp = W.make_prefill_inputs(lengths, hq, hv, seed=700 + j, device=dev)
         g_us = gpu_us(lambda: prefill.run(*dinp.args()))
         r = None if c_us is None else c_us / g_us
         if r:
             ratios.append(r)
-        rows_p.append({"num_seqs": len(lengths), "total_seq_len": sum(lengths), "us": round(g_us, 2),
+        rows_p.append({"record": rec, "split": split, "num_seqs": len(lengths),
+                       "total_seq_len": sum(lengths), "us": round(g_us, 2),
                        "cpu_us": c_us and round(c_us, 1), "speedup_vs_cpu": r and round(r, 1)})
     geo = math.exp(sum(math.log(r) for r in ratios) / len(ratios)) if ratios else None
     print(json.dumps({
-        "metric": "contest-shape replay latency (qk4_v8: Hq=Hk=4, Hv=8, d=128)", "unit": "us",
-        "data": "synthetic (seeded shapes spanning the contest workload axes)",
+        "metric": "contest-record replay latency (qk4_v8: Hq=Hk=4, Hv=8, d=128)", "unit": "us",
+        "data": "synthetic tensors with the shapes of every contest workload record "
+                "(54 decode, 100 prefill x {even, uneven} cu_seqlens)",
         "api": "gdn_b200.decode.run / gdn_b200.prefill.run, device-resident inputs",
         "cpu": {"impl": "oracle/gdn_oracle.c (C restatement of the reference definitions)",
-                "cores": c_oracle.max_threads()},
+                "cores": c_oracle.max_threads(), "note": "timed until the CPU budget is spent"},
         "geomean_speedup_vs_cpu": geo and round(geo, 1),
+        "prefill_us_total": {s: round(sum(r["us"] for r in rows_p if r["split"] == s), 1)
+                             for s in ("even", "uneven")},
         "decode": rows_d, "prefill": rows_p}), flush=True)
 
 
@@ -644,6 +911,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-pool", action="store_true", help="skip the pooled-decode leg")
+    ap.add_argument("--no-library", action="store_true",
+                    help="skip the FlashInfer library-baseline leg")
+    ap.add_argument("--library-only", action="store_true",
+                    help="run only the FlashInfer library-baseline leg and print its JSON")
     ap.add_argument("--pool-only", action="store_true",
                     help="run only the pooled-decode leg and print its JSON (profiling runs)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -683,6 +954,12 @@ def main():
             torch.cuda.set_device(dev)
             if rank == 0:
                 print(json.dumps(run_pool_bench(args, dev)), flush=True)
+            return
+        if args.library_only:
+            dev = torch.device("cuda", local_rank)
+            torch.cuda.set_device(dev)
+            if rank == 0:
+                print(json.dumps(run_library_baseline(args, dev)), flush=True)
             return
         if args.prefill_only:
             dev = torch.device("cuda", local_rank)

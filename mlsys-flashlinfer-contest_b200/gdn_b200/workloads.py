@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
+from pathlib import Path
 from typing import Optional, Sequence
 
 import torch
@@ -262,3 +263,46 @@ def contest_prefill_cases(n_random: int = 20, seed: int = 26) -> list:
         cases.append(split_lengths(max(total, n), n, gen))
     return cases
 
+
+
+# ---- contest records (exact axes) --------------------------------------------
+# data/contest_axes.json holds the axes of every contest workload record in the
+# reference's workloads/gdn/*.md, in record order (made by data/make_contest_axes.py):
+# 100 prefill records (total_seq_len, num_seqs) and 54 decode batch sizes.  The
+# per-sequence lengths live in the (unavailable) safetensors blobs, so each prefill
+# record is replayed with the two rewrites the reference's own scripts apply:
+# "even" (total split as evenly as possible, the first total % num_seqs sequences
+# one token longer: gdn_prefill/scripts/run_local_fast_even.py:31-43) and "uneven"
+# (num_seqs - 1 one-token sequences, then one long sequence:
+# gdn_prefill/scripts/run_local_fast_uneven.py:32-46).
+_AXES_PATH = Path(__file__).resolve().parent / "data" / "contest_axes.json"
+
+
+def contest_axes() -> dict:
+    import json
+    return json.loads(_AXES_PATH.read_text())
+
+
+def even_lengths(total: int, n: int) -> list:
+    base, rem = divmod(int(total), int(n))
+    return [base + 1 if i < rem else base for i in range(int(n))]
+
+
+def uneven_lengths(total: int, n: int) -> list:
+    if total < n:
+        raise ValueError(f"uneven layout needs total_seq_len >= num_seqs ({total} < {n})")
+    return [1] * (int(n) - 1) + [int(total) - (int(n) - 1)]
+
+
+def contest_prefill_records() -> list:
+    """[(record index, split name, lengths)] for every prefill record, even then
+    uneven."""
+    out = []
+    for i, (total, n) in enumerate(contest_axes()["prefill"]):
+        out.append((i, "even", even_lengths(total, n)))
+        out.append((i, "uneven", uneven_lengths(total, n)))
+    return out
+
+
+def contest_decode_records() -> list:
+    return list(contest_axes()["decode_batch"])
