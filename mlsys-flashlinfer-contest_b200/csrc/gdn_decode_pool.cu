@@ -624,6 +624,7 @@ cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
 
 cudaError_t launch_decode_pool(const DecodePoolArgs& a, cudaStream_t s) {
   if (a.B == 0 || a.T == 0) return cudaSuccess;
+  if (decode_pool_tc_supported(a)) return launch_decode_pool_tc(a, s);
   return a.state_bf16 ? launch_dtype<true>(a, s) : launch_dtype<false>(a, s);
 }
 

@@ -1274,6 +1274,9 @@ cudaError_t launch_wait_probe(uint64_t timeout_ns, uint32_t* result, cudaStream_
 cudaError_t read_status(uint32_t* out, bool clear) {
   cudaError_t e = cudaMemcpyFromSymbol(out, g_gdn_status, sizeof(uint32_t));
   if (e != cudaSuccess) return e;
+  uint32_t pool = 0;  // the pooled tensor-core decode keeps its own word
+  if ((e = read_pool_tc_status(&pool, clear)) != cudaSuccess) return e;
+  *out |= pool;
   if (clear) {
     const uint32_t zero = 0;
     e = cudaMemcpyToSymbol(g_gdn_status, &zero, sizeof(uint32_t));

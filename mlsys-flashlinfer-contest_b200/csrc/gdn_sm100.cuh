@@ -17,6 +17,7 @@ namespace sm100 {
 enum : uint32_t {
   kStatusPrefillTimeout = 1u << 0,
   kStatusProbeTimeout = 1u << 1,
+  kStatusPoolTimeout = 1u << 2,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

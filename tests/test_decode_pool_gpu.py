@@ -65,6 +65,41 @@ def test_pool_matches_oracle(T, bf16, l2, geom):
     _state_close(inter, inter_ref, bf16)
 
 
+@pytest.mark.parametrize("T", [2, 4, 7, 8, 9, 16, 17, 24, 25, 32])
+@pytest.mark.parametrize("l2", [False, True])
+@pytest.mark.parametrize("geom", [(5, 4, 8, 7), (40, 16, 32, 45)])
+def test_pool_bf16_multi_token_tensor_core(T, l2, geom):
+    """bf16 pools with 2..32 tokens and no per-token cache take the tensor-core
+    closed form (gdn_decode_pool_tc.cu): every token bound TP in {8, 16, 24, 32},
+    zero-state and no-write slots, in-kernel L2 norm, against the token-by-token
+    oracle."""
+    B, Hq, Hv, P = geom
+    inp = W.make_decode_pool_inputs(B, T, Hq, Hv, P, seed=1000 + 7 * T + l2 + B, device="cuda",
+                                    state_bf16=True, normalized_qk=not l2)
+    o_ref, pool_ref, _ = _oracle(inp, state_bf16=True, qk_l2norm=l2)
+    pool = inp.pool.clone()
+    o = decode.run_pool(inp.q, inp.k, inp.v, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                        pool, inp.in_slots, inp.out_slots, qk_l2norm=l2)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    _state_close(pool, pool_ref, True)
+
+
+@pytest.mark.parametrize("dt_bias", [-6.0, 4.0])
+def test_pool_bf16_multi_token_decay_extremes(dt_bias):
+    """Slow decay (the state and every delta carry across the tokens) and fast
+    decay (the decay products underflow) through the closed form."""
+    inp = W.make_decode_pool_inputs(6, 8, 4, 8, 8, seed=77, device="cuda", state_bf16=True)
+    inp.dt_bias[:] = dt_bias
+    o_ref, pool_ref, _ = _oracle(inp, state_bf16=True)
+    pool = inp.pool.clone()
+    o = decode.run_pool(inp.q, inp.k, inp.v, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                        pool, inp.in_slots, inp.out_slots)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    _state_close(pool, pool_ref, True)
+
+
 @pytest.mark.parametrize("T", [12, 32])
 def test_pool_bf16_many_tokens(T):
     """bf16 multi-token steps stage T tokens in shared memory: above T = 11 that is
