@@ -69,10 +69,10 @@ def test_pool_matches_oracle(T, bf16, l2, geom):
 @pytest.mark.parametrize("l2", [False, True])
 @pytest.mark.parametrize("geom", [(5, 4, 8, 7), (40, 16, 32, 45)])
 def test_pool_bf16_multi_token_tensor_core(T, l2, geom):
-    """bf16 pools with 2..32 tokens and no per-token cache take the tensor-core
-    closed form (gdn_decode_pool_tc.cu): every token bound TP in {8, 16, 24, 32},
-    zero-state and no-write slots, in-kernel L2 norm, against the token-by-token
-    oracle."""
+    """bf16 pools without a per-token cache: 6..16 tokens take the tensor-core
+    closed form (gdn_decode_pool_tc.cu, token bounds TP = 8 and 16), fewer and more
+    tokens the token-by-token kernel; zero-state and no-write slots, in-kernel L2
+    norm, against the token-by-token oracle."""
     B, Hq, Hv, P = geom
     inp = W.make_decode_pool_inputs(B, T, Hq, Hv, P, seed=1000 + 7 * T + l2 + B, device="cuda",
                                     state_bf16=True, normalized_qk=not l2)
