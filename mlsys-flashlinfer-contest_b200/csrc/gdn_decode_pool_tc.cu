@@ -19,23 +19,24 @@
 // on CUDA cores; this one spends T + 1 per element for all T tokens.
 //
 // Persistent and warp-specialised: one CTA per SM walks (sequence, v-head) units
-// blockIdx.x, blockIdx.x + gridDim.x, ... through an NS-stage shared-memory ring.
-//   * Warp 9 (loader) looks up unit j's slots and loads its state tile, k, q and
-//     v rows and gate inputs by TMA (128-byte swizzle) as soon as a stage frees.
-//   * Warp 8 (issuer), for the unit whose loads have landed, issues the MMA into
-//     one of two TMEM buffers and the tokens' Gram MMA [K;Q][K;Q]^T, then turns
-//     the previous unit's Gram products and gates into its tables (decay
-//     products, beta, update weights).
-//   * Warps 0-3 (thread = state row) read the row's 2T dot products, solve for
-//     delta, write the T outputs and the row's update weights.
-//   * Warps 0-7 form s_T = C s_0 + sum_tau w_tau k_tau from the state tile in
-//     shared memory (16-byte chunks, two full rows per warp instruction) and
-//     stream it to the pool.
-// Hand-offs are mbarriers (full / tables / empty per stage, MMA done / TMEM free
-// per buffer); every wait is bounded (2 s), after which the CTA sets a status bit
-// and stops.  q/k L2 normalisation (x / sqrt(sum x^2 + 1e-6)) is applied as
-// per-token factors on the dot products and the update weights; q and k
-// themselves are never rescaled, so the MMA operands stay exact.
+// blockIdx.x, blockIdx.x + gridDim.x, ... through an NS-stage shared-memory ring,
+// each role a warp (or several) that hands off to the next through mbarriers:
+//   * loader (warp 13): the unit's slots, then its state tile, k, q and v rows
+//     and gate inputs by TMA (128-byte swizzle) as soon as a stage frees;
+//   * issuer (warp 14): S_0 [K;Q]^T and the tokens' Gram [K;Q][K;Q]^T by tcgen05,
+//     each into one of two TMEM buffers;
+//   * gates (warp 15): decay g_t and beta_t of the unit's tokens;
+//   * tables (warp 12, TMEM lanes 0-31): the Gram rows -> decay products and the
+//     per-token factors of the solve and of the update;
+//   * solve (warps 0-3, thread = state row): the row's 2T dot products from TMEM,
+//     delta, the T outputs and the row's update weights;
+//   * update (warps 4-11): s_T = C s_0 + sum_tau w_tau k_tau from the state tile in
+//     shared memory (16-byte chunks, two full rows per warp instruction), streamed
+//     to the pool, while the solve warps work on the next unit.
+// Every wait is bounded (2 s), after which the CTA sets a status bit and stops.
+// q/k L2 normalisation (x / sqrt(sum x^2 + 1e-6)) is applied as per-token factors
+// on the dot products and the update weights; q and k themselves are never
+// rescaled, so the MMA operands stay exact.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <string.h>
@@ -53,11 +54,15 @@ __device__ uint32_t g_pool_tc_status = 0;
 namespace {
 using namespace sm100;
 
-constexpr int kConsumerWarps = 8;
-constexpr int kIssuerWarp = kConsumerWarps;      // MMAs, gates and tables (TMEM lane quarter 0)
-constexpr int kLoaderWarp = kConsumerWarps + 1;  // slots and TMA loads
-constexpr int kThreads = 32 * (kConsumerWarps + 2);
-constexpr uint32_t kConsumerBar = 1;  // named barrier of the consumer warps
+// Warp roles (TMEM lane quarter = warp % 4).
+constexpr int kSolveWarps = 4;                  // warps 0-3: thread = state row (quarters 0-3)
+constexpr int kUpdateWarps = 8;                 // warps 4-11: the new state, 16 rows each
+constexpr int kTablesWarp = 12;                 // reads the Gram rows (lanes 0-31: quarter 0)
+constexpr int kLoaderWarp = 13;                 // slots and TMA loads
+constexpr int kIssuerWarp = 14;                 // tcgen05.mma issue
+constexpr int kGatesWarp = 15;                  // decay and beta of every token
+constexpr int kThreads = 32 * 16;
+constexpr int kRowsPerUpdateWarp = kHead / kUpdateWarps;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr uint32_t kStateBytes = kHead * kHead * 2;  // one bf16 state tile
 constexpr uint32_t kKb = 16384;                      // one 64-column block of the state tile
@@ -101,16 +106,19 @@ struct Lay {
   static constexpr uint32_t ST_GA = ST_V + 2 * kVKb;             // a: [TP][8 heads] bf16
   static constexpr uint32_t ST_GB = ST_GA + align_up(TP * 16, 128);
   static constexpr uint32_t ST_TAB = ST_GB + align_up(TP * 16, 128);
-  // tables: Ak[TP][TP], Bq[TP][TP], Ck[TP], Cq[TP], beta[TP], wgt[TP], C_final, out slot
-  static constexpr uint32_t kTabFloats = 2 * TP * TP + 4 * TP + 4;
+  // tables: Ak[TP][TP], Bq[TP][TP], Ck[TP], Cq[TP], beta[TP], wgt[TP], g[TP], C_final, out slot
+  static constexpr int T_AK = 0, T_BQ = TP * TP, T_CK = 2 * TP * TP, T_CQ = T_CK + TP, T_BET = T_CQ + TP,
+                       T_WGT = T_BET + TP, T_G = T_WGT + TP, T_CF = T_G + TP, T_SLOT = T_CF + 1;
+  static constexpr uint32_t kTabFloats = T_SLOT + 3;
   static constexpr uint32_t kStage = align_up(ST_TAB + kTabFloats * 4, 1024);
-  // CTA-wide: W[2][128][TP] (per-row update weights, double-buffered), the
-  // issuer's gates gg[TP], A_log and dt_bias, barriers
+  // CTA-wide: W[2][128][TP] (per-row update weights, double-buffered), A_log and
+  // dt_bias, barriers
   static constexpr uint32_t OFF_W = NS * kStage;
-  static constexpr uint32_t OFF_GG = OFF_W + 2 * 128 * TP * 4;
-  static constexpr uint32_t OFF_HP = OFF_GG + TP * 4;
+  static constexpr uint32_t OFF_HP = OFF_W + 2 * 128 * TP * 4;
   static constexpr uint32_t OFF_BAR = OFF_HP + 2 * kMaxHv * 4;
-  static constexpr int kBars = 3 * NS + 6;  // full, tab, empty per stage; mma, free, gram per buffer
+  // per stage: full, gates, tables, empty; per buffer: mma, D1 read, Gram, Gram
+  // read, W written, W read
+  static constexpr int kBars = 4 * NS + 12;
   static constexpr uint32_t kBytes = OFF_BAR + kBars * 8 + 16 + 1024;
   static constexpr uint32_t kTmemCols = 4 * N1 <= 64 ? 64 : 128;  // D1 and Gram, two buffers each
 };
@@ -130,15 +138,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sb = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* full = bars;            // TMA of stage s landed
-  uint64_t* tabr = bars + NS;       // tables of stage s written (issuer)
-  uint64_t* empty = bars + 2 * NS;  // stage s consumed (8 consumer warps)
-  uint64_t* mmab = bars + 3 * NS;   // S_0 [K;Q]^T in TMEM buffer b (tcgen05.commit)
-  uint64_t* freeb = mmab + 2;       // TMEM buffer b read (4 warps)
+  uint64_t* gater = bars + NS;      // gates of stage s written (gates warp)
+  uint64_t* tabr = bars + 2 * NS;   // tables of stage s written (tables warp)
+  uint64_t* empty = bars + 3 * NS;  // stage s consumed (update warps)
+  uint64_t* mmab = bars + 4 * NS;   // S_0 [K;Q]^T in D1 buffer b (tcgen05.commit)
+  uint64_t* freeb = mmab + 2;       // D1 buffer b read (solve warps)
   uint64_t* gramb = freeb + 2;      // Gram MMA of buffer b done
+  uint64_t* gfree = gramb + 2;      // Gram buffer b read (tables warp)
+  uint64_t* wready = gfree + 2;     // W buffer b written (solve warps)
+  uint64_t* wfree = wready + 2;     // W buffer b read (update warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBars);
   volatile uint32_t* abort_flag = tmem_slot + 1;
   volatile int* waited_units = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  float* gg = reinterpret_cast<float*>(smem + L::OFF_GG);
   float* hA = reinterpret_cast<float*>(smem + L::OFF_HP);
   float* hD = hA + kMaxHv;
 
@@ -150,13 +161,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
+      mbar_init(&gater[i], 1);
       mbar_init(&tabr[i], 1);
-      mbar_init(&empty[i], kConsumerWarps);
+      mbar_init(&empty[i], kUpdateWarps);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&mmab[i], 1);
-      mbar_init(&freeb[i], 4);
+      mbar_init(&freeb[i], kSolveWarps);
       mbar_init(&gramb[i], 1);
+      mbar_init(&gfree[i], 1);
+      mbar_init(&wready[i], kSolveWarps);
+      mbar_init(&wfree[i], kUpdateWarps);
     }
     fence_mbar_init();
     *abort_flag = 0u;
@@ -184,6 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
   int issued = 0;  // loader: units whose loads were issued
+  const auto unit_head = [&](int j) {
+    return static_cast<int>((blockIdx.x + static_cast<int64_t>(j) * gridDim.x) % p.Hv);
+  };
+  const auto stage_tab = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStage + L::ST_TAB); };
 
   if (warp == kLoaderWarp) {
     // ============================ loader =====================================
@@ -200,9 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int sin = __shfl_sync(0xffffffffu, slot_in, j & 31);
       const int sout = __shfl_sync(0xffffffffu, slot_out, j & 31);
-      const int64_t u = blockIdx.x + static_cast<int64_t>(j) * gridDim.x;
-      const int64_t bi = u / p.Hv;
-      const int h = static_cast<int>(u % p.Hv);
+      const int64_t bi = (blockIdx.x + static_cast<int64_t>(j) * gridDim.x) / p.Hv;
+      const int h = unit_head(j);
       const int qh = h / static_cast<int>(p.Hv / p.Hq);
       const bool has_in = sin >= 0 && sin < p.pool_size;
       if (*abort_flag || (j >= NS && !mbar_wait_nap(&empty[s], ((j / NS) - 1) & 1, kTimeoutNs))) {
@@ -217,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) {
-        reinterpret_cast<int*>(st + L::ST_TAB)[L::kTabFloats - 1] = sout;
+        reinterpret_cast<int*>(stage_tab(s))[L::T_SLOT] = sout;
         mbar_arrive_expect_tx(&full[s], (has_in ? kStateBytes : 0u) + 6u * T * 128u + 2u * T * 16u);
         if (has_in) {
           const int tile = static_cast<int>(static_cast<int64_t>(sin) * p.Hv + h);
@@ -238,67 +256,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
   } else if (warp == kIssuerWarp) {
-    // ============================ issuer =====================================
-    // Unit jj: wait for its loads, issue S_0 [K;Q]^T and the Gram MMA; then the
-    // gates and tables of unit jj - 1, whose Gram MMA has had a unit's time to run.
-    for (int jj = 0; jj <= nh; ++jj) {
-      if (jj < nh) {
-        const int s = jj % NS, b = jj & 1;
-        const uint32_t sst = sb + s * L::kStage;
-        if (*abort_flag || !wait_step(&full[s], (jj / NS) & 1) ||
-            (jj >= 2 && !wait_step(&freeb[b], ((jj >> 1) - 1) & 1))) {
-          failed = true;
-          break;
-        }
-        if (lane == 0) *waited_units = jj + 1;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t tok16 = (sst + L::ST_TOK) >> 4, s16 = (sst + L::ST_S) >> 4;
-          const uint32_t idesc = idesc_bf16(128, N1, false, false);
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {  // S_0 [K;Q]^T -> D1 buffer b
-            const uint64_t a = sdesc_sw128_f(s16 + ((ks >> 2) * kKb + (ks & 3) * 32) / 16, 16, 1024);
-            const uint64_t bd = sdesc_sw128_f(tok16 + ((ks >> 2) * L::kTokKb + (ks & 3) * 32) / 16, 16, 1024);
-            mma_bf16_ss(tmem + b * N1, a, bd, idesc, ks > 0);
-          }
-          mma_commit(&mmab[b]);
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {  // [K;Q][K;Q]^T -> Gram buffer b (rows >= N1 unused)
-            const uint64_t d = sdesc_sw128_f(tok16 + ((ks >> 2) * L::kTokKb + (ks & 3) * 32) / 16, 16, 1024);
-            mma_bf16_ss(tmem + (2 + b) * N1, d, d, idesc, ks > 0);
-          }
-          mma_commit(&gramb[b]);
-        }
-        __syncwarp();
-      }
-      const int kk = jj - 1;
-      if (kk < 0) continue;
-      // ---- tables of unit kk
-      const int s = kk % NS, b = kk & 1;
-      uint8_t* st = smem + s * L::kStage;
+    // ============================ MMA issuer =================================
+    for (int jj = 0; jj < nh; ++jj) {
+      const int s = jj % NS, b = jj & 1;
       const uint32_t sst = sb + s * L::kStage;
-      const int h = static_cast<int>((blockIdx.x + static_cast<int64_t>(kk) * gridDim.x) % p.Hv);
-      float* tab = reinterpret_cast<float*>(st + L::ST_TAB);
-      float* Ak = tab;
-      float* Bq = Ak + TP * TP;
-      float* Ck = Bq + TP * TP;
-      float* Cq = Ck + TP;
-      float* bet = Cq + TP;
-      float* wgt = bet + TP;
-      float* cfin = wgt + TP;
-      if (lane < T) {  // gates of token `lane`: rows of 8 heads, this head at h & 7
-        const float a = __uint_as_float(lds_u16(sst + L::ST_GA + lane * 16 + (h & 7) * 2) << 16);
-        const float bb = __uint_as_float(lds_u16(sst + L::ST_GB + lane * 16 + (h & 7) * 2) << 16);
-        gg[lane] = expf(log_decay(hA[h], a, hD[h]));
-        bet[lane] = sigmoidf_acc(bb);
-      }
-      __syncwarp();
-      // Gram products: lane m holds row m of [K;Q][K;Q]^T (k rows m < TP, q rows
-      // TP + t), i.e. k_m . k_tau in column tau and q_t . k_tau on lane TP + t
-      if (!wait_step(&gramb[b], (kk >> 1) & 1)) {
+      if (*abort_flag || !wait_step(&full[s], (jj / NS) & 1) ||
+          (jj >= 2 && (!wait_step(&freeb[b], ((jj >> 1) - 1) & 1) ||
+                       !wait_step(&gfree[b], ((jj >> 1) - 1) & 1)))) {
         failed = true;
         break;
       }
+      if (lane == 0) *waited_units = jj + 1;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t tok16 = (sst + L::ST_TOK) >> 4, s16 = (sst + L::ST_S) >> 4;
+        const uint32_t idesc = idesc_bf16(128, N1, false, false);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {  // S_0 [K;Q]^T -> D1 buffer b
+          const uint64_t a = sdesc_sw128_f(s16 + ((ks >> 2) * kKb + (ks & 3) * 32) / 16, 16, 1024);
+          const uint64_t bd = sdesc_sw128_f(tok16 + ((ks >> 2) * L::kTokKb + (ks & 3) * 32) / 16, 16, 1024);
+          mma_bf16_ss(tmem + b * N1, a, bd, idesc, ks > 0);
+        }
+        mma_commit(&mmab[b]);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {  // [K;Q][K;Q]^T -> Gram buffer b (rows >= N1 unused)
+          const uint64_t d = sdesc_sw128_f(tok16 + ((ks >> 2) * L::kTokKb + (ks & 3) * 32) / 16, 16, 1024);
+          mma_bf16_ss(tmem + (2 + b) * N1, d, d, idesc, ks > 0);
+        }
+        mma_commit(&gramb[b]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == kGatesWarp) {
+    // ============================ gates ======================================
+    for (int jj = 0; jj < nh; ++jj) {
+      const int s = jj % NS;
+      const uint32_t sst = sb + s * L::kStage;
+      if (*abort_flag || !wait_step(&full[s], (jj / NS) & 1)) {
+        failed = true;
+        break;
+      }
+      const int h = unit_head(jj);
+      float* tab = stage_tab(s);
+      if (lane < T) {  // token `lane`: rows of 8 heads, this head at h & 7
+        const float a = __uint_as_float(lds_u16(sst + L::ST_GA + lane * 16 + (h & 7) * 2) << 16);
+        const float bb = __uint_as_float(lds_u16(sst + L::ST_GB + lane * 16 + (h & 7) * 2) << 16);
+        tab[L::T_G + lane] = expf(log_decay(hA[h], a, hD[h]));
+        tab[L::T_BET + lane] = sigmoidf_acc(bb);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&gater[s]);
+    }
+  } else if (warp == kTablesWarp) {
+    // ============================ tables =====================================
+    for (int kk = 0; kk < nh; ++kk) {
+      const int s = kk % NS, b = kk & 1;
+      if (*abort_flag || !wait_step(&gater[s], (kk / NS) & 1) || !wait_step(&gramb[b], (kk >> 1) & 1)) {
+        failed = true;
+        break;
+      }
+      float* tab = stage_tab(s);
+      const float* gg = tab + L::T_G;
+      // Gram products: lane m holds row m of [K;Q][K;Q]^T (k rows m < TP, q rows
+      // TP + t), i.e. k_m . k_tau in column tau and q_t . k_tau on lane TP + t
       tc_fence_after();
       float g[N1];
 #pragma unroll
@@ -306,6 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       reg_fence(g);
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&gfree[b]);
       // 1 / |k_tau| for every tau (lane tau holds k_tau . k_tau in column tau), and
       // 1 / |q_t| on lane TP + t (column TP + t)
       float rk[TP];
@@ -332,112 +354,121 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tau = TP - 1; tau >= 0; --tau) {
           if (tau <= t) {
             if (krow)
-              Ak[t * TP + tau] = tau < t ? d * rkt * rk[tau] * g[tau] : 0.f;
+              tab[L::T_AK + t * TP + tau] = tau < t ? d * rkt * rk[tau] * g[tau] : 0.f;
             else
-              Bq[t * TP + tau] = p.scale * d * rq * rk[tau] * g[tau];
+              tab[L::T_BQ + t * TP + tau] = p.scale * d * rq * rk[tau] * g[tau];
             if (tau > 0) d *= gg[tau];
           }
         }
         if (krow) {
-          Ck[t] = c * rkt;
+          tab[L::T_CK + t] = c * rkt;
           float dw = 1.f;  // D[T-1][t]
           for (int s2 = t + 1; s2 < T; ++s2) dw *= gg[s2];
-          wgt[t] = dw * rkt;
-          if (t == T - 1) *cfin = c;
+          tab[L::T_WGT + t] = dw * rkt;
+          if (t == T - 1) tab[L::T_CF] = c;
         } else {
-          Cq[t] = p.scale * c * rq;
+          tab[L::T_CQ + t] = p.scale * c * rq;
         }
       } else if (lane >= T && lane < TP) {  // padding entries of the update weights
-        wgt[lane] = 0.f;
+        tab[L::T_WGT + lane] = 0.f;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tabr[s]);
     }
-  } else {
-    // ============================ consumers ==================================
-    float* Wb = reinterpret_cast<float*>(smem + L::OFF_W);
+  } else if (warp < kSolveWarps) {
+    // ============================ solve (thread = state row) =================
     for (int jj = 0; jj < nh; ++jj) {
       const int s = jj % NS, b = jj & 1;
       const uint32_t sst = sb + s * L::kStage;
-      const float* tab = reinterpret_cast<const float*>(smem + s * L::kStage + L::ST_TAB);
-      const float* Ak = tab;
-      const float* Bq = Ak + TP * TP;
-      const float* Ck = Bq + TP * TP;
-      const float* Cq = Ck + TP;
-      const float* bet = Cq + TP;
-      const float* wgt = bet + TP;
-      if (!failed && !wait_step(&tabr[s], (jj / NS) & 1)) failed = true;
-      if (!failed) mbar_wait(&full[s], (jj / NS) & 1, kTimeoutNs);  // completed: acquires the tiles
-      const float cfin = tab[2 * TP * TP + 4 * TP];
-      const int sout = reinterpret_cast<const int*>(tab)[L::kTabFloats - 1];
-      const int64_t u = blockIdx.x + static_cast<int64_t>(jj) * gridDim.x;
-      const int64_t bi = u / p.Hv;
-      const int h = static_cast<int>(u % p.Hv);
-      float* W = Wb + b * 128 * TP;
-      if (warp < 4) {  // thread = state row
-        if (!failed && !wait_step(&mmab[b], (jj >> 1) & 1)) failed = true;
-        tc_fence_after();
-        float dk[N1];
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + b * N1;
-#pragma unroll
-        for (int c0 = 0; c0 < N1; c0 += 16) tmem_ld16(taddr + c0, dk + c0);
-        tmem_wait_ld();
-        reg_fence(dk);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&freeb[b]);
-        // v[t][row] from the swizzled v tile
-        const int row = tid, vkb = row >> 6, vcol = row & 63;
-        const uint32_t vbase = sst + L::ST_V + vkb * L::kVKb + (vcol & 7) * 2;
-        float delta[TP];
-        __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + (bi * p.T * p.Hv + h) * kHead + row;
-#pragma unroll
-        for (int t = 0; t < TP; ++t) {
-          if (t < T) {
-            const float vt = __uint_as_float(lds_u16(vbase + t * 128 + (((vcol >> 3) ^ (t & 7)) << 4)) << 16);
-            float dt = Ck[t] * dk[t];
-            float o = Cq[t] * dk[TP + t];
-#pragma unroll
-            for (int tau = 0; tau < t; ++tau) {
-              dt = fmaf(Ak[t * TP + tau], delta[tau], dt);
-              o = fmaf(Bq[t * TP + tau], delta[tau], o);
-            }
-            delta[t] = bet[t] * (vt - dt);
-            o = fmaf(Bq[t * TP + t], delta[t], o);
-            if (!failed) op[static_cast<int64_t>(t) * p.Hv * kHead] = __float2bfloat16_rn(o);
-          } else {
-            delta[t] = 0.f;
-          }
-        }
-        float* wr = W + row * TP;
-#pragma unroll
-        for (int t = 0; t < TP; t += 4)
-          *reinterpret_cast<float4*>(wr + t) =
-              make_float4(wgt[t] * delta[t], wgt[t + 1] * delta[t + 1], wgt[t + 2] * delta[t + 2],
-                          wgt[t + 3] * delta[t + 3]);
-      }
-      // the consumer warps agree to stop when any of them (or another role) gave up
-      if (named_sync_or(kConsumerBar, 32 * kConsumerWarps, failed || *abort_flag != 0u)) {
+      if (*abort_flag || !wait_step(&tabr[s], (jj / NS) & 1) || !wait_step(&mmab[b], (jj >> 1) & 1)) {
         failed = true;
         break;
       }
-      // s_T = C_{T-1} s_0 + sum_tau w_tau k_tau in 16-byte chunks.  Lane l keeps
-      // chunk l % 16 of its rows, so each token's k chunk is unpacked once per
-      // group of four rows; a warp instruction covers two full rows (512
-      // contiguous bytes of the pool).
+      mbar_wait(&full[s], (jj / NS) & 1, kTimeoutNs);  // completed: acquires the stage's tiles
+      const float* tab = stage_tab(s);
+      const int64_t bi = (blockIdx.x + static_cast<int64_t>(jj) * gridDim.x) / p.Hv;
+      const int h = unit_head(jj);
+      tc_fence_after();
+      float dk[N1];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + b * N1;
+#pragma unroll
+      for (int c0 = 0; c0 < N1; c0 += 16) tmem_ld16(taddr + c0, dk + c0);
+      tmem_wait_ld();
+      reg_fence(dk);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&freeb[b]);
+      // v[t][row] from the swizzled v tile
+      const int row = tid, vkb = row >> 6, vcol = row & 63;
+      const uint32_t vbase = sst + L::ST_V + vkb * L::kVKb + (vcol & 7) * 2;
+      float delta[TP];
+      __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + (bi * p.T * p.Hv + h) * kHead + row;
+#pragma unroll
+      for (int t = 0; t < TP; ++t) {
+        if (t < T) {
+          const float vt = __uint_as_float(lds_u16(vbase + t * 128 + (((vcol >> 3) ^ (t & 7)) << 4)) << 16);
+          float dt = tab[L::T_CK + t] * dk[t];
+          float o = tab[L::T_CQ + t] * dk[TP + t];
+#pragma unroll
+          for (int tau = 0; tau < t; ++tau) {
+            dt = fmaf(tab[L::T_AK + t * TP + tau], delta[tau], dt);
+            o = fmaf(tab[L::T_BQ + t * TP + tau], delta[tau], o);
+          }
+          delta[t] = tab[L::T_BET + t] * (vt - dt);
+          o = fmaf(tab[L::T_BQ + t * TP + t], delta[t], o);
+          op[static_cast<int64_t>(t) * p.Hv * kHead] = __float2bfloat16_rn(o);
+        } else {
+          delta[t] = 0.f;
+        }
+      }
+      // update weights w_tau delta_tau of this row, into W buffer b once the update
+      // warps are done with its previous contents
+      if (jj >= 2 && !wait_step(&wfree[b], ((jj >> 1) - 1) & 1)) {
+        failed = true;
+        break;
+      }
+      float* wr = reinterpret_cast<float*>(smem + L::OFF_W) + (b * 128 + row) * TP;
+#pragma unroll
+      for (int t = 0; t < TP; t += 4)
+        *reinterpret_cast<float4*>(wr + t) =
+            make_float4(tab[L::T_WGT + t] * delta[t], tab[L::T_WGT + t + 1] * delta[t + 1],
+                        tab[L::T_WGT + t + 2] * delta[t + 2], tab[L::T_WGT + t + 3] * delta[t + 3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wready[b]);
+    }
+  } else if (warp < kSolveWarps + kUpdateWarps) {
+    // ============================ update =====================================
+    // s_T = C_{T-1} s_0 + sum_tau w_tau k_tau in 16-byte chunks.  Warp u owns rows
+    // [16 u, 16 u + 16); lane l keeps chunk l % 16 of its rows, so each token's k
+    // chunk is unpacked once per group of four rows; a warp instruction covers two
+    // full rows (512 contiguous bytes of the pool).
+    const int uw = warp - kSolveWarps;
+    const int kc = lane & 15, kbk = kc >> 3, c = kc & 7;
+    for (int jj = 0; jj < nh; ++jj) {
+      const int s = jj % NS, b = jj & 1;
+      const uint32_t sst = sb + s * L::kStage;
+      if (*abort_flag || !wait_step(&wready[b], (jj >> 1) & 1)) {
+        failed = true;
+        break;
+      }
+      mbar_wait(&full[s], (jj / NS) & 1, kTimeoutNs);  // completed: acquires the stage's tiles
+      const float* tab = stage_tab(s);
+      const float cfin = tab[L::T_CF];
+      const int sout = reinterpret_cast<const int*>(tab)[L::T_SLOT];
+      const int h = unit_head(jj);
+      const float* W = reinterpret_cast<const float*>(smem + L::OFF_W) + b * 128 * TP;
       if (!p.no_state_update && sout >= 0 && sout < p.pool_size) {
-        const int kc = lane & 15, kb = kc >> 3, c = kc & 7;
         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.pool) +
                              (static_cast<int64_t>(sout) * p.Hv + h) * (kHead * kHead) + 8 * kc;
-        const uint32_t sblk = sst + L::ST_S + kb * kKb;
-        const uint32_t tblk = sst + L::ST_TOK + kb * L::kTokKb;
+        const uint32_t sblk = sst + L::ST_S + kbk * kKb;
+        const uint32_t tblk = sst + L::ST_TOK + kbk * L::kTokKb;
 #pragma unroll 1
-        for (int grp = 0; grp < 2; ++grp) {
+        for (int grp = 0; grp < kRowsPerUpdateWarp / 8; ++grp) {
           int rows[4];
           float x[4][8];
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            rows[r] = 16 * warp + 2 * (4 * grp + r) + (lane >> 4);
+            rows[r] = kRowsPerUpdateWarp * uw + 2 * (4 * grp + r) + (lane >> 4);
             const uint4 s4 = lds128(sblk + sw128_off(rows[r], c));
             const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
@@ -474,7 +505,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (lane == 0) {
+        mbar_arrive(&wfree[b]);
+        mbar_arrive(&empty[s]);
+      }
     }
   }
   if (failed) {
@@ -561,16 +595,17 @@ cudaError_t launch_tp(const DecodePoolArgs& a, cudaStream_t s) {
 }  // namespace
 
 bool decode_pool_tc_supported(const DecodePoolArgs& a) {
-  // bf16 pool, 6..16 tokens, no per-token state cache.  Measured on B200 at B = 256
-  // and 64, Hv = 32 (us per step, token-by-token kernel vs this one): T = 4 151 vs
-  // 168, T = 6 209 vs 182, T = 8 259 vs 198, T = 12 369 vs 265, T = 16 478 vs 318;
-  // this kernel's cost per (sequence, head) is mostly fixed (the per-unit hand-offs
-  // of its pipeline), the token-by-token kernel's grows with T.  TMA needs 16-byte
-  // aligned bases and row strides (the gate rows, Hv bf16 values: Hv % 8 == 0).
+  // bf16 pool, 3..16 tokens, no per-token state cache.  Measured on B200 at B = 256
+  // and 64, Hv = 32 (us per step at B = 256, token-by-token kernel vs this one):
+  // T = 2 107 vs 123, T = 3 127 vs 125, T = 4 150 vs 130, T = 8 259 vs 151,
+  // T = 16 477 vs 258.  This kernel's cost per (sequence, head) is mostly fixed
+  // (the per-unit hand-offs of its pipeline), the token-by-token kernel's grows with
+  // T.  TMA needs 16-byte aligned bases and row strides (the gate rows, Hv bf16
+  // values: Hv % 8 == 0).
   const auto al = [](const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 == 0; };
-  return a.state_bf16 && a.T >= 6 && a.T <= 16 && a.intermediate == nullptr && a.pool_size > 0 &&
-         a.Hv % 8 == 0 && a.Hv <= kMaxHv && al(a.pool) && al(a.q) && al(a.k) && al(a.v) && al(a.a) && al(a.b) &&
-         a.pool_size * a.Hv <= 0x7fffffffLL && a.B * a.T <= 0x7fffffffLL;
+  return a.state_bf16 && a.T >= 3 && a.T <= 16 && a.intermediate == nullptr && a.pool_size > 0 &&
+         a.Hv % 8 == 0 && a.Hv <= kMaxHv && al(a.pool) && al(a.q) && al(a.k) && al(a.v) && al(a.a) &&
+         al(a.b) && a.pool_size * a.Hv <= 0x7fffffffLL && a.B * a.T <= 0x7fffffffLL;
 }
 
 cudaError_t read_pool_tc_status(uint32_t* out, bool clear) {

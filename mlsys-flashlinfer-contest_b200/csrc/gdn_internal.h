@@ -57,10 +57,11 @@ struct DecodePoolArgs {
 };
 
 cudaError_t launch_decode_pool(const DecodePoolArgs& a, cudaStream_t s);
-// Tensor-core multi-token form for bf16 pools (6 <= T <= 16, no per-token state
+// Tensor-core multi-token form for bf16 pools (3 <= T <= 16, no per-token state
 // cache): the 2T dot products of every state row with the tokens' k and q in one
 // tcgen05 MMA, then a closed-form triangular solve and one rank-T state update;
-// persistent, warp-specialised (TMA loader, MMA issuer, eight consumer warps).
+// persistent, warp-specialised (TMA loader, MMA issuer, gates, tables, solve and
+// update warps).
 bool decode_pool_tc_supported(const DecodePoolArgs& a);
 cudaError_t launch_decode_pool_tc(const DecodePoolArgs& a, cudaStream_t s);
 cudaError_t read_pool_tc_status(uint32_t* out, bool clear);

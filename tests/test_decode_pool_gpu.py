@@ -69,7 +69,7 @@ def test_pool_matches_oracle(T, bf16, l2, geom):
 @pytest.mark.parametrize("l2", [False, True])
 @pytest.mark.parametrize("geom", [(5, 4, 8, 7), (40, 16, 32, 45)])
 def test_pool_bf16_multi_token_tensor_core(T, l2, geom):
-    """bf16 pools without a per-token cache: 6..16 tokens take the tensor-core
+    """bf16 pools without a per-token cache: 3..16 tokens take the tensor-core
     closed form (gdn_decode_pool_tc.cu, token bounds TP = 8 and 16), fewer and more
     tokens the token-by-token kernel; zero-state and no-write slots, in-kernel L2
     norm, against the token-by-token oracle."""
