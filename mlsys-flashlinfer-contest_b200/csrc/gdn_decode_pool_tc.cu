@@ -106,9 +106,11 @@ struct Lay {
   static constexpr uint32_t ST_GA = ST_V + 2 * kVKb;             // a: [TP][8 heads] bf16
   static constexpr uint32_t ST_GB = ST_GA + align_up(TP * 16, 128);
   static constexpr uint32_t ST_TAB = ST_GB + align_up(TP * 16, 128);
-  // tables: Ak[TP][TP], Bq[TP][TP], Ck[TP], Cq[TP], beta[TP], wgt[TP], g[TP], C_final, out slot
+  // tables: Ak[TP][TP], Bq[TP][TP], Ck[TP], Cq[TP], beta[TP], wgt[TP], the decay
+  // products D[TP][TP], C[TP], D[T-1][t] (DW[TP]), C_final, out slot
   static constexpr int T_AK = 0, T_BQ = TP * TP, T_CK = 2 * TP * TP, T_CQ = T_CK + TP, T_BET = T_CQ + TP,
-                       T_WGT = T_BET + TP, T_G = T_WGT + TP, T_CF = T_G + TP, T_SLOT = T_CF + 1;
+                       T_WGT = T_BET + TP, T_D = T_WGT + TP, T_C = T_D + TP * TP, T_DW = T_C + TP,
+                       T_CF = T_DW + TP, T_SLOT = T_CF + 1;
   static constexpr uint32_t kTabFloats = T_SLOT + 3;
   static constexpr uint32_t kStage = align_up(ST_TAB + kTabFloats * 4, 1024);
   // CTA-wide: W[2][128][TP] (per-row update weights, double-buffered), A_log and
@@ -298,12 +300,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int h = unit_head(jj);
       float* tab = stage_tab(s);
-      if (lane < T) {  // token `lane`: rows of 8 heads, this head at h & 7
+      // token `lane`: its rows of 8 heads hold this head at h & 7; lanes >= T carry
+      // g = 1 through the products below
+      float gl = 1.f;
+      if (lane < T) {
         const float a = __uint_as_float(lds_u16(sst + L::ST_GA + lane * 16 + (h & 7) * 2) << 16);
         const float bb = __uint_as_float(lds_u16(sst + L::ST_GB + lane * 16 + (h & 7) * 2) << 16);
-        tab[L::T_G + lane] = expf(log_decay(hA[h], a, hD[h]));
+        gl = expf(log_decay(hA[h], a, hD[h]));
         tab[L::T_BET + lane] = sigmoidf_acc(bb);
       }
+      // C_t = g_0 ... g_t (inclusive product scan) and the suffix products
+      // g_t ... g_{T-1}; D[T-1][t] = the suffix product from t + 1
+      float c = gl, suf = gl;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, c, d);
+        const float z = __shfl_down_sync(0xffffffffu, suf, d);
+        if (lane >= d) c *= y;
+        if (lane + d < 32) suf *= z;
+      }
+      const float dw = __shfl_down_sync(0xffffffffu, suf, 1);
+      // row t of D: D[t][tau] = g_{tau+1} ... g_t for tau <= t
+      float dd = 1.f;
+#pragma unroll
+      for (int tau = TP - 1; tau >= 0; --tau) {
+        const float gt = __shfl_sync(0xffffffffu, gl, tau);
+        if (lane < TP && tau <= lane) {
+          tab[L::T_D + lane * TP + tau] = dd;
+          dd *= gt;
+        }
+      }
+      if (lane < TP) {
+        tab[L::T_C + lane] = c;
+        tab[L::T_DW + lane] = lane + 1 < T ? dw : 1.f;
+      }
+      if (lane == T - 1) tab[L::T_CF] = c;
       __syncwarp();
       if (lane == 0) mbar_arrive(&gater[s]);
     }
@@ -316,7 +347,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       float* tab = stage_tab(s);
-      const float* gg = tab + L::T_G;
       // Gram products: lane m holds row m of [K;Q][K;Q]^T (k rows m < TP, q rows
       // TP + t), i.e. k_m . k_tau in column tau and q_t . k_tau on lane TP + t
       tc_fence_after();
@@ -336,38 +366,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float kk2 = __shfl_sync(0xffffffffu, g[tau], tau);
         rk[tau] = L2NORM ? rsqrtf(kk2 + 1e-6f) : 1.f;
       }
+      // lane t < T: row t of Ak and Ck, wgt; lane TP + t: row t of Bq and Cq.  One
+      // code path: the row factor, the diagonal mask and the target differ.
       const bool krow = lane < T, qrow = lane >= TP && lane < TP + T;
       const int t = krow ? lane : lane - TP;
+      float rkt = 1.f, rq = 1.f;
+#pragma unroll
+      for (int i = 0; i < N1; ++i) {
+        if (i < TP && i == t) rkt = rk[i];
+        if (L2NORM && i == lane) rq = rsqrtf(g[i] + 1e-6f);
+      }
       if (krow || qrow) {
-        // C_t and D[t][tau] as running products of the gates (as the token loop
-        // multiplies the state by each g in turn)
-        float c = 1.f;
-        for (int s2 = 0; s2 <= t; ++s2) c *= gg[s2];
-        float rq = 1.f, rkt = 1.f;
+        const float f = krow ? rkt : p.scale * rq;
+        float* dst = tab + (krow ? L::T_AK : L::T_BQ) + t * TP;
+        const float* drow = tab + L::T_D + t * TP;
 #pragma unroll
-        for (int i = 0; i < N1; ++i) {
-          if (L2NORM && qrow && i == lane) rq = rsqrtf(g[i] + 1e-6f);
-          if (i < TP && i == t) rkt = rk[i];
+        for (int tau = 0; tau < TP; ++tau) {
+          const bool in = krow ? tau < t : tau <= t;
+          if (tau <= t) dst[tau] = in ? f * drow[tau] * rk[tau] * g[tau] : 0.f;
         }
-        float d = 1.f;  // D[t][tau], tau = t, t-1, ..., 0
-#pragma unroll
-        for (int tau = TP - 1; tau >= 0; --tau) {
-          if (tau <= t) {
-            if (krow)
-              tab[L::T_AK + t * TP + tau] = tau < t ? d * rkt * rk[tau] * g[tau] : 0.f;
-            else
-              tab[L::T_BQ + t * TP + tau] = p.scale * d * rq * rk[tau] * g[tau];
-            if (tau > 0) d *= gg[tau];
-          }
-        }
+        const float ct = tab[L::T_C + t];
         if (krow) {
-          tab[L::T_CK + t] = c * rkt;
-          float dw = 1.f;  // D[T-1][t]
-          for (int s2 = t + 1; s2 < T; ++s2) dw *= gg[s2];
-          tab[L::T_WGT + t] = dw * rkt;
-          if (t == T - 1) tab[L::T_CF] = c;
+          tab[L::T_CK + t] = ct * rkt;
+          tab[L::T_WGT + t] = tab[L::T_DW + t] * rkt;
         } else {
-          tab[L::T_CQ + t] = p.scale * c * rq;
+          tab[L::T_CQ + t] = f * ct;
         }
       } else if (lane >= T && lane < TP) {  // padding entries of the update weights
         tab[L::T_WGT + lane] = 0.f;
