@@ -14,9 +14,12 @@
 // so a (sequence, v-head) needs only the 2T dot products of each state row with
 // the tokens' k and q -- one tcgen05 MMA, S_0 [K;Q]^T (M = 128 rows, N = 2 TP,
 // K = 128), whose bf16 operands are exact because the pool is bf16 -- a T x T
-// triangular solve per row in fp32, and one rank-T update of the state in fp32.
-// The token-by-token form spends four multiply-adds per state element and token
-// on CUDA cores; this one spends T + 1 per element for all T tokens.
+// triangular solve per row in fp32, and the rank-T update sum_tau w_tau k_tau as a
+// second MMA whose A operand is the weights split into three bf16 terms (~24
+// mantissa bits, an fp32 weight to rounding) and whose B operand is the bf16 k
+// rows, accumulated in fp32.  The
+// token-by-token form spends four multiply-adds per state element and token on CUDA
+// cores; this one spends one per element for all T tokens.
 //
 // Persistent and warp-specialised: one CTA per SM walks (sequence, v-head) units
 // blockIdx.x, blockIdx.x + gridDim.x, ... through an NS-stage shared-memory ring,
@@ -24,15 +27,17 @@
 //   * loader (warp 13): the unit's slots, then its state tile, k, q and v rows
 //     and gate inputs by TMA (128-byte swizzle) as soon as a stage frees;
 //   * issuer (warp 14): S_0 [K;Q]^T and the tokens' Gram [K;Q][K;Q]^T by tcgen05,
-//     each into one of two TMEM buffers;
+//     each into one of two TMEM buffers; update issuer (warp 16): the state update
+//     MMA D2 = W K;
 //   * gates (warp 15): decay g_t and beta_t of the unit's tokens;
 //   * tables (warp 12, TMEM lanes 0-31): the Gram rows -> decay products and the
 //     per-token factors of the solve and of the update;
 //   * solve (warps 0-3, thread = state row): the row's 2T dot products from TMEM,
-//     delta, the T outputs and the row's update weights;
-//   * update (warps 4-11): s_T = C s_0 + sum_tau w_tau k_tau from the state tile in
-//     shared memory (16-byte chunks, two full rows per warp instruction), streamed
-//     to the pool, while the solve warps work on the next unit.
+//     delta, the T outputs and the row's update weights w_tau delta_tau, written to
+//     TMEM as three bf16 terms;
+//   * update (warps 4-11): s_T = C s_0 + D2 into the state tile in shared memory,
+//     stored to the pool by one TMA store, while the solve warps work on the next
+//     unit.
 // Every wait is bounded (2 s), after which the CTA sets a status bit and stops.
 // q/k L2 normalisation (x / sqrt(sum x^2 + 1e-6)) is applied as per-token factors
 // on the dot products and the update weights; q and k themselves are never
@@ -61,18 +66,13 @@ constexpr int kTablesWarp = 12;                 // reads the Gram rows (lanes 0-
 constexpr int kLoaderWarp = 13;                 // slots and TMA loads
 constexpr int kIssuerWarp = 14;                 // tcgen05.mma issue
 constexpr int kGatesWarp = 15;                  // decay and beta of every token
-constexpr int kThreads = 32 * 16;
-constexpr int kRowsPerUpdateWarp = kHead / kUpdateWarps;
+constexpr int kUpdIssuerWarp = 16;              // tcgen05.mma issue of the state update
+constexpr int kThreads = 32 * 17;
+constexpr uint32_t kUpdateBar = 1;  // named barrier of the update warps
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr uint32_t kStateBytes = kHead * kHead * 2;  // one bf16 state tile
 constexpr uint32_t kKb = 16384;                      // one 64-column block of the state tile
 constexpr int kMaxHv = 256;                          // A_log / dt_bias staged in shared memory
-
-__device__ __forceinline__ void st_stream_u4(void* p, uint4 v) {
-  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
 
 __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
   uint16_t r;
@@ -113,16 +113,19 @@ struct Lay {
                        T_CF = T_DW + TP, T_SLOT = T_CF + 1;
   static constexpr uint32_t kTabFloats = T_SLOT + 3;
   static constexpr uint32_t kStage = align_up(ST_TAB + kTabFloats * 4, 1024);
-  // CTA-wide: W[2][128][TP] (per-row update weights, double-buffered), A_log and
-  // dt_bias, barriers
-  static constexpr uint32_t OFF_W = NS * kStage;
-  static constexpr uint32_t OFF_HP = OFF_W + 2 * 128 * TP * 4;
+  // CTA-wide: A_log and dt_bias, barriers
+  static constexpr uint32_t OFF_HP = NS * kStage;
   static constexpr uint32_t OFF_BAR = OFF_HP + 2 * kMaxHv * 4;
-  // per stage: full, gates, tables, empty; per buffer: mma, D1 read, Gram, Gram
-  // read, W written, W read
-  static constexpr int kBars = 4 * NS + 12;
+  // per stage: full, gates, tables, empty; per TMEM buffer: S_0 [K;Q]^T done, read;
+  // Gram done, read; update weights written; update MMA done; update read
+  static constexpr int kBars = 4 * NS + 14;
   static constexpr uint32_t kBytes = OFF_BAR + kBars * 8 + 16 + 1024;
-  static constexpr uint32_t kTmemCols = 4 * N1 <= 64 ? 64 : 128;  // D1 and Gram, two buffers each
+  // TMEM columns, two buffers of each: D1 (S_0 [K;Q]^T, N1), Gram (N1), the update
+  // weights as three bf16 A operands (hi, mid, lo: 8 columns each), D2 (the update,
+  // 128)
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t C_D1 = 0, C_G = 2 * N1, C_A2 = 4 * N1, C_D2 = 256;
+  static_assert(C_A2 + 48 <= C_D2, "TMEM columns overlap");
 };
 
 template <int TP, bool L2NORM>
@@ -147,8 +150,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* freeb = mmab + 2;       // D1 buffer b read (solve warps)
   uint64_t* gramb = freeb + 2;      // Gram MMA of buffer b done
   uint64_t* gfree = gramb + 2;      // Gram buffer b read (tables warp)
-  uint64_t* wready = gfree + 2;     // W buffer b written (solve warps)
-  uint64_t* wfree = wready + 2;     // W buffer b read (update warps)
+  uint64_t* a2ready = gfree + 2;    // update weights of buffer b in TMEM (solve warps)
+  uint64_t* d2full = a2ready + 2;   // the update MMA of buffer b done (tcgen05.commit)
+  uint64_t* d2free = d2full + 2;    // D2 buffer b read (update warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBars);
   volatile uint32_t* abort_flag = tmem_slot + 1;
   volatile int* waited_units = reinterpret_cast<volatile int*>(tmem_slot + 2);
@@ -165,15 +169,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&gater[i], 1);
       mbar_init(&tabr[i], 1);
-      mbar_init(&empty[i], kUpdateWarps);
+      mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&mmab[i], 1);
       mbar_init(&freeb[i], kSolveWarps);
       mbar_init(&gramb[i], 1);
       mbar_init(&gfree[i], 1);
-      mbar_init(&wready[i], kSolveWarps);
-      mbar_init(&wfree[i], kUpdateWarps);
+      mbar_init(&a2ready[i], kSolveWarps);
+      mbar_init(&d2full[i], 1);
+      mbar_init(&d2free[i], kUpdateWarps);
     }
     fence_mbar_init();
     *abort_flag = 0u;
@@ -183,6 +188,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     hA[i] = p.A_log[i];
     hD[i] = p.dt_bias[i];
   }
+  // The token tiles start as zeros: TMA writes only rows [0, T) and [TP, TP + T),
+  // and the update MMA multiplies rows [T, TP) by zero weights, which must not
+  // meet a NaN bit pattern left in shared memory.
+  for (int st = 0; st < NS; ++st)
+    for (uint32_t i = tid; i < 2 * L::kTokKb / 16; i += kThreads)
+      sts128(sb + st * L::kStage + L::ST_TOK + 16 * i, 0u, 0u, 0u, 0u);
+  fence_async_smem();
   if (warp == kLoaderWarp && lane == 0) {
     prefetch_tmap(&tm_pool);
     prefetch_tmap(&tm_q);
@@ -259,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kIssuerWarp) {
     // ============================ MMA issuer =================================
+    // Unit jj: S_0 [K;Q]^T and the Gram MMA once its loads landed.
     for (int jj = 0; jj < nh; ++jj) {
       const int s = jj % NS, b = jj & 1;
       const uint32_t sst = sb + s * L::kStage;
@@ -277,15 +290,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < 8; ++ks) {  // S_0 [K;Q]^T -> D1 buffer b
           const uint64_t a = sdesc_sw128_f(s16 + ((ks >> 2) * kKb + (ks & 3) * 32) / 16, 16, 1024);
           const uint64_t bd = sdesc_sw128_f(tok16 + ((ks >> 2) * L::kTokKb + (ks & 3) * 32) / 16, 16, 1024);
-          mma_bf16_ss(tmem + b * N1, a, bd, idesc, ks > 0);
+          mma_bf16_ss(tmem + L::C_D1 + b * N1, a, bd, idesc, ks > 0);
         }
         mma_commit(&mmab[b]);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // [K;Q][K;Q]^T -> Gram buffer b (rows >= N1 unused)
           const uint64_t d = sdesc_sw128_f(tok16 + ((ks >> 2) * L::kTokKb + (ks & 3) * 32) / 16, 16, 1024);
-          mma_bf16_ss(tmem + (2 + b) * N1, d, d, idesc, ks > 0);
+          mma_bf16_ss(tmem + L::C_G + b * N1, d, d, idesc, ks > 0);
         }
         mma_commit(&gramb[b]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == kUpdIssuerWarp) {
+    // ============================ update MMA issuer ==========================
+    // Unit u: D2 = W_hi K + W_mid K + W_lo K (W: the solve warps' update weights
+    // split into three bf16 terms in TMEM, ~24 mantissa bits in all; K: the token
+    // tile read as an MN-major operand), once the weights are in TMEM and the
+    // update warps have read D2 buffer b for unit u - 2.
+    for (int u = 0; u < nh; ++u) {
+      const int s = u % NS, b = u & 1;
+      if (*abort_flag || !wait_step(&a2ready[b], (u >> 1) & 1) ||
+          (u >= 2 && !wait_step(&d2free[b], ((u >> 1) - 1) & 1))) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t tok16 = (sb + s * L::kStage + L::ST_TOK) >> 4;
+        const uint64_t bk = sdesc_sw128_f(tok16, L::kTokKb, 1024);
+        const uint32_t idesc = idesc_bf16(128, 128, false, true);
+#pragma unroll
+        for (int part = 0; part < 3; ++part)
+          mma_bf16_ts(tmem + L::C_D2 + 128 * b, tmem + L::C_A2 + 24 * b + 8 * part, bk, idesc, part > 0);
+        mma_commit(&d2full[b]);
       }
       __syncwarp();
     }
@@ -352,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       float g[N1];
 #pragma unroll
-      for (int c0 = 0; c0 < N1; c0 += 16) tmem_ld16(tmem + (2 + b) * N1 + c0, g + c0);
+      for (int c0 = 0; c0 < N1; c0 += 16) tmem_ld16(tmem + L::C_G + b * N1 + c0, g + c0);
       tmem_wait_ld();
       reg_fence(g);
       tc_fence_before();
@@ -413,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = unit_head(jj);
       tc_fence_after();
       float dk[N1];
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + b * N1;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + L::C_D1 + b * N1;
 #pragma unroll
       for (int c0 = 0; c0 < N1; c0 += 16) tmem_ld16(taddr + c0, dk + c0);
       tmem_wait_ld();
@@ -444,33 +482,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           delta[t] = 0.f;
         }
       }
-      // update weights w_tau delta_tau of this row, into W buffer b once the update
-      // warps are done with its previous contents
-      if (jj >= 2 && !wait_step(&wfree[b], ((jj >> 1) - 1) & 1)) {
+      // update weights w_tau delta_tau of this row as three bf16 A operands of the
+      // update MMA, w = hi + mid + lo (K = 16 per operand; weights beyond T are
+      // zero), once the update MMA of unit jj - 2 has read the buffer
+      if (jj >= 2 && !wait_step(&d2full[b], ((jj >> 1) - 1) & 1)) {
         failed = true;
         break;
       }
-      float* wr = reinterpret_cast<float*>(smem + L::OFF_W) + (b * 128 + row) * TP;
+      uint32_t whi[8], wmid[8], wlo[8];
 #pragma unroll
-      for (int t = 0; t < TP; t += 4)
-        *reinterpret_cast<float4*>(wr + t) =
-            make_float4(tab[L::T_WGT + t] * delta[t], tab[L::T_WGT + t + 1] * delta[t + 1],
-                        tab[L::T_WGT + t + 2] * delta[t + 2], tab[L::T_WGT + t + 3] * delta[t + 3]);
+      for (int e = 0; e < 8; ++e) {
+        float w0 = 0.f, w1 = 0.f;
+        if (2 * e < TP) w0 = tab[L::T_WGT + 2 * e] * delta[2 * e];
+        if (2 * e + 1 < TP) w1 = tab[L::T_WGT + 2 * e + 1] * delta[2 * e + 1];
+        whi[e] = pack_bf16x2(w0, w1);
+        const float r0 = w0 - bf16_lo(whi[e]), r1 = w1 - bf16_hi(whi[e]);
+        wmid[e] = pack_bf16x2(r0, r1);
+        wlo[e] = pack_bf16x2(r0 - bf16_lo(wmid[e]), r1 - bf16_hi(wmid[e]));
+      }
+      const uint32_t a2 = tmem + (static_cast<uint32_t>(warp * 32) << 16) + L::C_A2 + 24 * b;
+      tmem_st8u(a2, whi);
+      tmem_st8u(a2 + 8, wmid);
+      tmem_st8u(a2 + 16, wlo);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&wready[b]);
+      if (lane == 0) mbar_arrive(&a2ready[b]);
     }
   } else if (warp < kSolveWarps + kUpdateWarps) {
     // ============================ update =====================================
-    // s_T = C_{T-1} s_0 + sum_tau w_tau k_tau in 16-byte chunks.  Warp u owns rows
-    // [16 u, 16 u + 16); lane l keeps chunk l % 16 of its rows, so each token's k
-    // chunk is unpacked once per group of four rows; a warp instruction covers two
-    // full rows (512 contiguous bytes of the pool).
-    const int uw = warp - kSolveWarps;
-    const int kc = lane & 15, kbk = kc >> 3, c = kc & 7;
+    // s_T = C_{T-1} s_0 + D2: warp w reads TMEM lanes of quarter w % 4 (thread =
+    // state row) and one 64-column half of D2; s_0 comes from the state tile in
+    // shared memory, and s_T goes back into it, in place, for one TMA store of the
+    // whole tile.
+    const int quarter = warp & 3, half = (warp - kSolveWarps) >> 2;
+    const int row = 32 * quarter + lane;
+    const bool leader = warp == kSolveWarps && lane == 0;
     for (int jj = 0; jj < nh; ++jj) {
       const int s = jj % NS, b = jj & 1;
+      uint8_t* st = smem + s * L::kStage;
       const uint32_t sst = sb + s * L::kStage;
-      if (*abort_flag || !wait_step(&wready[b], (jj >> 1) & 1)) {
+      if (*abort_flag || !wait_step(&d2full[b], (jj >> 1) & 1)) {
         failed = true;
         break;
       }
@@ -478,61 +530,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* tab = stage_tab(s);
       const float cfin = tab[L::T_CF];
       const int sout = reinterpret_cast<const int*>(tab)[L::T_SLOT];
-      const int h = unit_head(jj);
-      const float* W = reinterpret_cast<const float*>(smem + L::OFF_W) + b * 128 * TP;
-      if (!p.no_state_update && sout >= 0 && sout < p.pool_size) {
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.pool) +
-                             (static_cast<int64_t>(sout) * p.Hv + h) * (kHead * kHead) + 8 * kc;
-        const uint32_t sblk = sst + L::ST_S + kbk * kKb;
-        const uint32_t tblk = sst + L::ST_TOK + kbk * L::kTokKb;
-#pragma unroll 1
-        for (int grp = 0; grp < kRowsPerUpdateWarp / 8; ++grp) {
-          int rows[4];
-          float x[4][8];
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            rows[r] = kRowsPerUpdateWarp * uw + 2 * (4 * grp + r) + (lane >> 4);
-            const uint4 s4 = lds128(sblk + sw128_off(rows[r], c));
-            const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 v2 = __fmul2_rn(make_float2(bf16_lo(sw[e]), bf16_hi(sw[e])), make_float2(cfin, cfin));
-              x[r][2 * e] = v2.x;
-              x[r][2 * e + 1] = v2.y;
-            }
-          }
-#pragma unroll 2
-          for (int tau = 0; tau < T; ++tau) {
-            const uint4 k4 = lds128(tblk + sw128_off(tau, c));
-            const uint32_t kw[4] = {k4.x, k4.y, k4.z, k4.w};
-            float2 kf[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) kf[e] = make_float2(bf16_lo(kw[e]), bf16_hi(kw[e]));
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              const float w = W[rows[r] * TP + tau];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 v2 =
-                    __ffma2_rn(kf[e], make_float2(w, w), make_float2(x[r][2 * e], x[r][2 * e + 1]));
-                x[r][2 * e] = v2.x;
-                x[r][2 * e + 1] = v2.y;
-              }
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < 4; ++r)
-            st_stream_u4(dst + static_cast<int64_t>(rows[r]) * kHead,
-                         make_uint4(pack_bf16x2(x[r][0], x[r][1]), pack_bf16x2(x[r][2], x[r][3]),
-                                    pack_bf16x2(x[r][4], x[r][5]), pack_bf16x2(x[r][6], x[r][7])));
-        }
-      }
+      const bool store = !p.no_state_update && sout >= 0 && sout < p.pool_size;
+      tc_fence_after();
+      float d2[64];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + L::C_D2 + 128 * b + 64 * half;
+      tmem_ld32(taddr, d2);
+      tmem_ld32(taddr + 32, d2 + 32);
+      tmem_wait_ld();
+      reg_fence(d2);
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&wfree[b]);
+      if (lane == 0) mbar_arrive(&d2free[b]);
+      if (store) {
+        const uint32_t sblk = sst + L::ST_S + half * kKb;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {  // 16-byte chunk c of this row's half
+          const uint32_t addr = sblk + sw128_off(row, c);
+          const uint4 s4 = lds128(addr);
+          const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 v2 = __ffma2_rn(make_float2(bf16_lo(sw[e]), bf16_hi(sw[e])), make_float2(cfin, cfin),
+                                         make_float2(d2[8 * c + 2 * e], d2[8 * c + 2 * e + 1]));
+            o[e] = pack_bf16x2(v2.x, v2.y);
+          }
+          sts128(addr, o[0], o[1], o[2], o[3]);
+        }
+        fence_async_smem();
+      }
+      named_sync(kUpdateBar, 32 * kUpdateWarps);
+      if (leader) {
+        if (store) {
+          const int tile = static_cast<int>(static_cast<int64_t>(sout) * p.Hv + unit_head(jj));
+          tma_store_3d(&tm_pool, st + L::ST_S, 0, 0, tile);
+          tma_store_3d(&tm_pool, st + L::ST_S + kKb, 64, 0, tile);
+          bulk_commit();
+          bulk_wait_read_all();  // the tile is read before the stage is refilled
+        }
         mbar_arrive(&empty[s]);
       }
     }
+    if (leader) bulk_wait_all();
   }
   if (failed) {
     *abort_flag = 1u;
