@@ -518,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3, half = (warp - kSolveWarps) >> 2;
     const int row = 32 * quarter + lane;
     const bool leader = warp == kSolveWarps && lane == 0;
+    int prev_stage = -1;  // leader: stage whose store is still in flight
     for (int jj = 0; jj < nh; ++jj) {
       const int s = jj % NS, b = jj & 1;
       uint8_t* st = smem + s * L::kStage;
@@ -560,18 +561,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_async_smem();
       }
       named_sync(kUpdateBar, 32 * kUpdateWarps);
+      // One store group per unit (empty without write-back); a stage is released
+      // once its tile has been read out, one unit later, so the leader never waits
+      // for the store it just issued.
       if (leader) {
         if (store) {
           const int tile = static_cast<int>(static_cast<int64_t>(sout) * p.Hv + unit_head(jj));
           tma_store_3d(&tm_pool, st + L::ST_S, 0, 0, tile);
           tma_store_3d(&tm_pool, st + L::ST_S + kKb, 64, 0, tile);
-          bulk_commit();
-          bulk_wait_read_all();  // the tile is read before the stage is refilled
         }
-        mbar_arrive(&empty[s]);
+        bulk_commit();
+        bulk_wait_read_1();
+        if (prev_stage >= 0) mbar_arrive(&empty[prev_stage]);
+        prev_stage = s;
       }
     }
-    if (leader) bulk_wait_all();
+    if (leader) {
+      bulk_wait_all();
+      if (prev_stage >= 0) mbar_arrive(&empty[prev_stage]);
+    }
   }
   if (failed) {
     *abort_flag = 1u;
