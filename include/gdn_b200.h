@@ -202,8 +202,8 @@ int gdn_prefill_chunked_peers(const void *q, const void *k, const void *v, const
  * one chain per pair; 2..64 = that count for every sequence of at least 2 x that
  * many chunks) and a 256-byte aligned workspace of
  * gdn_prefill_segmented_workspace_bytes(N, Hv, segments) bytes (with segments 0,
- * sized for any bound: about 1.5 x SMs x 64 KiB of piece states plus the job
- * tables).  gdn_prefill_chunked_peers takes the same three arguments.
+ * sized for any bound: at most 1.5 x SMs x 64 KiB of piece states plus the
+ * job tables).  gdn_prefill_chunked_peers takes the same three arguments.
  */
 int gdn_prefill_segmented(const void *q, const void *k, const void *v, const float *state,
                           const float *A_log, const void *a, const float *dt_bias, const void *b,
@@ -239,14 +239,17 @@ int gdn_prefill_segmented_noalloc(const void *q, const void *k, const void *v, c
                                   void *stream);
 
 /* Upper bound of the automatic piece count for these sizes (1: the call is not
- * cut).  With segments 0 the call's first kernel picks each sequence's count
- * under it from the lengths on the device: the shortest longest-chain (pass 1 +
- * pass 2 pieces, ~2 ceil(chunks / pieces); whole sequences their length) whose
- * pass 1 fits one wave of SMs, with pieces of at least 2 chunks and counts of 1
- * or at least 3, and no cut at all unless it shortens the longest chain by a
- * fifth.  The bound is 1 when the (sequence, head) pairs are more than a third
- * of the SMs, else the largest G <= 8 with num_seqs * num_v_heads * (2G - 3) <=
- * 4 x SMs and total_seq_len >= 6 G chunks. */
+ * cut).  With segments 0 the call's first kernel picks, from the lengths on the
+ * device, how many shares w (1 to 3) of a cut sequence its first piece takes and
+ * each sequence's count under the bound: the shortest longest chain ((w + 1)
+ * shares of a cut sequence of w + pieces - 1 shares, plus one chunk-time per
+ * combine step; whole sequences their length) whose pass-1 F/P jobs fit w waves
+ * of the SMs its piece-0 jobs leave free, whose pass 2 fits one wave and whose
+ * piece states fit the workspace, with pieces of at least 2 chunks and counts of
+ * 1 or at least 3, and no cut at all unless it shortens the longest chain by a
+ * fifth.  The bound is 1 when the (sequence, head) pairs are more than half the
+ * SMs, else the largest G <= 16 with num_seqs * num_v_heads * (G - 1) <= 2 x SMs
+ * and total_seq_len >= 4 G chunks. */
 int gdn_prefill_segments(int64_t total_seq_len, int64_t num_seqs, int64_t num_v_heads);
 
 /*

@@ -170,19 +170,22 @@ static bool use_recurrent(int64_t T, int64_t N, int64_t Hv) {
 
 // Upper bound on the piece count of the sequence-parallel prefill (1: one chain
 // per (sequence, head)).  The job builder picks each sequence's count under it
-// from the lengths on the device (the shortest longest-chain whose pass 1 fits
-// one wave of SMs), so the host only rules out calls that cannot gain: more
-// (sequence, head) pairs than a third of the SMs (then not even equal sequences
-// could all be cut in 3 within one wave), or too few chunks in all; the bound is
-// the largest G <= 8 with N Hv (2G - 3) <= 4 SMs and T >= 6 G chunks.
+// from the lengths on the device (the shortest longest chain whose passes fit the
+// SMs: pass 1 within one to three waves of the SMs its piece-0 jobs leave free,
+// pass 2 within one wave), so the host only rules out calls that cannot gain:
+// more (sequence, head) pairs than half the SMs (then not even equal sequences
+// could all be cut in 3 with pass 2 in one wave), or too few chunks in all; the
+// bound is the largest G <= kMaxAutoSegments with N Hv (G - 1) <= 2 SMs and
+// T >= 4 G chunks.
 static int sm_count() { return gdn::device_sm_count(); }
+constexpr int kMaxAutoSegments = 16;
 
 static int choose_segments(int64_t T, int64_t N, int64_t Hv) {
-  if (N <= 0 || Hv <= 0 || 3 * N * Hv > sm_count()) return 1;
+  if (N <= 0 || Hv <= 0 || 2 * N * Hv > sm_count()) return 1;
   const int64_t chunks = T / gdn::kChunk;
   int best = 1;
-  for (int G = 3; G <= 8; ++G)
-    if (N * Hv * (2 * G - 3) <= 4 * sm_count() && chunks >= 6 * G) best = G;
+  for (int G = 3; G <= kMaxAutoSegments; ++G)
+    if (N * Hv * (G - 1) <= 2 * sm_count() && chunks >= 4 * G) best = G;
   return best;
 }
 
@@ -190,9 +193,9 @@ int gdn_prefill_segments(int64_t T, int64_t N, int64_t Hv) {
   return use_recurrent(T, N, Hv) ? 1 : choose_segments(T, N, Hv);
 }
 
-// segments 0: the automatic form (sized for the largest bound, 8)
+// segments 0: the automatic form (sized for the largest bound)
 size_t gdn_prefill_segmented_workspace_bytes(int64_t N, int64_t Hv, int segments) {
-  if (segments == 0) return gdn::prefill_segments_bytes(N, Hv, 8, true, sm_count());
+  if (segments == 0) return gdn::prefill_segments_bytes(N, Hv, kMaxAutoSegments, true, sm_count());
   return gdn::prefill_segments_bytes(N, Hv, segments, false, sm_count());
 }
 

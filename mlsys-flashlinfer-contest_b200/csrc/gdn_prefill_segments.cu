@@ -7,22 +7,27 @@
 //     S_b = S_{a-1} P + F,   P = A_a ... A_b,  A_t = g_t (I - beta_t k_t k_t^T),
 // F the final state of the same tokens from a zero state, and P the final state
 // from the identity with v = 0 (rows of the "state" are then k rows).  So a
-// sequence cut into G pieces at chunk boundaries runs as
+// sequence cut into p pieces at chunk boundaries runs as
 //   pass 1 (one launch): piece 0 from the initial state (outputs written, its
-//          final state = the start state of piece 1) and, for pieces 1..G-2,
+//          final state = the start state of piece 1) and, for pieces 1..p-2,
 //          F_g and P_g (outputs not written);
-//   combine (one launch): S_{g+1} = S_g P_g + F_g for g = 1..G-2, fp32 on CUDA
-//          cores;
-//   pass 2 (one launch): pieces 1..G-1 from their start states (outputs, and the
+//   combine (one launch): S_{g+1} = S_g P_g + F_g for g = 1..p-2, fp32 on CUDA
+//          cores, each S_{g+1} written over F_g;
+//   pass 2 (one launch): pieces 1..p-1 from their start states (outputs, and the
 //          final state of the last piece).
-// The chain is about 2/G of the sequence's chunks long instead of all of them,
-// for (3G-4)/G times the chunk work: worth it when the pairs fill few SMs.  The
-// jobs are built on the device from cu_seqlens (a one-CTA kernel), so the host
-// never reads the lengths.  With an automatic count the host gives only an upper
-// bound and the job builder picks each sequence's count in proportion to its
-// length (a ragged batch cuts its long sequences more), lowering the bound until
-// pass 1 fits one wave of SMs and dropping the cut when it would not shorten the
-// longest chain; a forced count cuts every sequence of at least 2G chunks into G.
+// Piece 0 may be w times as long as the others (w "shares" of the sequence out
+// of w + p - 1): pass 1 then lasts w shares, and the 2 (p - 2) F/P jobs of every
+// cut sequence may take w waves of the SMs that the piece-0 jobs leave free.
+// The chain is (w + 1) shares of the sequence instead of all of it, for
+// (w + 3 (p - 1) - 2) / (w + p - 1) times the chunk work: worth it when the pairs
+// fill few SMs.  The jobs are built on the device from cu_seqlens (a one-CTA
+// kernel), so the host never reads the lengths.  With an automatic count the
+// host gives only an upper bound and the job builder picks w and each
+// sequence's count from its length (a ragged batch cuts its long sequences
+// more), for the shortest longest chain whose pass 1 fits w waves, whose pass 2
+// fits one and whose piece states fit the pool, and drops the cut when it would
+// not shorten the longest chain; a forced count cuts every sequence of at least
+// 2G chunks into G equal pieces (w = 1).
 // The reference has no counterpart: its chunked pipeline (chunk_v12.py:36-116)
 // runs one state scan per (sequence, head).
 #include <mutex>
@@ -54,16 +59,18 @@ struct SegLayout {
   int32_t* pieces;  // [N]: pieces of each sequence (1 = whole)
   int64_t* base;    // [N]: first state of each cut sequence in the pool
   float* pool;      // [cap][Hv][128][128]: per cut sequence with p pieces, the start
-                    // states of pieces 1..p-1, then F_1..F_{p-2}, then P_1..P_{p-2}
+                    // state of piece 1, then F_1..F_{p-2} (the combine overwrites
+                    // F_g with the start state of piece g + 1), then P_1..P_{p-2}
   int64_t cap;      // states in the pool
 };
 
-// States a cut into p pieces keeps: p - 1 start states + 2 (p - 2) of F and P.
-__host__ __device__ inline int64_t states_of(int p) { return p >= 2 ? 3 * p - 5 : 0; }
+// States a cut into p pieces keeps: the start state of piece 1 + p - 2 of F
+// (later the start states of pieces 2..p-1) + p - 2 of P.
+__host__ __device__ inline int64_t states_of(int p) { return p >= 2 ? 2 * p - 3 : 0; }
 
-// Pool size: a forced count keeps N (3G - 5) states; an automatic one accepts a
-// cut only when its pass 1, sum of Hv (2p - 3) over cut sequences, fits `sms`,
-// and 3p - 5 <= 1.5 (2p - 3), so 1.5 sms / Hv states hold any accepted cut.
+// Pool size: a forced count keeps N (2G - 3) states; an automatic one at most
+// 1.5 sms / Hv (the job builder keeps every cut within it; a one-wave pass 1,
+// sum of Hv (2p - 3) over cut sequences <= sms, always fits).
 int64_t pool_states(int64_t N, int64_t Hv, int G, bool adaptive, int sms) {
   const int64_t full = N * states_of(G);
   if (!adaptive) return full;
@@ -90,37 +97,47 @@ SegLayout carve(void* ws, int64_t N, int64_t Hv, int G, bool adaptive, int sms, 
   return l;
 }
 
-// Pieces of a c-chunk sequence that bring its chain (pass 1 + pass 2, 2 ceil(c /
-// p) chunks; c when whole) down to x chunks: 1 when c <= x, else at least 3 (two
-// pieces would run one after the other, no shorter than the whole), and 0 when
-// no count within the bound g, with pieces of at least 2 chunks, does it.
-__device__ int pieces_for_chain(int64_t c, int64_t x, int g) {
+// Chunk-times of one combine step (S_{g+1} = S_g P_g + F_g runs p - 2 of them
+// one after the other), charged to a cut's chain when its piece count is chosen.
+constexpr int kCombineChunks = 1;
+
+// Pieces of a c-chunk sequence that bring its chain down to x chunk-times with
+// piece 0 of w shares: 1 when c <= x (whole), else the fewest p in [3, g] (two
+// pieces would run one after the other, no shorter than the whole) with pieces
+// of at least 2 chunks and (w + 1) ceil(c / (w + p - 1)) + kCombineChunks (p - 2)
+// <= x; 0 when there is none.  No p below the one whose shares are at most
+// x / (w + 1) chunks can do, so the count starts there (32-bit arithmetic: the
+// builder runs it a few hundred times).
+__device__ int pieces_for_chain(int c, int x, int g, int w) {
   if (c <= x) return 1;
-  const int64_t half = x / 2;
-  if (half < 1) return 0;
-  const int64_t p = max((c + half - 1) / half, int64_t(3));
-  return (p <= g && c >= 2 * p) ? static_cast<int>(p) : 0;
+  const int q = x / (w + 1);
+  if (q < 2) return 0;
+  for (int p = max((c + q - 1) / q - w + 1, 3); p <= g; ++p) {
+    const int shares = w + p - 1;
+    if (c < 2 * shares) return 0;
+    if ((w + 1) * ((c + shares - 1) / shares) + kCombineChunks * (p - 2) <= x) return p;
+  }
+  return 0;
 }
 
-__device__ int64_t warp_sum(int64_t v) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ int64_t warp_max(int64_t v) {
-  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-// One warp: choose every sequence's pieces, place their states in the pool and
-// write the jobs of both passes.  Automatic form: the shortest chain x (binary
-// search over 1..longest) whose pieces keep pass 1 within `sms` CTAs, sum of Hv
-// (2p - 3) over cut sequences + Hv per whole one; no cut unless x is at most
-// 4/5 of the longest sequence.  Job tables are job-major (slot j of every
-// sequence, then slot j + 1), so a grid's real jobs come before its empty ones.
-__global__ void __launch_bounds__(32) gdn_segment_jobs_kernel(
+// Three warps, one per w, search the automatic form side by side; warp 0 then
+// places every sequence's states in the pool and writes the jobs of both passes.
+// Automatic form: for w = 1, 2, 3 the shortest
+// chain x (binary search over 1..longest) with pieces whose F/P jobs, 2 Hv (p -
+// 2) per cut sequence, fit w waves of the SMs that pass 1's N Hv piece-0 (or
+// whole-sequence) jobs leave free, whose pass-2 jobs, Hv (p - 1) per cut
+// sequence, fit one wave, and whose states fit the pool; the w with the
+// shortest x wins (ties: the smaller w), and nothing is cut unless x is at most
+// 4/5 of the longest sequence.  With w = 1 the first rule is the one-wave pass 1
+// of equal pieces.  Job tables are job-major (slot j of every sequence, then
+// slot j + 1), so a grid's piece-0 jobs come before its F/P jobs and its real
+// jobs before its empty ones.
+constexpr int kJobWarps = 3;  // one per w
+__global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
     const int64_t* cu_seqlens, int64_t N, int64_t T, int64_t Hv, int G, int adaptive, int sms,
     const float* state, float* new_state, SegLayout l) {
-  const int lane = threadIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __shared__ int s_x[kJobWarps];
   const int64_t st = Hv * kHead * kHead;  // floats of one sequence's (or piece's) states
   auto bounds = [&](int64_t n, int64_t* bos, int64_t* eos) {
     *bos = min(max(cu_seqlens[n], int64_t(0)), T);
@@ -131,44 +148,73 @@ __global__ void __launch_bounds__(32) gdn_segment_jobs_kernel(
     bounds(n, &b, &e);
     return (e - b + kChunk - 1) / kChunk;
   };
-  int64_t x = 0;  // automatic form: the accepted chain (0: no cut)
+  int x = 0;  // automatic form: the accepted chain (0: no cut)
+  int w = 1;  // shares of piece 0
   if (adaptive) {
     // chunk counts of this lane's sequences, held in registers for the search
-    // (the host sends at most SMs / 3 sequences here; beyond 4 per lane they are
-    // read again)
+    // (beyond 4 per lane they are read again); the host only sends calls of at
+    // most SMs / 2 (sequence, head) pairs here, so every sum fits 32 bits
     constexpr int kCached = 4;
-    int64_t cc[kCached];
-    int64_t m = 0;
+    int cc[kCached];
+    unsigned m = 0;
 #pragma unroll
     for (int i = 0; i < kCached; ++i) {
       const int64_t n = lane + 32 * i;
-      cc[i] = n < N ? chunks(n) : 0;
-      m = max(m, cc[i]);
+      cc[i] = n < N ? static_cast<int>(chunks(n)) : 0;
+      m = max(m, static_cast<unsigned>(cc[i]));
     }
-    for (int64_t n = lane + 32 * kCached; n < N; n += 32) m = max(m, chunks(n));
-    const int64_t cmax = warp_max(m);
-    auto cost = [&](int64_t xx) {  // pass-1 CTAs for chain xx (huge when infeasible)
-      int64_t cst = 0;
-      auto add = [&](int64_t c) {
-        const int p = pieces_for_chain(c, xx, G);
-        cst += p == 0 ? (int64_t(1) << 40) : Hv * (p >= 3 ? 2 * p - 3 : 1);
+    for (int64_t n = lane + 32 * kCached; n < N; n += 32)
+      m = max(m, static_cast<unsigned>(chunks(n)));
+    const int cmax = static_cast<int>(__reduce_max_sync(0xffffffffu, m));
+    const int64_t free_sms = static_cast<int64_t>(sms) - N * Hv;
+    auto feasible = [&](int xx, int ww) {
+      unsigned fp = 0, p2 = 0, sts = 0;
+      bool bad = false;
+      auto add = [&](int c) {
+        const int p = pieces_for_chain(c, xx, G, ww);
+        bad |= p == 0;
+        if (p >= 3) {
+          fp += static_cast<unsigned>(2 * Hv * (p - 2));
+          p2 += static_cast<unsigned>(Hv * (p - 1));
+          sts += static_cast<unsigned>(states_of(p));
+        }
       };
 #pragma unroll
       for (int i = 0; i < kCached; ++i)
         if (lane + 32 * i < N) add(cc[i]);
-      for (int64_t n = lane + 32 * kCached; n < N; n += 32) add(chunks(n));
-      return warp_sum(cst);
+      for (int64_t n = lane + 32 * kCached; n < N; n += 32) add(static_cast<int>(chunks(n)));
+      if (__any_sync(0xffffffffu, bad)) return false;
+      return __reduce_add_sync(0xffffffffu, fp) <= ww * free_sms &&
+             __reduce_add_sync(0xffffffffu, p2) <= static_cast<unsigned>(sms) &&
+             __reduce_add_sync(0xffffffffu, sts) <= l.cap;
     };
-    int64_t lo = 1, hi = cmax;  // cost(cmax) = N Hv <= sms: feasible
-    while (lo < hi) {
-      const int64_t mid = (lo + hi) / 2;
-      if (cost(mid) <= sms) hi = mid; else lo = mid + 1;
+    // this warp's w: the shortest feasible chain (binary search; feasible(cmax):
+    // nothing is cut)
+    const int ww = wid + 1;
+    int lo = 1, hi = cmax;
+    if (free_sms > 0) {
+      while (lo < hi) {
+        const int mid = (lo + hi) / 2;
+        if (feasible(mid, ww)) hi = mid; else lo = mid + 1;
+      }
+    } else {
+      lo = cmax;
     }
-    if (cmax > 0 && 5 * lo <= 4 * cmax) x = lo;
+    if (lane == 0) s_x[wid] = lo;
+    __syncthreads();
+    int best = cmax;
+    for (int j = 0; j < kJobWarps; ++j)
+      if (s_x[j] < best) {
+        best = s_x[j];
+        w = j + 1;
+      }
+    if (cmax > 0 && 5 * best <= 4 * cmax) x = best;
+    else w = 1;
   }
+  if (wid != 0) return;
   auto pieces_of = [&](int64_t n) {
     const int64_t c = chunks(n);
-    if (adaptive) return x > 0 ? max(pieces_for_chain(c, x, G), 1) : 1;
+    if (adaptive) return x > 0 ? max(pieces_for_chain(static_cast<int>(c), x, G, w), 1) : 1;
     return c >= 2 * G ? G : 1;
   };
   // pieces and pool bases: an exclusive scan of the states over the sequences,
@@ -209,13 +255,17 @@ __global__ void __launch_bounds__(32) gdn_segment_jobs_kernel(
       continue;
     }
     const int64_t b0 = l.base[n];
+    // share boundaries: piece 0 = shares [0, w), piece g >= 1 = share w + g - 1
+    const int64_t shares = w + p - 1;
+    auto edge = [&](int64_t i) { return min(bos + (i * nch / shares) * kChunk, eos); };
     auto piece = [&](int g, int64_t* b, int64_t* e) {
-      *b = bos + (g * nch / p) * kChunk;
-      *e = min(bos + ((g + 1) * nch / p) * kChunk, eos);
+      *b = g == 0 ? bos : edge(w + g - 1);
+      *e = edge(w + g);
     };
+    // start state of piece g (1: from pass 1; g >= 2: the combine's, over F_{g-1})
     auto sin = [&](int g) { return l.pool + (b0 + (g - 1)) * st; };
-    auto fst = [&](int g) { return l.pool + (b0 + (p - 1) + (g - 1)) * st; };
-    auto pst = [&](int g) { return l.pool + (b0 + (p - 1) + (p - 2) + (g - 1)) * st; };
+    auto fst = [&](int g) { return l.pool + (b0 + g) * st; };
+    auto pst = [&](int g) { return l.pool + (b0 + (p - 1) + (g - 1)) * st; };
     int64_t b, e;
     piece(0, &b, &e);
     j1(0) = SegJob{b, e, s0, sin(1), 0u, 0u};
@@ -231,18 +281,21 @@ __global__ void __launch_bounds__(32) gdn_segment_jobs_kernel(
   }
 }
 
-// S_{g+1} = S_g P_g + F_g for every cut sequence and head, g = 1..G-2.  Rows r of
-// S_{g+1} depend only on rows r of S_g, so a CTA owns 8 rows of one head and
-// walks g in order with its rows in shared memory (no CTA waits on another);
-// small CTAs (4 warps, 20 KB of shared memory) let several share an SM.  A
-// thread computes a 2 x 4 tile (rows 2w, 2w+1 of warp w; columns 4 lane .. +3):
-// per k one float4 of P and two broadcast values of S for 8 FMAs.  P goes
-// through shared memory 32 rows (16 KB) at a time, the next tile's loads in
-// flight in registers while the current tile is used.
+// S_{g+1} = S_g P_g + F_g for every cut sequence and head, g = 1..p-2, each
+// written over F_g (the pool slot after S_g).  Rows r of S_{g+1} depend only on
+// rows r of S_g and F_g, so a CTA owns 8 rows of one head and walks g in order
+// with its rows in shared memory (no CTA waits on another, and a row of F_g is
+// read before the same CTA overwrites it).  The 128-long sums are split over the
+// CTA's 8 warps (16 k each), so a step is short even when few CTAs run: every
+// lane holds an 8 x 4 tile (the CTA's rows, columns 4 lane .. +3), takes its 16
+// rows of P_g straight from global memory (one float4 per k and lane: a warp
+// reads 512 contiguous bytes) with all 16 loads in flight at once, and the
+// broadcast S values from a k-major copy of the rows; the 8 partial tiles are
+// summed through shared memory with F_g.
 constexpr int kCombRows = 8;
-constexpr int kCombThreads = 32 * kCombRows / 2;
-constexpr int kCombKTile = 32;
-constexpr int kCombTiles = kHead / kCombKTile;  // per g
+constexpr int kCombWarps = 8;
+constexpr int kCombThreads = 32 * kCombWarps;
+constexpr int kCombK = kHead / kCombWarps;  // k per warp and step
 __global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64_t N, int64_t Hv,
                                                                            SegLayout l) {
   const int64_t cta = blockIdx.x;
@@ -256,77 +309,68 @@ __global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64
   const int64_t hmat = h * kHead * kHead;
   const int64_t st = Hv * kHead * kHead;
   const int64_t b0 = l.base[n];
-  const float* sin = l.pool + b0 * st;                    // start states of pieces 1..p-1
-  const float* fst = l.pool + (b0 + (p - 1)) * st;        // F_1..F_{p-2}
-  const float* pst = l.pool + (b0 + (2 * p - 3)) * st;    // P_1..P_{p-2}
-  __shared__ __align__(16) float s_s[kCombRows][kHead];
-  __shared__ __align__(16) float p_s[kCombKTile][kHead];
+  float* sin = l.pool + b0 * st;                    // S_1, then F_g -> S_{g+1}
+  const float* pst = l.pool + (b0 + (p - 1)) * st;  // P_1..P_{p-2}
+  __shared__ __align__(16) float s_t[kHead][kCombRows];               // S_g rows, k-major
+  __shared__ __align__(16) float red[kCombWarps][kCombRows][kHead];   // partial tiles
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  const int r0 = 2 * w, c0 = 4 * lane;
-  {
-    const float* S1 = sin + hrow;  // piece 1's start state (from pass 1)
-    for (int i = t; i < kCombRows * kHead / 4; i += kCombThreads)
-      reinterpret_cast<float4*>(&s_s[0][0])[i] = reinterpret_cast<const float4*>(S1)[i];
+  const int c0 = 4 * lane, k0 = w * kCombK;
+  for (int i = t; i < kCombRows * kHead; i += kCombThreads) {
+    const int r = i / kHead, k = i % kHead;
+    s_t[k][r] = sin[hrow + r * kHead + k];  // S_1 (from pass 1)
   }
-  // tile i of the whole walk: g = 1 + i / kCombTiles, rows 32 (i % kCombTiles) .. of P_g
-  const int ntiles = (p - 2) * kCombTiles;
-  auto tile_src = [&](int i) {
-    const int g = 1 + i / kCombTiles;
-    return reinterpret_cast<const float4*>(pst + (g - 1) * st + hmat +
-                                           (i % kCombTiles) * kCombKTile * kHead);
+  __syncthreads();
+  // this warp's 16 rows of P_g, all loads in flight at once; the next step's are
+  // issued as soon as this step's products are done, so they arrive during the
+  // reduction
+  auto load_p = [&](int g, float4* pk) {
+    const float* P = pst + (g - 1) * st + hmat + static_cast<int64_t>(k0) * kHead + c0;
+#pragma unroll
+    for (int k = 0; k < kCombK; ++k) pk[k] = *reinterpret_cast<const float4*>(P + k * kHead);
   };
-  constexpr int kPer = kCombKTile * kHead / 4 / kCombThreads;  // float4 per thread and tile
-  float4 nxt[kPer];  // this thread's share of the next tile
-  {
-    const float4* src = tile_src(0);
+  float4 pk[kCombK];
+  load_p(1, pk);
+  const int rr = t >> 5;  // the row this thread sums
+  for (int g = 1; g <= p - 2; ++g) {
+    float* out = sin + g * st + hrow + rr * kHead + c0;  // F_g, then S_{g+1} over it
+    float4 v = *reinterpret_cast<const float4*>(out);     // arrives during the products
+    float acc[kCombRows][4];
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) nxt[j] = src[t + kCombThreads * j];
-  }
-  float acc[2][4];
-  for (int i = 0; i < ntiles; ++i) {
-    const int g = 1 + i / kCombTiles, k0 = (i % kCombTiles) * kCombKTile;
-    if (k0 == 0) {  // a new g: start from F_g
-      const float* F = fst + (g - 1) * st + hrow;
+    for (int r = 0; r < kCombRows; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const float4 f = *reinterpret_cast<const float4*>(F + (r0 + r) * kHead + c0);
-        acc[r][0] = f.x;
-        acc[r][1] = f.y;
-        acc[r][2] = f.z;
-        acc[r][3] = f.w;
+    for (int k = 0; k < kCombK; ++k) {
+      const float4 s0 = *reinterpret_cast<const float4*>(&s_t[k0 + k][0]);
+      const float4 s1 = *reinterpret_cast<const float4*>(&s_t[k0 + k][4]);
+      const float sv[kCombRows] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int r = 0; r < kCombRows; ++r) {
+        acc[r][0] = fmaf(sv[r], pk[k].x, acc[r][0]);
+        acc[r][1] = fmaf(sv[r], pk[k].y, acc[r][1]);
+        acc[r][2] = fmaf(sv[r], pk[k].z, acc[r][2]);
+        acc[r][3] = fmaf(sv[r], pk[k].w, acc[r][3]);
       }
     }
-    __syncthreads();  // the previous tile is consumed (and s_s written)
+    if (g + 1 <= p - 2) load_p(g + 1, pk);
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) reinterpret_cast<float4*>(&p_s[0][0])[t + kCombThreads * j] = nxt[j];
-    __syncthreads();
-    if (i + 1 < ntiles) {
-      const float4* src = tile_src(i + 1);
+    for (int r = 0; r < kCombRows; ++r)
+      *reinterpret_cast<float4*>(&red[w][r][c0]) =
+          make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    __syncthreads();  // partial tiles written; every warp is done reading s_t
+    // thread t sums column 4 (t % 32) .. +3 of row t / 32 over the warps, plus F_g
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) nxt[j] = src[t + kCombThreads * j];
+    for (int j = 0; j < kCombWarps; ++j) {
+      const float4 q = *reinterpret_cast<const float4*>(&red[j][rr][c0]);
+      v.x += q.x;
+      v.y += q.y;
+      v.z += q.z;
+      v.w += q.w;
     }
-#pragma unroll 8
-    for (int k = 0; k < kCombKTile; ++k) {
-      const float4 pk = *reinterpret_cast<const float4*>(&p_s[k][c0]);
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const float sv = s_s[r0 + r][k0 + k];
-        acc[r][0] = fmaf(sv, pk.x, acc[r][0]);
-        acc[r][1] = fmaf(sv, pk.y, acc[r][1]);
-        acc[r][2] = fmaf(sv, pk.z, acc[r][2]);
-        acc[r][3] = fmaf(sv, pk.w, acc[r][3]);
-      }
-    }
-    if (k0 + kCombKTile == kHead) {  // S_{g+1} done: to the workspace and to s_s
-      __syncthreads();  // every thread is done reading s_s for this g
-      float* out = const_cast<float*>(sin) + g * st + hrow;
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const float4 v = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-        *reinterpret_cast<float4*>(out + (r0 + r) * kHead + c0) = v;
-        *reinterpret_cast<float4*>(&s_s[r0 + r][c0]) = v;
-      }
-    }
+    *reinterpret_cast<float4*>(out) = v;
+    s_t[c0 + 0][rr] = v.x;
+    s_t[c0 + 1][rr] = v.y;
+    s_t[c0 + 2][rr] = v.z;
+    s_t[c0 + 3][rr] = v.w;
+    __syncthreads();  // S_{g+1} in s_t; red free
   }
 }
 
@@ -345,7 +389,7 @@ cudaError_t launch_prefill_segmented(const PrefillArgs& a, int G, bool adaptive,
   size_t need = 0;
   const SegLayout l = carve(ws, a.N, a.Hv, G, adaptive, sms, &need);
   if (!ws || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return cudaErrorInvalidValue;
-  gdn_segment_jobs_kernel<<<1, 32, 0, s>>>(a.cu_seqlens, a.N, a.T, a.Hv, G, adaptive ? 1 : 0, sms,
+  gdn_segment_jobs_kernel<<<1, 32 * kJobWarps, 0, s>>>(a.cu_seqlens, a.N, a.T, a.Hv, G, adaptive ? 1 : 0, sms,
                                            a.state, a.new_state, l);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

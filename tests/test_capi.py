@@ -142,23 +142,25 @@ def test_decode_pool_validation_errors():
 def test_prefill_segment_choice():
     """Upper bound of the automatic piece count (148 SMs without a GPU; the device
     picks each sequence's count under it): a head shard of config 3 may be cut,
-    the full 32-head call is not."""
+    the full 32-head call (more pairs than half the SMs) is not."""
     L = N.lib()
     assert L.gdn_prefill_segments(65536, 4, 32) == 1     # 128 pairs
-    assert L.gdn_prefill_segments(65536, 4, 16) == 1     # 64 pairs: more than a third
-    assert L.gdn_prefill_segments(65536, 4, 8) == 8
-    assert L.gdn_prefill_segments(65536, 4, 4) == 8
-    assert L.gdn_prefill_segments(8192, 1, 8) == 8
-    assert L.gdn_prefill_segments(700, 1, 8) == 1        # 10 chunks: fewer than 6 x 3
+    assert L.gdn_prefill_segments(65536, 4, 16) == 5     # 64 pairs: 64 x 4 <= 2 x 148
+    assert L.gdn_prefill_segments(65536, 4, 8) == 10
+    assert L.gdn_prefill_segments(65536, 4, 4) == 16
+    assert L.gdn_prefill_segments(8192, 1, 8) == 16
+    assert L.gdn_prefill_segments(4096, 1, 8) == 16      # 64 chunks = 4 x 16
+    assert L.gdn_prefill_segments(700, 1, 8) == 1        # 10 chunks: fewer than 4 x 3
     assert L.gdn_prefill_segments(16, 1, 8) == 1         # the recurrent kernel's size
     assert L.gdn_prefill_workspace_bytes(65536, 4, 16, 32) == 0
     ws = L.gdn_prefill_workspace_bytes(65536, 4, 4, 4)
     assert ws == L.gdn_prefill_segmented_workspace_bytes(4, 4, 0)
-    # the automatic form's state pool: 1.5 x 148 / Hv states of Hv x 64 KiB, which
-    # holds the cut the device accepts for this shard (6 pieces: 5 + 2 x 4 states)
-    assert 4 * 4 * 65536 * (5 + 2 * 4) <= ws < (16 << 20)
-    # a forced count: N (3G - 5) states
-    assert L.gdn_prefill_segmented_workspace_bytes(4, 4, 6) >= 4 * 4 * 65536 * 13
+    # the automatic form's state pool: 1.5 x 148 / Hv states of Hv x 64 KiB (the
+    # device keeps every cut within it): 55 states for this shard
+    assert 4 * 65536 * 55 <= ws < (16 << 20)
+    # a forced count: N (2G - 3) states (start state of piece 1, F and P of the
+    # middle pieces; the combine writes the later start states over F)
+    assert L.gdn_prefill_segmented_workspace_bytes(4, 4, 6) >= 4 * 4 * 65536 * 9
     assert L.gdn_prefill_segmented_workspace_bytes(4, 4, 1) == 0
 
 
