@@ -138,6 +138,7 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
     const float* state, float* new_state, SegLayout l) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   __shared__ int s_x[kJobWarps];
+  __shared__ int s_c[kJobWarps][32];  // chunk counts of up to 32 sequences, per warp
   const int64_t st = Hv * kHead * kHead;  // floats of one sequence's (or piece's) states
   auto bounds = [&](int64_t n, int64_t* bos, int64_t* eos) {
     *bos = min(max(cu_seqlens[n], int64_t(0)), T);
@@ -188,17 +189,51 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
              __reduce_add_sync(0xffffffffu, p2) <= static_cast<unsigned>(sms) &&
              __reduce_add_sync(0xffffffffu, sts) <= l.cap;
     };
-    // this warp's w: the shortest feasible chain (binary search; feasible(cmax):
-    // nothing is cut)
+    // this warp's w: the shortest feasible chain x in [1, cmax] (feasible(cmax):
+    // nothing is cut; feasibility only grows with x).  Up to 32 sequences, every
+    // lane tests its own candidate x over all of them (chunk counts in shared
+    // memory), which narrows [lo, hi] 32-fold per round; beyond that, a binary
+    // search whose tests sum over the lanes' sequences.
     const int ww = wid + 1;
     int lo = 1, hi = cmax;
-    if (free_sms > 0) {
+    if (free_sms <= 0) {
+      lo = cmax;
+    } else if (N <= 32) {
+      if (lane < N) s_c[wid][lane] = cc[0];
+      __syncwarp();
+      while (lo < hi) {
+        const int span = hi - lo;  // candidates lo .. hi - 1; hi is feasible
+        const int xj = span <= 32 ? lo + lane : lo + static_cast<int>((int64_t(span) * lane) / 32);
+        bool ok = xj < hi;
+        if (ok) {
+          unsigned fp = 0, p2 = 0, sts = 0;
+          for (int n = 0; n < N && ok; ++n) {
+            const int pc = pieces_for_chain(s_c[wid][n], xj, G, ww);
+            ok = pc != 0;
+            if (pc >= 3) {
+              fp += static_cast<unsigned>(2 * Hv * (pc - 2));
+              p2 += static_cast<unsigned>(Hv * (pc - 1));
+              sts += static_cast<unsigned>(states_of(pc));
+            }
+          }
+          ok = ok && fp <= ww * free_sms && p2 <= static_cast<unsigned>(sms) && sts <= l.cap;
+        }
+        const unsigned okm = __ballot_sync(0xffffffffu, ok);
+        if (okm) {
+          const int j = __ffs(okm) - 1;  // the smallest feasible candidate
+          const int xprev = j == 0 ? lo - 1 : __shfl_sync(0xffffffffu, xj, j - 1);
+          hi = __shfl_sync(0xffffffffu, xj, j);
+          lo = xprev + 1;
+        } else {
+          lo = __shfl_sync(0xffffffffu, xj, 31) + 1;  // every candidate below hi failed
+          if (span <= 32) lo = hi;
+        }
+      }
+    } else {
       while (lo < hi) {
         const int mid = (lo + hi) / 2;
         if (feasible(mid, ww)) hi = mid; else lo = mid + 1;
       }
-    } else {
-      lo = cmax;
     }
     if (lane == 0) s_x[wid] = lo;
     __syncthreads();
@@ -256,8 +291,12 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
     }
     const int64_t b0 = l.base[n];
     // share boundaries: piece 0 = shares [0, w), piece g >= 1 = share w + g - 1
-    const int64_t shares = w + p - 1;
-    auto edge = [&](int64_t i) { return min(bos + (i * nch / shares) * kChunk, eos); };
+    // (32-bit division: a sequence has at most 2^25 chunks and i <= 18 shares)
+    const unsigned shares = static_cast<unsigned>(w + p - 1);
+    const unsigned nch32 = static_cast<unsigned>(nch);
+    auto edge = [&](int i) {
+      return min(bos + static_cast<int64_t>(static_cast<unsigned>(i) * nch32 / shares) * kChunk, eos);
+    };
     auto piece = [&](int g, int64_t* b, int64_t* e) {
       *b = g == 0 ? bos : edge(w + g - 1);
       *e = edge(w + g);

@@ -3,8 +3,9 @@ sequences cut into pieces whose start states come from each piece's transition
 matrix (S_{g+1} = S_g P_g + F_g), against the CPU oracles on the same inputs.
 Cases cover cut and uncut sequences in one call, empty and partial-chunk
 sequences, zero and given initial states, slow decay (the state carries across
-every piece boundary), q/k L2 norm, the gdn_prefill dispatch with a workspace,
-and the fused-gather routing that the multi-GPU path uses."""
+every piece boundary), q/k L2 norm, automatic cuts whose first piece is longer
+than the others, the gdn_prefill dispatch with a workspace, and the fused-gather
+routing that the multi-GPU path uses."""
 import ctypes
 
 import numpy as np
@@ -69,6 +70,37 @@ def test_segmented_close_to_chunked_long(lengths):
     o2, s2 = prefill.run_segmented(*inp.args(), segments=0)
     PT.assert_o_close(o2, o1)
     PT.assert_state_close(s2, s1.cpu().numpy(), PT.STATE_REL)
+
+
+# Automatic cuts with piece 0 of two shares (w = 2 under the job builder's rules):
+# 64 or 32 (sequence, head) pairs leave too few SMs for one wave of F/P jobs of
+# equal pieces, so the F/P jobs take two waves while piece 0 runs twice as long.
+# (lengths, Hq, Hv): 4 x 2048 at 16 heads (3 pieces each), a ragged batch at 16
+# heads (5 and 4 pieces, two sequences whole), 4 x 4096 at 8 heads (4 pieces).
+UNEVEN = [([2048] * 4, 8, 16), ([4096, 3000, 2048, 1024], 8, 16), ([4096] * 4, 4, 8)]
+
+
+@pytest.mark.parametrize("lengths,hq,hv", UNEVEN)
+def test_segmented_uneven_pieces_match_oracle(lengths, hq, hv):
+    inp = W.make_prefill_inputs(lengths, hq, hv, seed=60 + len(lengths) + hv,
+                                zero_state_every_other=True)
+    assert prefill.segments_for(sum(lengths), len(lengths), hv) >= 3
+    o_ref, s_ref = C.prefill(*inp.args(), nthreads=8)
+    o, ns = prefill.run_segmented(*PT.to_device(inp).args(), segments=0)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    PT.assert_state_close(ns, s_ref.numpy(), PT.STATE_REL)
+
+
+def test_segmented_uneven_slow_decay():
+    # the state carries across every piece boundary (dt_bias = -6)
+    inp = W.make_prefill_inputs([2048] * 4, 8, 16, seed=77)
+    inp.dt_bias[:] = -6.0
+    o_ref, s_ref = C.prefill(*inp.args(), nthreads=8)
+    o, ns = prefill.run_segmented(*PT.to_device(inp).args(), segments=0)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    PT.assert_state_close(ns, s_ref.numpy(), PT.STATE_REL)
 
 
 def test_dispatch_with_workspace_takes_segmented():
