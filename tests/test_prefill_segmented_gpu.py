@@ -93,14 +93,23 @@ def test_segmented_uneven_pieces_match_oracle(lengths, hq, hv):
 
 
 def test_segmented_uneven_slow_decay():
-    # the state carries across every piece boundary (dt_bias = -6)
-    inp = W.make_prefill_inputs([2048] * 4, 8, 16, seed=77)
+    # the state carries across every piece boundary (dt_bias = -6: per-token decay
+    # ~0.9975).  The bf16 state operand of the chunk step bounds the accuracy of any
+    # path at this decay (the one-chain kernel reaches ~1.0e-3 at 2048 such tokens),
+    # so the length stays at 1536 tokens (still cut in 3, shares 2, 1, 1), and the cut
+    # must add no error of its own to the one-chain kernel's
+    inp = W.make_prefill_inputs([1536] * 4, 8, 16, seed=77)
     inp.dt_bias[:] = -6.0
     o_ref, s_ref = C.prefill(*inp.args(), nthreads=8)
-    o, ns = prefill.run_segmented(*PT.to_device(inp).args(), segments=0)
+    d = PT.to_device(inp)
+    assert prefill.segments_for(1536 * 4, 4, 16) >= 3
+    o, ns = prefill.run_segmented(*d.args(), segments=0)
+    _, ns1 = prefill.run_chunked(*d.args())
     torch.cuda.synchronize()
     PT.assert_o_close(o, o_ref)
-    PT.assert_state_close(ns, s_ref.numpy(), PT.STATE_REL)
+    err = PT.assert_state_close(ns, s_ref.numpy(), PT.STATE_REL)
+    err1 = PT.state_rel_per_head(ns1, s_ref.numpy())
+    assert err <= 1.05 * err1 + 1e-5, (err, err1)
 
 
 def test_dispatch_with_workspace_takes_segmented():
