@@ -489,40 +489,79 @@ def time_calls(fn, reps, dev, dist):
 def prefill_e2e(cpu_inp, dev, reps, dist):
     """End to end through the public destination-passing API (prefill.launch): each
     call copies q, k, v, a, b, cu_seqlens and the initial states from pinned host
-    memory, runs, and copies o and the final states back to pinned host memory,
-    all inside the timed region (one stream, calls back to back)."""
+    memory, runs, and copies o and the final states back to pinned host memory, all
+    inside the timed region.  As a server taking a stream of prefill requests would,
+    the copies run on their own streams with two device buffer sets: call i+1's
+    inputs cross PCIe while call i's kernels run, and call i's outputs come back
+    during call i+1 (PCIe carries both directions at once)."""
     from gdn_b200 import prefill
     names = ("q", "k", "v", "state", "a", "b", "cu_seqlens")
     host = {n: getattr(cpu_inp, n).pin_memory() for n in names if getattr(cpu_inp, n) is not None}
-    devb = {n: torch.empty_like(t, device=dev) for n, t in host.items()}
+    devb = [{n: torch.empty_like(t, device=dev) for n, t in host.items()} for _ in range(2)]
     A_log, dt_bias = cpu_inp.A_log.to(dev), cpu_inp.dt_bias.to(dev)
     Nseq = cpu_inp.cu_seqlens.numel() - 1
     hv = cpu_inp.v.shape[1]
-    o_dev = torch.empty_like(devb["v"])
-    ns_dev = torch.empty((Nseq, hv, D, D), dtype=torch.float32, device=dev)
-    o_host = torch.empty(o_dev.shape, dtype=o_dev.dtype, pin_memory=True)
-    ns_host = torch.empty(ns_dev.shape, dtype=ns_dev.dtype, pin_memory=True)
+    o_dev = [torch.empty_like(devb[0]["v"]) for _ in range(2)]
+    ns_dev = [torch.empty((Nseq, hv, D, D), dtype=torch.float32, device=dev) for _ in range(2)]
+    o_host = [torch.empty(o_dev[0].shape, dtype=o_dev[0].dtype, pin_memory=True) for _ in range(2)]
+    ns_host = [torch.empty(ns_dev[0].shape, dtype=ns_dev[0].dtype, pin_memory=True)
+               for _ in range(2)]
     ws_bytes = prefill.workspace_bytes(cpu_inp.q.shape[0], Nseq, cpu_inp.q.shape[1], hv)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]     # inputs of set j landed
+    ev_used = [torch.cuda.Event() for _ in range(2)]   # the call is done with set j
+    ev_out = [torch.cuda.Event() for _ in range(2)]    # outputs of set j copied back
 
-    def call():
-        for n, t in host.items():
-            devb[n].copy_(t, non_blocking=True)
-        prefill.launch(devb["q"], devb["k"], devb["v"], devb.get("state"), A_log, devb["a"], dt_bias,
-                       devb["b"], devb["cu_seqlens"], cpu_inp.scale, o_dev, ns_dev,
+    def issue(i):
+        j = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_used[j])
+            for n, t in host.items():
+                devb[j][n].copy_(t, non_blocking=True)
+            ev_in[j].record(s_in)
+        stream.wait_event(ev_in[j])
+        stream.wait_event(ev_out[j])
+        d = devb[j]
+        prefill.launch(d["q"], d["k"], d["v"], d.get("state"), A_log, d["a"], dt_bias, d["b"],
+                       d["cu_seqlens"], cpu_inp.scale, o_dev[j], ns_dev[j],
                        workspace=ws if ws_bytes else None)
-        o_host.copy_(o_dev, non_blocking=True)
-        ns_host.copy_(ns_dev, non_blocking=True)
+        ev_used[j].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_used[j])
+            o_host[j].copy_(o_dev[j], non_blocking=True)
+            ns_host[j].copy_(ns_dev[j], non_blocking=True)
+            ev_out[j].record(s_out)
 
-    ms, _ = time_calls(call, reps, dev, dist)
+    for i in range(3):
+        issue(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    s_in.wait_stream(stream)
+    s_out.wait_stream(stream)
+    for i in range(reps):
+        issue(i)
+    stream.wait_event(ev_out[(reps - 1) % 2])
+    stream.wait_event(ev_out[reps % 2])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / reps
     h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = o_host.numel() * o_host.element_size() + ns_host.numel() * ns_host.element_size()
+    d2h = o_host[0].numel() * o_host[0].element_size() + ns_host[0].numel() * ns_host[0].element_size()
     T = cpu_inp.q.shape[0]
     return {"value": round(T / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_call": round(ms, 4), "calls": reps,
             "api": "gdn_b200.prefill.launch (destination passing)",
             "copies": "H2D of every input and D2H of o and the final states inside the timed "
-                      "region, serialised with the call on one stream"}
+                      "region; copies on their own streams with two buffer sets, so call "
+                      "i+1's inputs and call i-1's outputs cross PCIe while call i runs"}
 
 
 def cpu_prefill(lengths, hq, hv, seed, zero_every_other):
@@ -589,7 +628,7 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
             if full is not None and args.prefill_seqs == 4 and args.prefill_len == 16384 and seg_bound == 1:
                 r["roofline"]["traffic"] = int(full * hv / HV)  # this rank's heads
         if not args.no_e2e:
-            r["e2e"] = prefill_e2e(cpu_inp, dev, 3 if name == "config3" else 10, dist)
+            r["e2e"] = prefill_e2e(cpu_inp, dev, 8 if name == "config3" else 30, dist)
         if rank == 0 and world == 1 and not args.no_cpu:
             r["cpu_baseline"] = cpu_prefill(lengths, hq, hv, seed, zero_eo)
         res[name] = r
