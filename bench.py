@@ -611,15 +611,17 @@ def run_prefill_bench(args, rank, world, local_rank, dev, dist):
         ws_bytes = prefill.workspace_bytes(T, Nseq, hq, hv)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
         reps = args.prefill_steps if name == "config3" else max(args.prefill_steps * 5, 20)
-        ms, _ = time_calls(lambda: prefill.launch(*inp.args(), out, ns, workspace=ws if ws_bytes else None),
-                           reps, dev, dist)
+        ms, per = time_calls(lambda: prefill.launch(*inp.args(), out, ns, workspace=ws if ws_bytes else None),
+                             reps, dev, dist)
         seg_bound = prefill.segments_for(T, Nseq, hv)
         path = ("gdn_b200.prefill.launch: segmented prefill (job builder, pass 1, combine, pass 2; "
                 f"pieces picked on the device under a bound of {seg_bound})" if seg_bound > 1
                 else "gdn_b200.prefill.launch (fused chunked kernel)")
         # every rank walks all T tokens for its heads: the job's rate is T / (max-over-ranks time)
         r = {"metric": "gdn_prefill_tokens_per_s", "value": round(T / (ms / 1e3), 1),
-             "unit": "tokens/s", "ms_per_call": round(ms, 4), "steps": reps, "workload": desc,
+             "unit": "tokens/s", "ms_per_call": round(ms, 4),
+             "ms_per_call_median_rank0": round(statistics.median(per), 4), "steps": reps,
+             "workload": desc,
              "total_tokens": T, "num_seqs": Nseq, "path": path,
              "gpu_launches_per_call": 4 if seg_bound > 1 else 1,
              "roofline": prefill_roofline(T, Nseq, hq, hv, ms)}
@@ -965,7 +967,7 @@ def main():
                     help="sequences per rank (default 256 = BASELINE config 1; smaller only for profiling)")
     ap.add_argument("--prefill-seqs", type=int, default=4)
     ap.add_argument("--prefill-len", type=int, default=16384)
-    ap.add_argument("--prefill-steps", type=int, default=10)
+    ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the prefill leg and print its JSON (profiling runs)")
     ap.add_argument("--replay", action="store_true",
