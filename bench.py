@@ -314,7 +314,13 @@ def run_e2e(args, inp, dev, stream, dist, world):
     to pinned host memory, inside the timed region; the state stays resident in
     HBM (the decode state cache).  As a serving loop would, the copies run on their
     own streams with two device buffer sets, so step i+1's inputs cross PCIe while
-    step i's kernel runs and step i's output comes back during step i+1."""
+    step i's kernel runs and step i's output comes back during step i+1.  The loop
+    is timed twice: issued step by step from Python ("eager"), and as replays of a
+    CUDA graph that holds 40 such pipelined steps (copies, kernel launches and their
+    cross-stream event order, captured once), which is how a serving loop drives
+    it without the host's per-step launch cost.  The graph replays give the value:
+    the eager loop measures the host's Python speed as much as the transfer (its
+    windows are reported beside it)."""
     from gdn_b200 import decode
     host, dbuf = {}, [{}, {}]
     B = inp.v.shape[0]
@@ -338,62 +344,110 @@ def run_e2e(args, inp, dev, stream, dist, world):
     ev_used = [torch.cuda.Event() for _ in range(2)]   # kernel done with buffer i
     ev_out = [torch.cuda.Event() for _ in range(2)]    # output i copied back
 
-    def issue(i):
+    def issue(i, main, first=False):
+        # first: inside a graph capture, the first use of buffer i % 2 (nothing of
+        # this capture to wait for yet)
         j = i % 2
         with torch.cuda.stream(s_in):
-            s_in.wait_event(ev_used[j])
+            if not first:
+                s_in.wait_event(ev_used[j])
             for n in host:
                 dbuf[j][n].copy_(host[n][i % nsteps_host], non_blocking=True)
             ev_in[j].record(s_in)
-        stream.wait_event(ev_in[j])
-        stream.wait_event(ev_out[j])  # output buffer j read back
+        main.wait_event(ev_in[j])
+        if not first:
+            main.wait_event(ev_out[j])  # output buffer j read back
         d = dbuf[j]
         decode.launch(d["q"], d["k"], d["v"], states[i % 2], inp.A_log, d["a"], inp.dt_bias, d["b"],
                       inp.scale, o_dev[j], states[(i + 1) % 2])
-        ev_used[j].record(stream)
+        ev_used[j].record(main)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_used[j])
             o_host[j].copy_(o_dev[j], non_blocking=True)
             ev_out[j].record(s_out)
 
+    def timed_windows(run_window, nsteps):
+        ms_list = []
+        for _ in range(windows):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run_window()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms_list.append(e0.elapsed_time(e1))
+        t = torch.tensor(ms_list, dtype=torch.float64, device=dev)
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_list = [float(x) for x in t.tolist()]
+        per = sorted(w / nsteps * 1e3 for w in ms_list)
+        return sum(ms_list), per
+
+    def summary(ms, per, nsteps):
+        med = statistics.median(per)
+        return {"steps": nsteps * windows, "us_per_step": round(ms / (nsteps * windows) * 1e3, 2),
+                "us_per_step_median_window": round(med, 2),
+                "us_per_step_windows": [round(x, 2) for x in per],
+                "spread_pct": round((per[-1] - per[0]) / med * 100, 2)}
+
+    # eager: five windows of `steps` pipelined steps issued from Python
     for i in range(4):
-        issue(i)
+        issue(i, stream)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    # five windows of `steps` pipelined steps each: the value is their total; the
-    # windows' spread shows the run-to-run noise of the host copies
-    windows_ms = []
-    for w in range(windows):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+
+    def eager_window():
         s_in.wait_stream(stream)
         s_out.wait_stream(stream)
         for i in range(steps):
-            issue(i)
+            issue(i, stream)
         stream.wait_event(ev_out[(steps - 1) % 2])
         stream.wait_event(ev_out[steps % 2])
-        e1.record(stream)
-        torch.cuda.synchronize()
-        windows_ms.append(e0.elapsed_time(e1))
-    t = torch.tensor(windows_ms, dtype=torch.float64, device=dev)
+
+    eager_ms, eager_per = timed_windows(eager_window, steps)
+
+    # graph: 40 pipelined steps captured once (side streams forked from and joined
+    # back to the capture stream), replayed; a replay starts with its first upload
+    # and ends with its last read-back, ~1 % of 40 steps
+    g_steps = 40
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=cap):
+        s_in.wait_stream(cap)
+        s_out.wait_stream(cap)
+        for i in range(g_steps):
+            issue(i, cap, first=i < 2)
+        cap.wait_stream(s_in)
+        cap.wait_stream(s_out)
+    reps = max(steps // g_steps, 1)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
     if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    windows_ms = [float(x) for x in t.tolist()]
-    ms = sum(windows_ms)
-    total_steps = steps * windows
-    value = B_PER_RANK * HV * UNIT_BYTES * world * total_steps / (ms / 1e3) / 1e9
-    per_step_us = sorted(w / steps * 1e3 for w in windows_ms)
-    med = statistics.median(per_step_us)
-    return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "steps": total_steps, "us_per_step": round(ms / total_steps * 1e3, 2),
-            "us_per_step_median_window": round(med, 2),
-            "us_per_step_windows": [round(x, 2) for x in per_step_us],
-            "spread_pct": round((per_step_us[-1] - per_step_us[0]) / med * 100, 2),
-            "api": "gdn_b200.decode.launch (destination passing)",
-            "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's kernel (two buffer sets, "
-                          "copy streams); every copy is inside the timed region",
-            "state": "resident in HBM across steps"}
+        dist.barrier()
+
+    def graph_window():
+        for _ in range(reps):
+            graph.replay()
+
+    g_ms, g_per = timed_windows(graph_window, reps * g_steps)
+    total_steps = reps * g_steps * windows
+    value = B_PER_RANK * HV * UNIT_BYTES * world * total_steps / (g_ms / 1e3) / 1e9
+    eager_value = B_PER_RANK * HV * UNIT_BYTES * world * steps * windows / (eager_ms / 1e3) / 1e9
+    out = {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h}
+    out.update(summary(g_ms, g_per, reps * g_steps))
+    out.update({"api": "gdn_b200.decode.launch (destination passing), 40 pipelined steps "
+                       "captured in a CUDA graph and replayed",
+                "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's kernel (two "
+                              "buffer sets, copy streams); every copy is inside the timed region",
+                "eager": dict(value=round(eager_value, 2), **summary(eager_ms, eager_per, steps)),
+                "state": "resident in HBM across steps"})
+    del graph
+    return out
+
 
 def run_pool_bench(args, dev):
     """Pooled decode (C ABI gdn_decode_pool) at the config-1 batch: B = 256 sequences
