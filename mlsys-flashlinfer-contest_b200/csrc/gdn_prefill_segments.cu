@@ -252,8 +252,11 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
     if (adaptive) return x > 0 ? max(pieces_for_chain(static_cast<int>(c), x, G, w), 1) : 1;
     return c >= 2 * G ? G : 1;
   };
-  // pieces and pool bases: an exclusive scan of the states over the sequences,
-  // 32 at a time; a sequence whose states would pass the pool's end stays whole
+  // per block of 32 sequences: pieces and pool bases (an exclusive scan of the
+  // states; a sequence whose states would pass the pool's end stays whole), then
+  // the jobs of both passes, each lane writing its own sequence's slots (the
+  // real ones, then the empty rest) from registers
+  const SegJob none{0, 0, nullptr, nullptr, 0u, 0u};
   int64_t running = 0;
   for (int64_t n0 = 0; n0 < N; n0 += 32) {
     const int64_t n = n0 + lane;
@@ -265,58 +268,56 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
       if (lane >= o) incl += y;
     }
     const int64_t total = __shfl_sync(0xffffffffu, incl, 31);
-    if (n < N) {
-      if (running + incl > l.cap) p = 1;
-      l.pieces[n] = p;
-      l.base[n] = running + incl - need;
-    }
+    if (running + incl > l.cap) p = 1;
+    const int64_t b0 = running + incl - need;
     running += total;
-  }
-  // jobs (the same lane handled sequence n above)
-  const SegJob none{0, 0, nullptr, nullptr, 0u, 0u};
-  for (int64_t n = lane; n < N; n += 32) {
+    if (n >= N) continue;
+    l.pieces[n] = p;
+    l.base[n] = b0;
     int64_t bos, eos;
     bounds(n, &bos, &eos);
     const int64_t nch = (eos - bos + kChunk - 1) / kChunk;
-    const int p = l.pieces[n];
     auto j1 = [&](int j) -> SegJob& { return l.jobs1[j * N + n]; };
     auto j2 = [&](int j) -> SegJob& { return l.jobs2[j * N + n]; };
     const float* s0 = state ? state + n * st : nullptr;
     float* s_out = new_state + n * st;
-    for (int j = 0; j < 2 * G - 3; ++j) j1(j) = none;
-    for (int j = 0; j < G - 1; ++j) j2(j) = none;
+    int used1 = 1, used2 = 0;  // slots with real jobs
     if (p < 2) {
       j1(0) = SegJob{bos, eos, s0, s_out, 0u, 0u};
-      continue;
+    } else {
+      // share boundaries: piece 0 = shares [0, w), piece g >= 1 = share w + g - 1
+      // (32-bit division: a sequence has at most 2^25 chunks and i <= 64 shares)
+      const unsigned shares = static_cast<unsigned>(w + p - 1);
+      const unsigned nch32 = static_cast<unsigned>(nch);
+      auto edge = [&](int i) {
+        return min(bos + static_cast<int64_t>(static_cast<unsigned>(i) * nch32 / shares) * kChunk,
+                   eos);
+      };
+      auto piece = [&](int g, int64_t* b, int64_t* e) {
+        *b = g == 0 ? bos : edge(w + g - 1);
+        *e = edge(w + g);
+      };
+      // start state of piece g (1: from pass 1; g >= 2: the combine's, over F_{g-1})
+      auto sin = [&](int g) { return l.pool + (b0 + (g - 1)) * st; };
+      auto fst = [&](int g) { return l.pool + (b0 + g) * st; };
+      auto pst = [&](int g) { return l.pool + (b0 + (p - 1) + (g - 1)) * st; };
+      int64_t b, e;
+      piece(0, &b, &e);
+      j1(0) = SegJob{b, e, s0, sin(1), 0u, 0u};
+      for (int g = 1; g <= p - 2; ++g) {
+        piece(g, &b, &e);
+        j1(2 * g - 1) = SegJob{b, e, nullptr, fst(g), kJobNoOut, 0u};
+        j1(2 * g) = SegJob{b, e, nullptr, pst(g), kJobIdentity | kJobNoV | kJobNoOut, 0u};
+      }
+      for (int g = 1; g <= p - 1; ++g) {
+        piece(g, &b, &e);
+        j2(g - 1) = SegJob{b, e, sin(g), g == p - 1 ? s_out : nullptr, 0u, 0u};
+      }
+      used1 = 2 * p - 3;
+      used2 = p - 1;
     }
-    const int64_t b0 = l.base[n];
-    // share boundaries: piece 0 = shares [0, w), piece g >= 1 = share w + g - 1
-    // (32-bit division: a sequence has at most 2^25 chunks and i <= 18 shares)
-    const unsigned shares = static_cast<unsigned>(w + p - 1);
-    const unsigned nch32 = static_cast<unsigned>(nch);
-    auto edge = [&](int i) {
-      return min(bos + static_cast<int64_t>(static_cast<unsigned>(i) * nch32 / shares) * kChunk, eos);
-    };
-    auto piece = [&](int g, int64_t* b, int64_t* e) {
-      *b = g == 0 ? bos : edge(w + g - 1);
-      *e = edge(w + g);
-    };
-    // start state of piece g (1: from pass 1; g >= 2: the combine's, over F_{g-1})
-    auto sin = [&](int g) { return l.pool + (b0 + (g - 1)) * st; };
-    auto fst = [&](int g) { return l.pool + (b0 + g) * st; };
-    auto pst = [&](int g) { return l.pool + (b0 + (p - 1) + (g - 1)) * st; };
-    int64_t b, e;
-    piece(0, &b, &e);
-    j1(0) = SegJob{b, e, s0, sin(1), 0u, 0u};
-    for (int g = 1; g <= p - 2; ++g) {
-      piece(g, &b, &e);
-      j1(2 * g - 1) = SegJob{b, e, nullptr, fst(g), kJobNoOut, 0u};
-      j1(2 * g) = SegJob{b, e, nullptr, pst(g), kJobIdentity | kJobNoV | kJobNoOut, 0u};
-    }
-    for (int g = 1; g <= p - 1; ++g) {
-      piece(g, &b, &e);
-      j2(g - 1) = SegJob{b, e, sin(g), g == p - 1 ? s_out : nullptr, 0u, 0u};
-    }
+    for (int j = used1; j < 2 * G - 3; ++j) j1(j) = none;
+    for (int j = used2; j < G - 1; ++j) j2(j) = none;
   }
 }
 
@@ -328,14 +329,16 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
 // CTA's 8 warps (16 k each), so a step is short even when few CTAs run: every
 // lane holds an 8 x 4 tile (the CTA's rows, columns 4 lane .. +3), takes its 16
 // rows of P_g straight from global memory (one float4 per k and lane: a warp
-// reads 512 contiguous bytes) with all 16 loads in flight at once, and the
-// broadcast S values from a k-major copy of the rows; the 8 partial tiles are
-// summed through shared memory with F_g.
+// reads 512 contiguous bytes) with all 16 loads in flight at once, the next
+// step's issued as soon as this step's products are done, and the S values as
+// broadcast float4 reads of four k of one row; the 8 partial tiles are summed
+// through shared memory with F_g.  Every shared access is a float4 that is
+// either broadcast or spread over all banks.
 constexpr int kCombRows = 8;
 constexpr int kCombWarps = 8;
 constexpr int kCombThreads = 32 * kCombWarps;
 constexpr int kCombK = kHead / kCombWarps;  // k per warp and step
-__global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64_t N, int64_t Hv,
+__global__ void __launch_bounds__(kCombThreads, 2) gdn_segment_combine_kernel(int64_t N, int64_t Hv,
                                                                            SegLayout l) {
   const int64_t cta = blockIdx.x;
   const int rb = static_cast<int>(cta % (kHead / kCombRows));
@@ -350,18 +353,13 @@ __global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64
   const int64_t b0 = l.base[n];
   float* sin = l.pool + b0 * st;                    // S_1, then F_g -> S_{g+1}
   const float* pst = l.pool + (b0 + (p - 1)) * st;  // P_1..P_{p-2}
-  __shared__ __align__(16) float s_t[kHead][kCombRows];               // S_g rows, k-major
+  __shared__ __align__(16) float s_row[kCombRows][kHead];              // S_g rows
   __shared__ __align__(16) float red[kCombWarps][kCombRows][kHead];   // partial tiles
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int c0 = 4 * lane, k0 = w * kCombK;
-  for (int i = t; i < kCombRows * kHead; i += kCombThreads) {
-    const int r = i / kHead, k = i % kHead;
-    s_t[k][r] = sin[hrow + r * kHead + k];  // S_1 (from pass 1)
-  }
+  for (int i = t; i < kCombRows * kHead / 4; i += kCombThreads)  // S_1 (from pass 1)
+    reinterpret_cast<float4*>(&s_row[0][0])[i] = reinterpret_cast<const float4*>(sin + hrow)[i];
   __syncthreads();
-  // this warp's 16 rows of P_g, all loads in flight at once; the next step's are
-  // issued as soon as this step's products are done, so they arrive during the
-  // reduction
   auto load_p = [&](int g, float4* pk) {
     const float* P = pst + (g - 1) * st + hmat + static_cast<int64_t>(k0) * kHead + c0;
 #pragma unroll
@@ -369,7 +367,7 @@ __global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64
   };
   float4 pk[kCombK];
   load_p(1, pk);
-  const int rr = t >> 5;  // the row this thread sums
+  const int rr = w;  // the row this thread sums
   for (int g = 1; g <= p - 2; ++g) {
     float* out = sin + g * st + hrow + rr * kHead + c0;  // F_g, then S_{g+1} over it
     float4 v = *reinterpret_cast<const float4*>(out);     // arrives during the products
@@ -377,16 +375,18 @@ __global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64
 #pragma unroll
     for (int r = 0; r < kCombRows; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kCombK; ++k) {
-      const float4 s0 = *reinterpret_cast<const float4*>(&s_t[k0 + k][0]);
-      const float4 s1 = *reinterpret_cast<const float4*>(&s_t[k0 + k][4]);
-      const float sv[kCombRows] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    for (int k4 = 0; k4 < kCombK; k4 += 4) {
 #pragma unroll
       for (int r = 0; r < kCombRows; ++r) {
-        acc[r][0] = fmaf(sv[r], pk[k].x, acc[r][0]);
-        acc[r][1] = fmaf(sv[r], pk[k].y, acc[r][1]);
-        acc[r][2] = fmaf(sv[r], pk[k].z, acc[r][2]);
-        acc[r][3] = fmaf(sv[r], pk[k].w, acc[r][3]);
+        const float4 sv = *reinterpret_cast<const float4*>(&s_row[r][k0 + k4]);
+        const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          acc[r][0] = fmaf(s4[kk], pk[k4 + kk].x, acc[r][0]);
+          acc[r][1] = fmaf(s4[kk], pk[k4 + kk].y, acc[r][1]);
+          acc[r][2] = fmaf(s4[kk], pk[k4 + kk].z, acc[r][2]);
+          acc[r][3] = fmaf(s4[kk], pk[k4 + kk].w, acc[r][3]);
+        }
       }
     }
     if (g + 1 <= p - 2) load_p(g + 1, pk);
@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64
     for (int r = 0; r < kCombRows; ++r)
       *reinterpret_cast<float4*>(&red[w][r][c0]) =
           make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-    __syncthreads();  // partial tiles written; every warp is done reading s_t
+    __syncthreads();  // partial tiles written; every warp is done reading s_row
     // thread t sums column 4 (t % 32) .. +3 of row t / 32 over the warps, plus F_g
 #pragma unroll
     for (int j = 0; j < kCombWarps; ++j) {
@@ -405,11 +405,8 @@ __global__ void __launch_bounds__(kCombThreads) gdn_segment_combine_kernel(int64
       v.w += q.w;
     }
     *reinterpret_cast<float4*>(out) = v;
-    s_t[c0 + 0][rr] = v.x;
-    s_t[c0 + 1][rr] = v.y;
-    s_t[c0 + 2][rr] = v.z;
-    s_t[c0 + 3][rr] = v.w;
-    __syncthreads();  // S_{g+1} in s_t; red free
+    *reinterpret_cast<float4*>(&s_row[rr][c0]) = v;
+    __syncthreads();  // S_{g+1} in s_row; red free
   }
 }
 
