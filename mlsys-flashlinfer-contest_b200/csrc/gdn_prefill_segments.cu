@@ -108,20 +108,37 @@ constexpr int kCombineChunks = 1;
 // <= x; 0 when there is none.  No p below the one whose shares are at most
 // x / (w + 1) chunks can do, so the count starts there (32-bit arithmetic: the
 // builder runs it a few hundred times).
+// floor(a / b) and ceil(a / b) for 0 <= a < 2^26, 1 <= b: a float estimate
+// (off by a few units at most) set right by integer checks; an integer division
+// is a long dependent chain, and the builder's search runs hundreds of them
+// back to back.  No product below exceeds a + b.
+__device__ __forceinline__ int floor_div(int a, int b) {
+  int q = __float2int_rz(__fdividef(static_cast<float>(a), static_cast<float>(b)));
+  while (q > 0 && q * b > a) --q;
+  while ((q + 1) * b <= a) ++q;
+  return q;
+}
+__device__ __forceinline__ int ceil_div(int a, int b) { return floor_div(a + b - 1, b); }
+
 __device__ int pieces_for_chain(int c, int x, int g, int w) {
   if (c <= x) return 1;
-  const int q = x / (w + 1);
+  const int q = floor_div(x, w + 1);
   if (q < 2) return 0;
-  for (int p = max((c + q - 1) / q - w + 1, 3); p <= g; ++p) {
+  // no count reaches a chain below 2 sqrt((w + 1) c) - w - 1 ((w + 1) c / S + S,
+  // S = w + p - 1, is at least twice the root of the product): most candidates
+  // of the search end here, without the walk below
+  if (static_cast<float>(x) < 2.0f * sqrtf(static_cast<float>((w + 1) * c)) - w - 2) return 0;
+  for (int p = max(ceil_div(c, q) - w + 1, 3); p <= g; ++p) {
     const int shares = w + p - 1;
     if (c < 2 * shares) return 0;
-    if ((w + 1) * ((c + shares - 1) / shares) + kCombineChunks * (p - 2) <= x) return p;
+    if ((w + 1) * ceil_div(c, shares) + kCombineChunks * (p - 2) <= x) return p;
   }
   return 0;
 }
 
 // Three warps, one per w, search the automatic form side by side; warp 0 then
-// places every sequence's states in the pool and writes the jobs of both passes.
+// places every sequence's states in the pool and all three write the jobs of
+// both passes.
 // Automatic form: for w = 1, 2, 3 the shortest
 // chain x (binary search over 1..longest) with pieces whose F/P jobs, 2 Hv (p -
 // 2) per cut sequence, fit w waves of the SMs that pass 1's N Hv piece-0 (or
@@ -138,7 +155,6 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
     const float* state, float* new_state, SegLayout l) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   __shared__ int s_x[kJobWarps];
-  __shared__ int s_c[kJobWarps][32];  // chunk counts of up to 32 sequences, per warp
   const int64_t st = Hv * kHead * kHead;  // floats of one sequence's (or piece's) states
   auto bounds = [&](int64_t n, int64_t* bos, int64_t* eos) {
     *bos = min(max(cu_seqlens[n], int64_t(0)), T);
@@ -190,43 +206,55 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
              __reduce_add_sync(0xffffffffu, sts) <= l.cap;
     };
     // this warp's w: the shortest feasible chain x in [1, cmax] (feasible(cmax):
-    // nothing is cut; feasibility only grows with x).  Up to 32 sequences, every
-    // lane tests its own candidate x over all of them (chunk counts in shared
-    // memory), which narrows [lo, hi] 32-fold per round; beyond that, a binary
-    // search whose tests sum over the lanes' sequences.
+    // nothing is cut; feasibility only grows with x).  Up to 32 sequences, the
+    // warp tests 32 / lpc candidates per round (lpc = N rounded up to a power of
+    // two lanes each, a sequence per lane), narrowing [lo, hi] that much per
+    // round; beyond that, a binary search whose tests sum over the lanes'
+    // sequences.
     const int ww = wid + 1;
     int lo = 1, hi = cmax;
     if (free_sms <= 0) {
       lo = cmax;
     } else if (N <= 32) {
-      if (lane < N) s_c[wid][lane] = cc[0];
-      __syncwarp();
+      // lanes in groups of lpc (the power of two >= N), one sequence per lane and
+      // one candidate x per group: 32 / lpc candidates per round, the group's sums
+      // by xor shuffles within it
+      const int lpc = N <= 1 ? 1 : 1 << (32 - __clz(static_cast<int>(N) - 1));
+      const int nc = 32 / lpc, ci = lane / lpc, si = lane % lpc;
+      const int cs = si < N ? cc[0] : 0;  // chunks of this lane's sequence
+      const int c_mine = __shfl_sync(0xffffffffu, cs, si);  // lane si holds sequence si
       while (lo < hi) {
-        const int span = hi - lo;  // candidates lo .. hi - 1; hi is feasible
-        const int xj = span <= 32 ? lo + lane : lo + static_cast<int>((int64_t(span) * lane) / 32);
-        bool ok = xj < hi;
-        if (ok) {
-          unsigned fp = 0, p2 = 0, sts = 0;
-          for (int n = 0; n < N && ok; ++n) {
-            const int pc = pieces_for_chain(s_c[wid][n], xj, G, ww);
-            ok = pc != 0;
-            if (pc >= 3) {
-              fp += static_cast<unsigned>(2 * Hv * (pc - 2));
-              p2 += static_cast<unsigned>(Hv * (pc - 1));
-              sts += static_cast<unsigned>(states_of(pc));
-            }
+        const int span = hi - lo;  // candidates in [lo, hi); hi is feasible
+        const int xj = span <= nc ? lo + ci : lo + static_cast<int>((int64_t(span) * ci) / nc);
+        const bool valid = xj < hi;
+        unsigned fp = 0, p2 = 0, sts = 0;
+        bool bad = false;
+        if (valid && si < N) {
+          const int pc = pieces_for_chain(c_mine, xj, G, ww);
+          bad = pc == 0;
+          if (pc >= 3) {
+            fp = static_cast<unsigned>(2 * Hv * (pc - 2));
+            p2 = static_cast<unsigned>(Hv * (pc - 1));
+            sts = static_cast<unsigned>(states_of(pc));
           }
-          ok = ok && fp <= ww * free_sms && p2 <= static_cast<unsigned>(sms) && sts <= l.cap;
         }
-        const unsigned okm = __ballot_sync(0xffffffffu, ok);
+        for (int o = 1; o < lpc; o <<= 1) {
+          fp += __shfl_xor_sync(0xffffffffu, fp, o);
+          p2 += __shfl_xor_sync(0xffffffffu, p2, o);
+          sts += __shfl_xor_sync(0xffffffffu, sts, o);
+          bad |= __shfl_xor_sync(0xffffffffu, static_cast<int>(bad), o) != 0;
+        }
+        const bool ok = valid && !bad && fp <= ww * free_sms && p2 <= static_cast<unsigned>(sms) &&
+                        sts <= l.cap;
+        const unsigned okm = __ballot_sync(0xffffffffu, ok && si == 0);
         if (okm) {
-          const int j = __ffs(okm) - 1;  // the smallest feasible candidate
-          const int xprev = j == 0 ? lo - 1 : __shfl_sync(0xffffffffu, xj, j - 1);
-          hi = __shfl_sync(0xffffffffu, xj, j);
+          const int jl = __ffs(okm) - 1;  // leader lane of the smallest feasible candidate
+          const int xprev = jl == 0 ? lo - 1 : __shfl_sync(0xffffffffu, xj, jl - lpc);
+          hi = __shfl_sync(0xffffffffu, xj, jl);
           lo = xprev + 1;
         } else {
-          lo = __shfl_sync(0xffffffffu, xj, 31) + 1;  // every candidate below hi failed
-          if (span <= 32) lo = hi;
+          lo = __shfl_sync(0xffffffffu, xj, 32 - lpc) + 1;  // every candidate below hi failed
+          if (span <= nc) lo = hi;
         }
       }
     } else {
@@ -246,78 +274,88 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
     if (cmax > 0 && 5 * best <= 4 * cmax) x = best;
     else w = 1;
   }
-  if (wid != 0) return;
   auto pieces_of = [&](int64_t n) {
     const int64_t c = chunks(n);
     if (adaptive) return x > 0 ? max(pieces_for_chain(static_cast<int>(c), x, G, w), 1) : 1;
     return c >= 2 * G ? G : 1;
   };
-  // per block of 32 sequences: pieces and pool bases (an exclusive scan of the
-  // states; a sequence whose states would pass the pool's end stays whole), then
-  // the jobs of both passes, each lane writing its own sequence's slots (the
-  // real ones, then the empty rest) from registers
+  // per block of 32 sequences: warp 0 finds the pieces and pool bases (an
+  // exclusive scan of the states; a sequence whose states would pass the pool's
+  // end stays whole) into shared memory, then all threads write the block's job
+  // table entries, one entry each, slot by slot
+  __shared__ int s_p[32];
+  __shared__ int64_t s_b0[32], s_bos[32], s_eos[32];
   const SegJob none{0, 0, nullptr, nullptr, 0u, 0u};
+  const int s1 = 2 * G - 3, s2 = G - 1;  // slots per sequence in each pass
   int64_t running = 0;
   for (int64_t n0 = 0; n0 < N; n0 += 32) {
-    const int64_t n = n0 + lane;
-    int p = n < N ? pieces_of(n) : 1;
-    const int64_t need = states_of(p);
-    int64_t incl = need;
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+    const int nb = static_cast<int>(min(N - n0, int64_t(32)));
+    if (wid == 0) {
+      const int64_t n = n0 + lane;
+      int p = n < N ? pieces_of(n) : 1;
+      const int64_t need = states_of(p);
+      int64_t incl = need;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int64_t total = __shfl_sync(0xffffffffu, incl, 31);
+      if (running + incl > l.cap) p = 1;
+      if (n < N) {
+        int64_t bos, eos;
+        bounds(n, &bos, &eos);
+        s_p[lane] = p;
+        s_b0[lane] = running + incl - need;
+        s_bos[lane] = bos;
+        s_eos[lane] = eos;
+        l.pieces[n] = p;
+        l.base[n] = running + incl - need;
+      }
+      running += total;
     }
-    const int64_t total = __shfl_sync(0xffffffffu, incl, 31);
-    if (running + incl > l.cap) p = 1;
-    const int64_t b0 = running + incl - need;
-    running += total;
-    if (n >= N) continue;
-    l.pieces[n] = p;
-    l.base[n] = b0;
-    int64_t bos, eos;
-    bounds(n, &bos, &eos);
-    const int64_t nch = (eos - bos + kChunk - 1) / kChunk;
-    auto j1 = [&](int j) -> SegJob& { return l.jobs1[j * N + n]; };
-    auto j2 = [&](int j) -> SegJob& { return l.jobs2[j * N + n]; };
-    const float* s0 = state ? state + n * st : nullptr;
-    float* s_out = new_state + n * st;
-    int used1 = 1, used2 = 0;  // slots with real jobs
-    if (p < 2) {
-      j1(0) = SegJob{bos, eos, s0, s_out, 0u, 0u};
-    } else {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nb * (s1 + s2); idx += blockDim.x) {
+      const int k = idx % nb, j = idx / nb;  // sequence n0 + k, slot j (pass 1, then pass 2)
+      const int64_t n = n0 + k;
+      const int p = s_p[k];
+      const int64_t b0 = s_b0[k], bos = s_bos[k], eos = s_eos[k];
+      const float* s0 = state ? state + n * st : nullptr;
+      float* s_out = new_state + n * st;
       // share boundaries: piece 0 = shares [0, w), piece g >= 1 = share w + g - 1
       // (32-bit division: a sequence has at most 2^25 chunks and i <= 64 shares)
       const unsigned shares = static_cast<unsigned>(w + p - 1);
-      const unsigned nch32 = static_cast<unsigned>(nch);
+      const unsigned nch32 = static_cast<unsigned>((eos - bos + kChunk - 1) / kChunk);
       auto edge = [&](int i) {
         return min(bos + static_cast<int64_t>(static_cast<unsigned>(i) * nch32 / shares) * kChunk,
                    eos);
       };
-      auto piece = [&](int g, int64_t* b, int64_t* e) {
-        *b = g == 0 ? bos : edge(w + g - 1);
-        *e = edge(w + g);
-      };
-      // start state of piece g (1: from pass 1; g >= 2: the combine's, over F_{g-1})
-      auto sin = [&](int g) { return l.pool + (b0 + (g - 1)) * st; };
-      auto fst = [&](int g) { return l.pool + (b0 + g) * st; };
-      auto pst = [&](int g) { return l.pool + (b0 + (p - 1) + (g - 1)) * st; };
-      int64_t b, e;
-      piece(0, &b, &e);
-      j1(0) = SegJob{b, e, s0, sin(1), 0u, 0u};
-      for (int g = 1; g <= p - 2; ++g) {
-        piece(g, &b, &e);
-        j1(2 * g - 1) = SegJob{b, e, nullptr, fst(g), kJobNoOut, 0u};
-        j1(2 * g) = SegJob{b, e, nullptr, pst(g), kJobIdentity | kJobNoV | kJobNoOut, 0u};
+      auto pb = [&](int g) { return g == 0 ? bos : edge(w + g - 1); };  // piece g: [pb(g), edge(w+g))
+      auto pool = [&](int64_t i) { return l.pool + (b0 + i) * st; };
+      // pool slots of a cut: 0 = start state of piece 1, 1..p-2 = F_g (then the
+      // start state of piece g + 1), p-1..2p-4 = P_g
+      SegJob jb = none;
+      if (j < s1) {  // pass 1
+        if (p < 2) {
+          if (j == 0) jb = SegJob{bos, eos, s0, s_out, 0u, 0u};
+        } else if (j == 0) {
+          jb = SegJob{bos, edge(w), s0, pool(0), 0u, 0u};
+        } else if (j <= 2 * p - 4) {
+          const int g = (j + 1) / 2;
+          jb = (j & 1) ? SegJob{pb(g), edge(w + g), nullptr, pool(g), kJobNoOut, 0u}
+                       : SegJob{pb(g), edge(w + g), nullptr, pool(p - 1 + g - 1),
+                                kJobIdentity | kJobNoV | kJobNoOut, 0u};
+        }
+        l.jobs1[j * N + n] = jb;
+      } else {  // pass 2: piece g = j2 + 1 from its start state
+        const int j2 = j - s1;
+        if (p >= 2 && j2 < p - 1) {
+          const int g = j2 + 1;
+          jb = SegJob{pb(g), edge(w + g), pool(g - 1), g == p - 1 ? s_out : nullptr, 0u, 0u};
+        }
+        l.jobs2[j2 * N + n] = jb;
       }
-      for (int g = 1; g <= p - 1; ++g) {
-        piece(g, &b, &e);
-        j2(g - 1) = SegJob{b, e, sin(g), g == p - 1 ? s_out : nullptr, 0u, 0u};
-      }
-      used1 = 2 * p - 3;
-      used2 = p - 1;
     }
-    for (int j = used1; j < 2 * G - 3; ++j) j1(j) = none;
-    for (int j = used2; j < G - 1; ++j) j2(j) = none;
+    __syncthreads();
   }
 }
 
