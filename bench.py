@@ -459,8 +459,8 @@ def run_pool_bench(args, dev):
     hbm_peak, _, _, _ = measured_peaks()
     res = {}
     # bf16_t4 and bf16_t8 take the tensor-core closed form (gdn_decode_pool_tc.cu, 3..16 tokens)
-    for name, bf16, T in (("f32_t1", False, 1), ("bf16_t1", True, 1), ("bf16_t4", True, 4),
-                          ("bf16_t8", True, 8)):
+    for name, bf16, T in (("f32_t1", False, 1), ("f32_t4", False, 4), ("bf16_t1", True, 1),
+                          ("bf16_t4", True, 4), ("bf16_t8", True, 8)):
         inp = W.make_decode_pool_inputs(B_PER_RANK, T, HQ, HV, B_PER_RANK, seed=4242, device=dev,
                                         state_bf16=bf16)
         slots = torch.arange(B_PER_RANK, dtype=torch.int32, device=dev)
