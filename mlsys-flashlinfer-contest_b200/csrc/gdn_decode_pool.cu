@@ -562,6 +562,162 @@ __global__ void __launch_bounds__(kPackedThreads, 3) gdn_decode_pool_bf16_mtp_ke
   }
 }
 
+// Multi-token step on an fp32 pool, the same scheme as the bf16 one above: the
+// tokens staged in shared memory once per CTA, a thread's rows held in registers
+// across all of them, the four rows' dot products reduced together (octet_sum4)
+// and element pairs on the packed FMUL2 / FFMA2 path.  fp32 rows take twice the
+// registers, so a CTA of 128 threads owns 64 rows (two CTAs per head, four rows
+// per thread, all 16 loads of a thread issued at once) and four CTAs share an SM.
+constexpr int kF32MtpRows = 64;
+
+template <bool L2NORM, bool INTER>
+__global__ void __launch_bounds__(kPackedThreads, 4) gdn_decode_pool_f32_mtp_kernel(DecodePoolArgs p) {
+  constexpr int R = 4;  // rows per thread
+  extern __shared__ __align__(16) float tok[];  // [T][384]: q | k | v, then [T][2]: g, beta
+  const int T = static_cast<int>(p.T);
+  float* gb = tok + T * 3 * kHead;
+  const int64_t bh = blockIdx.x >> 1;  // b * Hv + h
+  const int half = static_cast<int>(blockIdx.x & 1);
+  const int64_t bidx = bh / p.Hv;
+  const int h = static_cast<int>(bh % p.Hv);
+  const int qh = h / static_cast<int>(p.Hv / p.Hq);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int oct = lane >> 3;
+  const int j = lane & 7;
+  const int row0 = half * kF32MtpRows + warp * (4 * R) + oct;  // rows row0 + 4 r
+  constexpr int64_t kTile = kHead * kHead;
+
+  const int32_t sin = p.in_slots[bidx];
+  const int32_t sout = p.out_slots ? p.out_slots[bidx] : sin;
+  const bool has_in = sin >= 0 && sin < p.pool_size;
+  const bool write_back = !p.no_state_update && sout >= 0 && sout < p.pool_size;
+
+  float s[R][16];
+  if (has_in) {
+    const int64_t base = (static_cast<int64_t>(sin) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead;
+#pragma unroll
+    for (int r = 0; r < R; ++r) load_row16<false>(p.pool, base + r * 4 * kHead, j, s[r]);
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int c = 0; c < 16; ++c) s[r][c] = 0.0f;
+  }
+
+  // stage the tokens: warp w takes tokens w, w + 4, ...; lane l holds elements 4l..4l+3
+  for (int t = warp; t < T; t += kPackedThreads / 32) {
+    const int64_t bt = bidx * p.T + t;
+    float qv[4], kv[4];
+    ld_bf16x4(static_cast<const __nv_bfloat16*>(p.q) + (bt * p.Hq + qh) * kHead + 4 * lane, qv);
+    ld_bf16x4(static_cast<const __nv_bfloat16*>(p.k) + (bt * p.Hq + qh) * kHead + 4 * lane, kv);
+    if constexpr (L2NORM) {
+      float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        sq = fmaf(qv[c], qv[c], sq);
+        sk = fmaf(kv[c], kv[c], sk);
+      }
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, d);
+        sk += __shfl_xor_sync(0xffffffffu, sk, d);
+      }
+      const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        qv[c] *= rq;
+        kv[c] *= rk;
+      }
+    }
+    float vv[4];
+    ld_bf16x4(static_cast<const __nv_bfloat16*>(p.v) + (bt * p.Hv + h) * kHead + 4 * lane, vv);
+    float* dst = tok + t * 3 * kHead + 4 * lane;
+    *reinterpret_cast<float4*>(dst) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+    *reinterpret_cast<float4*>(dst + kHead) = make_float4(kv[0], kv[1], kv[2], kv[3]);
+    *reinterpret_cast<float4*>(dst + 2 * kHead) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    if (lane == 0) {
+      gb[2 * t] = expf(log_decay(p.A_log[h], __bfloat162float(static_cast<const __nv_bfloat16*>(p.a)[bt * p.Hv + h]),
+                                 p.dt_bias[h]));
+      gb[2 * t + 1] = sigmoidf_acc(__bfloat162float(static_cast<const __nv_bfloat16*>(p.b)[bt * p.Hv + h]));
+    }
+  }
+  __syncthreads();
+
+#pragma unroll 1
+  for (int t = 0; t < T; ++t) {
+    const float* tq = tok + t * 3 * kHead;
+    // this lane's 16 elements of k and q: element 4 i + c is k[32 i + 4 j + c]
+    float kf[16], qf[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 k4 = *reinterpret_cast<const float4*>(tq + kHead + 32 * i + 4 * j);
+      const float4 q4 = *reinterpret_cast<const float4*>(tq + 32 * i + 4 * j);
+      kf[4 * i + 0] = k4.x;
+      kf[4 * i + 1] = k4.y;
+      kf[4 * i + 2] = k4.z;
+      kf[4 * i + 3] = k4.w;
+      qf[4 * i + 0] = q4.x;
+      qf[4 * i + 1] = q4.y;
+      qf[4 * i + 2] = q4.z;
+      qf[4 * i + 3] = q4.w;
+    }
+    const float g = gb[2 * t], beta = gb[2 * t + 1];
+    float part[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float2 d2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < 16; c += 2) {
+        const float2 sv = __fmul2_rn(make_float2(s[r][c], s[r][c + 1]), make_float2(g, g));
+        s[r][c] = sv.x;
+        s[r][c + 1] = sv.y;
+        d2 = __ffma2_rn(make_float2(kf[c], kf[c + 1]), sv, d2);
+      }
+      part[r] = d2.x + d2.y;
+    }
+    float delta[R];
+    {
+      const float red = octet_sum4(part, j);
+      const int obase = lane & ~7;
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        delta[r] = beta * (tq[2 * kHead + row0 + 4 * r] -
+                           __shfl_sync(0xffffffffu, red, obase + octet_sum4_lane(r)));
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float2 o2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < 16; c += 2) {
+        const float2 sv = __ffma2_rn(make_float2(kf[c], kf[c + 1]), make_float2(delta[r], delta[r]),
+                                     make_float2(s[r][c], s[r][c + 1]));
+        s[r][c] = sv.x;
+        s[r][c + 1] = sv.y;
+        o2 = __ffma2_rn(make_float2(qf[c], qf[c + 1]), sv, o2);
+      }
+      part[r] = o2.x + o2.y;
+    }
+    const int64_t bt = bidx * p.T + t;
+    __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + (bt * p.Hv + h) * kHead + row0;
+    {
+      const float o = octet_sum4(part, j);  // row 2 (j & 1) + ((j >> 1) & 1)
+      if (j < 4) orow[4 * (2 * (j & 1) + ((j >> 1) & 1))] = __float2bfloat16_rn(p.scale * o);
+    }
+    if (INTER) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        store_row16<false>(p.intermediate,
+                           (bt * p.Hv + h) * kTile + static_cast<int64_t>(row0 + 4 * r) * kHead, j, s[r]);
+    }
+  }
+  if (write_back) {
+    const int64_t base = (static_cast<int64_t>(sout) * p.Hv + h) * kTile + static_cast<int64_t>(row0) * kHead;
+#pragma unroll
+    for (int r = 0; r < R; ++r) store_row16<false>(p.pool, base + r * 4 * kHead, j, s[r]);
+  }
+}
+
 template <int U, bool BF16>
 cudaError_t launch_u(const DecodePoolArgs& a, cudaStream_t s) {
   const int64_t ctas = a.B * a.Hv * (kHead / (32 * U));
@@ -596,6 +752,19 @@ cudaError_t launch_dtype(const DecodePoolArgs& a, cudaStream_t s) {
                                  : (a.qk_l2norm ? gdn_decode_pool_bf16_mtp_kernel<true, false>
                                                 : gdn_decode_pool_bf16_mtp_kernel<false, false>);
     // T > 11 stages more than the 48 KiB default (T = 32: 49,408 B)
+    const cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kernel), static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    kernel<<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
+    return cudaGetLastError();
+  }
+  if (!BF16 && a.T > 1 && a.T <= kMtpMaxT) {  // four fp32 rows per thread, tokens in shared memory
+    const int64_t ctas = a.B * a.Hv * (kHead / kF32MtpRows);
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+    const size_t smem = static_cast<size_t>(a.T) * (3 * kHead + 2) * sizeof(float);
+    auto kernel = a.intermediate ? (a.qk_l2norm ? gdn_decode_pool_f32_mtp_kernel<true, true>
+                                                : gdn_decode_pool_f32_mtp_kernel<false, true>)
+                                 : (a.qk_l2norm ? gdn_decode_pool_f32_mtp_kernel<true, false>
+                                                : gdn_decode_pool_f32_mtp_kernel<false, false>);
     const cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kernel), static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     kernel<<<static_cast<unsigned>(ctas), kPackedThreads, smem, s>>>(a);
