@@ -458,7 +458,8 @@ def run_pool_bench(args, dev):
     from gdn_b200 import decode, workloads as W
     hbm_peak, _, _, _ = measured_peaks()
     res = {}
-    # bf16_t4 and bf16_t8 take the tensor-core closed form (gdn_decode_pool_tc.cu, 3..16 tokens)
+    # bf16_t4 and bf16_t8 take the tensor-core closed form (gdn_decode_pool_tc.cu, 3..16 tokens),
+    # f32_t4 the fp32 multi-token kernel
     for name, bf16, T in (("f32_t1", False, 1), ("f32_t4", False, 4), ("bf16_t1", True, 1),
                           ("bf16_t4", True, 4), ("bf16_t8", True, 8)):
         inp = W.make_decode_pool_inputs(B_PER_RANK, T, HQ, HV, B_PER_RANK, seed=4242, device=dev,
@@ -485,7 +486,8 @@ def run_pool_bench(args, dev):
         gbs = B_PER_RANK * HV * unit / (us / 1e6) / 1e9
         res[name] = {"state_dtype": "bf16" if bf16 else "f32", "tokens_per_seq": T,
                      "kernel": "gdn_decode_pool_tc_kernel (tcgen05 closed form)" if bf16 and 3 <= T <= 16
-                     else "gdn_decode_pool kernels (token by token)",
+                     else "gdn_decode_pool_f32_mtp_kernel (token by token, 64-row CTAs)"
+                     if not bf16 and T > 1 else "gdn_decode_pool kernels (token by token)",
                      "us_per_step": round(us, 2), "tokens_per_s": round(B_PER_RANK * T / (us / 1e6), 1),
                      "GB_per_s": round(gbs, 1), "roofline_frac": round(gbs / hbm_peak, 4),
                      "algorithmic_bytes_per_step": B_PER_RANK * HV * unit}
