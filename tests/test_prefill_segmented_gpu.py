@@ -112,6 +112,21 @@ def test_segmented_uneven_slow_decay():
     assert err <= 1.05 * err1 + 1e-5, (err, err1)
 
 
+@pytest.mark.parametrize("hq,hv", [(1, 2), (1, 1)])
+def test_segmented_many_sequences_match_oracle(hq, hv):
+    # more than 32 sequences: the job builder's binary search (sums over the lanes'
+    # sequences, several sequences per lane) instead of its lane-group search; one
+    # long sequence among many short ones is cut, the rest stay whole
+    lengths = [6000] + [200 + 7 * i for i in range(36)]
+    assert prefill.segments_for(sum(lengths), len(lengths), hv) >= 3
+    inp = W.make_prefill_inputs(lengths, hq, hv, seed=90 + hv, zero_state_every_other=True)
+    o_ref, s_ref = C.prefill(*inp.args(), nthreads=8)
+    o, ns = prefill.run_segmented(*PT.to_device(inp).args(), segments=0)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    PT.assert_state_close(ns, s_ref.numpy(), PT.STATE_REL)
+
+
 def test_dispatch_with_workspace_takes_segmented():
     # gdn_prefill (the reference-shaped entry) cuts when given the workspace it asks for
     inp = PT.to_device(W.make_prefill_inputs([8192], 4, 8, seed=12))
