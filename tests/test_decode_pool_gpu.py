@@ -115,6 +115,49 @@ def test_pool_bf16_many_tokens(T):
     _state_close(pool, pool_ref, True)
 
 
+@pytest.mark.parametrize("T", [2, 4, 8, 17, 32])
+@pytest.mark.parametrize("l2", [False, True])
+@pytest.mark.parametrize("geom", [(5, 4, 8, 7), (40, 16, 32, 45)])
+def test_pool_f32_multi_token(T, l2, geom):
+    """fp32 pools, 2..32 tokens without a per-token cache (the 64-row kernel: tokens
+    staged in shared memory, more than the 48 KiB default above T = 11); zero-state
+    and no-write slots, in-kernel L2 norm, against the token-by-token oracle."""
+    B, Hq, Hv, P = geom
+    inp = W.make_decode_pool_inputs(B, T, Hq, Hv, P, seed=2000 + 7 * T + l2 + B, device="cuda",
+                                    state_bf16=False, normalized_qk=not l2)
+    o_ref, pool_ref, _ = _oracle(inp, state_bf16=False, qk_l2norm=l2)
+    pool = inp.pool.clone()
+    o = decode.run_pool(inp.q, inp.k, inp.v, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                        pool, inp.in_slots, inp.out_slots, qk_l2norm=l2)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    _state_close(pool, pool_ref, False)
+
+
+@pytest.mark.parametrize("dt_bias", [-6.0, 4.0])
+def test_pool_f32_multi_token_decay_extremes(dt_bias):
+    inp = W.make_decode_pool_inputs(6, 8, 4, 8, 8, seed=78, device="cuda", state_bf16=False)
+    inp.dt_bias[:] = dt_bias
+    o_ref, pool_ref, _ = _oracle(inp, state_bf16=False)
+    pool = inp.pool.clone()
+    o = decode.run_pool(inp.q, inp.k, inp.v, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                        pool, inp.in_slots, inp.out_slots)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    _state_close(pool, pool_ref, False)
+
+
+def test_pool_f32_no_state_update_leaves_pool():
+    inp = W.make_decode_pool_inputs(4, 4, 4, 8, 6, seed=10, device="cuda", state_bf16=False)
+    o_ref, _, _ = _oracle(inp, state_bf16=False, no_state_update=True)
+    pool = inp.pool.clone()
+    o = decode.run_pool(inp.q, inp.k, inp.v, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+                        pool, inp.in_slots, inp.out_slots, no_state_update=True)
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    assert torch.equal(pool, inp.pool)
+
+
 def test_pool_no_state_update_leaves_pool():
     inp = W.make_decode_pool_inputs(4, 2, 4, 8, 6, seed=9, device="cuda", state_bf16=True)
     o_ref, _, _ = _oracle(inp, state_bf16=True, no_state_update=True)
