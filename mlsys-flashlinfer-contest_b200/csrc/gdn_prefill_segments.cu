@@ -98,16 +98,16 @@ SegLayout carve(void* ws, int64_t N, int64_t Hv, int G, bool adaptive, int sms, 
 }
 
 // Chunk-times of one combine step (S_{g+1} = S_g P_g + F_g runs p - 2 of them
-// one after the other), charged to a cut's chain when its piece count is chosen.
+// one after the other), charged to a cut's chain when its piece count is chosen,
+// and the fixed cost of cutting at all: the job builder, the combine and the
+// second pass launch one after the other, ~25 us before any piece work (their
+// launches, the combine's first loads, two more first chunks), about six
+// chunk-times.  Without it, short sequences were cut where the extra launches
+// cost more than the shorter chain saved (5 x 606 tokens at 8 heads: 77 us cut
+// against 52 us whole).
 constexpr int kCombineChunks = 1;
+constexpr int kCutChunks = 6;
 
-// Pieces of a c-chunk sequence that bring its chain down to x chunk-times with
-// piece 0 of w shares: 1 when c <= x (whole), else the fewest p in [3, g] (two
-// pieces would run one after the other, no shorter than the whole) with pieces
-// of at least 2 chunks and (w + 1) ceil(c / (w + p - 1)) + kCombineChunks (p - 2)
-// <= x; 0 when there is none.  No p below the one whose shares are at most
-// x / (w + 1) chunks can do, so the count starts there (32-bit arithmetic: the
-// builder runs it a few hundred times).
 // floor(a / b) and ceil(a / b) for 0 <= a < 2^26, 1 <= b: a float estimate
 // (off by a few units at most) set right by integer checks; an integer division
 // is a long dependent chain, and the builder's search runs hundreds of them
@@ -120,18 +120,30 @@ __device__ __forceinline__ int floor_div(int a, int b) {
 }
 __device__ __forceinline__ int ceil_div(int a, int b) { return floor_div(a + b - 1, b); }
 
+// Pieces of a c-chunk sequence in a cut call whose time is to stay within x
+// chunk-times (x below the longest sequence, so the call is cut): the call takes
+// pass 1 + the fixed cost + the combine + pass 2, and with piece 0 of w shares of
+// a sequence and every other piece one share, pass 1 lasts w times pass 2.  So a
+// sequence stays whole (1) when it fits pass 1, c <= w floor((x - kCutChunks) /
+// (w + 1)) (a longer whole sequence would hold pass 2 back); else it takes the
+// fewest p in [3, g] (two pieces would run one after the other, no shorter than
+// the whole) with pieces of at least 2 chunks and (w + 1) ceil(c / (w + p - 1)) +
+// kCombineChunks (p - 2) <= x - kCutChunks; 0 when there is none.  No p below the
+// one whose shares are at most (x - kCutChunks) / (w + 1) chunks can do, so the
+// count starts there.
 __device__ int pieces_for_chain(int c, int x, int g, int w) {
-  if (c <= x) return 1;
-  const int q = floor_div(x, w + 1);
-  if (q < 2) return 0;
+  const int xr = x - kCutChunks;  // what is left for the pieces and the combine
+  if (xr < 2 * (w + 1)) return 0;
+  const int q = floor_div(xr, w + 1);
+  if (c <= w * q) return 1;
   // no count reaches a chain below 2 sqrt((w + 1) c) - w - 1 ((w + 1) c / S + S,
   // S = w + p - 1, is at least twice the root of the product): most candidates
   // of the search end here, without the walk below
-  if (static_cast<float>(x) < 2.0f * sqrtf(static_cast<float>((w + 1) * c)) - w - 2) return 0;
+  if (static_cast<float>(xr) < 2.0f * sqrtf(static_cast<float>((w + 1) * c)) - w - 2) return 0;
   for (int p = max(ceil_div(c, q) - w + 1, 3); p <= g; ++p) {
     const int shares = w + p - 1;
     if (c < 2 * shares) return 0;
-    if ((w + 1) * ceil_div(c, shares) + kCombineChunks * (p - 2) <= x) return p;
+    if ((w + 1) * ceil_div(c, shares) + kCombineChunks * (p - 2) <= xr) return p;
   }
   return 0;
 }
@@ -140,12 +152,14 @@ __device__ int pieces_for_chain(int c, int x, int g, int w) {
 // places every sequence's states in the pool and all three write the jobs of
 // both passes.
 // Automatic form: for w = 1, 2, 3 the shortest
-// chain x (binary search over 1..longest) with pieces whose F/P jobs, 2 Hv (p -
-// 2) per cut sequence, fit w waves of the SMs that pass 1's N Hv piece-0 (or
-// whole-sequence) jobs leave free, whose pass-2 jobs, Hv (p - 1) per cut
-// sequence, fit one wave, and whose states fit the pool; the w with the
-// shortest x wins (ties: the smaller w), and nothing is cut unless x is at most
-// 4/5 of the longest sequence.  With w = 1 the first rule is the one-wave pass 1
+// call time x in chunk-times (search over 1..longest; x = longest is the uncut
+// call) whose pieces (pieces_for_chain: whole sequences within pass 1, cut ones
+// within pass 1 + the fixed cost + the combine + pass 2) have F/P jobs, 2 Hv (p -
+// 2) per cut sequence, that fit w waves of the SMs that pass 1's N Hv piece-0 (or
+// whole-sequence) jobs leave free, pass-2 jobs, Hv (p - 1) per cut sequence, that
+// fit one wave, and states that fit the pool; the w with the shortest x wins
+// (ties: the smaller w), and nothing is cut unless x is at most 4/5 of the
+// longest sequence.  With w = 1 the first rule is the one-wave pass 1
 // of equal pieces.  Job tables are job-major (slot j of every sequence, then
 // slot j + 1), so a grid's piece-0 jobs come before its F/P jobs and its real
 // jobs before its empty ones.
@@ -205,8 +219,8 @@ __global__ void __launch_bounds__(32 * kJobWarps) gdn_segment_jobs_kernel(
              __reduce_add_sync(0xffffffffu, p2) <= static_cast<unsigned>(sms) &&
              __reduce_add_sync(0xffffffffu, sts) <= l.cap;
     };
-    // this warp's w: the shortest feasible chain x in [1, cmax] (feasible(cmax):
-    // nothing is cut; feasibility only grows with x).  Up to 32 sequences, the
+    // this warp's w: the shortest feasible x in [1, cmax] (x = cmax: nothing is
+    // cut, feasible without a test; below it feasibility only grows with x).  Up to 32 sequences, the
     // warp tests 32 / lpc candidates per round (lpc = N rounded up to a power of
     // two lanes each, a sequence per lane), narrowing [lo, hi] that much per
     // round; beyond that, a binary search whose tests sum over the lanes'
