@@ -241,15 +241,16 @@ int gdn_prefill_segmented_noalloc(const void *q, const void *k, const void *v, c
 /* Upper bound of the automatic piece count for these sizes (1: the call is not
  * cut).  With segments 0 the call's first kernel picks, from the lengths on the
  * device, how many shares w (1 to 3) of a cut sequence its first piece takes and
- * each sequence's count under the bound: the shortest longest chain ((w + 1)
- * shares of a cut sequence of w + pieces - 1 shares, plus one chunk-time per
- * combine step; whole sequences their length) whose pass-1 F/P jobs fit w waves
- * of the SMs its piece-0 jobs leave free, whose pass 2 fits one wave and whose
- * piece states fit the workspace, with pieces of at least 2 chunks and counts of
- * 1 or at least 3, and no cut at all unless it shortens the longest chain by a
- * fifth.  The bound is 1 when the (sequence, head) pairs are more than half the
- * SMs, else the largest G <= 16 with num_seqs * num_v_heads * (G - 1) <= 2 x SMs
- * and total_seq_len >= 4 G chunks. */
+ * each sequence's count under the bound: the shortest call time (pass 1, a fixed
+ * cost of about six chunk-times for the extra launches, one chunk-time per
+ * combine step, pass 2 = pass 1 / w; whole sequences within pass 1) whose pass-1
+ * F/P jobs fit w waves of the SMs its piece-0 jobs leave free, whose pass 2 fits
+ * one wave and whose piece states fit the workspace, with pieces of at least 2
+ * chunks and counts of 1 or at least 3, and no cut at all unless it shortens the
+ * call by a fifth.  The bound is 1 when the (sequence, head) pairs are more than
+ * half the SMs or the call has fewer chunks in all than the shortest sequence
+ * such a cut can take (23 chunks), else the largest G <= 16 with num_seqs *
+ * num_v_heads * (G - 1) <= 2 x SMs and total_seq_len >= 4 G chunks. */
 int gdn_prefill_segments(int64_t total_seq_len, int64_t num_seqs, int64_t num_v_heads);
 
 /*

@@ -174,7 +174,8 @@ static bool use_recurrent(int64_t T, int64_t N, int64_t Hv) {
 // SMs: pass 1 within one to three waves of the SMs its piece-0 jobs leave free,
 // pass 2 within one wave), so the host only rules out calls that cannot gain:
 // more (sequence, head) pairs than half the SMs (then not even equal sequences
-// could all be cut in 3 with pass 2 in one wave), or too few chunks in all; the
+// could all be cut in 3 with pass 2 in one wave), or fewer chunks in all than
+// the shortest sequence the builder would cut (prefill_min_cut_chunks); the
 // bound is the largest G <= kMaxAutoSegments with N Hv (G - 1) <= 2 SMs and
 // T >= 4 G chunks.
 static int sm_count() { return gdn::device_sm_count(); }
@@ -183,6 +184,9 @@ constexpr int kMaxAutoSegments = 16;
 static int choose_segments(int64_t T, int64_t N, int64_t Hv) {
   if (N <= 0 || Hv <= 0 || 2 * N * Hv > sm_count()) return 1;
   const int64_t chunks = T / gdn::kChunk;
+  // no sequence can be long enough for the builder to accept a cut: the
+  // segmented form would only add its launches
+  if ((T + gdn::kChunk - 1) / gdn::kChunk < gdn::prefill_min_cut_chunks()) return 1;
   int best = 1;
   for (int G = 3; G <= kMaxAutoSegments; ++G)
     if (N * Hv * (G - 1) <= 2 * sm_count() && chunks >= 4 * G) best = G;

@@ -120,6 +120,8 @@ cudaError_t launch_prefill_recurrent(const PrefillArgs& a, cudaStream_t s);
 // picks each sequence's count (pass 1 within `sms` CTAs); else every sequence of
 // at least 2 segments chunks is cut into `segments`.
 size_t prefill_segments_bytes(int64_t N, int64_t Hv, int segments, bool adaptive, int sms);
+// The fewest chunks a sequence needs before the automatic form can cut it.
+int prefill_min_cut_chunks();
 cudaError_t launch_prefill_segmented(const PrefillArgs& a, int segments, bool adaptive, int sms,
                                      void* workspace, size_t workspace_bytes, cudaStream_t s);
 // The same with the workspace in a file-scope device array of kNoAllocScratchBytes

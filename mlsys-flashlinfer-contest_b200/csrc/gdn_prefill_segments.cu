@@ -464,6 +464,23 @@ __global__ void __launch_bounds__(kCombThreads, 2) gdn_segment_combine_kernel(in
 
 }  // namespace
 
+// The fewest chunks a sequence needs before the job builder's automatic form can
+// accept any cut of it (x at most 4/5 of the sequence, pieces_for_chain's cost
+// with the fixed cut cost); a call with fewer chunks in all cannot be cut.
+int prefill_min_cut_chunks() {
+  static const int c_min = [] {
+    for (int c = 1; c < (1 << 16); ++c)
+      for (int w = 1; w <= 3; ++w)
+        for (int p = 3; 2 * (w + p - 1) <= c; ++p) {
+          const int shares = w + p - 1;
+          const int x = (w + 1) * ((c + shares - 1) / shares) + kCombineChunks * (p - 2) + kCutChunks;
+          if (5 * x <= 4 * c) return c;
+        }
+    return 1 << 16;
+  }();
+  return c_min;
+}
+
 size_t prefill_segments_bytes(int64_t N, int64_t Hv, int segments, bool adaptive, int sms) {
   if (segments < 2 || N <= 0) return 0;
   size_t bytes = 0;
