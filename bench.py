@@ -316,7 +316,7 @@ def run_e2e(args, inp, dev, stream, dist, world):
     own streams with two device buffer sets, so step i+1's inputs cross PCIe while
     step i's kernel runs and step i's output comes back during step i+1.  The loop
     is timed twice: issued step by step from Python ("eager"), and as replays of a
-    CUDA graph that holds 40 such pipelined steps (copies, kernel launches and their
+    CUDA graph that holds 100 such pipelined steps (copies, kernel launches and their
     cross-stream event order, captured once), which is how a serving loop drives
     it without the host's per-step launch cost.  The graph replays give the value:
     the eager loop measures the host's Python speed as much as the transfer (its
@@ -406,10 +406,10 @@ def run_e2e(args, inp, dev, stream, dist, world):
 
     eager_ms, eager_per = timed_windows(eager_window, steps)
 
-    # graph: 40 pipelined steps captured once (side streams forked from and joined
+    # graph: 100 pipelined steps captured once (side streams forked from and joined
     # back to the capture stream), replayed; a replay starts with its first upload
-    # and ends with its last read-back, ~1 % of 40 steps
-    g_steps = 40
+    # and ends with its last read-back, ~0.7 % of 100 steps
+    g_steps = 100
     graph = torch.cuda.CUDAGraph()
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(stream)
@@ -439,7 +439,7 @@ def run_e2e(args, inp, dev, stream, dist, world):
     out = {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h}
     out.update(summary(g_ms, g_per, reps * g_steps))
-    out.update({"api": "gdn_b200.decode.launch (destination passing), 40 pipelined steps "
+    out.update({"api": "gdn_b200.decode.launch (destination passing), 100 pipelined steps "
                        "captured in a CUDA graph and replayed",
                 "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's kernel (two "
                               "buffer sets, copy streams); every copy is inside the timed region",
