@@ -151,6 +151,9 @@ def test_prefill_segment_choice():
     assert L.gdn_prefill_segments(8192, 1, 8) == 16
     assert L.gdn_prefill_segments(4096, 1, 8) == 16      # 64 chunks = 4 x 16
     assert L.gdn_prefill_segments(700, 1, 8) == 1        # 10 chunks: fewer than 4 x 3
+    # fewer chunks in all than the shortest sequence the job builder would cut (23)
+    assert L.gdn_prefill_segments(1408, 1, 8) == 1       # 22 chunks
+    assert L.gdn_prefill_segments(1472, 1, 8) == 5       # 23 chunks; 4 G <= 23
     assert L.gdn_prefill_segments(16, 1, 8) == 1         # the recurrent kernel's size
     assert L.gdn_prefill_workspace_bytes(65536, 4, 16, 32) == 0
     ws = L.gdn_prefill_workspace_bytes(65536, 4, 4, 4)
