@@ -138,6 +138,13 @@ struct ChunkParams {
   int dbg_seq, dbg_head, dbg_chunk;
 };
 
+// A call of more (sequence, head) pairs than SMs runs in waves, and the CTA
+// scheduler hands out CTAs in index order: with the longest sequences first,
+// the short ones fill in behind them instead of a long one starting last
+// (longest-processing-time order, by chunk count).  The ORDER instantiation does
+// this; one warp ranks up to 64 sequences.
+constexpr int kOrderMaxSeqs = 64;
+
 // Tensor maps of the peer output buffers (n_peers used).
 struct PeerMaps {
   CUtensorMap m[kMaxPeers];
@@ -176,10 +183,59 @@ __device__ __forceinline__ void load_table16(const float* src, float* v) {
   }
 }
 
+// ORDER: lane i of the calling warp takes sequences i and i + 32 (N <= 64) with
+// the key (chunks << 6) | (63 - index), unique, so that more chunks rank first and
+// equal counts keep their order (lengths clamped as the chunk loop clamps them);
+// the rank of a sequence is the number of larger keys.  The sequence of rank n
+// and its bounds go to *seq_slot and seq_bounds[0..1].  Kept out of line (one
+// call per CTA): inlined, the ordered calls ran up to 1.3 % slower.  All four
+// loads are issued at once, and four partial counts keep the additions
+// independent.
+__device__ __noinline__ void rank_longest_first(const int64_t* cu, int ns, int64_t T, int64_t n,
+                                                int lane, int* seq_slot, int64_t* seq_bounds) {
+  // indices clamped into cu[0..ns]; the values of lanes past ns are not used
+  int64_t c[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) c[u] = cu[min(lane + 32 * (u >> 1) + (u & 1), ns)];
+  int64_t b[2], e[2];
+  int key[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    b[u] = min(max(c[2 * u], int64_t(0)), T);
+    e[u] = min(max(c[2 * u + 1], b[u]), T);
+    key[u] = lane + 32 * u < ns
+                 ? static_cast<int>(((e[u] - b[u] + kChunk - 1) / kChunk) << 6) | (63 - lane - 32 * u)
+                 : -1;
+  }
+  int r0[4] = {0, 0, 0, 0}, r1[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int kj = __shfl_sync(0xffffffffu, key[0], j);
+    r0[j & 3] += kj > key[0] ? 1 : 0;
+    r1[j & 3] += kj > key[1] ? 1 : 0;
+  }
+  if (ns > 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int kj = __shfl_sync(0xffffffffu, key[1], j);
+      r0[j & 3] += kj > key[0] ? 1 : 0;
+      r1[j & 3] += kj > key[1] ? 1 : 0;
+    }
+  }
+  const int q0 = r0[0] + r0[1] + r0[2] + r0[3], q1 = r1[0] + r1[1] + r1[2] + r1[3];
+  const int u = (key[0] >= 0 && q0 == n) ? 0 : (key[1] >= 0 && q1 == n) ? 1 : -1;  // exactly one
+  if (u >= 0) {
+    *seq_slot = lane + 32 * u;
+    seq_bounds[0] = b[u];
+    seq_bounds[1] = e[u];
+  }
+}
+
 // L2: q/k L2 norm folded in as per-token factors; JOBS: the segmented prefill's
-// job table (identity start, v = 0, no outputs, optional final state).  Both are
-// separate instantiations so the plain kernel carries none of it.
-template <bool DEBUG, bool L2, bool JOBS>
+// job table (identity start, v = 0, no outputs, optional final state); ORDER
+// (without JOBS): CTA group r runs the r-th longest sequence.  All are separate
+// instantiations so the plain kernel carries none of it.
+template <bool DEBUG, bool L2, bool JOBS, bool ORDER>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                                const __grid_constant__ CUtensorMap tm_k,
@@ -195,9 +251,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // per-token gate tables (G_*), double-buffered by chunk parity: the tables
   // of chunk c+1 are computed while chunk c's tensor-core work runs.
   float* gates_buf = reinterpret_cast<float*>(smem + OFF_MISC);  // [2][kGateFloats]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_MISC + kMiscBarOff);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  volatile uint32_t* abort_flag = tmem_slot + 1;  // a compute thread gave up on a wait
   float* At = reinterpret_cast<float*>(smem + OFF_AT);   // A column-major: At[k][i] = A[i][k]
   float* Tcm = reinterpret_cast<float*>(smem + OFF_TC);  // Tcm[j][i] = T[i][j]
   float* Mcm = reinterpret_cast<float*>(smem + OFF_MC);  // (A21 T11) column-major, pitch 36
@@ -211,10 +264,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int g = lane >> 2, tq = lane & 3;  // mma.sync fragment coordinates
   const int rowv = 32 * quarter + lane;    // TMEM lane (accumulator row) of this thread
   const int h = static_cast<int>(blockIdx.x % p.Hv);
-  const int64_t n = blockIdx.x / p.Hv;
+  int64_t n = blockIdx.x / p.Hv;
   const int qh = h / (p.Hv / p.Hq);
   constexpr int64_t kStateFloats = kHead * kHead;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_MISC + kMiscBarOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile uint32_t* abort_flag = tmem_slot + 1;  // a compute thread gave up on a wait
+  int* seq_slot = reinterpret_cast<int*>(tmem_slot + 2);  // sequence of this CTA group (ORDER)
+  int64_t* seq_bounds = reinterpret_cast<int64_t*>(tmem_slot + 4);  // its [bos, eos)
+
+  // Barriers, tensor-map prefetch and the TMEM allocation, then a CTA barrier.
+  auto setup = [&]() {
+    if (tid == 0) {
+      for (int i = 0; i < kNumBars; ++i)
+        mbar_init(&bars[i], (i >= RDY_S && i <= RDY_V) ? kComputeWarps : i == RDY_T1 ? 4 : 1);
+      fence_mbar_init();
+      *abort_flag = 0u;
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      if (p.tma_out) prefetch_tmap(&tm_o);
+    }
+    if (warp == 0) {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  };
+
   int64_t bos, eos;
+  if constexpr (ORDER) {
+    // warp 1 finds the sequence of rank n while warp 0 sets up; the bounds it
+    // read come along, so no second load of cu_seqlens follows
+    if (warp == 1) rank_longest_first(p.cu_seqlens, static_cast<int>(p.N), p.T, n, lane, seq_slot, seq_bounds);
+    setup();
+    // (clamped again, so that every access stays in bounds whatever the slot held)
+    n = min(max(static_cast<int64_t>(*seq_slot), int64_t(0)), p.N - 1);
+    bos = min(max(seq_bounds[0], int64_t(0)), p.T);
+    eos = min(max(seq_bounds[1], bos), p.T);
+  }
+
   const float* state_in;  // this head's initial state (nullptr: zero)
   float* ns_rows;         // this head's final state (nullptr: not stored)
   uint32_t jflags = 0;
@@ -226,8 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     ns_rows = jb.state_out ? jb.state_out + h * kStateFloats : nullptr;
     jflags = jb.flags;
   } else {
-    bos = min(max(p.cu_seqlens[n], int64_t(0)), p.T);
-    eos = min(max(p.cu_seqlens[n + 1], bos), p.T);
+    if constexpr (!ORDER) {
+      bos = min(max(p.cu_seqlens[n], int64_t(0)), p.T);
+      eos = min(max(p.cu_seqlens[n + 1], bos), p.T);
+    }
     state_in = p.state ? p.state + (n * p.Hv + h) * kStateFloats : nullptr;
     ns_rows = p.new_state + (n * p.Hv + h) * kStateFloats;
   }
@@ -240,27 +333,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ns_rows)
       for (int i = tid; i < kHead * kHead / 4; i += kThreads)
         reinterpret_cast<float4*>(ns_rows)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (ORDER) {
+      if (warp == 0) tmem_dealloc(*tmem_slot, kTmemCols);
+    }
     return;
   }
   const int nchunks = static_cast<int>((Ltot + kChunk - 1) / kChunk);
 
-  if (tid == 0) {
-    for (int i = 0; i < kNumBars; ++i)
-      mbar_init(&bars[i], (i >= RDY_S && i <= RDY_V) ? kComputeWarps : i == RDY_T1 ? 4 : 1);
-    fence_mbar_init();
-    *abort_flag = 0u;
-    prefetch_tmap(&tm_q);
-    prefetch_tmap(&tm_k);
-    prefetch_tmap(&tm_v);
-    if (p.tma_out) prefetch_tmap(&tm_o);
-  }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
+  if constexpr (!ORDER) setup();
   const uint32_t tmem = *tmem_slot;
   const long long t_base = DEBUG ? clock64() : 0;
   bool failed = false;  // this thread gave up on a wait
@@ -1228,12 +1308,17 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   if (tma_out && (e = make_head_map(&mo, a.out, out_heads, a.T)) != cudaSuccess) return e;
   for (int r = 0; tma_out && r < a.n_peers; ++r)
     if ((e = make_head_map(&pm.m[r], a.peer_out[r], out_heads, a.T)) != cudaSuccess) return e;
-  auto kernel = gdn_prefill_chunked_kernel<DEBUG, false, false>;
-  const int variant = (a.qk_l2norm ? 1 : 0) + (a.jobs ? 2 : 0);
+  auto kernel = gdn_prefill_chunked_kernel<DEBUG, false, false, false>;
+  const bool order = !a.jobs && a.N <= kOrderMaxSeqs && a.N * a.Hv > device_sm_count();
+  const int variant = (a.qk_l2norm ? 1 : 0) + (a.jobs ? 2 : 0) + (order ? 4 : 0);
   if constexpr (!DEBUG) {
-    constexpr decltype(kernel) kernels[4] = {
-        gdn_prefill_chunked_kernel<false, false, false>, gdn_prefill_chunked_kernel<false, true, false>,
-        gdn_prefill_chunked_kernel<false, false, true>, gdn_prefill_chunked_kernel<false, true, true>};
+    constexpr decltype(kernel) kernels[6] = {
+        gdn_prefill_chunked_kernel<false, false, false, false>,
+        gdn_prefill_chunked_kernel<false, true, false, false>,
+        gdn_prefill_chunked_kernel<false, false, true, false>,
+        gdn_prefill_chunked_kernel<false, true, true, false>,
+        gdn_prefill_chunked_kernel<false, false, false, true>,
+        gdn_prefill_chunked_kernel<false, true, false, true>};
     kernel = kernels[variant];
   } else if (a.jobs || a.qk_l2norm) {
     return cudaErrorInvalidValue;  // the debug build covers the plain kernel only

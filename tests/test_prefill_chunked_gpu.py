@@ -171,6 +171,39 @@ def test_chunked_deterministic():
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
 
 
+@pytest.mark.parametrize("lengths", [
+    # 40 sequences at 8 heads (320 pairs, more than the SMs): both halves of the
+    # kernel's 64-sequence ranking, equal lengths, empty sequences, long ones late
+    [5, 700, 64, 64, 0, 130, 1, 900, 63, 300] * 4,
+    # 24 sequences (192 pairs): 23 one-token sequences and the long one last
+    [1] * 23 + [1500],
+])
+def test_chunked_multiwave_longest_first_bitwise(lengths):
+    """A call with more (sequence, head) pairs than SMs hands its CTAs out
+    longest sequence first (by chunk count).  A pair computes the same wherever its CTA sits in
+    the grid, so the call must equal, bit for bit, one call per sequence (a
+    single wave, not reordered), and the C oracle within the contract bounds."""
+    cpu = W.make_prefill_inputs(lengths, 4, 8, seed=len(lengths) + 11, zero_state_every_other=True)
+    o_ref, s_ref = C.prefill(*cpu.args())
+    inp = PT.to_device(cpu)
+    o, ns = chunked(*inp.args())
+    torch.cuda.synchronize()
+    PT.assert_o_close(o, o_ref)
+    PT.assert_state_close(ns, s_ref.numpy(), PT.STATE_REL)
+    cu = cpu.cu_seqlens.tolist()
+    for i in range(len(lengths)):
+        b0, e0 = cu[i], cu[i + 1]
+        if e0 == b0:  # empty: zero final state (a call of no tokens is not made)
+            assert not torch.any(ns[i]), f"sequence {i} is empty: its final state must be zero"
+            continue
+        one = W.PrefillInputs(inp.q[b0:e0], inp.k[b0:e0], inp.v[b0:e0], inp.state[i:i + 1],
+                              inp.A_log, inp.a[b0:e0], inp.dt_bias, inp.b[b0:e0],
+                              torch.tensor([0, e0 - b0], dtype=torch.int64, device="cuda"), inp.scale)
+        o1, s1 = chunked(*one.args())
+        assert torch.equal(o1, o[b0:e0]), f"sequence {i} ({e0 - b0} tokens): output differs"
+        assert torch.equal(s1[0], ns[i]), f"sequence {i} ({e0 - b0} tokens): final state differs"
+
+
 def test_no_timeout_status_after_runs():
     st = ctypes.c_uint32(0)
     N.check(N.lib().gdn_read_status(ctypes.byref(st), 1))
