@@ -366,26 +366,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float neg_exp_A = -expf(p.A_log[h]);
     const float dt_bias_h = p.dt_bias[h];
 
-    // ---- initial state -> TMEM (row rowv, columns [32 cq, 32 cq + 32)) -----
-    {
-      const float* src = state_in && !init_identity ? state_in + rowv * kHead + 32 * cq : nullptr;
-      float v[32];
-#pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4) {
-        float4 x = src ? ld_stream_f4(src + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[4 * q4] = x.x;
-        v[4 * q4 + 1] = x.y;
-        v[4 * q4 + 2] = x.z;
-        v[4 * q4 + 3] = x.w;
-      }
-      if (init_identity) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = (rowv == 32 * cq + i) ? 1.f : 0.f;
-      }
-      tmem_st32(tq_st, v);
-      tmem_wait_st();
-    }
-
     // One arrival per warp on a compute -> issue-warp barrier after this
     // thread's TMEM operand stores (waited), optionally with its shared-memory
     // operand writes made visible to the async proxy first.
@@ -489,8 +469,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (part == 0) gates_buf[(cc & 1) * kGateFloats + (r < 64 ? G_RK + r : G_RQ + r - 64)] = rsqrtf(acc + 1e-6f);
     };
 
+    if (warp == 1) prefetch_gates(0);  // in flight during the state load
+
+    // ---- initial state -> TMEM (row rowv, columns [32 cq, 32 cq + 32)) -----
+    {
+      const float* src = state_in && !init_identity ? state_in + rowv * kHead + 32 * cq : nullptr;
+      float v[32];
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4) {
+        float4 x = src ? ld_stream_f4(src + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[4 * q4] = x.x;
+        v[4 * q4 + 1] = x.y;
+        v[4 * q4 + 2] = x.z;
+        v[4 * q4 + 3] = x.w;
+      }
+      if (init_identity) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = (rowv == 32 * cq + i) ? 1.f : 0.f;
+      }
+      tmem_st32(tq_st, v);
+      tmem_wait_st();
+    }
+
     if (warp == 1) {
-      prefetch_gates(0);
       compute_gates(0);
       if (Ltot > kChunk) prefetch_gates(1);
     }
@@ -1011,6 +1012,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_store_3d(&pm.m[r], smem + OFF_O + 8192, 64, gh, tl);
         }
         bulk_commit();
+        // the tile has been read once this returns; the global writes complete
+        // with the grid (a fused gather waits for its peer writes as well)
         bulk_wait_all();
       }
     }
@@ -1192,8 +1195,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) p.debug[DBG_MCLK + i] = static_cast<float>(mclk[i]);
     }
 #undef MPHASE
-    // drain the tensor pipe, the output stores and any loads still in flight
-    // before the CTA exits
+    // drain the tensor pipe, the output stores (their reads of shared memory;
+    // peer writes in full) and any loads still in flight before the CTA exits
     bulk_wait_all();
     mma_commit(&bars[BAR_END]);
     if (!mbar_wait(&bars[BAR_END], 0, kTimeoutNs)) ok = false;
