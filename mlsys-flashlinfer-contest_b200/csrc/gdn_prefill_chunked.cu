@@ -1012,8 +1012,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_store_3d(&pm.m[r], smem + OFF_O + 8192, 64, gh, tl);
         }
         bulk_commit();
-        // the tile has been read once this returns; the global writes complete
-        // with the grid (a fused gather waits for its peer writes as well)
         bulk_wait_all();
       }
     }
@@ -1195,8 +1193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) p.debug[DBG_MCLK + i] = static_cast<float>(mclk[i]);
     }
 #undef MPHASE
-    // drain the tensor pipe, the output stores (their reads of shared memory;
-    // peer writes in full) and any loads still in flight before the CTA exits
+    // drain the tensor pipe, the output stores and any loads still in flight
+    // before the CTA exits
     bulk_wait_all();
     mma_commit(&bars[BAR_END]);
     if (!mbar_wait(&bars[BAR_END], 0, kTimeoutNs)) ok = false;
