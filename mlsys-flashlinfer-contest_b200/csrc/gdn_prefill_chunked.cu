@@ -82,6 +82,13 @@ constexpr uint32_t OFF_O = (OFF_TC2 + 32 * 20 * 4 + 1023) / 1024 * 1024;  // out
 // [cb 2][t 64][128 B] (TMA store source; written by the output epilogue, stored
 // by the issue thread once the next chunk's T tiles are signalled)
 constexpr uint32_t OFF_MISC = OFF_O + 16384;
+// The final state passes through per-warp transpose tiles laid over the inverse's
+// scratch (free after the last chunk): 32 rows x 16 floats at a pitch of 20
+// floats, so that both the per-lane row writes and the row-segment reads are
+// 16-byte accesses with the fewest bank wavefronts.
+constexpr int kXposePitch = 20;
+constexpr int kXposeFloats = 32 * kXposePitch;
+static_assert(OFF_AT + 16 * kXposeFloats * 4 <= OFF_O, "transpose tiles overlap the output tile");
 // Per-token tables of one chunk (floats), double-buffered by chunk parity.
 constexpr int G_GAM = 0;     // gamma_t * log2(e) (cumulative log-decay)
 constexpr int G_BET = 64;    // beta_t (0 past the end of the sequence)
@@ -180,6 +187,37 @@ __device__ __forceinline__ void load_table16(const float* src, float* v) {
     v[4 * q + 1] = x.y;
     v[4 * q + 2] = x.z;
     v[4 * q + 3] = x.w;
+  }
+}
+
+// The final state of one warp's 32 x 32 block (rows = TMEM lanes of the warp's
+// quarter, 32 columns from tq) to HBM, coalesced: each half of 16 columns passes
+// from the lane that owns the row through the warp's transpose tile in shared
+// memory, and lane l stores rows 8 j + l / 4 at column 4 (l % 4) in 16-byte
+// pieces (a warp instruction covers eight 64-byte row segments).  Each lane
+// storing its own row puts 32 rows 512 bytes apart in every instruction, one
+// transaction per lane (~2 us per CTA).  Kept out of line: the chunk loop's code
+// is sensitive to what surrounds it (the same treatment of the initial-state load,
+// as a call before the loop, slowed the loop by 1.5 %).
+__device__ __noinline__ void state_from_tmem(float* blk, float* scr, uint32_t tq, int lane) {
+  float v[32];
+  tmem_ld32(tq, v);
+  tmem_wait_ld();
+  reg_fence(v);
+  const int r0 = lane >> 2, c0 = 4 * (lane & 3);
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      *reinterpret_cast<float4*>(scr + lane * kXposePitch + 4 * k) =
+          make_float4(v[16 * hf + 4 * k], v[16 * hf + 4 * k + 1], v[16 * hf + 4 * k + 2],
+                      v[16 * hf + 4 * k + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      st_stream_f4(blk + (8 * j + r0) * kHead + 16 * hf + c0,
+                   *reinterpret_cast<const float4*>(scr + (8 * j + r0) * kXposePitch + c0));
+    __syncwarp();  // read before the next half is written
   }
 }
 
@@ -1021,15 +1059,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_mma(BAR_ST, static_cast<uint32_t>((nchunks - 1) & 1));
       if (!failed && ns_rows) {
         if (dbg_cta && nchunks - 1 == p.dbg_chunk) dump_state();
-        float* dst = ns_rows + rowv * kHead + 32 * cq;
-        float v[32];
-        tmem_ld32(tq_st, v);
-        tmem_wait_ld();
-        reg_fence(v);
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4)
-          st_stream_f4(dst + q4 * 4,
-                       make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
+        // (the transpose tile is free: every warp is past the last chunk's
+        // inverse, whose scratch it is)
+        state_from_tmem(ns_rows + (32 * quarter) * kHead + 32 * cq, At + warp * kXposeFloats, tq_st,
+                        lane);
       }
     }
   } else if (lane == 0) {
