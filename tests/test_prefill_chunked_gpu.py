@@ -177,6 +177,10 @@ def test_chunked_deterministic():
     [5, 700, 64, 64, 0, 130, 1, 900, 63, 300] * 4,
     # 24 sequences (192 pairs): 23 one-token sequences and the long one last
     [1] * 23 + [1500],
+    # 64 sequences, the most the kernel ranks (lengths rising, so the order reverses)
+    [1 + 37 * i for i in range(64)],
+    # 65 sequences: more than it ranks, run in input order
+    [1 + 37 * i for i in range(65)],
 ])
 def test_chunked_multiwave_longest_first_bitwise(lengths):
     """A call with more (sequence, head) pairs than SMs hands its CTAs out
