@@ -89,6 +89,9 @@ constexpr uint32_t OFF_MISC = OFF_O + 16384;
 constexpr int kXposePitch = 20;
 constexpr int kXposeFloats = 32 * kXposePitch;
 static_assert(OFF_AT + 16 * kXposeFloats * 4 <= OFF_O, "transpose tiles overlap the output tile");
+// the initial state staged by TMA (4 x 16 KiB, 1024-byte aligned for the swizzle)
+// over the inverse's scratch and the output tile, both free before the first chunk
+static_assert(OFF_AT % 1024 == 0 && OFF_AT + 65536 <= OFF_MISC, "staged state tile");
 // Per-token tables of one chunk (floats), double-buffered by chunk parity.
 constexpr int G_GAM = 0;     // gamma_t * log2(e) (cumulative log-decay)
 constexpr int G_BET = 64;    // beta_t (0 past the end of the sequence)
@@ -121,7 +124,7 @@ constexpr uint32_t kTmaBytes = 2 * kKQStage / 2 + kVStage;  // K 16K + Q 16K + V
 // RDY_T1: warps 12-15, once the T~ rows 32-63 are written).
 enum : int {
   BAR_TMA0 = 0, BAR_TMA1, BAR_M1, BAR_KQS, BAR_M3, BAR_PV, BAR_ST,
-  RDY_S, RDY_T, RDY_V, BAR_END, RDY_T1, kNumBars
+  RDY_S, RDY_T, RDY_V, BAR_END, RDY_T1, BAR_STATE, kNumBars
 };
 
 struct ChunkParams {
@@ -271,14 +274,18 @@ __device__ __noinline__ void rank_longest_first(const int64_t* cu, int ns, int64
 
 // L2: q/k L2 norm folded in as per-token factors; JOBS: the segmented prefill's
 // job table (identity start, v = 0, no outputs, optional final state); ORDER
-// (without JOBS): CTA group r runs the r-th longest sequence.  All are separate
-// instantiations so the plain kernel carries none of it.
-template <bool DEBUG, bool L2, bool JOBS, bool ORDER>
+// (without JOBS): CTA group r runs the r-th longest sequence; STAGED (without
+// JOBS, a given initial state): the issue thread brings the initial state tile
+// into shared memory by TMA (tm_s).  All are separate instantiations so the plain
+// kernel carries none of it (as a runtime switch, the staging slowed the chunk
+// loop of every call by ~2.4 %).
+template <bool DEBUG, bool L2, bool JOBS, bool ORDER, bool STAGED>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_chunked_kernel(const __grid_constant__ CUtensorMap tm_q,
                                const __grid_constant__ CUtensorMap tm_k,
                                const __grid_constant__ CUtensorMap tm_v,
                                const __grid_constant__ CUtensorMap tm_o,
+                               const __grid_constant__ CUtensorMap tm_s,
                                const __grid_constant__ PeerMaps pm, const ChunkParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Align by offsetting the __shared__ array itself (not through an integer
@@ -322,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
       if (p.tma_out) prefetch_tmap(&tm_o);
+      if (STAGED) prefetch_tmap(&tm_s);
     }
     if (warp == 0) {
       tmem_alloc(tmem_slot, kTmemCols);
@@ -513,13 +521,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       const float* src = state_in && !init_identity ? state_in + rowv * kHead + 32 * cq : nullptr;
       float v[32];
+      if constexpr (STAGED) {
+        // the issue thread loads the tile by TMA, columns [32 c, 32 c + 32) at
+        // OFF_AT + 16 KiB c in the 128-byte swizzle, so this thread's eight
+        // 16-byte pieces of row rowv come from shared memory (four wavefronts per
+        // warp read, the fewest) instead of 512-byte-strided global loads (one
+        // transaction per lane)
+        wait_mma(BAR_STATE, 0u);
+        const uint32_t srow = sb + OFF_AT + cq * 16384 + rowv * 128;
 #pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4) {
-        float4 x = src ? ld_stream_f4(src + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[4 * q4] = x.x;
-        v[4 * q4 + 1] = x.y;
-        v[4 * q4 + 2] = x.z;
-        v[4 * q4 + 3] = x.w;
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const uint4 w = lds128(srow + ((q4 ^ (rowv & 7)) << 4));
+          v[4 * q4] = __uint_as_float(w.x);
+          v[4 * q4 + 1] = __uint_as_float(w.y);
+          v[4 * q4 + 2] = __uint_as_float(w.z);
+          v[4 * q4 + 3] = __uint_as_float(w.w);
+        }
+      } else {
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          float4 x = src ? ld_stream_f4(src + q4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[4 * q4] = x.x;
+          v[4 * q4 + 1] = x.y;
+          v[4 * q4 + 2] = x.z;
+          v[4 * q4 + 3] = x.w;
+        }
       }
       if (init_identity) {
 #pragma unroll
@@ -1126,6 +1152,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
 
+    // the initial state tile (plain and ORDER instantiations), before the first chunk
+    constexpr bool state_tma = STAGED;
+    if (state_tma) {
+      mbar_arrive_expect_tx(&bars[BAR_STATE], kHead * kHead * 4);
+      const int row0 = static_cast<int>((n * p.Hv + h) * kHead);
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tma_load_2d(smem + OFF_AT + c * 16384, &tm_s, &bars[BAR_STATE], 32 * c, row0);
+    }
     issue_loads(0);
     if (nchunks > 1) issue_loads(1);
     bool ok = mma1(0);
@@ -1231,6 +1266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bulk_wait_all();
     mma_commit(&bars[BAR_END]);
     if (!mbar_wait(&bars[BAR_END], 0, kTimeoutNs)) ok = false;
+    if (state_tma && !mbar_wait(&bars[BAR_STATE], 0, kTimeoutNs)) ok = false;
     for (int cc = tma_done; cc < tma_issued; ++cc)
       if (!mbar_wait(&bars[BAR_TMA0 + (cc & 1)], static_cast<uint32_t>((cc >> 1) & 1), kTimeoutNs))
         ok = false;
@@ -1292,10 +1328,26 @@ cudaError_t encode_head_map(CUtensorMap* m, const void* base, int64_t heads, int
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// The initial state [rows = N Hv 128][128] fp32, box 32 columns x 128 rows (one
+// column quarter of a tile), 128-byte swizzle.
+cudaError_t encode_state_map(CUtensorMap* m, const void* base, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHead), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHead) * 4};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // Encoding a tensor map costs about a microsecond of host time and a call needs
-// four; a small per-thread cache of encoded maps, keyed by what the encoding
-// depends on (base address, heads, T), skips it when a caller reuses its
-// buffers (a serving loop, or the caching allocator handing back a block).
+// four or five; a small per-thread cache of encoded maps, keyed by what the
+// encoding depends on (base address, heads, T; heads = 0 marks a state map of T
+// rows), skips it when a caller reuses its buffers (a serving loop, or the caching
+// allocator handing back a block).
 cudaError_t make_head_map(CUtensorMap* m, const void* base, int64_t heads, int64_t T) {
   struct Entry {
     const void* base;
@@ -1310,7 +1362,7 @@ cudaError_t make_head_map(CUtensorMap* m, const void* base, int64_t heads, int64
       *m = cache[i].map;
       return cudaSuccess;
     }
-  const cudaError_t e = encode_head_map(m, base, heads, T);
+  const cudaError_t e = heads == 0 ? encode_state_map(m, base, T) : encode_head_map(m, base, heads, T);
   if (e != cudaSuccess) return e;
   cache[next] = Entry{base, heads, T, *m};
   next = (next + 1) % kEntries;
@@ -1326,7 +1378,7 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
     return cudaMemsetAsync(a.new_state, 0,
                            static_cast<size_t>(a.N) * a.Hv * kHead * kHead * sizeof(float), s);
   }
-  CUtensorMap mq, mk, mv, mo;
+  CUtensorMap mq, mk, mv, mo, ms;
   PeerMaps pm;
   memset(&pm, 0, sizeof(pm));
   cudaError_t e;
@@ -1339,20 +1391,39 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   for (int r = 0; r < a.n_peers; ++r)
     if (reinterpret_cast<uintptr_t>(a.peer_out[r]) % 16 != 0) tma_out = 0;
   memset(&mo, 0, sizeof(mo));
+  memset(&ms, 0, sizeof(ms));
+  // The initial state by TMA (the STAGED instantiation) when the sequences average
+  // at most 16 chunks: it saves ~1.5 us per CTA (a 64 KiB state read as 512-byte-
+  // strided rows costs a transaction per lane), but its chunk loop runs ~2.4 %
+  // slower (~0.1 us per chunk), so long chains keep the plain kernel (measured:
+  // one-chunk calls 11.8 -> 10.2 us, BASELINE config 2 164.8 -> 158.7 us, a 57-way
+  // even split of 8192 tokens 93.2 -> 87.0 us; config 3, 256 chunks per CTA, would
+  // go 1043.5 -> 1065 us).  Not for job tables, whose start states lie in two
+  // buffers; TMA wants a 16-byte aligned base.
+  const int64_t state_rows = a.N * a.Hv * kHead;
+  const int tma_state = (!a.jobs && a.state && reinterpret_cast<uintptr_t>(a.state) % 16 == 0 &&
+                         state_rows < 0x7fffffffLL && a.T <= 16 * kChunk * a.N) ? 1 : 0;
+  if (tma_state && (e = make_head_map(&ms, a.state, 0, state_rows)) != cudaSuccess) return e;
   if (tma_out && (e = make_head_map(&mo, a.out, out_heads, a.T)) != cudaSuccess) return e;
   for (int r = 0; tma_out && r < a.n_peers; ++r)
     if ((e = make_head_map(&pm.m[r], a.peer_out[r], out_heads, a.T)) != cudaSuccess) return e;
-  auto kernel = gdn_prefill_chunked_kernel<DEBUG, false, false, false>;
+  auto kernel = gdn_prefill_chunked_kernel<DEBUG, false, false, false, false>;
   const bool order = !a.jobs && a.N <= kOrderMaxSeqs && a.N * a.Hv > device_sm_count();
-  const int variant = (a.qk_l2norm ? 1 : 0) + (a.jobs ? 2 : 0) + (order ? 4 : 0);
+  // (jobs x {l2}) or (plain x {l2} x {order} x {staged})
+  const int variant = a.jobs ? (a.qk_l2norm ? 1 : 0)
+                             : 2 + (a.qk_l2norm ? 1 : 0) + (order ? 2 : 0) + (tma_state ? 4 : 0);
   if constexpr (!DEBUG) {
-    constexpr decltype(kernel) kernels[6] = {
-        gdn_prefill_chunked_kernel<false, false, false, false>,
-        gdn_prefill_chunked_kernel<false, true, false, false>,
-        gdn_prefill_chunked_kernel<false, false, true, false>,
-        gdn_prefill_chunked_kernel<false, true, true, false>,
-        gdn_prefill_chunked_kernel<false, false, false, true>,
-        gdn_prefill_chunked_kernel<false, true, false, true>};
+    constexpr decltype(kernel) kernels[10] = {
+        gdn_prefill_chunked_kernel<false, false, true, false, false>,
+        gdn_prefill_chunked_kernel<false, true, true, false, false>,
+        gdn_prefill_chunked_kernel<false, false, false, false, false>,
+        gdn_prefill_chunked_kernel<false, true, false, false, false>,
+        gdn_prefill_chunked_kernel<false, false, false, true, false>,
+        gdn_prefill_chunked_kernel<false, true, false, true, false>,
+        gdn_prefill_chunked_kernel<false, false, false, false, true>,
+        gdn_prefill_chunked_kernel<false, true, false, false, true>,
+        gdn_prefill_chunked_kernel<false, false, false, true, true>,
+        gdn_prefill_chunked_kernel<false, true, false, true, true>};
     kernel = kernels[variant];
   } else if (a.jobs || a.qk_l2norm) {
     return cudaErrorInvalidValue;  // the debug build covers the plain kernel only
@@ -1368,7 +1439,7 @@ cudaError_t launch_impl(const PrefillArgs& a, float* debug, int dbg_seq, int dbg
   for (int r = 0; r < a.n_peers; ++r) p.peer_out[r] = static_cast<__nv_bfloat16*>(a.peer_out[r]);
   const int64_t ctas = (a.jobs ? a.njobs : a.N) * a.Hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  kernel<<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, pm, p);
+  kernel<<<static_cast<unsigned>(ctas), kThreads, kSmemBytes, s>>>(mq, mk, mv, mo, ms, pm, p);
   return cudaGetLastError();
 }
 
