@@ -208,6 +208,30 @@ def test_chunked_multiwave_longest_first_bitwise(lengths):
         assert torch.equal(s1[0], ns[i]), f"sequence {i} ({e0 - b0} tokens): final state differs"
 
 
+@pytest.mark.parametrize("geom", [(4, 8), (16, 32)])
+def test_chunked_staged_state_matches_plain_bitwise(geom):
+    """Calls of short sequences (T <= 1024 N) with an initial state read it through
+    shared memory (TMA) instead of from global memory.  One 1100-token sequence
+    alone (18 chunks on average: the plain kernel) and with an empty sequence beside
+    it (9 on average: the staged kernel) must give the same output and final state
+    bit for bit, the empty one a zero state."""
+    Hq, Hv = geom
+    one = W.make_prefill_inputs([1100], Hq, Hv, seed=23)
+    d1 = PT.to_device(one)
+    o1, s1 = chunked(*d1.args())
+    state2 = torch.cat([d1.state, torch.randn_like(d1.state)])
+    cu2 = torch.tensor([0, 1100, 1100], dtype=torch.int64, device="cuda")
+    d2 = W.PrefillInputs(d1.q, d1.k, d1.v, state2, d1.A_log, d1.a, d1.dt_bias, d1.b, cu2, d1.scale)
+    o2, s2 = chunked(*d2.args())
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+    assert torch.equal(s1[0], s2[0])
+    assert not torch.any(s2[1])
+    o_ref, s_ref = C.prefill(*W.make_prefill_inputs([1100], Hq, Hv, seed=23).args())
+    PT.assert_o_close(o1, o_ref)
+    PT.assert_state_close(s1, s_ref.numpy(), PT.STATE_REL)
+
+
 def test_no_timeout_status_after_runs():
     st = ctypes.c_uint32(0)
     N.check(N.lib().gdn_read_status(ctypes.byref(st), 1))
